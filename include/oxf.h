@@ -1,0 +1,215 @@
+/*
+ * oxf.h — C ABI of the B200 (sm_100a) kernels that replace OxideForge's
+ * cuda-oxide kernel module.
+ *
+ * The reference's device boundary is `#[cuda_module] mod kernels`
+ * (src/cuda/device/module.rs:5-263): 24 `#[kernel]` entry points taking
+ * `#[repr(C)]` slice descriptors {ptr,len} by value (src/cuda/span.rs:7-10,
+ * 45-48), usize/f32 scalars and `BinaryOp` as repr(u8) (src/cuda.rs:3-10).
+ * Each function below names the reference entry point it replaces.
+ *
+ * Conventions
+ *  - All matrices are contiguous row-major f32 in device memory, owned by
+ *    the caller. No entry point allocates device memory; the only scratch
+ *    any of them needs (3xTF32 operand splits) is caller-provided.
+ *  - Every call is asynchronous on the given stream (NULL = legacy default
+ *    stream) and acts on the calling thread's current CUDA device.
+ *  - Every call returns an oxf_status. On error, oxf_last_error_string()
+ *    describes it (thread-local). No entry point aborts the process.
+ *  - Where the reference asserts a shape (`assert!` in the src/cuda/container files),
+ *    the same check returns OXF_ERR_INVALID_ARG. The reference's caps
+ *    (cols <= 1024 for row kernels, M/N/K % 16 for the GEMM) are lifted.
+ */
+#ifndef OXF_H
+#define OXF_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* oxf_stream; /* == cudaStream_t */
+
+typedef enum {
+  OXF_OK = 0,
+  OXF_ERR_INVALID_ARG = 1,
+  OXF_ERR_UNSUPPORTED_SHAPE = 2,
+  OXF_ERR_CUDA = 3,
+  OXF_ERR_TIMEOUT = 4,
+  OXF_ERR_DEVICE_CHECK = 5,
+  OXF_ERR_IO = 6,
+  OXF_ERR_STATE = 7
+} oxf_status;
+
+/* DeviceSliceDescriptor<f32> (span.rs:7-10) and
+ * DeviceSliceMutDescriptor<f32> (span.rs:45-48). */
+typedef struct { const float* ptr; size_t len; } oxf_cslice;
+typedef struct { float* ptr; size_t len; } oxf_slice;
+
+/* BinaryOp, src/cuda.rs:3-10. */
+typedef enum { OXF_ADD = 0, OXF_SUB = 1, OXF_MUL = 2, OXF_DIV = 3 } oxf_binary_op;
+
+/* Activation, src/net/linear.rs:14-19. */
+typedef enum { OXF_ACT_IDENTITY = 0, OXF_ACT_GELU = 1, OXF_ACT_RELU = 2, OXF_ACT_SILU = 3 }
+    oxf_activation;
+
+/* The closures the reference passes to slice_for_each (module.rs:59-67)
+ * cannot cross a C ABI; these are the ones its callers use:
+ *   SCALE        x * p             (Matrix::scale, matrix.rs:30; linear.rs:383)
+ *   ADD_SCALAR   x + p             (matrix.rs:34)
+ *   ACT_FORWARD  act(x)            (linear.rs:225-230), act = (int)p
+ *   ACT_DERIV    act'(x)           (linear.rs:262), act = (int)p
+ *   HALF_SQUARE  0.5 * x * x       (linear.rs:327)                      */
+typedef enum {
+  OXF_UNARY_SCALE = 0,
+  OXF_UNARY_ADD_SCALAR = 1,
+  OXF_UNARY_ACT_FORWARD = 2,
+  OXF_UNARY_ACT_DERIV = 3,
+  OXF_UNARY_HALF_SQUARE = 4
+} oxf_unary_op;
+
+/* ---------------------------------------------------------------- status */
+const char* oxf_last_error_string(void);
+/* Reads and clears the device error word that bounded in-kernel waits set
+ * (0 = none). Synchronises the current device. */
+oxf_status oxf_device_error(uint32_t* code);
+/* Library version string. */
+const char* oxf_version(void);
+
+/* ---------------------------------------------------------------- elementwise */
+/* slice_binary (module.rs:36-43): out = lhs op rhs over min(len). */
+oxf_status oxf_slice_binary(oxf_cslice lhs, oxf_cslice rhs, oxf_slice out, oxf_binary_op op,
+                            oxf_stream stream);
+/* slice_binary_assign (module.rs:48-54): target op= rhs. */
+oxf_status oxf_slice_binary_assign(oxf_slice target, oxf_cslice rhs, oxf_binary_op op,
+                                   oxf_stream stream);
+/* slice_for_each (module.rs:59-64) for the enumerated closures above. */
+oxf_status oxf_slice_unary(oxf_slice span, oxf_unary_op op, float param, oxf_stream stream);
+/* target = target - lr * grad (Linear::learn's scale + Sub, linear.rs:383-390,
+ * fused). */
+oxf_status oxf_sgd_update(oxf_slice target, oxf_cslice grad, float lr, oxf_stream stream);
+/* out = (y - t) * (1/cols): gradient of sum(loss_rows) (no reference
+ * counterpart; loss_rows is linear.rs:325-333). */
+oxf_status oxf_mse_grad(oxf_cslice y, oxf_cslice target, oxf_slice out, size_t cols,
+                        oxf_stream stream);
+/* Linear::loss_rows (linear.rs:325-333) fused: row_loss[r] = mean_j 0.5(y-t)^2. */
+oxf_status oxf_loss_rows(oxf_cslice y, oxf_cslice target, oxf_slice row_loss, size_t cols,
+                         oxf_stream stream);
+
+/* ---------------------------------------------------------------- reductions */
+/* slice_sum + host re-launch loop (module.rs:69-74, span.rs:301-385) as one
+ * launch: *result = sum(span). result is a device pointer to one float. */
+oxf_status oxf_slice_sum(oxf_cslice span, float* result, oxf_stream stream);
+/* slice_max (module.rs:92-97, span.rs:318-333); empty -> f32::MIN. */
+oxf_status oxf_slice_max(oxf_cslice span, float* result, oxf_stream stream);
+/* matrix_sum_rows (module.rs:102-108): result[r] = sum_j M[r,j]. */
+oxf_status oxf_matrix_sum_rows(oxf_cslice matrix, oxf_slice result, size_t cols,
+                               oxf_stream stream);
+/* Column sums: result[j] = sum_r M[r,j]; replaces the reference's bias
+ * gradient sum_rows(transpose(G)) (linear.rs:267-270). If accumulate != 0
+ * the sums are added to result. */
+oxf_status oxf_matrix_sum_cols(oxf_cslice matrix, oxf_slice result, size_t cols, int accumulate,
+                               oxf_stream stream);
+
+/* ---------------------------------------------------------------- row kernels */
+/* matrix_softmax_rows (module.rs:111-116) with matrix_causal_mask
+ * (module.rs:245-250) and the attention scale (attention.rs:372) folded in:
+ * row r of `cols` entries becomes softmax(scale * x) with entries
+ * j > (r % causal_period) masked to -inf first when causal_period != 0. */
+oxf_status oxf_matrix_softmax_rows(oxf_slice matrix, size_t cols, float scale,
+                                   size_t causal_period, oxf_stream stream);
+/* matrix_layer_norm_rows (module.rs:118-127), in place. gamma/beta may be
+ * NULL (the reference is non-affine). */
+oxf_status oxf_matrix_layer_norm_rows(oxf_slice matrix, size_t cols, float epsilon,
+                                      const float* gamma, const float* beta, oxf_stream stream);
+/* rms_norm_assign (module.rs:226-231), in place; gamma may be NULL. */
+oxf_status oxf_rms_norm_assign(oxf_slice matrix, size_t cols, float epsilon, const float* gamma,
+                               oxf_stream stream);
+/* softmax_rows_backward (module.rs:141-151): dx = scale * p*(dy - sum(p*dy)). */
+oxf_status oxf_softmax_rows_backward(oxf_cslice probabilities, oxf_cslice output_gradient,
+                                     oxf_slice result, size_t cols, float scale,
+                                     oxf_stream stream);
+/* layer_norm_backward (module.rs:153-163), non-affine. */
+oxf_status oxf_layer_norm_backward(oxf_cslice input, oxf_cslice output_gradient,
+                                   oxf_slice result, size_t cols, float epsilon,
+                                   oxf_stream stream);
+/* matrix_rms_norm_backward (module.rs:252-262), non-affine. */
+oxf_status oxf_matrix_rms_norm_backward(oxf_cslice input, oxf_cslice output_gradient,
+                                        oxf_slice result, size_t cols, float epsilon,
+                                        oxf_stream stream);
+/* matrix_binary_assign_by_rows (module.rs:129-139): M[i,j] op= row[j]. */
+oxf_status oxf_matrix_binary_assign_by_rows(oxf_slice matrix, oxf_cslice row, size_t cols,
+                                            oxf_binary_op op, oxf_stream stream);
+/* matrix_causal_mask (module.rs:245-250): M[i,j] = -inf for j > i. */
+oxf_status oxf_matrix_causal_mask(oxf_slice matrix, size_t cols, oxf_stream stream);
+/* matrix_transpose (module.rs:193-203): out[cols,rows] = in[rows,cols]^T. */
+oxf_status oxf_matrix_transpose(oxf_cslice input, oxf_slice result, size_t rows, size_t cols,
+                                oxf_stream stream);
+
+/* ---------------------------------------------------------------- GEMM */
+typedef enum { OXF_PREC_TF32 = 0, OXF_PREC_TF32X3 = 1 } oxf_precision;
+
+/* One (batched) GEMM with a fused epilogue:
+ *   acc = alpha * op(A)·op(B)                         [M,N] per batch item
+ *   acc += beta * C          (beta != 0, not with accumulate)
+ *   acc += bias[n]           (bias != NULL)
+ *   acc += R[m,n]            (residual != NULL)
+ *   P[m,n] = acc             (pre_out != NULL: pre-activation store)
+ *   acc *= act'(X[m,n])      (grad_act != IDENTITY, X = aux)
+ *   acc = act(acc)           (act != IDENTITY)
+ *   C = acc, or C += acc atomically (accumulate != 0; allows split_k > 1)
+ * A is [M,K] (a_trans = 0) or stored as [K,M] (a_trans = 1, A = storedᵀ).
+ * B is [K,N] (b_trans = 0) or stored as [N,K] (b_trans = 1).
+ * Leading dimensions are in elements; *_stride are batch strides in
+ * elements (0 = the operand is shared by every batch item). The order
+ * GEMM -> bias -> residual -> activation is Linear::affine_on + activate_on
+ * (linear.rs:185-230). The TF32 path truncates operands to TF32 in the
+ * tensor core; OXF_PREC_TF32X3 splits each operand into hi+lo TF32 parts
+ * (needs `workspace`, see oxf_gemm_workspace_size). */
+typedef struct {
+  int M, N, K, batch;
+  int a_trans, b_trans;
+  const float* A; long long lda; long long stride_a;
+  const float* B; long long ldb; long long stride_b;
+  float* C; long long ldc; long long stride_c;
+  float alpha, beta;
+  const float* bias;
+  const float* residual; long long ldr; long long stride_r;
+  float* pre_out; long long ldp; long long stride_p;
+  const float* aux; long long ldx; long long stride_x;
+  int act;        /* oxf_activation applied last */
+  int grad_act;   /* oxf_activation whose derivative at aux multiplies acc */
+  int accumulate; /* 1: C += result with atomics */
+  int split_k;    /* 0/1 = none; >1 requires accumulate */
+  int precision;  /* oxf_precision */
+  void* workspace; size_t workspace_bytes;
+} oxf_gemm_desc;
+
+/* Fills a descriptor with defaults (batch 1, alpha 1, tight leading dims
+ * for the given shape/transposes, everything else off). */
+void oxf_gemm_desc_init(oxf_gemm_desc* d, int M, int N, int K, int a_trans, int b_trans,
+                        const float* A, const float* B, float* C);
+/* Bytes of workspace the descriptor needs (0 for plain TF32). */
+size_t oxf_gemm_workspace_size(const oxf_gemm_desc* d);
+oxf_status oxf_gemm(const oxf_gemm_desc* d, oxf_stream stream);
+
+/* matrix_multiply (module.rs:179-191) with the reference's argument order:
+ * result[rows,cols] = lhs[rows,len] · rhs[len,cols], TF32 operands, f32
+ * accumulation. The reference asserts rows, cols, len % 16 == 0
+ * (matrix.rs:147-149); this entry point accepts any sizes. */
+oxf_status oxf_matrix_multiply(oxf_cslice lhs, oxf_cslice rhs, oxf_slice result, size_t len,
+                               size_t rows, size_t cols, oxf_stream stream);
+
+/* Reference-algorithm restatement, for measurement only: the reference's
+ * 32x32-tile, 128-thread, mma.sync.m16n8k8 TF32, 2-stage cp.async GEMM
+ * (gemm.rs:202-373) written in CUDA C++. Same contract and asserts as
+ * matrix_multiply (rows, cols, len % 16 == 0). */
+oxf_status oxf_matrix_multiply_refalgo(oxf_cslice lhs, oxf_cslice rhs, oxf_slice result,
+                                       size_t len, size_t rows, size_t cols, oxf_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,174 @@
+/*
+ * oxf_oracle.h — CPU oracle for the OxideForge compute hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY. This is a scalar C restatement of the reference
+ * algorithms (MeccBai/oxide-forge, Rust + cuda-oxide). Only tests/, the
+ * smoke() check in __graft_entry__.py and bench.py's CPU-baseline / reference
+ * arm may load it, and only as the checker or the timed CPU baseline. The
+ * product path (liboxf.so) never links or calls it.
+ *
+ * PARITY UNPINNED: the reference has no tests, golden vectors or fixtures,
+ * and it cannot be built or run here (Rust/cuda-oxide toolchain absent). The
+ * oracle is pinned instead by hand-derived known-answer cases and by golden
+ * fixtures from an independent numpy f64 restatement (tests/golden/).
+ *
+ * Every function cites the reference file:line whose arithmetic it restates.
+ * All matrices are contiguous row-major f32 (the reference's only layout,
+ * docs/api.md "Conventions").
+ */
+#ifndef OXF_ORACLE_H
+#define OXF_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* BinaryOp, src/cuda.rs:3-10 (repr(u8): Add, Sub, Mul, Div). */
+enum { OXO_ADD = 0, OXO_SUB = 1, OXO_MUL = 2, OXO_DIV = 3 };
+/* Activation, src/net/linear.rs:14-19. */
+enum { OXO_IDENTITY = 0, OXO_GELU = 1, OXO_RELU = 2, OXO_SILU = 3 };
+/* NormType, src/net/transformer.rs:7-13. */
+enum { OXO_NORM_RMS = 0, OXO_NORM_LAYER = 1 };
+/* GEMM operand rounding: exact f32 products, TF32 round-to-nearest-away
+ * (cvt.rna.tf32.f32, gemm.rs:286-347), or TF32 truncation (tensor cores that
+ * read raw f32 and drop the low 13 mantissa bits). */
+enum { OXO_GEMM_F32 = 0, OXO_GEMM_TF32_RNA = 1, OXO_GEMM_TF32_RZ = 2 };
+
+/* Number of worker threads used by the threaded entry points (0 = all
+ * online cores). Returns the count now in effect. */
+int oxo_set_threads(int n);
+int oxo_get_threads(void);
+
+float oxo_tf32_rna(float x);
+float oxo_tf32_rz(float x);
+
+/* C[M,N] = alpha * op(A)·op(B) (+ beta*C).  a_trans: A stored as [K,M]
+ * (A = stored^T); b_trans: B stored as [N,K].  Row-major, f32 accumulation in
+ * ascending k.  matrix_multiply_device, gemm.rs:202-373 (reference only has
+ * the NN form; Xᵀ·G and G·Wᵀ go through matrix_transpose, convert.rs:17-63). */
+void oxo_gemm(const float* A, const float* B, float* C, size_t M, size_t N, size_t K,
+              int a_trans, int b_trans, int rounding, float alpha, float beta);
+/* Same arithmetic, threaded over rows of C. */
+void oxo_gemm_mt(const float* A, const float* B, float* C, size_t M, size_t N, size_t K,
+                 int a_trans, int b_trans, int rounding, float alpha, float beta);
+/* f64 reference product of f32 inputs (tolerance budgeting). */
+void oxo_gemm_f64(const float* A, const float* B, double* C, size_t M, size_t N, size_t K,
+                  int a_trans, int b_trans);
+
+/* Elementwise, src/cuda/device/elementwise.rs:5-13,45-68. */
+float oxo_apply_binary(float lhs, float rhs, int op);
+void oxo_binary(const float* lhs, const float* rhs, float* out, size_t n, int op);
+void oxo_binary_assign(float* target, const float* rhs, size_t n, int op);
+/* row.rs:179-191: M[i,j] op= v[j]. */
+void oxo_binary_assign_by_rows(float* m, const float* row, size_t rows, size_t cols, int op);
+
+/* Activation::forward / derivative, linear.rs:21-70. */
+float oxo_act_forward(int act, float x);
+float oxo_act_derivative(int act, float x);
+void oxo_activate(float* x, size_t n, int act);
+
+/* row.rs:16-53 (per-row sum). */
+void oxo_sum_rows(const float* m, float* out, size_t rows, size_t cols);
+/* Column sum = sum_rows(transpose(G)), linear.rs:267-270. */
+void oxo_sum_cols(const float* m, float* out, size_t rows, size_t cols);
+/* layout.rs:9-55. out[cols,rows] = in[rows,cols]^T. */
+void oxo_transpose(const float* in, float* out, size_t rows, size_t cols);
+/* row.rs:5-14: M[i,j] = -inf for j > i; rows counted modulo `period`
+ * (period = rows gives the reference's single-matrix behaviour). */
+void oxo_causal_mask(float* m, size_t rows, size_t cols, size_t period);
+
+/* In-place row softmax, row.rs:55-113; `scale` multiplies the row first
+ * (attention.rs:372 applies 1/sqrt(d) before softmax); causal_period != 0
+ * masks j > (row % causal_period) first (attention.rs:347-357). */
+void oxo_softmax_rows(float* m, size_t rows, size_t cols, float scale, size_t causal_period);
+/* row.rs:115-177 (eps = 1e-5 at norm.rs:45). Optional gamma/beta (may be NULL). */
+void oxo_layer_norm_rows(float* m, size_t rows, size_t cols, float eps, const float* gamma,
+                         const float* beta);
+/* row.rs:349-396. Optional gamma. */
+void oxo_rms_norm_rows(float* m, size_t rows, size_t cols, float eps, const float* gamma);
+/* row.rs:193-237: dx = p*(dy - sum(p*dy)); `scale` multiplies dx afterwards
+ * (attention.rs:302-304). */
+void oxo_softmax_backward(const float* p, const float* dy, float* dx, size_t rows, size_t cols,
+                          float scale);
+/* row.rs:239-347. */
+void oxo_layer_norm_backward(const float* x, const float* dy, float* dx, size_t rows, size_t cols,
+                             float eps);
+/* row.rs:398-468. */
+void oxo_rms_norm_backward(const float* x, const float* dy, float* dx, size_t rows, size_t cols,
+                           float eps);
+
+/* Linear::loss_rows, linear.rs:325-333: per row mean_j 0.5*(y-t)^2. */
+void oxo_loss_rows(const float* y, const float* t, float* row_loss, size_t rows, size_t cols);
+/* Gradient of sum_rows(loss_rows) w.r.t. y: (y - t)/cols. (No reference
+ * counterpart; defined to match loss_rows.) */
+void oxo_mse_grad(const float* y, const float* t, float* g, size_t rows, size_t cols);
+
+/* ---- Executors (single sequence, reference semantics) ------------------- */
+
+/* One Linear layer: W [in,out] row-major, optional bias [out]. */
+typedef struct {
+    float* w;
+    float* b; /* NULL = no bias */
+    size_t in, out;
+    int act;
+} oxo_linear;
+
+/* Linear::forward, linear.rs:116-206: Y = act(X·W + b + R). If `pre` is not
+ * NULL the pre-activation X·W + b + R is stored there too. `rounding` selects
+ * the GEMM operand rounding. */
+void oxo_linear_forward(const oxo_linear* l, const float* x, const float* residual, float* y,
+                        float* pre, size_t rows, int rounding);
+
+/* MLP (MlpExecutor, mlp.rs:14-168). res_start/res_end < 0: no residual. */
+typedef struct {
+    oxo_linear* layers;
+    size_t n_layers;
+    int res_start, res_end;
+} oxo_mlp;
+
+/* mlp.rs:53-85. `tape` (may be NULL) receives layer inputs: tape[i] is an
+ * [rows, layers[i].in] buffer the caller owns, tape[0] = input copy. */
+void oxo_mlp_forward(const oxo_mlp* m, const float* x, float* y, float** tape, size_t rows,
+                     int rounding);
+/* mlp.rs:121-168: backward with immediate SGD per layer (linear.rs:373-391).
+ * Writes dX to dx. */
+void oxo_mlp_backward(oxo_mlp* m, float* const* tape, const float* dy, float* dx, size_t rows,
+                      float lr, int rounding);
+
+/* Single-head, single-block Post-Norm transformer
+ * (encoder.rs:94-187, inference.rs:76-109, attention.rs:221-321). */
+typedef struct {
+    size_t seq, hidden, out;
+    int norm;     /* OXO_NORM_* */
+    oxo_linear q, k, v;
+    float* position; /* [seq, hidden] */
+    oxo_mlp ffn;
+    oxo_linear o;
+} oxo_transformer;
+
+/* Inference forward (InferenceTransformer::forward; causal != 0 gives the
+ * decoder's forward_mask, decoder.rs:50-52). y: [seq, out]. */
+void oxo_transformer_forward(const oxo_transformer* t, const float* x, float* y, int causal,
+                             int rounding);
+
+/* Training step on one sequence: TrainingTransformer::forward followed by
+ * backward(dL/dy, lr) with the reference's immediate per-layer SGD
+ * (encoder.rs:114-186). dL/dy = oxo_mse_grad(y, target). Writes y (output),
+ * row_loss [seq] (may be NULL) and dx (input gradient, may be NULL).
+ * If `grads` is not NULL and lr == 0, the parameter gradients are ADDED
+ * into it in checkpoint cursor order (q, k, v, position, ffn layers, out;
+ * weight then bias per Linear) instead of being applied. */
+void oxo_transformer_train_step(oxo_transformer* t, const float* x, const float* target,
+                                float* y, float* row_loss, float* dx, float lr, float* grads,
+                                int rounding);
+
+/* Number of f32 parameters in cursor order (inference.rs:52-66). */
+size_t oxo_transformer_param_count(const oxo_transformer* t);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,314 @@
+// abi.cu — the extern "C" entry points declared in include/oxf.h.
+//
+// Each function validates its arguments the way the reference's launchers
+// assert them (src/cuda/container/*.rs), minus the caps this build lifts,
+// then forwards to the kernels in rows.cu / gemm.cu on the caller's stream.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "../../include/oxf.h"
+#include "status.cuh"
+
+namespace oxf {
+
+// rows.cu
+oxf_status rows_softmax(float*, long long, long long, float, long long, cudaStream_t);
+oxf_status rows_softmax_bwd(const float*, const float*, float*, long long, long long, float,
+                            cudaStream_t);
+oxf_status rows_layernorm(float*, long long, long long, float, const float*, const float*,
+                          cudaStream_t);
+oxf_status rows_layernorm_bwd(const float*, const float*, float*, long long, long long, float,
+                              cudaStream_t);
+oxf_status rows_rmsnorm(float*, long long, long long, float, const float*, cudaStream_t);
+oxf_status rows_rmsnorm_bwd(const float*, const float*, float*, long long, long long, float,
+                            cudaStream_t);
+oxf_status rows_sum(const float*, float*, long long, long long, cudaStream_t);
+oxf_status rows_loss(const float*, const float*, float*, long long, long long, cudaStream_t);
+oxf_status ew_binary(const float*, const float*, float*, long long, int, cudaStream_t);
+oxf_status ew_binary_assign(float*, const float*, long long, int, cudaStream_t);
+oxf_status ew_unary(float*, long long, int, float, cudaStream_t);
+oxf_status ew_sgd(float*, const float*, long long, float, cudaStream_t);
+oxf_status ew_mse_grad(const float*, const float*, float*, long long, long long, cudaStream_t);
+oxf_status ew_by_rows(float*, const float*, long long, long long, int, cudaStream_t);
+oxf_status causal_mask(float*, long long, long long, cudaStream_t);
+oxf_status cols_sum(const float*, float*, long long, long long, int, cudaStream_t);
+oxf_status transpose(const float*, float*, long long, long long, cudaStream_t);
+oxf_status slice_reduce(const float*, long long, float*, int, cudaStream_t);
+// gemm.cu
+oxf_status gemm_run(const oxf_gemm_desc*, cudaStream_t);
+size_t gemm_workspace_bytes(const oxf_gemm_desc*);
+oxf_status gemm_refalgo(const float*, const float*, float*, size_t, size_t, size_t,
+                        cudaStream_t);
+oxf_status gemm_read_device_error(uint32_t*);
+
+namespace {
+thread_local char g_last_error[512] = "";
+}
+
+oxf_status set_error(oxf_status st, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return st;
+}
+
+}  // namespace oxf
+
+using namespace oxf;
+
+namespace {
+
+inline cudaStream_t S(oxf_stream s) { return reinterpret_cast<cudaStream_t>(s); }
+
+oxf_status need(bool cond, const char* what) {
+  return cond ? OXF_OK : set_error(OXF_ERR_INVALID_ARG, "%s", what);
+}
+
+#define OXF_TRY(x)                   \
+  do {                               \
+    oxf_status _st = (x);            \
+    if (_st != OXF_OK) return _st;   \
+  } while (0)
+
+bool valid_op(int op) { return op >= OXF_ADD && op <= OXF_DIV; }
+bool valid_act(int a) { return a >= OXF_ACT_IDENTITY && a <= OXF_ACT_SILU; }
+
+// rows = len / cols with the reference's shape checks: a row kernel needs
+// cols > 0 and a whole number of rows (norm.rs:12,30,54; rows.rs:73).
+oxf_status rows_of(size_t len, size_t cols, long long* rows, const char* who) {
+  if (len == 0) {
+    *rows = 0;
+    return OXF_OK;
+  }
+  if (cols == 0) return set_error(OXF_ERR_INVALID_ARG, "%s: cols must be > 0", who);
+  if (len % cols) return set_error(OXF_ERR_INVALID_ARG, "%s: len %% cols != 0", who);
+  *rows = static_cast<long long>(len / cols);
+  return OXF_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* oxf_last_error_string(void) { return g_last_error; }
+
+const char* oxf_version(void) { return "oxf-b200 0.1 (sm_100a)"; }
+
+oxf_status oxf_device_error(uint32_t* code) {
+  if (!code) return set_error(OXF_ERR_INVALID_ARG, "oxf_device_error: null code");
+  OXF_TRY(check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize"));
+  return gemm_read_device_error(code);
+}
+
+// ---------------------------------------------------------------- elementwise
+oxf_status oxf_slice_binary(oxf_cslice lhs, oxf_cslice rhs, oxf_slice out, oxf_binary_op op,
+                            oxf_stream stream) {
+  OXF_TRY(need(valid_op(op), "oxf_slice_binary: bad op"));
+  size_t n = out.len < lhs.len ? out.len : lhs.len;
+  n = n < rhs.len ? n : rhs.len;  // elementwise.rs:53 bounds all three
+  if (n && (!lhs.ptr || !rhs.ptr || !out.ptr))
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_slice_binary: null pointer");
+  return ew_binary(lhs.ptr, rhs.ptr, out.ptr, static_cast<long long>(n), op, S(stream));
+}
+
+oxf_status oxf_slice_binary_assign(oxf_slice target, oxf_cslice rhs, oxf_binary_op op,
+                                   oxf_stream stream) {
+  OXF_TRY(need(valid_op(op), "oxf_slice_binary_assign: bad op"));
+  const size_t n = target.len < rhs.len ? target.len : rhs.len;  // elementwise.rs:65
+  if (n && (!target.ptr || !rhs.ptr))
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_slice_binary_assign: null pointer");
+  return ew_binary_assign(target.ptr, rhs.ptr, static_cast<long long>(n), op, S(stream));
+}
+
+oxf_status oxf_slice_unary(oxf_slice span, oxf_unary_op op, float param, oxf_stream stream) {
+  if (op < OXF_UNARY_SCALE || op > OXF_UNARY_HALF_SQUARE)
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_slice_unary: bad op");
+  if ((op == OXF_UNARY_ACT_FORWARD || op == OXF_UNARY_ACT_DERIV) &&
+      !valid_act(static_cast<int>(param)))
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_slice_unary: bad activation");
+  if (span.len && !span.ptr) return set_error(OXF_ERR_INVALID_ARG, "oxf_slice_unary: null");
+  return ew_unary(span.ptr, static_cast<long long>(span.len), op, param, S(stream));
+}
+
+oxf_status oxf_sgd_update(oxf_slice target, oxf_cslice grad, float lr, oxf_stream stream) {
+  OXF_TRY(need(target.len == grad.len, "oxf_sgd_update: length mismatch"));
+  if (target.len && (!target.ptr || !grad.ptr))
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_sgd_update: null pointer");
+  return ew_sgd(target.ptr, grad.ptr, static_cast<long long>(target.len), lr, S(stream));
+}
+
+oxf_status oxf_mse_grad(oxf_cslice y, oxf_cslice target, oxf_slice out, size_t cols,
+                        oxf_stream stream) {
+  OXF_TRY(need(y.len == target.len && y.len == out.len, "oxf_mse_grad: length mismatch"));
+  long long rows = 0;
+  OXF_TRY(rows_of(y.len, cols, &rows, "oxf_mse_grad"));
+  return ew_mse_grad(y.ptr, target.ptr, out.ptr, static_cast<long long>(y.len),
+                     static_cast<long long>(cols ? cols : 1), S(stream));
+}
+
+oxf_status oxf_loss_rows(oxf_cslice y, oxf_cslice target, oxf_slice row_loss, size_t cols,
+                         oxf_stream stream) {
+  OXF_TRY(need(y.len == target.len, "oxf_loss_rows: length mismatch"));
+  long long rows = 0;
+  OXF_TRY(rows_of(y.len, cols, &rows, "oxf_loss_rows"));
+  OXF_TRY(need(row_loss.len >= static_cast<size_t>(rows), "oxf_loss_rows: result too short"));
+  return rows_loss(y.ptr, target.ptr, row_loss.ptr, rows, static_cast<long long>(cols),
+                   S(stream));
+}
+
+// ---------------------------------------------------------------- reductions
+oxf_status oxf_slice_sum(oxf_cslice span, float* result, oxf_stream stream) {
+  OXF_TRY(need(result != nullptr, "oxf_slice_sum: null result"));
+  return slice_reduce(span.ptr, static_cast<long long>(span.len), result, 0, S(stream));
+}
+
+oxf_status oxf_slice_max(oxf_cslice span, float* result, oxf_stream stream) {
+  OXF_TRY(need(result != nullptr, "oxf_slice_max: null result"));
+  return slice_reduce(span.ptr, static_cast<long long>(span.len), result, 1, S(stream));
+}
+
+oxf_status oxf_matrix_sum_rows(oxf_cslice matrix, oxf_slice result, size_t cols,
+                               oxf_stream stream) {
+  long long rows = 0;
+  OXF_TRY(rows_of(matrix.len, cols, &rows, "oxf_matrix_sum_rows"));
+  OXF_TRY(need(result.len >= static_cast<size_t>(rows), "oxf_matrix_sum_rows: result too short"));
+  return rows_sum(matrix.ptr, result.ptr, rows, static_cast<long long>(cols), S(stream));
+}
+
+oxf_status oxf_matrix_sum_cols(oxf_cslice matrix, oxf_slice result, size_t cols, int accumulate,
+                               oxf_stream stream) {
+  long long rows = 0;
+  OXF_TRY(rows_of(matrix.len, cols, &rows, "oxf_matrix_sum_cols"));
+  OXF_TRY(need(result.len >= cols, "oxf_matrix_sum_cols: result too short"));
+  return cols_sum(matrix.ptr, result.ptr, rows, static_cast<long long>(cols), accumulate,
+                  S(stream));
+}
+
+// ---------------------------------------------------------------- row kernels
+oxf_status oxf_matrix_softmax_rows(oxf_slice matrix, size_t cols, float scale,
+                                   size_t causal_period, oxf_stream stream) {
+  long long rows = 0;
+  OXF_TRY(rows_of(matrix.len, cols, &rows, "oxf_matrix_softmax_rows"));
+  return rows_softmax(matrix.ptr, rows, static_cast<long long>(cols), scale,
+                      static_cast<long long>(causal_period), S(stream));
+}
+
+oxf_status oxf_matrix_layer_norm_rows(oxf_slice matrix, size_t cols, float epsilon,
+                                      const float* gamma, const float* beta, oxf_stream stream) {
+  long long rows = 0;
+  OXF_TRY(rows_of(matrix.len, cols, &rows, "oxf_matrix_layer_norm_rows"));
+  return rows_layernorm(matrix.ptr, rows, static_cast<long long>(cols), epsilon, gamma, beta,
+                        S(stream));
+}
+
+oxf_status oxf_rms_norm_assign(oxf_slice matrix, size_t cols, float epsilon, const float* gamma,
+                               oxf_stream stream) {
+  long long rows = 0;
+  OXF_TRY(rows_of(matrix.len, cols, &rows, "oxf_rms_norm_assign"));
+  return rows_rmsnorm(matrix.ptr, rows, static_cast<long long>(cols), epsilon, gamma, S(stream));
+}
+
+oxf_status oxf_softmax_rows_backward(oxf_cslice probabilities, oxf_cslice output_gradient,
+                                     oxf_slice result, size_t cols, float scale,
+                                     oxf_stream stream) {
+  OXF_TRY(need(probabilities.len == output_gradient.len && probabilities.len == result.len,
+               "oxf_softmax_rows_backward: shape mismatch"));  // norm.rs:78-80
+  long long rows = 0;
+  OXF_TRY(rows_of(result.len, cols, &rows, "oxf_softmax_rows_backward"));
+  return rows_softmax_bwd(probabilities.ptr, output_gradient.ptr, result.ptr, rows,
+                          static_cast<long long>(cols), scale, S(stream));
+}
+
+oxf_status oxf_layer_norm_backward(oxf_cslice input, oxf_cslice output_gradient,
+                                   oxf_slice result, size_t cols, float epsilon,
+                                   oxf_stream stream) {
+  OXF_TRY(need(input.len == output_gradient.len && input.len == result.len,
+               "oxf_layer_norm_backward: shape mismatch"));  // norm.rs:104-106
+  long long rows = 0;
+  OXF_TRY(rows_of(result.len, cols, &rows, "oxf_layer_norm_backward"));
+  return rows_layernorm_bwd(input.ptr, output_gradient.ptr, result.ptr, rows,
+                            static_cast<long long>(cols), epsilon, S(stream));
+}
+
+oxf_status oxf_matrix_rms_norm_backward(oxf_cslice input, oxf_cslice output_gradient,
+                                        oxf_slice result, size_t cols, float epsilon,
+                                        oxf_stream stream) {
+  OXF_TRY(need(input.len == output_gradient.len && input.len == result.len,
+               "oxf_matrix_rms_norm_backward: shape mismatch"));  // norm.rs:130-132
+  long long rows = 0;
+  OXF_TRY(rows_of(result.len, cols, &rows, "oxf_matrix_rms_norm_backward"));
+  return rows_rmsnorm_bwd(input.ptr, output_gradient.ptr, result.ptr, rows,
+                          static_cast<long long>(cols), epsilon, S(stream));
+}
+
+oxf_status oxf_matrix_binary_assign_by_rows(oxf_slice matrix, oxf_cslice row, size_t cols,
+                                            oxf_binary_op op, oxf_stream stream) {
+  OXF_TRY(need(valid_op(op), "oxf_matrix_binary_assign_by_rows: bad op"));
+  OXF_TRY(need(row.len == cols, "oxf_matrix_binary_assign_by_rows: cols != row.len"));  // rows.rs:18
+  long long rows = 0;
+  OXF_TRY(rows_of(matrix.len, cols, &rows, "oxf_matrix_binary_assign_by_rows"));
+  return ew_by_rows(matrix.ptr, row.ptr, static_cast<long long>(matrix.len),
+                    static_cast<long long>(cols ? cols : 1), op, S(stream));
+}
+
+oxf_status oxf_matrix_causal_mask(oxf_slice matrix, size_t cols, oxf_stream stream) {
+  long long rows = 0;
+  OXF_TRY(rows_of(matrix.len, cols, &rows, "oxf_matrix_causal_mask"));
+  return causal_mask(matrix.ptr, rows, static_cast<long long>(cols), S(stream));
+}
+
+oxf_status oxf_matrix_transpose(oxf_cslice input, oxf_slice result, size_t rows, size_t cols,
+                                oxf_stream stream) {
+  OXF_TRY(need(input.len == rows * cols && result.len == rows * cols,
+               "oxf_matrix_transpose: shape mismatch"));
+  return transpose(input.ptr, result.ptr, static_cast<long long>(rows),
+                   static_cast<long long>(cols), S(stream));
+}
+
+// ---------------------------------------------------------------- GEMM
+void oxf_gemm_desc_init(oxf_gemm_desc* d, int M, int N, int K, int a_trans, int b_trans,
+                        const float* A, const float* B, float* C) {
+  std::memset(d, 0, sizeof(*d));
+  d->M = M; d->N = N; d->K = K; d->batch = 1;
+  d->a_trans = a_trans; d->b_trans = b_trans;
+  d->A = A; d->lda = a_trans ? M : K;
+  d->B = B; d->ldb = b_trans ? K : N;
+  d->C = C; d->ldc = N;
+  d->alpha = 1.0f;
+  d->ldr = d->ldp = d->ldx = N;
+  d->act = d->grad_act = OXF_ACT_IDENTITY;
+  d->precision = OXF_PREC_TF32;
+}
+
+size_t oxf_gemm_workspace_size(const oxf_gemm_desc* d) { return gemm_workspace_bytes(d); }
+
+oxf_status oxf_gemm(const oxf_gemm_desc* d, oxf_stream stream) {
+  if (d && (!valid_act(d->act) || !valid_act(d->grad_act)))
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: bad activation");
+  return gemm_run(d, S(stream));
+}
+
+oxf_status oxf_matrix_multiply(oxf_cslice lhs, oxf_cslice rhs, oxf_slice result, size_t len,
+                               size_t rows, size_t cols, oxf_stream stream) {
+  OXF_TRY(need(lhs.len >= rows * len && rhs.len >= len * cols && result.len >= rows * cols,
+               "oxf_matrix_multiply: slice shorter than its shape"));
+  if (rows > 0x7fffffffu || cols > 0x7fffffffu || len > 0x7fffffffu)
+    return set_error(OXF_ERR_UNSUPPORTED_SHAPE, "oxf_matrix_multiply: dimension too large");
+  oxf_gemm_desc d;
+  oxf_gemm_desc_init(&d, static_cast<int>(rows), static_cast<int>(cols), static_cast<int>(len), 0,
+                     0, lhs.ptr, rhs.ptr, result.ptr);
+  return gemm_run(&d, S(stream));
+}
+
+oxf_status oxf_matrix_multiply_refalgo(oxf_cslice lhs, oxf_cslice rhs, oxf_slice result,
+                                       size_t len, size_t rows, size_t cols, oxf_stream stream) {
+  OXF_TRY(need(lhs.len >= rows * len && rhs.len >= len * cols && result.len >= rows * cols,
+               "oxf_matrix_multiply_refalgo: slice shorter than its shape"));
+  return gemm_refalgo(lhs.ptr, rhs.ptr, result.ptr, len, rows, cols, S(stream));
+}
+
+}  // extern "C"

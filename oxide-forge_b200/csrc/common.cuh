@@ -1,0 +1,69 @@
+// common.cuh — device arithmetic shared by the GEMM epilogue and the
+// elementwise/row kernels.
+#pragma once
+#include <cuda_runtime.h>
+
+#include "../../include/oxf.h"
+
+namespace oxf {
+
+// apply_binary, src/cuda/device/elementwise.rs:5-13.
+__device__ __forceinline__ float apply_binary(float lhs, float rhs, int op) {
+  switch (op) {
+    case OXF_ADD: return lhs + rhs;
+    case OXF_SUB: return lhs - rhs;
+    case OXF_MUL: return lhs * rhs;
+    default: return lhs / rhs;
+  }
+}
+
+// Activation::forward / derivative, src/net/linear.rs:21-70 (tanh GELU with
+// GELU_SCALE = 0.7978846, GELU_CUBIC = 0.044715).
+constexpr float kGeluScale = 0.7978846f;
+constexpr float kGeluCubic = 0.044715f;
+
+__device__ __forceinline__ float act_forward(int act, float x) {
+  switch (act) {
+    case OXF_ACT_GELU: {
+      const float inner = kGeluScale * (x + kGeluCubic * x * x * x);
+      return 0.5f * x * (1.0f + tanhf(inner));
+    }
+    case OXF_ACT_RELU: return x > 0.0f ? x : 0.0f;
+    case OXF_ACT_SILU: return x / (1.0f + expf(-x));
+    default: return x;
+  }
+}
+
+__device__ __forceinline__ float act_derivative(int act, float x) {
+  switch (act) {
+    case OXF_ACT_GELU: {
+      const float quad = kGeluScale * 3.0f * kGeluCubic;
+      const float inner = kGeluScale * (x + kGeluCubic * x * x * x);
+      const float th = tanhf(inner);
+      const float dinner = kGeluScale + quad * x * x;
+      return 0.5f * (1.0f + th) + 0.5f * x * (1.0f - th * th) * dinner;
+    }
+    case OXF_ACT_RELU: return x > 0.0f ? 1.0f : 0.0f;
+    case OXF_ACT_SILU: {
+      const float e = expf(-x);
+      return 1.0f / (1.0f + e) + x * e / ((1.0f + e) * (1.0f + e));
+    }
+    default: return 1.0f;
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace oxf

@@ -1,0 +1,805 @@
+// gemm.cu — TF32 GEMM on the 5th-generation tensor cores (sm_100a).
+//
+// Replaces matrix_multiply (src/cuda/device/module.rs:179-191 ->
+// src/cuda/device/gemm.rs:202-373) and the transposes the reference runs
+// before every backward product (src/net/linear.rs:381,432;
+// src/net/transformer/attention.rs:297-307,367): operands are read in the
+// layout they are stored in, K-major or MN-major, straight from HBM by TMA.
+//
+// Kernel shape (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: fills a STAGES-deep shared-memory ring
+//               (128B-swizzled tiles, mbarrier transaction counts)
+//   warp 1      TMEM allocator + MMA issuer: tcgen05.mma.kind::tf32,
+//               M=128 x N=BN x K=8 per instruction, accumulators in TMEM,
+//               tcgen05.commit frees ring slots and publishes accumulators
+//   warps 2..5  epilogue: tcgen05.ld, fused alpha/beta/bias/residual/
+//               pre-activation store/activation(-gradient), global stores
+// Two TMEM accumulators (2*BN columns) let the epilogue of tile i overlap
+// the main loop of tile i+1. No cluster multicast is used anywhere.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "ptx.cuh"
+#include "status.cuh"
+
+namespace oxf {
+
+constexpr int BM = 128;       // tile rows (TMEM lanes)
+constexpr int BK = 32;        // K elements per ring slot: 32 x f32 = one 128-byte swizzle row
+constexpr int UMMA_K = 8;     // K per tcgen05.mma.kind::tf32
+constexpr int EPI_WARPS = 4;  // warps 2..5
+constexpr int GEMM_THREADS = 64 + 32 * EPI_WARPS;
+constexpr int GROUP_M = 16;   // raster grouping for L2 reuse
+
+struct GemmArgs {
+  int M, N, K, batch;
+  int a_mn, b_mn;  // operand stored MN-major (contiguous along M / N)
+  int a3d, b3d;    // tensor map carries a batch coordinate
+  int tiles_m, tiles_n, splits, kblocks;
+  long long units;
+  uint32_t idesc;
+  float* C; long long ldc, sc;
+  float alpha, beta;
+  const float* bias;
+  const float* R; long long ldr, sr;
+  float* P; long long ldp, sp;
+  const float* X; long long ldx, sx;
+  int act, grad_act, accumulate, vec_ok;
+};
+
+template <int BN, int STAGES, bool SPLIT3>
+struct GemmCfg {
+  static constexpr int A_BYTES = BM * BK * 4;
+  static constexpr int B_BYTES = BN * BK * 4;
+  static constexpr int OPS = SPLIT3 ? 2 : 1;  // hi (+ lo) copies of each operand
+  static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * OPS;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int CTRL_BYTES = 1024;
+  static constexpr int SMEM_BYTES = 1024 + CTRL_BYTES + STAGES * STAGE_BYTES;
+  static_assert(TMEM_COLS >= 32 && TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0,
+                "TMEM allocation must be a power of two in [32, 512]");
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be a multiple of 32 in [32,256]");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+};
+
+template <int STAGES>
+struct GemmCtrl {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint32_t tmem_base;
+  volatile uint32_t abort_flag;
+};
+
+__device__ __forceinline__ void decode_unit(const GemmArgs& a, long long u, int& b, int& tm,
+                                            int& tn, int& kb0, int& kb1) {
+  const long long tiles = static_cast<long long>(a.tiles_m) * a.tiles_n;
+  const long long per_split = tiles * a.batch;
+  const int s = static_cast<int>(u / per_split);
+  const long long r = u - static_cast<long long>(s) * per_split;
+  b = static_cast<int>(r / tiles);
+  const long long t = r - static_cast<long long>(b) * tiles;
+  const long long group_size = static_cast<long long>(GROUP_M) * a.tiles_n;
+  const int g = static_cast<int>(t / group_size);
+  const int first_m = g * GROUP_M;
+  const int gm = min(a.tiles_m - first_m, GROUP_M);
+  const int inner = static_cast<int>(t - static_cast<long long>(g) * group_size);
+  tm = first_m + inner % gm;
+  tn = inner / gm;
+  kb0 = static_cast<int>((static_cast<long long>(s) * a.kblocks) / a.splits);
+  kb1 = static_cast<int>((static_cast<long long>(s + 1) * a.kblocks) / a.splits);
+}
+
+// Shared-memory descriptor of one K=8 slice of an operand tile.
+//  K-major tile: rows of 128 B (32 K values), 8-row swizzle atoms 1024 B
+//    apart (SBO); K slice kk starts kk*32 B into the row.
+//  MN-major tile: 32-element MN chunks of 32 K rows (4 KB, LBO apart);
+//    K slice kk is the kk-th 8-row atom (1024 B).
+__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int mn_major, int kk) {
+  return mn_major ? make_smem_desc_sw128(base + kk * 1024, 4096, 1024)
+                  : make_smem_desc_sw128(base + kk * 32, 16, 1024);
+}
+
+template <int ROWS>
+__device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* map, uint64_t* bar,
+                                             int mn_major, int is3d, int row0, int k0, int b) {
+  if (!mn_major) {
+    if (is3d) tma_load_3d(dst, map, bar, k0, row0, b);
+    else tma_load_2d(dst, map, bar, k0, row0);
+  } else {
+#pragma unroll
+    for (int c = 0; c < ROWS / 32; ++c) {
+      if (is3d) tma_load_3d(dst + c * 4096, map, bar, row0 + 32 * c, k0, b);
+      else tma_load_2d(dst + c * 4096, map, bar, row0 + 32 * c, k0);
+    }
+  }
+}
+
+__device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int b, int m, int n0,
+                                               float (&v)[32]) {
+  float* crow = a.C + b * a.sc + static_cast<long long>(m) * a.ldc;
+  const float* rrow = a.R ? a.R + b * a.sr + static_cast<long long>(m) * a.ldr : nullptr;
+  float* prow = a.P ? a.P + b * a.sp + static_cast<long long>(m) * a.ldp : nullptr;
+  const float* xrow = a.X ? a.X + b * a.sx + static_cast<long long>(m) * a.ldx : nullptr;
+  const bool full = a.vec_ok && (n0 + 32 <= a.N);
+  if (full) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      float4 acc = make_float4(v[j] * a.alpha, v[j + 1] * a.alpha, v[j + 2] * a.alpha,
+                               v[j + 3] * a.alpha);
+      if (a.beta != 0.0f) {
+        const float4 c = *reinterpret_cast<const float4*>(crow + n0 + j);
+        acc.x += a.beta * c.x; acc.y += a.beta * c.y; acc.z += a.beta * c.z; acc.w += a.beta * c.w;
+      }
+      if (a.bias) {
+        const float4 bb = *reinterpret_cast<const float4*>(a.bias + n0 + j);
+        acc.x += bb.x; acc.y += bb.y; acc.z += bb.z; acc.w += bb.w;
+      }
+      if (rrow) {
+        const float4 r = *reinterpret_cast<const float4*>(rrow + n0 + j);
+        acc.x += r.x; acc.y += r.y; acc.z += r.z; acc.w += r.w;
+      }
+      if (prow) *reinterpret_cast<float4*>(prow + n0 + j) = acc;
+      if (xrow) {
+        const float4 x = *reinterpret_cast<const float4*>(xrow + n0 + j);
+        acc.x *= act_derivative(a.grad_act, x.x);
+        acc.y *= act_derivative(a.grad_act, x.y);
+        acc.z *= act_derivative(a.grad_act, x.z);
+        acc.w *= act_derivative(a.grad_act, x.w);
+      }
+      if (a.act != OXF_ACT_IDENTITY) {
+        acc.x = act_forward(a.act, acc.x); acc.y = act_forward(a.act, acc.y);
+        acc.z = act_forward(a.act, acc.z); acc.w = act_forward(a.act, acc.w);
+      }
+      if (a.accumulate) atomicAdd(reinterpret_cast<float4*>(crow + n0 + j), acc);
+      else *reinterpret_cast<float4*>(crow + n0 + j) = acc;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int n = n0 + j;
+      if (n >= a.N) continue;
+      float acc = v[j] * a.alpha;
+      if (a.beta != 0.0f) acc += a.beta * crow[n];
+      if (a.bias) acc += a.bias[n];
+      if (rrow) acc += rrow[n];
+      if (prow) prow[n] = acc;
+      if (xrow) acc *= act_derivative(a.grad_act, xrow[n]);
+      acc = act_forward(a.act, acc);
+      if (a.accumulate) atomicAdd(crow + n, acc);
+      else crow[n] = acc;
+    }
+  }
+}
+
+template <int BN, int STAGES, bool SPLIT3>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_tf32_tcgen05(const __grid_constant__ CUtensorMap tmA,
+                      const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmA_lo,
+                      const __grid_constant__ CUtensorMap tmB_lo, const GemmArgs args) {
+  using Cfg = GemmCfg<BN, STAGES, SPLIT3>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  auto* ctrl = reinterpret_cast<GemmCtrl<STAGES>*>(base);
+  uint8_t* ring = base + Cfg::CTRL_BYTES;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&ctrl->full[s], 1);
+      mbar_init(&ctrl->empty[s], 1);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ctrl->tfull[i], 1);
+      mbar_init(&ctrl->tempty[i], 32 * EPI_WARPS);
+    }
+    ctrl->abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (SPLIT3) {
+      tma_prefetch_desc(&tmA_lo);
+      tma_prefetch_desc(&tmB_lo);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(&ctrl->tmem_base, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = ctrl->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      long long fills = 0;
+      for (long long u = blockIdx.x; u < args.units && !ctrl->abort_flag; u += gridDim.x) {
+        int b, tm, tn, kb0, kb1;
+        decode_unit(args, u, b, tm, tn, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&ctrl->empty[stage], phase ^ 1u, DEVERR_GEMM_WAIT_EMPTY)) {
+            ctrl->abort_flag = 1;
+            break;
+          }
+          if (ctrl->abort_flag) break;
+          uint8_t* slot = ring + stage * Cfg::STAGE_BYTES;
+          mbar_arrive_expect_tx(&ctrl->full[stage], Cfg::STAGE_BYTES);
+          const int k0 = kb * BK;
+          load_operand<BM>(slot, &tmA, &ctrl->full[stage], args.a_mn, args.a3d, tm * BM, k0, b);
+          load_operand<BN>(slot + Cfg::A_BYTES, &tmB, &ctrl->full[stage], args.b_mn, args.b3d,
+                           tn * BN, k0, b);
+          if (SPLIT3) {
+            uint8_t* lo = slot + Cfg::A_BYTES + Cfg::B_BYTES;
+            load_operand<BM>(lo, &tmA_lo, &ctrl->full[stage], args.a_mn, args.a3d, tm * BM, k0,
+                             b);
+            load_operand<BN>(lo + Cfg::A_BYTES, &tmB_lo, &ctrl->full[stage], args.b_mn,
+                             args.b3d, tn * BN, k0, b);
+          }
+          ++fills;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Never leave the CTA with bulk copies still landing in its shared
+      // memory: wait for the most recent fill of every slot.
+      const long long first = fills > STAGES ? fills - STAGES : 0;
+      for (long long j = first; j < fills; ++j)
+        mbar_wait(&ctrl->full[j % STAGES], static_cast<uint32_t>((j / STAGES) & 1),
+                  DEVERR_GEMM_DRAIN);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      int local = 0;
+      for (long long u = blockIdx.x; u < args.units && !ctrl->abort_flag;
+           u += gridDim.x, ++local) {
+        int b, tm, tn, kb0, kb1;
+        decode_unit(args, u, b, tm, tn, kb0, kb1);
+        const int acc_slot = local & 1;
+        const uint32_t use = static_cast<uint32_t>(local >> 1);
+        if (!mbar_wait(&ctrl->tempty[acc_slot], (use & 1u) ^ 1u, DEVERR_GEMM_WAIT_TMEM_EMPTY)) {
+          ctrl->abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc_slot * BN);
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&ctrl->full[stage], phase, DEVERR_GEMM_WAIT_FULL)) {
+            ctrl->abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(ring + stage * Cfg::STAGE_BYTES);
+          const uint32_t b_base = a_base + Cfg::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+            const uint64_t da = operand_desc(a_base, args.a_mn, kk);
+            const uint64_t db = operand_desc(b_base, args.b_mn, kk);
+            const uint32_t accumulate = (kb > kb0 || kk > 0) ? 1u : 0u;
+            if (SPLIT3) {
+              const uint32_t lo_base = b_base + Cfg::B_BYTES;
+              const uint64_t da_lo = operand_desc(lo_base, args.a_mn, kk);
+              const uint64_t db_lo = operand_desc(lo_base + Cfg::A_BYTES, args.b_mn, kk);
+              umma_tf32(d_tmem, da_lo, db, args.idesc, accumulate);
+              umma_tf32(d_tmem, da, db_lo, args.idesc, 1u);
+              umma_tf32(d_tmem, da, db, args.idesc, 1u);
+            } else {
+              umma_tf32(d_tmem, da, db, args.idesc, accumulate);
+            }
+          }
+          umma_commit(&ctrl->empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&ctrl->tfull[acc_slot]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_local = quarter * 32 + lane;
+    int local = 0;
+    for (long long u = blockIdx.x; u < args.units; u += gridDim.x, ++local) {
+      int b, tm, tn, kb0, kb1;
+      decode_unit(args, u, b, tm, tn, kb0, kb1);
+      const int acc_slot = local & 1;
+      const uint32_t use = static_cast<uint32_t>(local >> 1);
+      if (!mbar_wait(&ctrl->tfull[acc_slot], use & 1u, DEVERR_GEMM_WAIT_TMEM_FULL)) {
+        ctrl->abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int m = tm * BM + row_local;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                             static_cast<uint32_t>(acc_slot * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int n0 = tn * BN + c * 32;
+        if (n0 >= args.N) break;  // uniform across the warp
+        float v[32];
+        tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), v);
+        if (m < args.M) epilogue_chunk(args, b, m, n0, v);
+      }
+      tc_fence_before();
+      mbar_arrive(&ctrl->tempty[acc_slot]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- 3xTF32 split
+// hi = TF32 (round to nearest, ties away) of x, lo = x - hi; both f32.
+__global__ void split_tf32_kernel(const float* __restrict__ src, long long ld, long long stride,
+                                  int inner, int outer, float* __restrict__ hi,
+                                  float* __restrict__ lo) {
+  const long long per = static_cast<long long>(inner) * outer;
+  const int b = blockIdx.y;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < per;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / inner, c = i - r * inner;
+    const float x = src[b * stride + r * ld + c];
+    uint32_t h;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
+    const float hf = __uint_as_float(h);
+    hi[b * per + i] = hf;
+    lo[b * per + i] = x - hf;
+  }
+}
+
+// ---------------------------------------------------------------- SIMT fallback
+// Used only for shapes TMA cannot describe (leading dimension not a multiple
+// of 4 elements, misaligned base, K == 0). Operands are rounded to TF32 like
+// the reference (gemm.rs:286-347) unless `exact`.
+__global__ void gemm_simt_kernel(const GemmArgs a, const float* __restrict__ A, long long lda,
+                                 long long sa, const float* __restrict__ B, long long ldb,
+                                 long long sb, int exact) {
+  __shared__ float As[32][33];
+  __shared__ float Bs[32][33];
+  const int b = blockIdx.z;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+  const int m0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int k0 = 0; k0 < a.K; k0 += 32) {
+    for (int i = ty; i < 32; i += 8) {
+      const int m = m0 + i, k = k0 + tx;
+      float va = 0.f;
+      if (m < a.M && k < a.K)
+        va = a.a_mn ? A[b * sa + static_cast<long long>(k) * lda + m]
+                    : A[b * sa + static_cast<long long>(m) * lda + k];
+      const int kb = k0 + i, n = n0 + tx;
+      float vb = 0.f;
+      if (kb < a.K && n < a.N)
+        vb = a.b_mn ? B[b * sb + static_cast<long long>(kb) * ldb + n]
+                    : B[b * sb + static_cast<long long>(n) * ldb + kb];
+      if (!exact) {
+        uint32_t h;
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(va));
+        va = __uint_as_float(h);
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(vb));
+        vb = __uint_as_float(h);
+      }
+      As[i][tx] = va;
+      Bs[i][tx] = vb;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) {
+      const float bv = Bs[k][tx];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[r] += As[ty + 8 * r][k] * bv;
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int m = m0 + ty + 8 * r, n = n0 + tx;
+    if (m >= a.M || n >= a.N) continue;
+    float* crow = a.C + b * a.sc + static_cast<long long>(m) * a.ldc;
+    float v = acc[r] * a.alpha;
+    if (a.beta != 0.0f) v += a.beta * crow[n];
+    if (a.bias) v += a.bias[n];
+    if (a.R) v += a.R[b * a.sr + static_cast<long long>(m) * a.ldr + n];
+    if (a.P) a.P[b * a.sp + static_cast<long long>(m) * a.ldp + n] = v;
+    if (a.X) v *= act_derivative(a.grad_act, a.X[b * a.sx + static_cast<long long>(m) * a.ldx + n]);
+    v = act_forward(a.act, v);
+    if (a.accumulate) atomicAdd(crow + n, v);
+    else crow[n] = v;
+  }
+}
+
+// ---------------------------------------------------------------- reference algorithm
+// Measurement-only restatement of the reference GEMM (gemm.rs:131-373):
+// 32x32 output tile per 128-thread CTA, four warps of 16x16 (two
+// mma.sync.m16n8k8 TF32 each), K tiles of 16 staged by 4-byte cp.async in two
+// buffers, B transposed into shared memory with a row stride of 20 floats.
+__device__ __forceinline__ void cp_async4_zfill(float* smem, const float* gmem, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(smem)),
+               "l"(gmem), "r"(valid ? 4 : 0)
+               : "memory");
+}
+
+__device__ __forceinline__ uint32_t tf32_rna_bits(float x) {
+  uint32_t h;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
+  return h;
+}
+
+__global__ void __launch_bounds__(128) gemm_refalgo_kernel(const float* __restrict__ A,
+                                                           const float* __restrict__ B,
+                                                           float* __restrict__ C, int len,
+                                                           int rows, int cols) {
+  constexpr int T = 32, KT = 16, STRIDE = 20, STAGE = T * STRIDE;
+  __shared__ __align__(16) float sa[2 * STAGE];
+  __shared__ __align__(16) float sb[2 * STAGE];
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int group = lane / 4, tig = lane % 4;
+  const int wr = warp / 2, wc = warp % 2;
+  const int br = blockIdx.y * T, bc = blockIdx.x * T;
+  float acc0[4] = {0, 0, 0, 0}, acc1[4] = {0, 0, 0, 0};
+  auto prefetch = [&](int buf, int k0) {
+    for (int l = 0; l < 4; ++l) {
+      const int li = tid + l * 128;
+      const int ar = li / KT, ak = li % KT, gr = br + ar;
+      const bool av = gr < rows;
+      cp_async4_zfill(&sa[buf * STAGE + ar * STRIDE + ak], av ? A + (size_t)gr * len + k0 + ak : A,
+                      av);
+      const int bk = li / T, bcol = li % T, gc = bc + bcol;
+      const bool bv = gc < cols;
+      cp_async4_zfill(&sb[buf * STAGE + bcol * STRIDE + bk],
+                      bv ? B + (size_t)(k0 + bk) * cols + gc : B, bv);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  const int tiles = len / KT;
+  prefetch(0, 0);
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  for (int t = 0; t < tiles; ++t) {
+    const int rb = (t % 2) * STAGE;
+    if (t + 1 < tiles) prefetch((t + 1) % 2, (t + 1) * KT);
+#pragma unroll
+    for (int kh = 0; kh < 2; ++kh) {
+      const int lk = kh * 8, ar0 = wr * 16, bc0 = wc * 16;
+      uint32_t a0 = tf32_rna_bits(sa[rb + (ar0 + group) * STRIDE + lk + tig]);
+      uint32_t a1 = tf32_rna_bits(sa[rb + (ar0 + group + 8) * STRIDE + lk + tig]);
+      uint32_t a2 = tf32_rna_bits(sa[rb + (ar0 + group) * STRIDE + lk + tig + 4]);
+      uint32_t a3 = tf32_rna_bits(sa[rb + (ar0 + group + 8) * STRIDE + lk + tig + 4]);
+      uint32_t b00 = tf32_rna_bits(sb[rb + (bc0 + group) * STRIDE + lk + tig]);
+      uint32_t b01 = tf32_rna_bits(sb[rb + (bc0 + group) * STRIDE + lk + tig + 4]);
+      uint32_t b10 = tf32_rna_bits(sb[rb + (bc0 + group + 8) * STRIDE + lk + tig]);
+      uint32_t b11 = tf32_rna_bits(sb[rb + (bc0 + group + 8) * STRIDE + lk + tig + 4]);
+      asm volatile(
+          "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+          "{%8,%9}, {%0,%1,%2,%3};"
+          : "+f"(acc0[0]), "+f"(acc0[1]), "+f"(acc0[2]), "+f"(acc0[3])
+          : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b00), "r"(b01));
+      asm volatile(
+          "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+          "{%8,%9}, {%0,%1,%2,%3};"
+          : "+f"(acc1[0]), "+f"(acc1[1]), "+f"(acc1[2]), "+f"(acc1[3])
+          : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b10), "r"(b11));
+    }
+    if (t + 1 < tiles) {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+      __syncthreads();
+    }
+  }
+  for (int r = 0; r < 4; ++r) {
+    const int orow = br + wr * 16 + group + (r >= 2 ? 8 : 0);
+    const int ocol = bc + wc * 16 + tig * 2 + r % 2;
+    if (orow < rows && ocol < cols) C[(size_t)orow * cols + ocol] = acc0[r];
+    if (orow < rows && ocol + 8 < cols) C[(size_t)orow * cols + ocol + 8] = acc1[r];
+  }
+}
+
+// ================================================================== host side
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+constexpr int kMaxDevices = 64;
+
+int sm_count(int dev) {
+  static int counts[kMaxDevices] = {0};
+  if (dev < 0 || dev >= kMaxDevices) return 148;
+  if (counts[dev] == 0) {
+    int c = 0;
+    cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev);
+    counts[dev] = c > 0 ? c : 148;
+  }
+  return counts[dev];
+}
+
+// 2-D (or 3-D with a batch dimension) f32 tensor map, 128B swizzle,
+// zero fill outside the tensor.
+bool encode_map(CUtensorMap* map, const float* ptr, long long inner, long long outer,
+                long long ld, int batch, long long bstride, int box_inner, int box_outer,
+                int* is3d) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  const bool three = batch > 1 && bstride != 0;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer),
+                        static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 4, static_cast<cuuint64_t>(bstride) * 4};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, three ? 3 : 2, const_cast<float*>(ptr),
+                   dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  *is3d = three ? 1 : 0;
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, int STAGES, bool SPLIT3>
+oxf_status launch_tcgen05(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta_lo,
+                          const CUtensorMap& tb_lo, GemmArgs& args, cudaStream_t stream,
+                          int dev) {
+  using Cfg = GemmCfg<BN, STAGES, SPLIT3>;
+  static bool configured[kMaxDevices] = {false};
+  if (dev >= 0 && dev < kMaxDevices && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tf32_tcgen05<BN, STAGES, SPLIT3>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(gemm)");
+    configured[dev] = true;
+  }
+  args.idesc = make_idesc_tf32(BM, BN, args.a_mn != 0, args.b_mn != 0);
+  const long long grid = std::min<long long>(args.units, sm_count(dev));
+  gemm_tf32_tcgen05<BN, STAGES, SPLIT3><<<static_cast<unsigned>(grid), GEMM_THREADS,
+                                          Cfg::SMEM_BYTES, stream>>>(ta, tb, ta_lo, tb_lo, args);
+  return check_launch("gemm_tf32_tcgen05");
+}
+
+// Chooses how many K splits an accumulating GEMM uses: minimises
+// waves * k-blocks-per-unit plus a per-split epilogue cost.
+int choose_splits(long long tiles, int kblocks, int sms) {
+  int best = 1;
+  double best_cost = 1e300;
+  for (int s = 1; s <= 32 && s <= kblocks; ++s) {
+    const long long units = tiles * s;
+    const long long waves = (units + sms - 1) / sms;
+    const double cost = static_cast<double>(waves) * ((kblocks + s - 1) / s) + 2.0 * s;
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
+}
+
+bool tma_ok_ptr(const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+size_t gemm_workspace_bytes(const oxf_gemm_desc* d) {
+  if (!d || d->precision != OXF_PREC_TF32X3) return 0;
+  const long long ba = d->stride_a ? d->batch : 1;
+  const long long bb = d->stride_b ? d->batch : 1;
+  const long long ea = static_cast<long long>(d->M) * d->K * ba;
+  const long long eb = static_cast<long long>(d->K) * d->N * bb;
+  // hi and lo of each operand, each region rounded up to 256 bytes
+  auto r = [](long long e) { return ((e * 4 + 255) / 256) * 256; };
+  return static_cast<size_t>(2 * r(ea) + 2 * r(eb));
+}
+
+oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
+  if (!d) return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: null descriptor");
+  if (d->M < 0 || d->N < 0 || d->K < 0 || d->batch < 1)
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: negative shape or batch < 1");
+  if (d->M == 0 || d->N == 0) return OXF_OK;
+  if (!d->A || !d->B || !d->C) return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: null operand");
+  const int split = d->split_k > 1 ? d->split_k : 1;
+  if (split > 1 && !d->accumulate)
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: split_k > 1 requires accumulate");
+  if (d->accumulate && d->beta != 0.0f)
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: beta must be 0 with accumulate");
+  if (d->precision != OXF_PREC_TF32 && d->precision != OXF_PREC_TF32X3)
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: unknown precision %d", d->precision);
+  const long long min_lda = d->a_trans ? d->M : d->K;
+  const long long min_ldb = d->b_trans ? d->K : d->N;
+  if (d->lda < min_lda || d->ldb < min_ldb || d->ldc < d->N)
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: leading dimension too small");
+  if ((d->residual && d->ldr < d->N) || (d->pre_out && d->ldp < d->N) ||
+      (d->aux && d->ldx < d->N))
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: epilogue leading dimension too small");
+  if (d->aux && d->grad_act == OXF_ACT_IDENTITY)
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: aux given without grad_act");
+  if (d->accumulate && (d->pre_out || d->act != OXF_ACT_IDENTITY) && split > 1)
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: split_k cannot fuse activation");
+
+  int dev = 0;
+  cudaGetDevice(&dev);
+
+  GemmArgs a{};
+  a.M = d->M; a.N = d->N; a.K = d->K; a.batch = d->batch;
+  a.a_mn = d->a_trans ? 1 : 0;
+  a.b_mn = d->b_trans ? 0 : 1;
+  a.C = d->C; a.ldc = d->ldc; a.sc = d->stride_c;
+  a.alpha = d->alpha; a.beta = d->beta;
+  a.bias = d->bias;
+  a.R = d->residual; a.ldr = d->ldr; a.sr = d->stride_r;
+  a.P = d->pre_out; a.ldp = d->ldp; a.sp = d->stride_p;
+  a.X = d->aux; a.ldx = d->ldx; a.sx = d->stride_x;
+  a.act = d->act; a.grad_act = d->aux ? d->grad_act : OXF_ACT_IDENTITY;
+  a.accumulate = d->accumulate ? 1 : 0;
+  auto vec = [](const void* p, long long ld, long long st) {
+    return p == nullptr || (aligned16(p) && ld % 4 == 0 && st % 4 == 0);
+  };
+  a.vec_ok = vec(d->C, d->ldc, d->stride_c) && vec(d->residual, d->ldr, d->stride_r) &&
+             vec(d->pre_out, d->ldp, d->stride_p) && vec(d->aux, d->ldx, d->stride_x) &&
+             (d->bias == nullptr || aligned16(d->bias));
+
+  // TMA needs 16-byte aligned bases, leading dimensions and batch strides.
+  const bool tma_ok = d->K > 0 && tma_ok_ptr(d->A) && tma_ok_ptr(d->B) && d->lda % 4 == 0 &&
+                      d->ldb % 4 == 0 && d->stride_a % 4 == 0 && d->stride_b % 4 == 0;
+  if (!tma_ok) {
+    a.splits = 1;
+    if (d->K == 0) {
+      // C = epilogue(0): run the SIMT kernel with an empty K loop.
+    }
+    dim3 grid((d->N + 31) / 32, (d->M + 31) / 32, d->batch);
+    gemm_simt_kernel<<<grid, dim3(32, 8), 0, stream>>>(a, d->A, d->lda, d->stride_a, d->B,
+                                                        d->ldb, d->stride_b,
+                                                        d->precision == OXF_PREC_TF32X3);
+    return check_launch("gemm_simt_kernel");
+  }
+
+  const bool split3 = d->precision == OXF_PREC_TF32X3;
+  const float* A = d->A;
+  const float* B = d->B;
+  long long lda = d->lda, ldb = d->ldb, sa = d->stride_a, sb = d->stride_b;
+  const float *A_lo = nullptr, *B_lo = nullptr;
+  if (split3) {
+    const size_t need = gemm_workspace_bytes(d);
+    if (!d->workspace || d->workspace_bytes < need)
+      return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: TF32X3 needs %zu bytes of workspace",
+                       need);
+    if (!aligned16(d->workspace))
+      return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: workspace must be 16-byte aligned");
+    const long long ba = d->stride_a ? d->batch : 1;
+    const long long bb = d->stride_b ? d->batch : 1;
+    const long long a_inner = d->a_trans ? d->M : d->K, a_outer = d->a_trans ? d->K : d->M;
+    const long long b_inner = d->b_trans ? d->K : d->N, b_outer = d->b_trans ? d->N : d->K;
+    auto r = [](long long e) { return ((e * 4 + 255) / 256) * 256; };
+    uint8_t* ws = static_cast<uint8_t*>(d->workspace);
+    float* a_hi = reinterpret_cast<float*>(ws);
+    float* a_lo = reinterpret_cast<float*>(ws + r(a_inner * a_outer * ba));
+    float* b_hi = reinterpret_cast<float*>(ws + 2 * r(a_inner * a_outer * ba));
+    float* b_lo = reinterpret_cast<float*>(ws + 2 * r(a_inner * a_outer * ba) +
+                                           r(b_inner * b_outer * bb));
+    const int threads = 256;
+    auto blocks = [&](long long e) {
+      return static_cast<unsigned>(std::min<long long>((e + threads - 1) / threads, 4096));
+    };
+    split_tf32_kernel<<<dim3(blocks(a_inner * a_outer), static_cast<unsigned>(ba)), threads, 0,
+                        stream>>>(d->A, d->lda, d->stride_a, static_cast<int>(a_inner),
+                                  static_cast<int>(a_outer), a_hi, a_lo);
+    split_tf32_kernel<<<dim3(blocks(b_inner * b_outer), static_cast<unsigned>(bb)), threads, 0,
+                        stream>>>(d->B, d->ldb, d->stride_b, static_cast<int>(b_inner),
+                                  static_cast<int>(b_outer), b_hi, b_lo);
+    oxf_status st = check_launch("split_tf32_kernel");
+    if (st != OXF_OK) return st;
+    A = a_hi; A_lo = a_lo; B = b_hi; B_lo = b_lo;
+    lda = a_inner; ldb = b_inner;
+    sa = d->stride_a ? a_inner * a_outer : 0;
+    sb = d->stride_b ? b_inner * b_outer : 0;
+  }
+
+  // Tile width along N.
+  const int sms = sm_count(dev);
+  int BN = 256;
+  if (split3 || d->N <= 128) BN = 128;
+  if (d->N <= 64) BN = 64;
+  if (!split3 && BN == 256) {
+    const long long t256 = static_cast<long long>((d->M + BM - 1) / BM) * ((d->N + 255) / 256) *
+                           d->batch;
+    if (t256 < sms && !d->accumulate) BN = 128;  // more, smaller tiles when the grid is thin
+  }
+  a.tiles_m = (d->M + BM - 1) / BM;
+  a.tiles_n = (d->N + BN - 1) / BN;
+  a.kblocks = (d->K + BK - 1) / BK;
+  const long long tiles = static_cast<long long>(a.tiles_m) * a.tiles_n * d->batch;
+  if (d->accumulate) {
+    a.splits = split > 1 ? std::min(split, a.kblocks) : choose_splits(tiles, a.kblocks, sms);
+  } else {
+    a.splits = 1;
+  }
+  a.units = tiles * a.splits;
+
+  CUtensorMap ta, tb, ta_lo, tb_lo;
+  std::memset(&ta_lo, 0, sizeof(ta_lo));
+  std::memset(&tb_lo, 0, sizeof(tb_lo));
+  int a3d = 0, b3d = 0, dummy = 0;
+  const long long a_inner = d->a_trans ? d->M : d->K, a_outer = d->a_trans ? d->K : d->M;
+  const long long b_inner = d->b_trans ? d->K : d->N, b_outer = d->b_trans ? d->N : d->K;
+  const int a_box_outer = a.a_mn ? 32 : BM;
+  const int b_box_outer = a.b_mn ? 32 : BN;
+  bool ok = encode_map(&ta, A, a_inner, a_outer, lda, d->batch, sa, 32, a_box_outer, &a3d) &&
+            encode_map(&tb, B, b_inner, b_outer, ldb, d->batch, sb, 32, b_box_outer, &b3d);
+  if (ok && split3)
+    ok = encode_map(&ta_lo, A_lo, a_inner, a_outer, lda, d->batch, sa, 32, a_box_outer, &dummy) &&
+         encode_map(&tb_lo, B_lo, b_inner, b_outer, ldb, d->batch, sb, 32, b_box_outer, &dummy);
+  if (!ok) return set_error(OXF_ERR_CUDA, "oxf_gemm: cuTensorMapEncodeTiled failed");
+  a.a3d = a3d;
+  a.b3d = b3d;
+
+  if (split3) return launch_tcgen05<128, 3, true>(ta, tb, ta_lo, tb_lo, a, stream, dev);
+  if (BN == 256) return launch_tcgen05<256, 4, false>(ta, tb, ta, tb, a, stream, dev);
+  if (BN == 128) return launch_tcgen05<128, 6, false>(ta, tb, ta, tb, a, stream, dev);
+  return launch_tcgen05<64, 8, false>(ta, tb, ta, tb, a, stream, dev);
+}
+
+oxf_status gemm_refalgo(const float* A, const float* B, float* C, size_t len, size_t rows,
+                        size_t cols, cudaStream_t stream) {
+  if (rows % 16 || cols % 16 || len % 16)
+    return set_error(OXF_ERR_INVALID_ARG,
+                     "matrix_multiply_refalgo: rows, cols and len must be multiples of 16");
+  if (rows == 0 || cols == 0) return OXF_OK;
+  dim3 grid(static_cast<unsigned>((cols + 31) / 32), static_cast<unsigned>((rows + 31) / 32));
+  gemm_refalgo_kernel<<<grid, 128, 0, stream>>>(A, B, C, static_cast<int>(len),
+                                                static_cast<int>(rows), static_cast<int>(cols));
+  return check_launch("gemm_refalgo_kernel");
+}
+
+oxf_status gemm_read_device_error(uint32_t* code) {
+  uint32_t v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_oxf_device_error, sizeof(v));
+  if (e != cudaSuccess) return check_cuda(e, "read device error word");
+  const uint32_t zero = 0;
+  e = cudaMemcpyToSymbol(g_oxf_device_error, &zero, sizeof(zero));
+  if (e != cudaSuccess) return check_cuda(e, "clear device error word");
+  *code = v;
+  return OXF_OK;
+}
+
+}  // namespace oxf

@@ -1,0 +1,46 @@
+// status.cuh — host-side error state shared by every C-ABI entry point, and
+// the per-translation-unit device error word that bounded waits report to.
+#pragma once
+#include <cstdint>
+#include <cstdio>
+#include <cuda_runtime.h>
+
+#include "../../include/oxf.h"
+
+namespace oxf {
+
+// Records a message for oxf_last_error_string() and returns `st`.
+oxf_status set_error(oxf_status st, const char* fmt, ...);
+
+inline oxf_status check_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return OXF_OK;
+  return set_error(OXF_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// Launch-error check after a kernel launch (does not synchronise).
+inline oxf_status check_launch(const char* what) {
+  return check_cuda(cudaGetLastError(), what);
+}
+
+// Device error codes written by bounded waits (first error wins).
+enum DeviceErrorCode : uint32_t {
+  DEVERR_NONE = 0,
+  DEVERR_GEMM_WAIT_EMPTY = 0x101,
+  DEVERR_GEMM_WAIT_FULL = 0x102,
+  DEVERR_GEMM_WAIT_TMEM_EMPTY = 0x103,
+  DEVERR_GEMM_WAIT_TMEM_FULL = 0x104,
+  DEVERR_GEMM_DRAIN = 0x105,
+};
+
+}  // namespace oxf
+
+// One error word per translation unit that includes this header. Only the
+// GEMM translation unit has waits; it exposes the word through
+// oxf_device_error().
+static __device__ unsigned int g_oxf_device_error = 0;
+
+namespace oxf {
+__device__ __forceinline__ void report_device_error(uint32_t code) {
+  atomicCAS(&g_oxf_device_error, 0u, code);
+}
+}  // namespace oxf

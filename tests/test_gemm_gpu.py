@@ -1,0 +1,201 @@
+"""GPU parity of the tcgen05 TF32 GEMM (and its fused epilogue) against the
+oracle's float64 product, through the C ABI.
+
+Tolerances (north_star): plain TF32 <= 5e-3, 3xTF32 <= 1e-4, both as
+max|gpu - exact| / max|exact| over the output. The reference rounds operands
+to TF32 with round-to-nearest-away (gemm.rs:286-347); the tcgen05 path drops
+the low 13 mantissa bits instead, which the 5e-3 bound covers.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+TF32_TOL = 5e-3
+TF32X3_TOL = 1e-4
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def K():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from oxf import kernels
+    yield kernels
+    assert kernels.device_error() == 0, "a bounded in-kernel wait timed out"
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def operands(rng, M, N, Kd, at, bt, batch=None, dist="uniform"):
+    gen = (lambda s: rng.uniform(-1, 1, s)) if dist == "uniform" else rng.standard_normal
+    a_shape = (Kd, M) if at else (M, Kd)
+    b_shape = (N, Kd) if bt else (Kd, N)
+    if batch:
+        a_shape, b_shape = (batch,) + a_shape, (batch,) + b_shape
+    return gen(a_shape).astype(np.float32), gen(b_shape).astype(np.float32)
+
+
+def exact(A, B, at, bt):
+    return O.gemm_f64(A, B, a_trans=at, b_trans=bt)
+
+
+SHAPES = [
+    (128, 128, 32),     # one tile, one k-block
+    (256, 64, 128),     # config 1 (Linear [256,128]x[128,64])
+    (300, 200, 72),     # ragged M, N, K tails
+    (128, 256, 1024),   # one BN=256 tile, deep K
+    (1024, 1024, 1024),
+    (516, 772, 260),
+]
+
+
+@pytest.mark.parametrize("at,bt", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("M,N,Kd", SHAPES)
+def test_gemm_modes_tf32(K, rng, M, N, Kd, at, bt):
+    A, B = operands(rng, M, N, Kd, at, bt)
+    out = torch.empty((M, N), device="cuda")
+    K.gemm(dev(A), dev(B), out, a_trans=bool(at), b_trans=bool(bt))
+    assert rel_err(host(out), exact(A, B, at, bt)) < TF32_TOL
+
+
+@pytest.mark.parametrize("at,bt", [(0, 0), (1, 0), (0, 1)])
+@pytest.mark.parametrize("M,N,Kd", [(256, 64, 128), (300, 200, 72), (512, 384, 1024)])
+def test_gemm_tf32x3(K, rng, M, N, Kd, at, bt):
+    A, B = operands(rng, M, N, Kd, at, bt, dist="normal")
+    out = torch.empty((M, N), device="cuda")
+    ws = torch.empty(K.gemm_workspace_bytes(M, N, Kd, bool(at), bool(bt)) // 4 + 64,
+                     device="cuda")
+    K.gemm(dev(A), dev(B), out, a_trans=bool(at), b_trans=bool(bt), precision=1, workspace=ws)
+    assert rel_err(host(out), exact(A, B, at, bt)) < TF32X3_TOL
+
+
+def test_matrix_multiply_reference_signature(K, rng):
+    """matrix_multiply(lhs, rhs, out, len, rows, cols) of module.rs:179-191
+    on config 1's shapes and distributions."""
+    x = rng.uniform(-1, 1, (256, 128)).astype(np.float32)
+    w = rng.uniform(-1 / np.sqrt(128), 1 / np.sqrt(128), (128, 64)).astype(np.float32)
+    out = torch.empty((256, 64), device="cuda")
+    K.matrix_multiply(dev(x), dev(w), out)
+    assert rel_err(host(out), exact(x, w, 0, 0)) < TF32_TOL
+    # and against the oracle's emulation of the reference's RNA operand rounding
+    assert rel_err(host(out), O.gemm(x, w, rounding=O.GEMM_TF32_RNA)) < TF32_TOL
+
+
+def test_unaligned_leading_dims_use_fallback(K, rng):
+    # K = 33 gives a row pitch of 132 bytes, which TMA cannot describe
+    for M, N, Kd in [(129, 257, 33), (7, 5, 3), (64, 64, 0)]:
+        A, B = operands(rng, M, N, Kd, 0, 0)
+        out = torch.empty((M, N), device="cuda")
+        K.gemm(dev(A), dev(B), out)
+        want = exact(A, B, 0, 0) if Kd else np.zeros((M, N))
+        assert np.abs(host(out) - want).max() <= TF32_TOL * max(1.0, np.abs(want).max())
+
+
+@pytest.mark.parametrize("at,bt", [(0, 1), (0, 0), (1, 0)])
+def test_batched_gemm(K, rng, at, bt):
+    # per-sequence attention products: [batch, S, S] = Q_b · K_bᵀ etc.
+    batch, M, N, Kd = 3, 160, 96, 64
+    A, B = operands(rng, M, N, Kd, at, bt, batch=batch)
+    out = torch.empty((batch, M, N), device="cuda")
+    K.gemm(dev(A), dev(B), out, a_trans=bool(at), b_trans=bool(bt))
+    got = host(out)
+    for b in range(batch):
+        assert rel_err(got[b], exact(A[b], B[b], at, bt)) < TF32_TOL, b
+
+
+def test_batched_shared_operand(K, rng):
+    batch, M, N, Kd = 4, 128, 192, 96
+    A = rng.uniform(-1, 1, (batch, M, Kd)).astype(np.float32)
+    B = rng.uniform(-1, 1, (Kd, N)).astype(np.float32)
+    out = torch.empty((batch, M, N), device="cuda")
+    K.gemm(dev(A), dev(B), out)
+    got = host(out)
+    for b in range(batch):
+        assert rel_err(got[b], exact(A[b], B, 0, 0)) < TF32_TOL
+
+
+def test_fused_linear_epilogue(K, rng):
+    """Y = gelu(X·W + b + R) with the pre-activation stored (Linear::affine_on
+    + activate_on, linear.rs:185-230)."""
+    M, N, Kd = 384, 320, 256
+    X, W = operands(rng, M, N, Kd, 0, 0)
+    b = (0.1 * rng.standard_normal(N)).astype(np.float32)
+    R = rng.standard_normal((M, N)).astype(np.float32)
+    out = torch.empty((M, N), device="cuda")
+    pre = torch.empty((M, N), device="cuda")
+    K.gemm(dev(X), dev(W), out, bias=dev(b), residual=dev(R), pre_out=pre, act=1)
+    z = exact(X, W, 0, 0) + b + R
+    assert rel_err(host(pre), z) < TF32_TOL
+    assert rel_err(host(out), O.act_forward(O.GELU, z.astype(np.float32))) < TF32_TOL
+
+
+def test_grad_activation_epilogue(K, rng):
+    """dZ = (G·Wᵀ) ⊙ gelu'(Z) fused (linear.rs:254-264 then 431-434)."""
+    M, N, Kd = 256, 192, 128
+    G = rng.standard_normal((M, Kd)).astype(np.float32)
+    W = rng.uniform(-0.2, 0.2, (N, Kd)).astype(np.float32)  # stored [in=N, out=Kd]
+    Z = rng.standard_normal((M, N)).astype(np.float32)
+    out = torch.empty((M, N), device="cuda")
+    K.gemm(dev(G), dev(W), out, b_trans=True, aux=dev(Z), grad_act=1)
+    want = exact(G, W, 0, 1) * O.act_derivative(O.GELU, Z)
+    assert rel_err(host(out), want) < TF32_TOL
+
+
+def test_alpha_beta(K, rng):
+    M, N, Kd = 200, 136, 64
+    A, B = operands(rng, M, N, Kd, 0, 0)
+    C0 = rng.standard_normal((M, N)).astype(np.float32)
+    out = dev(C0)
+    K.gemm(dev(A), dev(B), out, alpha=0.125, beta=-2.0)
+    assert rel_err(host(out), 0.125 * exact(A, B, 0, 0) - 2.0 * C0) < TF32_TOL
+
+
+@pytest.mark.parametrize("split", [0, 1, 3, 16])
+def test_accumulate_split_k(K, rng, split):
+    """W-gradient shape Xᵀ·G with a long K, accumulated atomically into an
+    existing gradient buffer (split_k = 0 lets the library choose)."""
+    M, N, Kd = 256, 384, 4096
+    X = rng.standard_normal((Kd, M)).astype(np.float32)
+    G = rng.standard_normal((Kd, N)).astype(np.float32)
+    G0 = rng.standard_normal((M, N)).astype(np.float32)
+    out = dev(G0)
+    K.gemm(dev(X), dev(G), out, a_trans=True, accumulate=True, split_k=split, alpha=0.5)
+    assert rel_err(host(out), G0 + 0.5 * exact(X, G, 1, 0)) < TF32_TOL
+
+
+def test_refalgo_matches_reference_rounding(K, rng):
+    """The measurement-only restatement of the reference kernel rounds
+    operands RNA like gemm.rs; compare with the oracle's RNA emulation."""
+    M, N, Kd = 256, 192, 128
+    A, B = operands(rng, M, N, Kd, 0, 0)
+    out = torch.empty((M, N), device="cuda")
+    K.matrix_multiply_refalgo(dev(A), dev(B), out)
+    assert rel_err(host(out), O.gemm(A, B, rounding=O.GEMM_TF32_RNA)) < 1e-5
+    with pytest.raises(Exception):
+        K.matrix_multiply_refalgo(dev(A[:, :100]), dev(B[:100]), out[:, :].view(M, N))
+
+
+def test_large_square(K, rng):
+    """Size-independent check at a sweep size: C·1 == A·(B·1) row sums."""
+    n = 4096
+    A = torch.empty((n, n), device="cuda").uniform_(-1, 1)
+    B = torch.empty((n, n), device="cuda").uniform_(-1, 1)
+    out = torch.empty((n, n), device="cuda")
+    K.gemm(A, B, out)
+    ones = torch.ones((n, 1), device="cuda", dtype=torch.float64)
+    lhs = out.double() @ ones
+    rhs = A.double() @ (B.double() @ ones)
+    assert ((lhs - rhs).abs().max() / rhs.abs().max()).item() < TF32_TOL

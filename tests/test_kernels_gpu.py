@@ -1,0 +1,186 @@
+"""GPU parity of the row, elementwise and reduction kernels against the CPU
+oracle, through the C ABI. Tolerance (north_star): norm / softmax /
+elementwise <= 1e-5, measured as max|gpu - oracle| / max|oracle| per output.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def K():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from oxf import kernels
+    return kernels
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+# widths: warp-per-row tiers, block-per-row tiers, the 16384 cap, ragged
+# widths (looped path) and a width past the register cap
+WIDTHS = [1, 3, 4, 36, 128, 1000, 1024, 2048, 2052, 4096, 8192, 12288, 16384, 20000]
+ROWS = [1, 7, 33]
+
+
+def cases(rng, widths=WIDTHS, rows=ROWS):
+    for c in widths:
+        for r in rows:
+            if r * c > 2_000_000:
+                continue
+            yield r, c
+
+
+def test_softmax_rows(K, rng):
+    for r, c in cases(rng):
+        x = rng.standard_normal((r, c)).astype(np.float32) * 3
+        for scale, period in [(1.0, 0), (0.125, 0), (1.0, r)]:
+            want = O.softmax_rows(x, scale, period)
+            got = host(K.softmax_rows(dev(x), scale, period))
+            assert rel_err(got, want) < TOL, (r, c, scale, period)
+
+
+def test_softmax_causal_period_batched(K, rng):
+    # 3 sequences of 16 rows each: row index is taken modulo the period
+    x = rng.standard_normal((48, 16)).astype(np.float32)
+    got = host(K.softmax_rows(dev(x), 0.5, 16))
+    assert rel_err(got, O.softmax_rows(x, 0.5, 16)) < TOL
+    assert np.all(got[np.arange(48) % 16 == 0, 1:] == 0.0)
+
+
+def test_layer_norm_rows(K, rng):
+    for r, c in cases(rng):
+        x = (rng.standard_normal((r, c)) * 2 + 0.5).astype(np.float32)
+        assert rel_err(host(K.layer_norm_rows(dev(x))), O.layer_norm_rows(x)) < TOL, (r, c)
+
+
+def test_layer_norm_affine(K, rng):
+    for c in [36, 1024, 2048, 20000]:
+        x = rng.standard_normal((5, c)).astype(np.float32)
+        g = (1 + 0.1 * rng.standard_normal(c)).astype(np.float32)
+        b = (0.1 * rng.standard_normal(c)).astype(np.float32)
+        got = host(K.layer_norm_rows(dev(x), 1e-5, dev(g), dev(b)))
+        assert rel_err(got, O.layer_norm_rows(x, 1e-5, g, b)) < TOL
+
+
+def test_rms_norm_rows(K, rng):
+    for r, c in cases(rng):
+        x = rng.standard_normal((r, c)).astype(np.float32)
+        assert rel_err(host(K.rms_norm_rows(dev(x))), O.rms_norm_rows(x)) < TOL, (r, c)
+    x = rng.standard_normal((4, 1024)).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(1024)).astype(np.float32)
+    assert rel_err(host(K.rms_norm_rows(dev(x), 1e-5, dev(g))), O.rms_norm_rows(x, 1e-5, g)) < TOL
+
+
+def test_backward_kernels(K, rng):
+    for r, c in cases(rng):
+        x = rng.standard_normal((r, c)).astype(np.float32)
+        dy = rng.standard_normal((r, c)).astype(np.float32)
+        p = O.softmax_rows(x)
+        out = torch.empty((r, c), device="cuda")
+        assert rel_err(host(K.softmax_backward(dev(p), dev(dy), out, 0.5)),
+                       O.softmax_backward(p, dy, 0.5)) < TOL, (r, c)
+        assert rel_err(host(K.layer_norm_backward(dev(x), dev(dy), out)),
+                       O.layer_norm_backward(x, dy)) < 2 * TOL, (r, c)
+        assert rel_err(host(K.rms_norm_backward(dev(x), dev(dy), out)),
+                       O.rms_norm_backward(x, dy)) < TOL, (r, c)
+
+
+def test_row_and_column_sums(K, rng):
+    for r, c in cases(rng, rows=[1, 7, 257]):
+        x = rng.standard_normal((r, c)).astype(np.float32)
+        out = torch.empty(r, device="cuda")
+        assert rel_err(host(K.sum_rows(dev(x), out)), O.sum_rows(x)) < TOL, (r, c)
+        outc = torch.empty(c, device="cuda")
+        assert rel_err(host(K.sum_cols(dev(x), outc)), O.sum_cols(x)) < 1e-5, (r, c)
+        K.sum_cols(dev(x), outc, accumulate=True)
+        assert rel_err(host(outc), 2 * O.sum_cols(x)) < 1e-5
+
+
+def test_loss_rows_and_mse_grad(K, rng):
+    for r, c in cases(rng, widths=[1, 36, 1024, 2048, 20000]):
+        y = rng.standard_normal((r, c)).astype(np.float32)
+        t = rng.standard_normal((r, c)).astype(np.float32)
+        out = torch.empty(r, device="cuda")
+        assert rel_err(host(K.loss_rows(dev(y), dev(t), out)), O.loss_rows(y, t)) < TOL
+        g = torch.empty((r, c), device="cuda")
+        assert rel_err(host(K.mse_grad(dev(y), dev(t), g)), O.mse_grad(y, t)) < TOL
+
+
+@pytest.mark.parametrize("n", [0, 1, 3, 4, 1001, 4096, 1 << 20])
+def test_elementwise(K, rng, n):
+    a = rng.standard_normal(n).astype(np.float32)
+    b = (rng.standard_normal(n) + 3).astype(np.float32)
+    out = torch.empty(n, device="cuda")
+    if n == 0:
+        K.binary(dev(a), dev(b), out, 0)  # empty slices are a no-op
+        return
+    for op in range(4):
+        assert rel_err(host(K.binary(dev(a), dev(b), out, op)), O.binary(a, b, op)) < TOL
+        t = dev(a)
+        K.binary_assign(t, dev(b), op)
+        assert rel_err(host(t), O.binary(a, b, op)) < TOL
+    for act in (O.GELU, O.RELU, O.SILU):
+        assert rel_err(host(K.unary(dev(a), 2, act)), O.act_forward(act, a)) < TOL
+        assert rel_err(host(K.unary(dev(a), 3, act)), O.act_derivative(act, a)) < TOL
+    assert rel_err(host(K.unary(dev(a), 0, 0.25)), a * np.float32(0.25)) < TOL
+    assert rel_err(host(K.unary(dev(a), 1, 2.0)), a + np.float32(2.0)) < TOL
+    assert rel_err(host(K.unary(dev(a), 4)), 0.5 * a * a) < TOL
+    w = dev(a)
+    K.sgd_update(w, dev(b), 0.01)
+    assert rel_err(host(w), a - b * np.float32(0.01)) < TOL
+
+
+@pytest.mark.parametrize("c", [1, 3, 4, 1024, 1030])
+def test_binary_assign_by_rows(K, rng, c):
+    m = rng.standard_normal((9, c)).astype(np.float32)
+    v = (rng.standard_normal(c) + 2).astype(np.float32)
+    for op in range(4):
+        got = host(K.binary_assign_by_rows(dev(m), dev(v), op))
+        assert rel_err(got, O.binary_assign_by_rows(m, v, op)) < TOL
+
+
+def test_causal_mask_and_transpose(K, rng):
+    for r, c in [(1, 1), (5, 9), (33, 33), (100, 64), (1024, 1024)]:
+        m = rng.standard_normal((r, c)).astype(np.float32)
+        got = host(K.causal_mask(dev(m)))
+        np.testing.assert_array_equal(got, O.causal_mask(m))
+        out = torch.empty((c, r), device="cuda")
+        np.testing.assert_array_equal(host(K.transpose(dev(m), out)), m.T)
+
+
+def test_slice_reductions(K, rng):
+    for n in [0, 1, 1000, 1 << 20]:
+        x = rng.standard_normal(n).astype(np.float32)
+        out = torch.empty(1, device="cuda")
+        s = host(K.slice_sum(dev(x), out))[0]
+        assert abs(s - x.astype(np.float64).sum()) < 1e-4 * max(1.0, np.abs(x).sum())
+        mx = host(K.slice_max(dev(x), out))[0]
+        assert mx == (x.max() if n else np.float32(-3.4028235e38))
+
+
+def test_shape_validation_matches_reference_asserts(K):
+    from oxf._lib import OxfError, check, lib
+    t = torch.zeros(10, device="cuda")
+    # len % cols != 0 (norm.rs:12 needs whole rows)
+    with pytest.raises(OxfError):
+        check(lib().oxf_matrix_softmax_rows(K.ms(t), 3, 1.0, 0, None))
+    # row vector length must equal cols (rows.rs:18)
+    with pytest.raises(OxfError):
+        K.binary_assign_by_rows(torch.zeros(3, 4, device="cuda"), torch.zeros(5, device="cuda"), 0)

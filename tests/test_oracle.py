@@ -1,0 +1,196 @@
+"""CPU tests of the oracle itself: hand-derived known answers, the numpy
+golden fixtures (independent restatement), and finite-difference checks of
+every backward formula. These pin the checker before any GPU test trusts it.
+"""
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import rel_err
+
+GOLDEN = np.load(Path(__file__).resolve().parent / "golden" / "golden.npz")
+
+
+# ---------------------------------------------------------------- known answers
+def test_softmax_constant_row_is_uniform():
+    x = np.full((3, 37), 2.5, np.float32)
+    np.testing.assert_allclose(O.softmax_rows(x), 1.0 / 37, rtol=1e-6)
+
+
+def test_layer_norm_of_arithmetic_row():
+    # row [a, a+1, ..., a+n-1]: mean a+(n-1)/2, var (n^2-1)/12
+    n, a = 8, 3.0
+    x = (a + np.arange(n, dtype=np.float32))[None, :]
+    var = (n * n - 1) / 12.0
+    want = (np.arange(n) - (n - 1) / 2.0) / np.sqrt(var + 1e-5)
+    np.testing.assert_allclose(O.layer_norm_rows(x)[0], want, rtol=1e-5, atol=1e-6)
+
+
+def test_rms_norm_of_unit_row():
+    x = np.where(np.arange(10) % 2 == 0, 1.0, -1.0).astype(np.float32)[None, :]
+    np.testing.assert_allclose(O.rms_norm_rows(x)[0], x[0] / np.sqrt(1.0 + 1e-5), rtol=1e-6)
+
+
+def test_gelu_at_zero_and_limits():
+    z = np.array([0.0, 10.0, -10.0], np.float32)
+    y = O.act_forward(O.GELU, z)
+    assert y[0] == 0.0 and abs(y[1] - 10.0) < 1e-5 and abs(y[2]) < 1e-5
+    assert abs(O.act_derivative(O.GELU, np.array([0.0], np.float32))[0] - 0.5) < 1e-7
+
+
+def test_identity_linear():
+    x = np.random.default_rng(0).standard_normal((5, 4)).astype(np.float32)
+    lin = O.LinearParams(np.eye(4, dtype=np.float32))
+    y, _ = O.linear_forward(lin, x)
+    np.testing.assert_array_equal(y, x)
+
+
+def test_causal_mask_upper_triangle():
+    m = O.causal_mask(np.zeros((4, 4), np.float32))
+    assert np.isneginf(m[np.triu_indices(4, 1)]).all() and (m[np.tril_indices(4)] == 0).all()
+
+
+def test_tf32_rounding_bit_patterns():
+    # 1 + 2^-11 is a tie between 1 and 1 + 2^-10: RNA rounds away, RZ truncates.
+    x = np.float32(1.0 + 2.0 ** -11)
+    assert O.tf32_rna(float(x)) == 1.0 + 2.0 ** -10
+    assert O.tf32_rz(float(x)) == 1.0
+    assert O.tf32_rna(-float(x)) == -(1.0 + 2.0 ** -10)
+    assert O.tf32_rna(1.0 + 2.0 ** -12) == 1.0
+
+
+# ---------------------------------------------------------------- golden fixtures
+@pytest.mark.parametrize("name,fn", [
+    ("softmax", lambda x: O.softmax_rows(x)),
+    ("layer_norm", lambda x: O.layer_norm_rows(x)),
+    ("rms_norm", lambda x: O.rms_norm_rows(x)),
+    ("gelu", lambda x: O.act_forward(O.GELU, x)),
+    ("gelu_d", lambda x: O.act_derivative(O.GELU, x)),
+    ("sum_rows", lambda x: O.sum_rows(x)),
+    ("sum_cols", lambda x: O.sum_cols(x)),
+])
+def test_oracle_matches_golden_forward(name, fn):
+    assert rel_err(fn(GOLDEN["rows_x"]), GOLDEN[name]) < 2e-6
+
+
+def test_oracle_matches_golden_backward():
+    x, dy = GOLDEN["rows_x"], GOLDEN["rows_dy"]
+    p = O.softmax_rows(x)
+    assert rel_err(O.softmax_backward(p, dy), GOLDEN["softmax_bwd"]) < 2e-6
+    assert rel_err(O.layer_norm_backward(x, dy), GOLDEN["layer_norm_bwd"]) < 2e-6
+    assert rel_err(O.rms_norm_backward(x, dy), GOLDEN["rms_norm_bwd"]) < 2e-6
+    assert rel_err(O.loss_rows(x, GOLDEN["loss_t"]), GOLDEN["loss_rows"]) < 2e-6
+
+
+@pytest.mark.parametrize("rounding,tol", [(O.GEMM_F32, 1e-6), (O.GEMM_TF32_RNA, 2e-3),
+                                          (O.GEMM_TF32_RZ, 4e-3)])
+def test_oracle_gemm_golden(rounding, tol):
+    c = O.gemm(GOLDEN["gemm_a"], GOLDEN["gemm_b"], rounding=rounding)
+    assert rel_err(c, GOLDEN["gemm_c"]) < tol
+
+
+def test_oracle_gemm_transposed_modes():
+    A, B = GOLDEN["gemm_a"], GOLDEN["gemm_b"]
+    want = GOLDEN["gemm_c"]
+    assert rel_err(O.gemm(A.T.copy(), B, a_trans=True), want) < 1e-6
+    assert rel_err(O.gemm(A, B.T.copy(), b_trans=True), want) < 1e-6
+    assert rel_err(O.gemm(A.T.copy(), B.T.copy(), a_trans=True, b_trans=True), want) < 1e-6
+
+
+def _tiny_transformer(norm):
+    g = GOLDEN
+    k = f"tf_{norm}_"
+    lin = lambda n, act=O.IDENTITY: O.LinearParams(g[k + n], None, act)
+    ffn = O.MlpParams([lin("w1", O.GELU), lin("w2")])
+    nt = O.NORM_LAYER if norm == "layer" else O.NORM_RMS
+    return O.TransformerParams(lin("wq"), lin("wk"), lin("wv"), g[k + "pos"], ffn, lin("wo"), nt,
+                               g[k + "x"].shape[0])
+
+
+@pytest.mark.parametrize("norm", ["layer", "rms"])
+def test_oracle_transformer_step_golden(norm):
+    """Full training step (forward, backward, immediate SGD) against the
+    numpy restatement of encoder.rs:114-186."""
+    t = _tiny_transformer(norm)
+    k = f"tf_{norm}_"
+    y, loss, dx = O.transformer_train_step(t, GOLDEN[k + "x"], GOLDEN[k + "t"], 0.05)
+    assert rel_err(y, GOLDEN[k + "y"]) < 1e-5
+    assert rel_err(dx, GOLDEN[k + "dx"]) < 1e-4
+    for name, arr in [("wq", t.q.w), ("wk", t.k.w), ("wv", t.v.w), ("pos", t.position),
+                      ("w1", t.ffn.layers[0].w), ("w2", t.ffn.layers[1].w), ("wo", t.o.w)]:
+        assert rel_err(arr, GOLDEN[k + name + "_new"]) < 1e-5, name
+
+
+# ---------------------------------------------------------------- finite differences
+def _fd_check(f, x, dy, analytic, h=1e-3, n_probe=12, rng=None):
+    """Central differences of sum(f(x) * dy) w.r.t. probed entries of x."""
+    rng = rng or np.random.default_rng(7)
+    x = x.astype(np.float64)
+    idx = [tuple(rng.integers(0, s) for s in x.shape) for _ in range(n_probe)]
+    for i in idx:
+        xp, xm = x.copy(), x.copy()
+        xp[i] += h
+        xm[i] -= h
+        num = ((f(xp.astype(np.float32)).astype(np.float64) - f(xm.astype(np.float32))) * dy).sum() / (2 * h)
+        assert abs(num - analytic[i]) < 2e-2 * max(1.0, abs(num)), (i, num, analytic[i])
+
+
+def test_fd_layer_norm_backward(rng):
+    x = rng.standard_normal((3, 16)).astype(np.float32)
+    dy = rng.standard_normal((3, 16)).astype(np.float32)
+    _fd_check(O.layer_norm_rows, x, dy, O.layer_norm_backward(x, dy))
+
+
+def test_fd_rms_norm_backward(rng):
+    x = rng.standard_normal((3, 16)).astype(np.float32)
+    dy = rng.standard_normal((3, 16)).astype(np.float32)
+    _fd_check(O.rms_norm_rows, x, dy, O.rms_norm_backward(x, dy))
+
+
+def test_fd_softmax_backward(rng):
+    x = rng.standard_normal((3, 16)).astype(np.float32)
+    dy = rng.standard_normal((3, 16)).astype(np.float32)
+    _fd_check(O.softmax_rows, x, dy, O.softmax_backward(O.softmax_rows(x), dy))
+
+
+def test_fd_gelu_derivative(rng):
+    x = rng.standard_normal((4, 8)).astype(np.float32)
+    dy = rng.standard_normal((4, 8)).astype(np.float32)
+    _fd_check(lambda v: O.act_forward(O.GELU, v), x, dy, O.act_derivative(O.GELU, x) * dy)
+
+
+def test_fd_transformer_input_gradient():
+    """dL/dx of the oracle's training step against central differences of
+    the summed row loss (lr = 0 leaves the weights untouched)."""
+    t = _tiny_transformer("layer")
+    x, tg = GOLDEN["tf_layer_x"], GOLDEN["tf_layer_t"]
+    _, _, dx = O.transformer_train_step(t.copy(), x, tg, 0.0)
+
+    def loss(xx):
+        y = O.transformer_forward(t, xx)
+        return O.loss_rows(y, tg).astype(np.float64).sum()
+
+    rng = np.random.default_rng(3)
+    for _ in range(6):
+        i = (rng.integers(0, x.shape[0]), rng.integers(0, x.shape[1]))
+        xp, xm = x.astype(np.float64).copy(), x.astype(np.float64).copy()
+        xp[i] += 1e-2
+        xm[i] -= 1e-2
+        num = (loss(xp.astype(np.float32)) - loss(xm.astype(np.float32))) / 2e-2
+        assert abs(num - dx[i]) < 5e-3 + 5e-2 * abs(num), (i, num, dx[i])
+
+
+def test_grads_accumulate_equals_immediate_update():
+    """Deferred update from accumulated gradients == the reference's
+    immediate per-layer SGD for one sequence (the DP step relies on it)."""
+    t1 = _tiny_transformer("rms")
+    t2 = t1.copy()
+    x, tg = GOLDEN["tf_rms_x"], GOLDEN["tf_rms_t"]
+    O.transformer_train_step(t1, x, tg, 0.05)
+    g = np.zeros(t2.flat().size, np.float32)
+    O.transformer_train_step(t2, x, tg, 0.0, grads=g)
+    assert rel_err(t2.flat() - 0.05 * g, t1.flat()) < 1e-6
