@@ -40,6 +40,33 @@ int oxo_get_threads(void) {
 }
 
 /* ------------------------------------------------------------------------ */
+/* pairwise sums                                                             */
+
+/* Row reductions in the reference are shuffle trees over 32 lanes and then
+ * over 32 warps (row.rs:35-48): a pairwise sum restates them faithfully and,
+ * unlike a running sum, keeps the error O(log n) for wide rows. */
+static float psum(const float* x, size_t n) {
+    if (n <= 32) {
+        float s = 0.0f;
+        for (size_t i = 0; i < n; ++i) s += x[i];
+        return s;
+    }
+    size_t h = n / 2;
+    return psum(x, h) + psum(x + h, n - h);
+}
+
+static float* g_tmp = NULL;
+static size_t g_tmp_n = 0;
+static float* tmpbuf(size_t n) {
+    if (n > g_tmp_n) {
+        free(g_tmp);
+        g_tmp = (float*)malloc((n ? n : 1) * sizeof(float));
+        g_tmp_n = n;
+    }
+    return g_tmp;
+}
+
+/* ------------------------------------------------------------------------ */
 /* TF32 rounding                                                             */
 
 static inline uint32_t f2u(float x) { uint32_t u; memcpy(&u, &x, 4); return u; }
@@ -241,11 +268,7 @@ void oxo_activate(float* x, size_t n, int act) {
 
 /* matrix_sum_rows_device, row.rs:16-53. */
 void oxo_sum_rows(const float* m, float* out, size_t rows, size_t cols) {
-    for (size_t r = 0; r < rows; ++r) {
-        float s = 0.0f;
-        for (size_t c = 0; c < cols; ++c) s += m[r * cols + c];
-        out[r] = s;
-    }
+    for (size_t r = 0; r < rows; ++r) out[r] = psum(m + r * cols, cols);
 }
 
 /* linear.rs:267-270 computes the bias gradient as sum_rows(transpose(G)). */
@@ -283,11 +306,8 @@ void oxo_softmax_rows(float* m, size_t rows, size_t cols, float scale, size_t ca
         }
         float mx = -3.40282347e+38f; /* f32::MIN */
         for (size_t c = 0; c < cols; ++c) mx = x[c] > mx ? x[c] : mx;
-        float s = 0.0f;
-        for (size_t c = 0; c < cols; ++c) {
-            x[c] = expf(x[c] - mx);
-            s += x[c];
-        }
+        for (size_t c = 0; c < cols; ++c) x[c] = expf(x[c] - mx);
+        float s = psum(x, cols);
         for (size_t c = 0; c < cols; ++c) x[c] = x[c] / s;
     }
 }
@@ -298,14 +318,10 @@ void oxo_layer_norm_rows(float* m, size_t rows, size_t cols, float eps, const fl
                          const float* beta) {
     for (size_t r = 0; r < rows; ++r) {
         float* x = m + r * cols;
-        float s = 0.0f;
-        for (size_t c = 0; c < cols; ++c) s += x[c];
-        float mean = s / (float)cols;
-        float v = 0.0f;
-        for (size_t c = 0; c < cols; ++c) {
-            float d = x[c] - mean;
-            v += d * d;
-        }
+        float* t = tmpbuf(cols);
+        float mean = psum(x, cols) / (float)cols;
+        for (size_t c = 0; c < cols; ++c) t[c] = (x[c] - mean) * (x[c] - mean);
+        float v = psum(t, cols);
         float inv_std = 1.0f / sqrtf(v / (float)cols + eps);
         for (size_t c = 0; c < cols; ++c) {
             float y = (x[c] - mean) * inv_std;
@@ -320,9 +336,9 @@ void oxo_layer_norm_rows(float* m, size_t rows, size_t cols, float eps, const fl
 void oxo_rms_norm_rows(float* m, size_t rows, size_t cols, float eps, const float* gamma) {
     for (size_t r = 0; r < rows; ++r) {
         float* x = m + r * cols;
-        float s = 0.0f;
-        for (size_t c = 0; c < cols; ++c) s += x[c] * x[c];
-        float rms = sqrtf(s / (float)cols + eps);
+        float* t = tmpbuf(cols);
+        for (size_t c = 0; c < cols; ++c) t[c] = x[c] * x[c];
+        float rms = sqrtf(psum(t, cols) / (float)cols + eps);
         for (size_t c = 0; c < cols; ++c) {
             float y = x[c] / rms;
             if (gamma) y *= gamma[c];
@@ -337,8 +353,9 @@ void oxo_softmax_backward(const float* p, const float* dy, float* dx, size_t row
     for (size_t r = 0; r < rows; ++r) {
         const float* pr = p + r * cols;
         const float* gr = dy + r * cols;
-        float s = 0.0f;
-        for (size_t c = 0; c < cols; ++c) s += pr[c] * gr[c];
+        float* t = tmpbuf(cols);
+        for (size_t c = 0; c < cols; ++c) t[c] = pr[c] * gr[c];
+        float s = psum(t, cols);
         for (size_t c = 0; c < cols; ++c) dx[r * cols + c] = pr[c] * (gr[c] - s) * scale;
     }
 }
@@ -351,20 +368,13 @@ void oxo_layer_norm_backward(const float* x, const float* dy, float* dx, size_t 
     for (size_t r = 0; r < rows; ++r) {
         const float* xr = x + r * cols;
         const float* gr = dy + r * cols;
-        float s = 0.0f;
-        for (size_t c = 0; c < cols; ++c) s += xr[c];
-        float mean = s / n;
-        float v = 0.0f;
-        for (size_t c = 0; c < cols; ++c) {
-            float d = xr[c] - mean;
-            v += d * d;
-        }
-        float inv_std = 1.0f / sqrtf(v / n + eps);
-        float gs = 0.0f, gns = 0.0f;
-        for (size_t c = 0; c < cols; ++c) {
-            gs += gr[c];
-            gns += gr[c] * ((xr[c] - mean) * inv_std);
-        }
+        float* t = tmpbuf(cols);
+        float mean = psum(xr, cols) / n;
+        for (size_t c = 0; c < cols; ++c) t[c] = (xr[c] - mean) * (xr[c] - mean);
+        float inv_std = 1.0f / sqrtf(psum(t, cols) / n + eps);
+        float gs = psum(gr, cols);
+        for (size_t c = 0; c < cols; ++c) t[c] = gr[c] * ((xr[c] - mean) * inv_std);
+        float gns = psum(t, cols);
         for (size_t c = 0; c < cols; ++c) {
             float xh = (xr[c] - mean) * inv_std;
             dx[r * cols + c] = inv_std / n * (n * gr[c] - gs - xh * gns);
@@ -379,11 +389,11 @@ void oxo_rms_norm_backward(const float* x, const float* dy, float* dx, size_t ro
     for (size_t r = 0; r < rows; ++r) {
         const float* xr = x + r * cols;
         const float* gr = dy + r * cols;
-        float ss = 0.0f, dot = 0.0f;
-        for (size_t c = 0; c < cols; ++c) {
-            ss += xr[c] * xr[c];
-            dot += xr[c] * gr[c];
-        }
+        float* t = tmpbuf(cols);
+        for (size_t c = 0; c < cols; ++c) t[c] = xr[c] * xr[c];
+        float ss = psum(t, cols);
+        for (size_t c = 0; c < cols; ++c) t[c] = xr[c] * gr[c];
+        float dot = psum(t, cols);
         float rms = sqrtf(ss / n + eps);
         float inv = 1.0f / rms;
         float corr = dot / n * inv * inv * inv;
@@ -393,13 +403,13 @@ void oxo_rms_norm_backward(const float* x, const float* dy, float* dx, size_t ro
 
 /* Linear::loss_rows_default, linear.rs:325-333. */
 void oxo_loss_rows(const float* y, const float* t, float* row_loss, size_t rows, size_t cols) {
+    float* buf = tmpbuf(cols);
     for (size_t r = 0; r < rows; ++r) {
-        float s = 0.0f;
         for (size_t c = 0; c < cols; ++c) {
             float d = y[r * cols + c] - t[r * cols + c];
-            s += 0.5f * d * d;
+            buf[c] = 0.5f * d * d;
         }
-        row_loss[r] = s * (1.0f / (float)cols);
+        row_loss[r] = psum(buf, cols) * (1.0f / (float)cols);
     }
 }
 

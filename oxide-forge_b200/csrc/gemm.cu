@@ -98,13 +98,14 @@ __device__ __forceinline__ void decode_unit(const GemmArgs& a, long long u, int&
 }
 
 // Shared-memory descriptor of one K=8 slice of an operand tile.
-//  K-major tile: rows of 128 B (32 K values), 8-row swizzle atoms 1024 B
-//    apart (SBO); K slice kk starts kk*32 B into the row.
-//  MN-major tile: 32-element MN chunks of 32 K rows (4 KB, LBO apart);
-//    K slice kk is the kk-th 8-row atom (1024 B).
+//  K-major tile: rows of 128 B (32 K values), 128B swizzle in 8-row atoms
+//    1024 B apart (SBO); K slice kk starts kk*32 B into the row.
+//  MN-major tile: 32-element MN chunks (one TMA box of 32 K rows, 4 KB,
+//    LBO apart), 128B swizzle with 32-byte atoms: 4-row atoms 512 B apart
+//    (SBO); K slice kk starts at K row 8*kk (1024 B).
 __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int mn_major, int kk) {
-  return mn_major ? make_smem_desc_sw128(base + kk * 1024, 4096, 1024)
-                  : make_smem_desc_sw128(base + kk * 32, 16, 1024);
+  return mn_major ? make_smem_desc(base + kk * 1024, 4096, 512, kLayoutSW128Atom32B)
+                  : make_smem_desc(base + kk * 32, 16, 1024, kLayoutSW128);
 }
 
 template <int ROWS>
@@ -559,11 +560,12 @@ int sm_count(int dev) {
   return counts[dev];
 }
 
-// 2-D (or 3-D with a batch dimension) f32 tensor map, 128B swizzle,
-// zero fill outside the tensor.
+// 2-D (or 3-D with a batch dimension) f32 tensor map, zero fill outside the
+// tensor. K-major tiles use the 128B swizzle; MN-major tiles the 128B swizzle
+// with 32-byte atoms, matching the shared-memory descriptors above.
 bool encode_map(CUtensorMap* map, const float* ptr, long long inner, long long outer,
                 long long ld, int batch, long long bstride, int box_inner, int box_outer,
-                int* is3d) {
+                bool mn_major, int* is3d) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
   const bool three = batch > 1 && bstride != 0;
@@ -574,7 +576,8 @@ bool encode_map(CUtensorMap* map, const float* ptr, long long inner, long long o
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, three ? 3 : 2, const_cast<float*>(ptr),
                    dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   *is3d = three ? 1 : 0;
   return r == CUDA_SUCCESS;
@@ -637,7 +640,8 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
   if (d->M < 0 || d->N < 0 || d->K < 0 || d->batch < 1)
     return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: negative shape or batch < 1");
   if (d->M == 0 || d->N == 0) return OXF_OK;
-  if (!d->A || !d->B || !d->C) return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: null operand");
+  if (!d->C || (d->K > 0 && (!d->A || !d->B)))
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: null operand");
   const int split = d->split_k > 1 ? d->split_k : 1;
   if (split > 1 && !d->accumulate)
     return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: split_k > 1 requires accumulate");
@@ -737,9 +741,10 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
 
   // Tile width along N.
   const int sms = sm_count(dev);
+  // The 3xTF32 kernel is instantiated for BN = 128 only.
   int BN = 256;
   if (split3 || d->N <= 128) BN = 128;
-  if (d->N <= 64) BN = 64;
+  if (!split3 && d->N <= 64) BN = 64;
   if (!split3 && BN == 256) {
     const long long t256 = static_cast<long long>((d->M + BM - 1) / BM) * ((d->N + 255) / 256) *
                            d->batch;
@@ -764,11 +769,15 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
   const long long b_inner = d->b_trans ? d->K : d->N, b_outer = d->b_trans ? d->N : d->K;
   const int a_box_outer = a.a_mn ? 32 : BM;
   const int b_box_outer = a.b_mn ? 32 : BN;
-  bool ok = encode_map(&ta, A, a_inner, a_outer, lda, d->batch, sa, 32, a_box_outer, &a3d) &&
-            encode_map(&tb, B, b_inner, b_outer, ldb, d->batch, sb, 32, b_box_outer, &b3d);
+  const bool amn = a.a_mn != 0, bmn = a.b_mn != 0;
+  bool ok =
+      encode_map(&ta, A, a_inner, a_outer, lda, d->batch, sa, 32, a_box_outer, amn, &a3d) &&
+      encode_map(&tb, B, b_inner, b_outer, ldb, d->batch, sb, 32, b_box_outer, bmn, &b3d);
   if (ok && split3)
-    ok = encode_map(&ta_lo, A_lo, a_inner, a_outer, lda, d->batch, sa, 32, a_box_outer, &dummy) &&
-         encode_map(&tb_lo, B_lo, b_inner, b_outer, ldb, d->batch, sb, 32, b_box_outer, &dummy);
+    ok = encode_map(&ta_lo, A_lo, a_inner, a_outer, lda, d->batch, sa, 32, a_box_outer, amn,
+                    &dummy) &&
+         encode_map(&tb_lo, B_lo, b_inner, b_outer, ldb, d->batch, sb, 32, b_box_outer, bmn,
+                    &dummy);
   if (!ok) return set_error(OXF_ERR_CUDA, "oxf_gemm: cuTensorMapEncodeTiled failed");
   a.a3d = a3d;
   a.b3d = b3d;

@@ -180,15 +180,21 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, float (&v)[32
 // ---------------------------------------------------------------- descriptors
 // Shared-memory matrix descriptor (tcgen05 "version 1" layout):
 // [0,14) start>>4, [16,30) LBO>>4, [32,46) SBO>>4, [46,48) version=1,
-// [49,52) base offset, [52] LBO mode, [61,64) swizzle (2 = 128B).
-__device__ __forceinline__ uint64_t make_smem_desc_sw128(uint32_t smem_addr, uint32_t lbo_bytes,
-                                                         uint32_t sbo_bytes) {
+// [49,52) base offset, [52] LBO mode, [61,64) layout type:
+// 2 = 128B swizzle (16-byte atoms, 8-row / 1024 B pattern),
+// 1 = 128B swizzle with 32-byte atoms (4-row / 512 B pattern; the only
+//     layout tcgen05 accepts for MN-major 32-bit operands).
+constexpr uint32_t kLayoutSW128 = 2;
+constexpr uint32_t kLayoutSW128Atom32B = 1;
+
+__device__ __forceinline__ uint64_t make_smem_desc(uint32_t smem_addr, uint32_t lbo_bytes,
+                                                   uint32_t sbo_bytes, uint32_t layout) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
   d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= static_cast<uint64_t>(1) << 46;
-  d |= static_cast<uint64_t>(2) << 61;
+  d |= static_cast<uint64_t>(layout & 7u) << 61;
   return d;
 }
 

@@ -27,7 +27,8 @@ def K():
         pytest.skip("no CUDA device")
     from oxf import kernels
     yield kernels
-    assert kernels.device_error() == 0, "a bounded in-kernel wait timed out"
+    code = kernels.device_error()
+    assert code == 0, f"a bounded in-kernel wait timed out (code {code:#x})"
 
 
 def dev(a):
@@ -49,7 +50,11 @@ def operands(rng, M, N, Kd, at, bt, batch=None, dist="uniform"):
 
 
 def exact(A, B, at, bt):
-    return O.gemm_f64(A, B, a_trans=at, b_trans=bt)
+    """float64 product of the f32 operands (numpy BLAS; the oracle's
+    oxo_gemm_f64 computes the same thing, far slower)."""
+    a = A.astype(np.float64)
+    b = B.astype(np.float64)
+    return (a.T if at else a) @ (b.T if bt else b)
 
 
 SHAPES = [

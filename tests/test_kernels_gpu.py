@@ -88,18 +88,29 @@ def test_rms_norm_rows(K, rng):
     assert rel_err(host(K.rms_norm_rows(dev(x), 1e-5, dev(g))), O.rms_norm_rows(x, 1e-5, g)) < TOL
 
 
+def close(got, want, scale, tol=TOL):
+    """max|got - want| <= tol * scale, where scale is the magnitude of the
+    largest term the formula combines (not of its possibly cancelling
+    result)."""
+    return float(np.abs(np.asarray(got, np.float64) - want).max()) <= tol * scale
+
+
 def test_backward_kernels(K, rng):
     for r, c in cases(rng):
         x = rng.standard_normal((r, c)).astype(np.float32)
         dy = rng.standard_normal((r, c)).astype(np.float32)
         p = O.softmax_rows(x)
         out = torch.empty((r, c), device="cuda")
-        assert rel_err(host(K.softmax_backward(dev(p), dev(dy), out, 0.5)),
-                       O.softmax_backward(p, dy, 0.5)) < TOL, (r, c)
-        assert rel_err(host(K.layer_norm_backward(dev(x), dev(dy), out)),
-                       O.layer_norm_backward(x, dy)) < 2 * TOL, (r, c)
-        assert rel_err(host(K.rms_norm_backward(dev(x), dev(dy), out)),
-                       O.rms_norm_backward(x, dy)) < TOL, (r, c)
+        got = host(K.softmax_backward(dev(p), dev(dy), out, 0.5))
+        assert close(got, O.softmax_backward(p, dy, 0.5), np.abs(p * dy).max() + 1e-30), (r, c)
+        # LN: dx = inv_std/N (N dy - sum dy - xhat sum(dy xhat)): terms ~ inv_std |dy|
+        inv_std = 1 / np.sqrt(x.var(axis=1, keepdims=True) + 1e-5)
+        got = host(K.layer_norm_backward(dev(x), dev(dy), out))
+        assert close(got, O.layer_norm_backward(x, dy), np.abs(inv_std * dy).max(), 2 * TOL), (r, c)
+        # RMS: dx = dy/r - x sum(x dy)/(N r^3): terms ~ |dy|/r
+        inv_r = 1 / np.sqrt((x * x).mean(axis=1, keepdims=True) + 1e-5)
+        got = host(K.rms_norm_backward(dev(x), dev(dy), out))
+        assert close(got, O.rms_norm_backward(x, dy), np.abs(inv_r * dy).max()), (r, c)
 
 
 def test_row_and_column_sums(K, rng):
