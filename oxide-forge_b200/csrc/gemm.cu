@@ -41,6 +41,7 @@ struct GemmArgs {
   int M, N, K, batch;
   int a_mn, b_mn;  // operand stored MN-major (contiguous along M / N)
   int a3d, b3d;    // tensor map carries a batch coordinate
+  int a_chunked, b_chunked;  // MN-major tile loaded by one (32, K, chunk) box
   int tiles_m, tiles_n, splits, kblocks;
   long long units;
   uint32_t idesc;
@@ -110,10 +111,15 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int mn_major, in
 
 template <int ROWS>
 __device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* map, uint64_t* bar,
-                                             int mn_major, int is3d, int row0, int k0, int b) {
+                                             int mn_major, int is3d, int chunked, int row0, int k0,
+                                             int b) {
   if (!mn_major) {
     if (is3d) tma_load_3d(dst, map, bar, k0, row0, b);
     else tma_load_2d(dst, map, bar, k0, row0);
+  } else if (chunked) {
+    // One box covers all ROWS/32 chunks: smem chunk c lands at c * 4096 B.
+    if (is3d) tma_load_4d(dst, map, bar, 0, k0, row0 / 32, b);
+    else tma_load_3d(dst, map, bar, 0, k0, row0 / 32);
   } else {
 #pragma unroll
     for (int c = 0; c < ROWS / 32; ++c) {
@@ -244,15 +250,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           uint8_t* slot = ring + stage * Cfg::STAGE_BYTES;
           mbar_arrive_expect_tx(&ctrl->full[stage], Cfg::STAGE_BYTES);
           const int k0 = kb * BK;
-          load_operand<BM>(slot, &tmA, &ctrl->full[stage], args.a_mn, args.a3d, tm * BM, k0, b);
+          load_operand<BM>(slot, &tmA, &ctrl->full[stage], args.a_mn, args.a3d, args.a_chunked,
+                           tm * BM, k0, b);
           load_operand<BN>(slot + Cfg::A_BYTES, &tmB, &ctrl->full[stage], args.b_mn, args.b3d,
-                           tn * BN, k0, b);
+                           args.b_chunked, tn * BN, k0, b);
           if (SPLIT3) {
             uint8_t* lo = slot + Cfg::A_BYTES + Cfg::B_BYTES;
-            load_operand<BM>(lo, &tmA_lo, &ctrl->full[stage], args.a_mn, args.a3d, tm * BM, k0,
-                             b);
+            load_operand<BM>(lo, &tmA_lo, &ctrl->full[stage], args.a_mn, args.a3d,
+                             args.a_chunked, tm * BM, k0, b);
             load_operand<BN>(lo + Cfg::A_BYTES, &tmB_lo, &ctrl->full[stage], args.b_mn,
-                             args.b3d, tn * BN, k0, b);
+                             args.b3d, args.b_chunked, tn * BN, k0, b);
           }
           ++fills;
           if (++stage == STAGES) {
@@ -569,6 +576,22 @@ bool encode_map(CUtensorMap* map, const float* ptr, long long inner, long long o
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
   const bool three = batch > 1 && bstride != 0;
+  if (mn_major && box_outer > 32) {
+    // Chunked MN-major view: (32 elements, K rows, inner/32 chunks[, batch]).
+    // Only used when inner % 32 == 0, so no box reads past a row's end.
+    cuuint64_t dims[4] = {32, static_cast<cuuint64_t>(outer), static_cast<cuuint64_t>(inner / 32),
+                          static_cast<cuuint64_t>(batch)};
+    cuuint64_t strides[3] = {static_cast<cuuint64_t>(ld) * 4, 128,
+                             static_cast<cuuint64_t>(bstride) * 4};
+    cuuint32_t box[4] = {32, 32, static_cast<cuuint32_t>(box_outer / 32), 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, three ? 4 : 3, const_cast<float*>(ptr),
+                     dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    *is3d = three ? 1 : 0;
+    return r == CUDA_SUCCESS;
+  }
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer),
                         static_cast<cuuint64_t>(batch)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 4, static_cast<cuuint64_t>(bstride) * 4};
@@ -767,8 +790,12 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
   int a3d = 0, b3d = 0, dummy = 0;
   const long long a_inner = d->a_trans ? d->M : d->K, a_outer = d->a_trans ? d->K : d->M;
   const long long b_inner = d->b_trans ? d->K : d->N, b_outer = d->b_trans ? d->N : d->K;
-  const int a_box_outer = a.a_mn ? 32 : BM;
-  const int b_box_outer = a.b_mn ? 32 : BN;
+  // MN-major tiles whose extent is a multiple of 32 load in one chunked box
+  // (box_outer carries the tile rows); otherwise one 32x32 box per chunk.
+  a.a_chunked = a.a_mn && (a_inner % 32 == 0) ? 1 : 0;
+  a.b_chunked = a.b_mn && (b_inner % 32 == 0) ? 1 : 0;
+  const int a_box_outer = a.a_mn ? (a.a_chunked ? BM : 32) : BM;
+  const int b_box_outer = a.b_mn ? (a.b_chunked ? BN : 32) : BN;
   const bool amn = a.a_mn != 0, bmn = a.b_mn != 0;
   bool ok =
       encode_map(&ta, A, a_inner, a_outer, lda, d->batch, sa, 32, a_box_outer, amn, &a3d) &&
