@@ -1,0 +1,349 @@
+#!/usr/bin/env python
+"""Benchmark: Transformer fwd+bwd tokens/s (BASELINE.json metric) on the
+training config: single-head Post-Norm transformer, seq 1024, hidden 2048,
+FFN 2048->8192->2048 GELU, NormType::Layer, output width = hidden,
+Xavier-uniform weights, inputs and MSE targets N(0,1); a global batch of
+128 sequences, data-parallel over the GPUs (one process per GPU, NCCL
+all-reduce of parameter gradients), one SGD step per batch.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl oxf|reference]
+
+For N > 1 launch under torch.distributed.run (RANK / LOCAL_RANK /
+WORLD_SIZE / MASTER_* from the environment). Rank 0 prints one JSON line.
+
+  value       tokens/s of the whole job with inputs resident in HBM
+              (device time, CUDA events, max over ranks)
+  e2e         the same metric through the public step API with host
+              buffers: pinned host -> device copies of each step's inputs and
+              targets and a device -> host read of the loss, every step
+  roofline    the TF32 GEMMs (the dominant kernel class): algorithmic flops
+              over their CUDA-event time inside the timed region, against
+              cuBLAS TF32 measured on this GPU in the same run
+  cpu_baseline the C oracle (oracle/) training one sequence on the host cores
+--impl reference times that CPU implementation alone (the reference itself
+is Rust + cuda-oxide and cannot be built in this image).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "oxide-forge_b200"))
+
+SEQ, HIDDEN, FFN, GLOBAL_BATCH, LR = 1024, 2048, 8192, 128, 1e-3
+METRIC = "Transformer fwd+bwd tokens/s"
+UNIT = "tokens/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="oxf", choices=["oxf", "reference"])
+    ap.add_argument("--global-batch", type=int, default=GLOBAL_BATCH)
+    ap.add_argument("--seq", type=int, default=SEQ)
+    ap.add_argument("--hidden", type=int, default=HIDDEN)
+    ap.add_argument("--ffn", type=int, default=FFN)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+def config_dict(a, world, l2_note=True):
+    return {"workload": "C5 single-head Post-Norm transformer training step (fwd+bwd+SGD)",
+            "model": "oxide-forge transformer block", "seq_len": a.seq, "hidden": a.hidden,
+            "ffn": a.ffn, "out": a.hidden, "norm": "layer", "global_batch": a.global_batch,
+            "tokens_per_step": a.global_batch * a.seq, "parallelism": f"dp{world}",
+            "lr": LR, "l2": "inputs larger than L2 (1 GiB activations); no flush needed"}
+
+
+def flops_per_token(a) -> float:
+    """fwd flops/token = 2*(3H^2 + 2SH + 2HF + HO); training = 3x fwd."""
+    H, S, F, O = a.hidden, a.seq, a.ffn, a.hidden
+    return 3 * 2 * (3 * H * H + 2 * S * H + 2 * H * F + H * O)
+
+
+# ------------------------------------------------------------------ CPU side
+def cpu_train_sequence(a, threads: int = 0):
+    """One oracle training step on one sequence of the workload; returns
+    (seconds, threads used)."""
+    import numpy as np
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+    from oxf import models
+    n = O.set_threads(threads)
+    cfg = models.transformer_config(a.seq, a.hidden, a.ffn, norm=1)
+    flat = models.init_transformer_params(cfg, seed=0)
+    parts = models.split_params(cfg, flat)
+    it = iter(parts)
+    lin = lambda act=O.IDENTITY: O.LinearParams(next(it), None, act)
+    q, k, v = lin(), lin(), lin()
+    pos = next(it)
+    ffn = O.MlpParams([lin(O.GELU), lin()])
+    o = lin()
+    t = O.TransformerParams(q, k, v, pos, ffn, o, O.NORM_LAYER, a.seq)
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((a.seq, a.hidden)).astype(np.float32)
+    tg = rng.standard_normal((a.seq, a.hidden)).astype(np.float32)
+    t0 = time.perf_counter()
+    O.transformer_train_step(t, x, tg, LR, rounding=O.GEMM_TF32_RNA)
+    return time.perf_counter() - t0, n
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    times = []
+    cores = 0
+    for i in range(a.warmup + a.steps):
+        dt, cores = cpu_train_sequence(a)
+        if i >= a.warmup:
+            times.append(dt)
+    sec = statistics.median(times)
+    value = a.seq / sec
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+            "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32 (tf32-rounded GEMM operands)",
+            "data": "synthetic (seeded N(0,1) inputs/targets, Xavier-uniform weights)",
+            "config": config_dict(a, 1),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": f"1 sequence of {a.seq} tokens per step (median of "
+                                       f"{a.steps})"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "note": "the reference (Rust + cuda-oxide) cannot be built in this image; this is "
+                    "the C oracle restatement of its algorithm on the host cores"}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def start(self):
+        def run():
+            while not self._stop.is_set():
+                try:
+                    out = subprocess.run(["nvidia-smi", "-i", str(self.gpu),
+                                          f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits"],
+                                         capture_output=True, text=True, timeout=5).stdout
+                    self.rows.append([c.strip() for c in out.strip().split(",")])
+                except Exception:
+                    pass
+                self._stop.wait(0.2)
+        self._t = threading.Thread(target=run, daemon=True)
+        self._t.start()
+
+    def stop(self):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+        mhz, maxmhz, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            try:
+                mhz.append(float(r[1]))
+                maxmhz = max(maxmhz, float(r[2]))
+                for n, v in zip(names, r[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                pass
+        return {"sm_mhz": statistics.median(mhz) if mhz else None,
+                "sm_max_mhz": maxmhz or None, "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+# ------------------------------------------------------------------ GPU side
+def cublas_tf32_peak(torch) -> float:
+    """TF32 dense GEMM throughput of cuBLAS (torch.matmul) at 8192^3,
+    best of 10 after warm-up: the roofline denominator for TF32 kernels."""
+    n = 8192
+    a = torch.randn(n, n, device="cuda")
+    b = torch.randn(n, n, device="cuda")
+    c = torch.empty(n, n, device="cuda")
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    for _ in range(3):
+        torch.matmul(a, b, out=c)
+    best = float("inf")
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(10):
+        s.record()
+        torch.matmul(a, b, out=c)
+        e.record()
+        e.synchronize()
+        best = min(best, s.elapsed_time(e))
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    del a, b, c
+    return 2 * n ** 3 / (best * 1e-3) / 1e12
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+        return
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from oxf import _lib, models
+    from oxf.dp import DataParallelTrainer
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    lib = _lib.lib()
+
+    cfg = models.transformer_config(a.seq, a.hidden, a.ffn, norm=_lib.NORM_LAYER)
+    local_batch = a.global_batch // world
+    stream = torch.cuda.current_stream()
+    model = models.Transformer(cfg, max_batch=local_batch, stream=stream)
+    model.set_params(models.init_transformer_params(cfg, seed=0))
+    trainer = DataParallelTrainer(model, a.global_batch, LR, a.seq)
+    trainer.broadcast_params(model.params)
+
+    rows = local_batch * a.seq
+    g = torch.Generator(device="cuda").manual_seed(1000 + rank)
+    x = torch.randn(rows, a.hidden, device="cuda", generator=g)
+    t = torch.randn(rows, a.hidden, device="cuda", generator=g)
+
+    peak = cublas_tf32_peak(torch)
+
+    # ---------------- device-resident timing
+    for _ in range(a.warmup):
+        trainer.step(x, t)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    model.set_timing(True)
+    launches0 = lib.oxf_kernel_launches()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(a.steps):
+        loss = trainer.step(x, t)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    elapsed_ms = ev0.elapsed_time(ev1)
+    launches = lib.oxf_kernel_launches() - launches0
+    gemm_ms, gemm_flops, gemm_launches = model.read_timing()
+    model.set_timing(False)
+    clk = clocks.stop()
+    if world > 1:
+        dist.barrier()
+        tt = torch.tensor([elapsed_ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        elapsed_ms = tt.item()
+    tokens = a.global_batch * a.seq * a.steps
+    value = tokens / (elapsed_ms * 1e-3)
+    final_loss = float(loss.item())
+
+    # ---------------- end-to-end through host buffers
+    e2e = None
+    if not a.no_e2e:
+        xh = torch.randn(rows, a.hidden, generator=torch.Generator().manual_seed(7 + rank)).pin_memory()
+        th = torch.randn(rows, a.hidden, generator=torch.Generator().manual_seed(9 + rank)).pin_memory()
+        xd = torch.empty_like(x)
+        td = torch.empty_like(t)
+        lh = torch.empty(1).pin_memory()
+
+        def e2e_step():
+            xd.copy_(xh, non_blocking=True)
+            td.copy_(th, non_blocking=True)
+            l = trainer.step(xd, td)
+            lh.copy_(l, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            return float(lh.item())
+
+        for _ in range(max(1, a.warmup)):
+            e2e_step()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        w0 = time.perf_counter()
+        for _ in range(a.steps):
+            e2e_step()
+        e2e_s = time.perf_counter() - w0
+        if world > 1:
+            tt = torch.tensor([e2e_s], device="cuda")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            e2e_s = tt.item()
+        e2e = {"value": tokens / e2e_s, "unit": UNIT,
+               "h2d_bytes_per_step": int(xh.numel() * 4 + th.numel() * 4),
+               "d2h_bytes_per_step": 4,
+               "api": "oxf.dp.DataParallelTrainer.step (liboxf.so engine) with pinned host "
+                      "inputs/targets copied every step; wall clock, max over ranks"}
+
+    # ---------------- CPU baseline (rank 0, N = 1)
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu:
+        try:
+            dt, cores = cpu_train_sequence(a)
+            cpu = {"value": a.seq / dt, "unit": UNIT, "cores": cores, "kind": "port",
+                   "sample": f"one {a.seq}-token sequence, full fwd+bwd+SGD, C oracle "
+                             f"(TF32-RNA operand rounding), {cores} threads, {dt:.1f} s"}
+        except Exception as ex:  # the oracle is only a reported baseline
+            cpu = {"value": None, "unit": UNIT, "cores": 0, "kind": "port",
+                   "sample": f"unavailable: {ex}"}
+
+    if rank == 0:
+        achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
+        fpt = flops_per_token(a)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": elapsed_ms / a.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32 (TF32 tensor-core products, f32 accumulation)",
+            "data": "synthetic (seeded N(0,1) inputs/targets, Xavier-uniform weights)",
+            "config": config_dict(a, world),
+            "e2e": e2e,
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": (achieved / peak) if achieved else None,
+                         "traffic": None, "kernel": "gemm_tf32_tcgen05 (all GEMMs of a step)",
+                         "gemm_launches_per_step": gemm_launches // max(1, a.steps),
+                         "gemm_share_of_step": gemm_ms / elapsed_ms if elapsed_ms else None,
+                         "peak_source": "cuBLAS TF32 8192^3 (torch.matmul) measured in this run"},
+            "model_tflops": value * fpt / 1e12,
+            "cpu_baseline": cpu,
+            "clocks": clk,
+            "final_loss": final_loss,
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -70,6 +70,9 @@ typedef enum {
   OXF_UNARY_HALF_SQUARE = 4
 } oxf_unary_op;
 
+/* NormType, src/net/transformer.rs:7-13 (Rms = 0, Layer = 1). */
+typedef enum { OXF_NORM_RMS = 0, OXF_NORM_LAYER = 1 } oxf_norm_type;
+
 /* ---------------------------------------------------------------- status */
 const char* oxf_last_error_string(void);
 /* Reads and clears the device error word that bounded in-kernel waits set
@@ -77,6 +80,8 @@ const char* oxf_last_error_string(void);
 oxf_status oxf_device_error(uint32_t* code);
 /* Library version string. */
 const char* oxf_version(void);
+/* Kernels this library has launched in this process (all devices). */
+unsigned long long oxf_kernel_launches(void);
 
 /* ---------------------------------------------------------------- elementwise */
 /* slice_binary (module.rs:36-43): out = lhs op rhs over min(len). */
@@ -127,6 +132,21 @@ oxf_status oxf_matrix_layer_norm_rows(oxf_slice matrix, size_t cols, float epsil
 /* rms_norm_assign (module.rs:226-231), in place; gamma may be NULL. */
 oxf_status oxf_rms_norm_assign(oxf_slice matrix, size_t cols, float epsilon, const float* gamma,
                                oxf_stream stream);
+/* Normalization::forward (attention.rs:157-162) out of place: output =
+ * LayerNorm or RMSNorm of input by rows (input == output is allowed). */
+oxf_status oxf_norm_rows(oxf_cslice input, oxf_slice output, size_t cols, int norm_type,
+                         float epsilon, const float* gamma, const float* beta, oxf_stream stream);
+/* Normalization::backward (attention.rs:164-174). */
+oxf_status oxf_norm_rows_backward(oxf_cslice input, oxf_cslice output_gradient, oxf_slice result,
+                                  size_t cols, int norm_type, float epsilon, oxf_stream stream);
+/* out[i] = lhs[i] op rhs[i % rhs.len]: the position table added to every
+ * sequence of a batch (inference.rs:78, encoder.rs:117). */
+oxf_status oxf_slice_binary_broadcast(oxf_cslice lhs, oxf_cslice rhs, oxf_slice out,
+                                      oxf_binary_op op, oxf_stream stream);
+/* gradient[i] *= act'(pre_activation[i]): Linear::backward's clone +
+ * derivative + multiply (linear.rs:254-265) in one pass. */
+oxf_status oxf_slice_mul_act_derivative(oxf_slice gradient, oxf_cslice pre_activation,
+                                        oxf_activation act, oxf_stream stream);
 /* softmax_rows_backward (module.rs:141-151): dx = scale * p*(dy - sum(p*dy)). */
 oxf_status oxf_softmax_rows_backward(oxf_cslice probabilities, oxf_cslice output_gradient,
                                      oxf_slice result, size_t cols, float scale,

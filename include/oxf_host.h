@@ -1,0 +1,133 @@
+/*
+ * oxf_host.h — C ABI of the host executors (the batched MLP and transformer
+ * engines of oxide-forge_b200/host/engine.hpp).
+ *
+ * These replace the reference's executor layer for the hot path:
+ *   InferenceTransformer / TrainingTransformer (src/net/transformer/
+ *   encoder.rs:37-187, decoder.rs:7-53, inference.rs:76-109),
+ *   Attention (src/net/transformer/attention.rs:177-402),
+ *   MlpExecutor / InferenceMLP / TrainingMlp (src/net/mlp.rs:14-269),
+ *   Linear (src/net/linear.rs:72-533).
+ * The reference drives one [seq, hidden] sequence per call; these drive
+ * `batch` independent sequences (or rows) per call with the same
+ * arithmetic. Parameters and gradients are flat f32 device arenas in
+ * checkpoint cursor order (inference.rs:52-66, metadata.rs:21-68): per
+ * Linear the weight [in, out] row-major, then its bias; for the transformer
+ * q, k, v, position [seq, hidden], the feed-forward layers, the output.
+ * Device pointers unless a name ends in _host. Same error conventions as
+ * oxf.h.
+ */
+#ifndef OXF_HOST_H
+#define OXF_HOST_H
+
+#include "oxf.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* One Linear layer (linear.rs:72-86): weights [in,out], optional bias. */
+typedef struct {
+  int in, out;
+  int act;  /* oxf_activation */
+  int bias; /* 0/1 */
+} oxf_layer_spec;
+
+#define OXF_MAX_LAYERS 16
+
+/* MlpExecutor (mlp.rs:14-19). res_start/res_end = -1: no residual. */
+typedef struct {
+  int n_layers;
+  oxf_layer_spec layers[OXF_MAX_LAYERS];
+  int res_start, res_end;
+} oxf_mlp_spec;
+
+/* Single-block Post-Norm transformer (TransformerMetadata,
+ * inference.rs:12-24). */
+typedef struct {
+  int seq, hidden;
+  int norm; /* oxf_norm_type */
+  oxf_layer_spec q, k, v;
+  oxf_mlp_spec ffn;
+  oxf_layer_spec out;
+} oxf_transformer_spec;
+
+typedef struct oxf_transformer_s* oxf_transformer;
+typedef struct oxf_mlp_s* oxf_mlp;
+
+/* ---------------------------------------------------------------- transformer */
+/* Builds an engine for up to max_batch sequences on the current device;
+ * work runs on `stream` (NULL: a stream the engine creates). Parameters
+ * start at zero. */
+oxf_status oxf_transformer_create(const oxf_transformer_spec* spec, int max_batch,
+                                  oxf_stream stream, oxf_transformer* out);
+oxf_status oxf_transformer_destroy(oxf_transformer t);
+size_t oxf_transformer_param_count(oxf_transformer t);
+/* Device arenas (param_count floats each), cursor order. */
+float* oxf_transformer_params(oxf_transformer t);
+float* oxf_transformer_grads(oxf_transformer t);
+oxf_stream oxf_transformer_stream(oxf_transformer t);
+/* Host <-> device copies of the parameter arena (synchronous). */
+oxf_status oxf_transformer_set_params_host(oxf_transformer t, const float* params_host);
+oxf_status oxf_transformer_get_params_host(oxf_transformer t, float* params_host);
+
+/* InferenceTransformer::forward (encoder.rs:55-57) or the decoder's masked
+ * forward (decoder.rs:50-52, causal = 1): x [batch*seq, hidden] ->
+ * y [batch*seq, out] (y may be NULL: read it with oxf_transformer_output). */
+oxf_status oxf_transformer_forward(oxf_transformer t, const float* x, int batch, int causal,
+                                   float* y);
+/* TrainingTransformer::forward (encoder.rs:114-133). */
+oxf_status oxf_transformer_train_forward(oxf_transformer t, const float* x, int batch);
+/* Per-row loss (Linear::loss_rows, linear.rs:325-333) and dL/dy =
+ * (y - target)/out against `target` [batch*seq, out]. */
+oxf_status oxf_transformer_set_target(oxf_transformer t, const float* target);
+/* Or a caller-computed dL/dy [batch*seq, out]. */
+oxf_status oxf_transformer_set_output_gradient(oxf_transformer t, const float* dy);
+/* TrainingTransformer::backward (encoder.rs:135-186) in stages 0 (output
+ * Linear), 1 (feed-forward), 2 (attention, Q/K/V, position). Parameter
+ * gradients ACCUMULATE into the gradient arena; nothing is updated. */
+oxf_status oxf_transformer_backward_stage(oxf_transformer t, int stage);
+/* [offset, offset+count) of the gradient arena that stage writes. */
+oxf_status oxf_transformer_bucket(oxf_transformer t, int stage, size_t* offset, size_t* count);
+oxf_status oxf_transformer_zero_grads(oxf_transformer t);
+/* params -= lr * grads (the reference's per-Linear SGD, linear.rs:373-391,
+ * and position update, encoder.rs:180-184, applied once). */
+oxf_status oxf_transformer_sgd(oxf_transformer t, float lr);
+/* Device views of the last output [batch*seq, out], per-row loss
+ * [batch*seq] and input gradient [batch*seq, hidden]. */
+oxf_status oxf_transformer_output(oxf_transformer t, const float** y, const float** row_loss,
+                                  const float** input_gradient);
+/* GEMM timing: while on, CUDA events bracket every GEMM the engine
+ * launches; read returns the summed device time (ms), summed algorithmic
+ * flops (2*M*N*K per product) and launch count since the last read, and
+ * resets them. Synchronises on the recorded events. */
+oxf_status oxf_transformer_set_timing(oxf_transformer t, int on);
+oxf_status oxf_transformer_read_timing(oxf_transformer t, double* gemm_ms, double* gemm_flops,
+                                       int* launches);
+/* One data-parallel-free training step through host memory: copies x and
+ * target from the host, runs forward, loss, backward, and SGD on the mean
+ * gradient (lr / batch), and returns the mean row loss. */
+oxf_status oxf_transformer_train_step_host(oxf_transformer t, const float* x_host,
+                                           const float* target_host, int batch, float lr,
+                                           float* mean_loss_host);
+
+/* ---------------------------------------------------------------- MLP */
+oxf_status oxf_mlp_create(const oxf_mlp_spec* spec, size_t max_rows, oxf_stream stream,
+                          oxf_mlp* out);
+oxf_status oxf_mlp_destroy(oxf_mlp m);
+size_t oxf_mlp_param_count(oxf_mlp m);
+float* oxf_mlp_params(oxf_mlp m);
+float* oxf_mlp_grads(oxf_mlp m);
+/* MlpExecutor::forward (mlp.rs:53-85): y [rows, out] = MLP(x [rows, in]).
+ * x must stay valid until oxf_mlp_backward. */
+oxf_status oxf_mlp_forward(oxf_mlp m, const float* x, float* y, size_t rows);
+/* MlpExecutor::backward (mlp.rs:121-168) without the update: accumulates
+ * parameter gradients, writes dx [rows, in] (may be NULL). */
+oxf_status oxf_mlp_backward(oxf_mlp m, const float* dy, float* dx, size_t rows);
+oxf_status oxf_mlp_zero_grads(oxf_mlp m);
+oxf_status oxf_mlp_sgd(oxf_mlp m, float lr);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -111,22 +111,30 @@ static inline float b_at(const float* B, size_t N, size_t K, int bt, size_t k, s
 static void gemm_rows(const float* A, const float* B, float* C, size_t M, size_t N, size_t K,
                       int at, int bt, int rounding, float alpha, float beta, size_t r0,
                       size_t r1) {
-    float* acc = (float*)malloc(N * sizeof(float));
+    float* acc = (float*)malloc((N ? N : 1) * sizeof(float));
     float* arow = (float*)malloc((K ? K : 1) * sizeof(float));
     for (size_t m = r0; m < r1; ++m) {
-        for (size_t n = 0; n < N; ++n) acc[n] = 0.0f;
         for (size_t k = 0; k < K; ++k) arow[k] = round_op(a_at(A, M, K, at, m, k), rounding);
-        for (size_t k = 0; k < K; ++k) {
-            const float a = arow[k];
-            if (!bt) {
+        if (bt) {
+            /* B stored [N,K]: each output is a contiguous dot product. */
+            for (size_t n = 0; n < N; ++n) {
+                const float* brow = B + n * K;
+                float s = 0.0f;
+                if (rounding == OXO_GEMM_F32)
+                    for (size_t k = 0; k < K; ++k) s += arow[k] * brow[k];
+                else
+                    for (size_t k = 0; k < K; ++k) s += arow[k] * round_op(brow[k], rounding);
+                acc[n] = s;
+            }
+        } else {
+            for (size_t n = 0; n < N; ++n) acc[n] = 0.0f;
+            for (size_t k = 0; k < K; ++k) {
+                const float a = arow[k];
                 const float* brow = B + k * N;
-                if (rounding == OXO_GEMM_F32) {
+                if (rounding == OXO_GEMM_F32)
                     for (size_t n = 0; n < N; ++n) acc[n] += a * brow[n];
-                } else {
+                else
                     for (size_t n = 0; n < N; ++n) acc[n] += a * round_op(brow[n], rounding);
-                }
-            } else {
-                for (size_t n = 0; n < N; ++n) acc[n] += a * round_op(B[n * K + k], rounding);
             }
         }
         for (size_t n = 0; n < N; ++n) {

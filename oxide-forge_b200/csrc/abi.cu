@@ -5,6 +5,7 @@
 // then forwards to the kernels in rows.cu / gemm.cu on the caller's stream.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -18,11 +19,15 @@ namespace oxf {
 oxf_status rows_softmax(float*, long long, long long, float, long long, cudaStream_t);
 oxf_status rows_softmax_bwd(const float*, const float*, float*, long long, long long, float,
                             cudaStream_t);
-oxf_status rows_layernorm(float*, long long, long long, float, const float*, const float*,
-                          cudaStream_t);
+oxf_status rows_layernorm(const float*, float*, long long, long long, float, const float*,
+                          const float*, cudaStream_t);
 oxf_status rows_layernorm_bwd(const float*, const float*, float*, long long, long long, float,
                               cudaStream_t);
-oxf_status rows_rmsnorm(float*, long long, long long, float, const float*, cudaStream_t);
+oxf_status rows_rmsnorm(const float*, float*, long long, long long, float, const float*,
+                        cudaStream_t);
+oxf_status ew_binary_bcast(const float*, const float*, float*, long long, long long, int,
+                           cudaStream_t);
+oxf_status ew_mul_act_deriv(float*, const float*, long long, int, cudaStream_t);
 oxf_status rows_rmsnorm_bwd(const float*, const float*, float*, long long, long long, float,
                             cudaStream_t);
 oxf_status rows_sum(const float*, float*, long long, long long, cudaStream_t);
@@ -46,7 +51,10 @@ oxf_status gemm_read_device_error(uint32_t*);
 
 namespace {
 thread_local char g_last_error[512] = "";
+std::atomic<unsigned long long> g_launches{0};
 }
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 oxf_status set_error(oxf_status st, const char* fmt, ...) {
   va_list ap;
@@ -97,6 +105,8 @@ extern "C" {
 const char* oxf_last_error_string(void) { return g_last_error; }
 
 const char* oxf_version(void) { return "oxf-b200 0.1 (sm_100a)"; }
+
+unsigned long long oxf_kernel_launches(void) { return g_launches.load(); }
 
 oxf_status oxf_device_error(uint32_t* code) {
   if (!code) return set_error(OXF_ERR_INVALID_ARG, "oxf_device_error: null code");
@@ -201,15 +211,61 @@ oxf_status oxf_matrix_layer_norm_rows(oxf_slice matrix, size_t cols, float epsil
                                       const float* gamma, const float* beta, oxf_stream stream) {
   long long rows = 0;
   OXF_TRY(rows_of(matrix.len, cols, &rows, "oxf_matrix_layer_norm_rows"));
-  return rows_layernorm(matrix.ptr, rows, static_cast<long long>(cols), epsilon, gamma, beta,
-                        S(stream));
+  return rows_layernorm(matrix.ptr, matrix.ptr, rows, static_cast<long long>(cols), epsilon,
+                        gamma, beta, S(stream));
 }
 
 oxf_status oxf_rms_norm_assign(oxf_slice matrix, size_t cols, float epsilon, const float* gamma,
                                oxf_stream stream) {
   long long rows = 0;
   OXF_TRY(rows_of(matrix.len, cols, &rows, "oxf_rms_norm_assign"));
-  return rows_rmsnorm(matrix.ptr, rows, static_cast<long long>(cols), epsilon, gamma, S(stream));
+  return rows_rmsnorm(matrix.ptr, matrix.ptr, rows, static_cast<long long>(cols), epsilon, gamma,
+                      S(stream));
+}
+
+oxf_status oxf_norm_rows(oxf_cslice input, oxf_slice output, size_t cols, int norm_type,
+                         float epsilon, const float* gamma, const float* beta,
+                         oxf_stream stream) {
+  OXF_TRY(need(input.len == output.len, "oxf_norm_rows: length mismatch"));
+  OXF_TRY(need(norm_type == OXF_NORM_RMS || norm_type == OXF_NORM_LAYER,
+               "oxf_norm_rows: bad norm type"));
+  long long rows = 0;
+  OXF_TRY(rows_of(input.len, cols, &rows, "oxf_norm_rows"));
+  if (norm_type == OXF_NORM_LAYER)
+    return rows_layernorm(input.ptr, output.ptr, rows, static_cast<long long>(cols), epsilon,
+                          gamma, beta, S(stream));
+  OXF_TRY(need(beta == nullptr, "oxf_norm_rows: RMS norm takes no beta"));
+  return rows_rmsnorm(input.ptr, output.ptr, rows, static_cast<long long>(cols), epsilon, gamma,
+                      S(stream));
+}
+
+oxf_status oxf_norm_rows_backward(oxf_cslice input, oxf_cslice output_gradient, oxf_slice result,
+                                  size_t cols, int norm_type, float epsilon, oxf_stream stream) {
+  if (norm_type == OXF_NORM_LAYER)
+    return oxf_layer_norm_backward(input, output_gradient, result, cols, epsilon, stream);
+  if (norm_type == OXF_NORM_RMS)
+    return oxf_matrix_rms_norm_backward(input, output_gradient, result, cols, epsilon, stream);
+  return set_error(OXF_ERR_INVALID_ARG, "oxf_norm_rows_backward: bad norm type");
+}
+
+oxf_status oxf_slice_binary_broadcast(oxf_cslice lhs, oxf_cslice rhs, oxf_slice out,
+                                      oxf_binary_op op, oxf_stream stream) {
+  OXF_TRY(need(valid_op(op), "oxf_slice_binary_broadcast: bad op"));
+  OXF_TRY(need(lhs.len == out.len, "oxf_slice_binary_broadcast: lhs/out length mismatch"));
+  if (lhs.len == 0) return OXF_OK;
+  OXF_TRY(need(rhs.len > 0 && lhs.len % rhs.len == 0,
+               "oxf_slice_binary_broadcast: rhs length must divide lhs length"));
+  return ew_binary_bcast(lhs.ptr, rhs.ptr, out.ptr, static_cast<long long>(lhs.len),
+                         static_cast<long long>(rhs.len), op, S(stream));
+}
+
+oxf_status oxf_slice_mul_act_derivative(oxf_slice gradient, oxf_cslice pre_activation,
+                                        oxf_activation act, oxf_stream stream) {
+  OXF_TRY(need(valid_act(act), "oxf_slice_mul_act_derivative: bad activation"));
+  OXF_TRY(need(gradient.len == pre_activation.len,
+               "oxf_slice_mul_act_derivative: length mismatch"));
+  return ew_mul_act_deriv(gradient.ptr, pre_activation.ptr,
+                          static_cast<long long>(gradient.len), act, S(stream));
 }
 
 oxf_status oxf_softmax_rows_backward(oxf_cslice probabilities, oxf_cslice output_gradient,

@@ -191,17 +191,16 @@ __global__ void softmax_bwd_kernel(const float* __restrict__ p, const float* __r
 // ------------------------------------------------------------------ LayerNorm
 // row.rs:115-177: mean, biased variance of (x - mean), 1/sqrt(var + eps).
 template <int G, int NV>
-__global__ void layernorm_fwd_kernel(float* __restrict__ m, long long rows, int cols, float eps,
-                                     const float* __restrict__ gamma,
+__global__ void layernorm_fwd_kernel(const float* in, float* out, long long rows, int cols,
+                                     float eps, const float* __restrict__ gamma,
                                      const float* __restrict__ beta) {
   __shared__ float red[2 * (G / 32)];
   long long r;
   int t;
   if (!row_index<G>(rows, r, t)) return;
   const int cols4 = cols >> 2;
-  float* row = m + r * cols;
   Row<G, NV> x;
-  x.load(row, t, cols4, 0.f);
+  x.load(in + r * cols, t, cols4, 0.f);
   float s = 0.f;
 #pragma unroll
   for (int j = 0; j < NV; ++j) s += hsum(x.v[j]);
@@ -230,7 +229,7 @@ __global__ void layernorm_fwd_kernel(float* __restrict__ m, long long rows, int 
       a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
     }
   }
-  x.store(row, t, cols4);
+  x.store(out + r * cols, t, cols4);
 }
 
 // row.rs:239-347: dx = inv_std/N * (N*dy - sum(dy) - xhat*sum(dy*xhat)).
@@ -286,16 +285,15 @@ __global__ void layernorm_bwd_kernel(const float* __restrict__ xin, const float*
 // ------------------------------------------------------------------ RMSNorm
 // row.rs:349-396: y = x / sqrt(mean(x^2) + eps).
 template <int G, int NV>
-__global__ void rmsnorm_fwd_kernel(float* __restrict__ m, long long rows, int cols, float eps,
-                                   const float* __restrict__ gamma) {
+__global__ void rmsnorm_fwd_kernel(const float* in, float* out, long long rows, int cols,
+                                   float eps, const float* __restrict__ gamma) {
   __shared__ float red[G / 32];
   long long r;
   int t;
   if (!row_index<G>(rows, r, t)) return;
   const int cols4 = cols >> 2;
-  float* row = m + r * cols;
   Row<G, NV> x;
-  x.load(row, t, cols4, 0.f);
+  x.load(in + r * cols, t, cols4, 0.f);
   float s = 0.f;
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
@@ -314,7 +312,7 @@ __global__ void rmsnorm_fwd_kernel(float* __restrict__ m, long long rows, int co
       a.x *= g.x; a.y *= g.y; a.z *= g.z; a.w *= g.w;
     }
   }
-  x.store(row, t, cols4);
+  x.store(out + r * cols, t, cols4);
 }
 
 // row.rs:398-468: dx = dy/r - x*(sum(x*dy)/N)/r^3.
@@ -551,7 +549,8 @@ __device__ __forceinline__ float unary_apply(int op, float x, float p) {
   }
 }
 
-enum EwOp { EW_BINARY, EW_BINARY_ASSIGN, EW_UNARY, EW_SGD, EW_MSE_GRAD, EW_BY_ROWS };
+enum EwOp { EW_BINARY, EW_BINARY_ASSIGN, EW_UNARY, EW_SGD, EW_MSE_GRAD, EW_BY_ROWS,
+             EW_BINARY_BCAST, EW_MUL_ACT_DERIV };
 
 // Grid-stride elementwise kernel; VEC processes float4s.
 template <bool VEC>
@@ -563,16 +562,23 @@ __global__ void elementwise_kernel(int kind, int op, float* __restrict__ out,
   if constexpr (VEC) {
     const long long n4 = n >> 2;
     for (; i < n4; i += stride) {
-      float4 x = (kind == EW_BINARY) ? reinterpret_cast<const float4*>(a)[i]
-                                     : reinterpret_cast<const float4*>(out)[i];
+      float4 x = (kind == EW_BINARY || kind == EW_BINARY_BCAST)
+                     ? reinterpret_cast<const float4*>(a)[i]
+                     : reinterpret_cast<const float4*>(out)[i];
       float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
       if (kind == EW_BINARY || kind == EW_BINARY_ASSIGN || kind == EW_SGD ||
           kind == EW_MSE_GRAD)
         y = reinterpret_cast<const float4*>(b)[i];
       if (kind == EW_MSE_GRAD) x = reinterpret_cast<const float4*>(a)[i];
-      if (kind == EW_BY_ROWS) y = reinterpret_cast<const float4*>(b)[(i * 4 % cols) >> 2];
+      if (kind == EW_BY_ROWS || kind == EW_BINARY_BCAST)
+        y = reinterpret_cast<const float4*>(b)[(i * 4 % cols) >> 2];
+      if (kind == EW_MUL_ACT_DERIV) y = reinterpret_cast<const float4*>(b)[i];
       float4 r;
       switch (kind) {
+        case EW_MUL_ACT_DERIV:
+          r = make_float4(x.x * act_derivative(op, y.x), x.y * act_derivative(op, y.y),
+                          x.z * act_derivative(op, y.z), x.w * act_derivative(op, y.w));
+          break;
         case EW_UNARY:
           r = make_float4(unary_apply(op, x.x, p), unary_apply(op, x.y, p),
                           unary_apply(op, x.z, p), unary_apply(op, x.w, p));
@@ -591,14 +597,16 @@ __global__ void elementwise_kernel(int kind, int op, float* __restrict__ out,
     }
   } else {
     for (; i < n; i += stride) {
-      float x = (kind == EW_BINARY || kind == EW_MSE_GRAD) ? a[i] : out[i];
+      float x = (kind == EW_BINARY || kind == EW_MSE_GRAD || kind == EW_BINARY_BCAST) ? a[i]
+                                                                                   : out[i];
       float y = 0.f;
       if (kind == EW_BINARY || kind == EW_BINARY_ASSIGN || kind == EW_SGD ||
-          kind == EW_MSE_GRAD)
+          kind == EW_MSE_GRAD || kind == EW_MUL_ACT_DERIV)
         y = b[i];
-      if (kind == EW_BY_ROWS) y = b[i % cols];
+      if (kind == EW_BY_ROWS || kind == EW_BINARY_BCAST) y = b[i % cols];
       float r;
       switch (kind) {
+        case EW_MUL_ACT_DERIV: r = x * act_derivative(op, y); break;
         case EW_UNARY: r = unary_apply(op, x, p); break;
         case EW_SGD: r = x - y * p; break;
         case EW_MSE_GRAD: r = (x - y) * p; break;
@@ -737,13 +745,15 @@ OXF_ROW_LAUNCHER(SoftmaxBwdL, softmax_bwd_kernel,
                  P_(const float* p, const float* dy, float* dx, int cols, float scale),
                  P_(p, dy, dx, rows, cols, scale))
 OXF_ROW_LAUNCHER(LnFwdL, layernorm_fwd_kernel,
-                 P_(float* m, int cols, float eps, const float* g, const float* b),
-                 P_(m, rows, cols, eps, g, b))
+                 P_(const float* in, float* out, int cols, float eps, const float* g,
+                    const float* b),
+                 P_(in, out, rows, cols, eps, g, b))
 OXF_ROW_LAUNCHER(LnBwdL, layernorm_bwd_kernel,
                  P_(const float* x, const float* dy, float* dx, int cols, float eps),
                  P_(x, dy, dx, rows, cols, eps))
-OXF_ROW_LAUNCHER(RmsFwdL, rmsnorm_fwd_kernel, P_(float* m, int cols, float eps, const float* g),
-                 P_(m, rows, cols, eps, g))
+OXF_ROW_LAUNCHER(RmsFwdL, rmsnorm_fwd_kernel,
+                 P_(const float* in, float* out, int cols, float eps, const float* g),
+                 P_(in, out, rows, cols, eps, g))
 OXF_ROW_LAUNCHER(RmsBwdL, rmsnorm_bwd_kernel,
                  P_(const float* x, const float* dy, float* dx, int cols, float eps),
                  P_(x, dy, dx, rows, cols, eps))
@@ -777,7 +787,7 @@ oxf_status elementwise(int kind, int op, float* out, const float* a, const float
                        float p, long long cols, cudaStream_t s) {
   if (n <= 0) return OXF_OK;
   bool vec = al(out) && al(a) && al(b) && (n % 4 == 0);
-  if (kind == EW_BY_ROWS) vec = vec && (cols % 4 == 0);
+  if (kind == EW_BY_ROWS || kind == EW_BINARY_BCAST) vec = vec && (cols % 4 == 0);
   if (vec)
     elementwise_kernel<true><<<ew_blocks(n / 4), 256, 0, s>>>(kind, op, out, a, b, n, p, cols);
   else
@@ -805,13 +815,13 @@ oxf_status rows_softmax_bwd(const float* p, const float* dy, float* dx, long lon
   return looped(LOOP_SOFTMAX_BWD, dx, p, dy, rows, cols, scale, 0.f, 0, nullptr, nullptr, s);
 }
 
-oxf_status rows_layernorm(float* m, long long rows, long long cols, float eps, const float* g,
-                          const float* b, cudaStream_t s) {
+oxf_status rows_layernorm(const float* in, float* out, long long rows, long long cols, float eps,
+                          const float* g, const float* b, cudaStream_t s) {
   if (rows == 0 || cols == 0) return OXF_OK;
-  if (al(m) && al(g) && al(b) &&
-      dispatch_row<LnFwdL>(rows, cols, s, m, static_cast<int>(cols), eps, g, b))
+  if (al(in) && al(out) && al(g) && al(b) &&
+      dispatch_row<LnFwdL>(rows, cols, s, in, out, static_cast<int>(cols), eps, g, b))
     return check_launch("layernorm_fwd_kernel");
-  return looped(LOOP_LN, m, m, nullptr, rows, cols, eps, 0.f, 0, g, b, s);
+  return looped(LOOP_LN, out, in, nullptr, rows, cols, eps, 0.f, 0, g, b, s);
 }
 
 oxf_status rows_layernorm_bwd(const float* x, const float* dy, float* dx, long long rows,
@@ -823,12 +833,13 @@ oxf_status rows_layernorm_bwd(const float* x, const float* dy, float* dx, long l
   return looped(LOOP_LN_BWD, dx, x, dy, rows, cols, eps, 0.f, 0, nullptr, nullptr, s);
 }
 
-oxf_status rows_rmsnorm(float* m, long long rows, long long cols, float eps, const float* g,
-                        cudaStream_t s) {
+oxf_status rows_rmsnorm(const float* in, float* out, long long rows, long long cols, float eps,
+                        const float* g, cudaStream_t s) {
   if (rows == 0 || cols == 0) return OXF_OK;
-  if (al(m) && al(g) && dispatch_row<RmsFwdL>(rows, cols, s, m, static_cast<int>(cols), eps, g))
+  if (al(in) && al(out) && al(g) &&
+      dispatch_row<RmsFwdL>(rows, cols, s, in, out, static_cast<int>(cols), eps, g))
     return check_launch("rmsnorm_fwd_kernel");
-  return looped(LOOP_RMS, m, m, nullptr, rows, cols, eps, 0.f, 0, g, nullptr, s);
+  return looped(LOOP_RMS, out, in, nullptr, rows, cols, eps, 0.f, 0, g, nullptr, s);
 }
 
 oxf_status rows_rmsnorm_bwd(const float* x, const float* dy, float* dx, long long rows,
@@ -878,6 +889,13 @@ oxf_status ew_by_rows(float* m, const float* row, long long n, long long cols, i
                       cudaStream_t s) {
   return elementwise(EW_BY_ROWS, op, m, nullptr, row, n, 0.f, cols, s);
 }
+oxf_status ew_binary_bcast(const float* a, const float* b, float* out, long long n,
+                           long long period, int op, cudaStream_t s) {
+  return elementwise(EW_BINARY_BCAST, op, out, a, b, n, 0.f, period, s);
+}
+oxf_status ew_mul_act_deriv(float* g, const float* pre, long long n, int act, cudaStream_t s) {
+  return elementwise(EW_MUL_ACT_DERIV, act, g, nullptr, pre, n, 0.f, 1, s);
+}
 
 oxf_status causal_mask(float* m, long long rows, long long cols, cudaStream_t s) {
   if (rows == 0 || cols == 0) return OXF_OK;
@@ -917,6 +935,7 @@ oxf_status transpose(const float* in, float* out, long long rows, long long cols
 
 oxf_status slice_reduce(const float* x, long long n, float* result, int is_max, cudaStream_t s) {
   fill_kernel<<<1, 1, 0, s>>>(result, is_max ? -FLT_MAX : 0.f);
+  count_launch();
   if (n > 0) {
     const unsigned blocks = ew_blocks((n + 3) / 4);
     slice_reduce_kernel<<<blocks, 256, 0, s>>>(x, n, result, is_max);

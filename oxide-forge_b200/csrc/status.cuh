@@ -17,8 +17,13 @@ inline oxf_status check_cuda(cudaError_t e, const char* what) {
   return set_error(OXF_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
-// Launch-error check after a kernel launch (does not synchronise).
+// Counts kernel launches made through this library (oxf_kernel_launches).
+void count_launch();
+
+// Launch-error check after a kernel launch (does not synchronise); every
+// launch site calls it exactly once, so it also counts launches.
 inline oxf_status check_launch(const char* what) {
+  count_launch();
   return check_cuda(cudaGetLastError(), what);
 }
 

@@ -63,6 +63,7 @@ _lib = None
 _SIGS = {
     "oxf_last_error_string": (C.c_char_p, []),
     "oxf_version": (C.c_char_p, []),
+    "oxf_kernel_launches": (C.c_ulonglong, []),
     "oxf_device_error": (C.c_int, [C.POINTER(C.c_uint32)]),
     "oxf_slice_binary": (C.c_int, [CSlice, CSlice, Slice, C.c_int, C.c_void_p]),
     "oxf_slice_binary_assign": (C.c_int, [Slice, CSlice, C.c_int, C.c_void_p]),
@@ -78,6 +79,12 @@ _SIGS = {
     "oxf_matrix_layer_norm_rows": (C.c_int, [Slice, C.c_size_t, C.c_float, C.c_void_p,
                                              C.c_void_p, C.c_void_p]),
     "oxf_rms_norm_assign": (C.c_int, [Slice, C.c_size_t, C.c_float, C.c_void_p, C.c_void_p]),
+    "oxf_norm_rows": (C.c_int, [CSlice, Slice, C.c_size_t, C.c_int, C.c_float, C.c_void_p,
+                                C.c_void_p, C.c_void_p]),
+    "oxf_norm_rows_backward": (C.c_int, [CSlice, CSlice, Slice, C.c_size_t, C.c_int, C.c_float,
+                                         C.c_void_p]),
+    "oxf_slice_binary_broadcast": (C.c_int, [CSlice, CSlice, Slice, C.c_int, C.c_void_p]),
+    "oxf_slice_mul_act_derivative": (C.c_int, [Slice, CSlice, C.c_int, C.c_void_p]),
     "oxf_softmax_rows_backward": (C.c_int, [CSlice, CSlice, Slice, C.c_size_t, C.c_float,
                                             C.c_void_p]),
     "oxf_layer_norm_backward": (C.c_int, [CSlice, CSlice, Slice, C.c_size_t, C.c_float,

@@ -1,0 +1,92 @@
+"""Data-parallel training of the transformer across the GPUs of one node.
+
+The reference is single-GPU (src/cuda/runtime.rs:34-45) and applies SGD
+per sequence inside backward (src/net/linear.rs:350-391). Here a step takes
+a global batch of independent sequences, shards it across ranks (one
+process per GPU, torch.distributed over NCCL), computes per-rank gradient
+sums with the engine, all-reduces them in three buckets (output Linear,
+feed-forward, attention + position; cursor order, contiguous) while the
+next backward stage runs, and applies one SGD update with the gradient
+averaged over the global batch:  W -= lr * (1/B) * sum_b grad_b.
+For one sequence this is exactly the reference's update (every weight is
+used for dX before it is updated, so deferring the update changes nothing).
+
+The model object only needs the engine interface used below, so the same
+driver runs over `gloo` on CPU in tests with a host stand-in model.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+def world() -> tuple[int, int]:
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_rank(), dist.get_world_size()
+    return 0, 1
+
+
+def shard(global_batch: int, rank: int, world_size: int) -> tuple[int, int]:
+    """[start, stop) of the sequences rank `rank` owns: contiguous, equal
+    shares (global_batch must divide evenly so every rank runs the same
+    collective schedule)."""
+    if global_batch % world_size:
+        raise ValueError(f"global batch {global_batch} does not divide over {world_size} ranks")
+    per = global_batch // world_size
+    return rank * per, (rank + 1) * per
+
+
+class DataParallelTrainer:
+    """SGD on the mean gradient of a sharded global batch.
+
+    model: an engine with train_forward(x), set_target(t) -> row losses,
+    backward_stage(s), bucket(s) -> (offset, count), grads (flat tensor),
+    zero_grads(), sgd(lr).
+    """
+
+    STAGES = (0, 1, 2)
+
+    def __init__(self, model, global_batch: int, lr: float, seq: int, group=None,
+                 overlap: bool = True):
+        self.model = model
+        self.rank, self.world = world()
+        self.global_batch = global_batch
+        self.local = shard(global_batch, self.rank, self.world)
+        self.local_batch = self.local[1] - self.local[0]
+        self.lr = lr
+        self.seq = seq
+        self.group = group
+        self.overlap = overlap
+        self._loss_buf = None
+
+    def broadcast_params(self, params: torch.Tensor) -> None:
+        """Every rank starts from rank 0's parameters."""
+        if self.world > 1:
+            dist.broadcast(params, 0, group=self.group)
+
+    def step(self, x: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
+        """One step on this rank's shard (x, target already on the device,
+        [local_batch*seq, width]). Returns the global mean row loss as a
+        one-element tensor on the model's device (not synchronised)."""
+        m = self.model
+        m.zero_grads()
+        m.train_forward(x)
+        row_loss = m.set_target(target)
+        works = []
+        for s in self.STAGES:
+            m.backward_stage(s)
+            if self.world > 1:
+                off, cnt = m.bucket(s)
+                bucket = m.grads[off:off + cnt]
+                if self.overlap:
+                    works.append(dist.all_reduce(bucket, group=self.group, async_op=True))
+                else:
+                    dist.all_reduce(bucket, group=self.group)
+        loss = row_loss.sum().reshape(1)
+        if self.world > 1:
+            works.append(dist.all_reduce(loss, group=self.group, async_op=self.overlap))
+            for w in works:
+                if w is not None:
+                    w.wait()
+        m.sgd(self.lr / self.global_batch)
+        return loss / (self.global_batch * self.seq)

@@ -112,6 +112,28 @@ def rms_norm_rows(m, eps=1e-5, gamma=None, stream=None):
     return m
 
 
+def norm_rows(x, out, norm_type, eps=1e-5, gamma=None, beta=None, stream=None):
+    check(lib().oxf_norm_rows(cs(x), ms(out), x.shape[-1], int(norm_type), float(eps), ptr(gamma),
+                              ptr(beta), _stream(stream)))
+    return out
+
+
+def norm_rows_backward(x, dy, out, norm_type, eps=1e-5, stream=None):
+    check(lib().oxf_norm_rows_backward(cs(x), cs(dy), ms(out), x.shape[-1], int(norm_type),
+                                       float(eps), _stream(stream)))
+    return out
+
+
+def binary_broadcast(a, b, out, op, stream=None):
+    check(lib().oxf_slice_binary_broadcast(cs(a), cs(b), ms(out), op, _stream(stream)))
+    return out
+
+
+def mul_act_derivative(g, pre, act, stream=None):
+    check(lib().oxf_slice_mul_act_derivative(ms(g), cs(pre), int(act), _stream(stream)))
+    return g
+
+
 def softmax_backward(p, dy, out, scale=1.0, stream=None):
     check(lib().oxf_softmax_rows_backward(cs(p), cs(dy), ms(out), p.shape[-1], float(scale),
                                           _stream(stream)))

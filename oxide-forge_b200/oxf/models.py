@@ -1,0 +1,292 @@
+"""Python driver of the host executors (include/oxf_host.h).
+
+`Transformer` and `Mlp` wrap the C++ engines; their parameter and gradient
+arenas are exposed as zero-copy torch views (via __cuda_array_interface__)
+in checkpoint cursor order, so a data-parallel driver can all-reduce the
+gradient buckets with torch.distributed. All compute runs in liboxf.so on
+the engine's stream (by default torch's current stream).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._host_sigs import LayerSpec, MlpSpec, TransformerSpec
+from ._lib import check, lib
+
+
+class _DeviceArray:
+    """Borrowed device memory exposed through __cuda_array_interface__."""
+
+    def __init__(self, ptr: int, shape, owner):
+        self.__cuda_array_interface__ = {
+            "shape": tuple(int(s) for s in shape), "typestr": "<f4",
+            "data": (int(ptr), False), "version": 3, "strides": None}
+        self._owner = owner
+
+
+def device_view(ptr: int, shape, owner=None) -> torch.Tensor:
+    if int(np.prod(shape)) == 0:
+        return torch.empty(shape, device="cuda")
+    return torch.as_tensor(_DeviceArray(ptr, shape, owner), device="cuda")
+
+
+@dataclass
+class Layer:
+    """One Linear (linear.rs:72-86): weights [in, out], optional bias."""
+    in_: int
+    out: int
+    act: int = _lib.ACT_IDENTITY
+    bias: bool = False
+
+    def spec(self) -> LayerSpec:
+        return LayerSpec(self.in_, self.out, self.act, int(self.bias))
+
+    def shapes(self):
+        return [(self.in_, self.out)] + ([(self.out,)] if self.bias else [])
+
+    def count(self) -> int:
+        return self.in_ * self.out + (self.out if self.bias else 0)
+
+
+@dataclass
+class MlpConfig:
+    layers: list
+    res_range: tuple | None = None
+
+    def spec(self) -> MlpSpec:
+        s = MlpSpec()
+        s.n_layers = len(self.layers)
+        for i, l in enumerate(self.layers):
+            s.layers[i] = l.spec()
+        s.res_start, s.res_end = self.res_range if self.res_range else (-1, -1)
+        return s
+
+    def shapes(self):
+        return [sh for l in self.layers for sh in l.shapes()]
+
+
+@dataclass
+class TransformerConfig:
+    seq: int
+    hidden: int
+    ffn: MlpConfig
+    out: int
+    norm: int = _lib.NORM_LAYER
+    qkv_dim: int | None = None
+    qkv_act: int = _lib.ACT_IDENTITY
+    out_act: int = _lib.ACT_IDENTITY
+    bias: bool = False
+
+    def layers(self):
+        d = self.qkv_dim or self.hidden
+        q = Layer(self.hidden, d, self.qkv_act, self.bias)
+        k = Layer(self.hidden, d, self.qkv_act, self.bias)
+        v = Layer(self.hidden, self.hidden, self.qkv_act, self.bias)
+        o = Layer(self.hidden, self.out, self.out_act, self.bias)
+        return q, k, v, o
+
+    def spec(self) -> TransformerSpec:
+        q, k, v, o = self.layers()
+        return TransformerSpec(self.seq, self.hidden, self.norm, q.spec(), k.spec(), v.spec(),
+                               self.ffn.spec(), o.spec())
+
+    def shapes(self):
+        """Cursor order (inference.rs:52-66): q, k, v, position, ffn, out."""
+        q, k, v, o = self.layers()
+        return (q.shapes() + k.shapes() + v.shapes() + [(self.seq, self.hidden)] +
+                self.ffn.shapes() + o.shapes())
+
+    def param_count(self) -> int:
+        return int(sum(np.prod(s) for s in self.shapes()))
+
+
+def transformer_config(seq, hidden, ffn, out=None, norm=_lib.NORM_LAYER, bias=False,
+                       ffn_act=_lib.ACT_GELU) -> TransformerConfig:
+    """The BASELINE transformer shape: FFN hidden -> ffn (GELU) -> hidden."""
+    mlp = MlpConfig([Layer(hidden, ffn, ffn_act, bias), Layer(ffn, hidden, _lib.ACT_IDENTITY, bias)])
+    return TransformerConfig(seq, hidden, mlp, out or hidden, norm, bias=bias)
+
+
+def init_transformer_params(cfg: TransformerConfig, seed: int = 0,
+                            pos_std: float = 0.02) -> np.ndarray:
+    """Xavier-uniform weights (bound sqrt(6/(fan_in+fan_out))), position
+    N(0, pos_std), biases 0.01*N(0,1); from a seeded host RNG."""
+    rng = np.random.default_rng(seed)
+    out = []
+    for i, sh in enumerate(cfg.shapes()):
+        if len(sh) == 1:
+            out.append(0.01 * rng.standard_normal(sh))
+        elif sh == (cfg.seq, cfg.hidden) and i == _position_index(cfg):
+            out.append(pos_std * rng.standard_normal(sh))
+        else:
+            b = np.sqrt(6.0 / (sh[0] + sh[1]))
+            out.append(rng.uniform(-b, b, sh))
+    return np.concatenate([a.astype(np.float32).ravel() for a in out])
+
+
+def _position_index(cfg: TransformerConfig) -> int:
+    q, k, v, _ = cfg.layers()
+    return len(q.shapes()) + len(k.shapes()) + len(v.shapes())
+
+
+def split_params(cfg, flat: np.ndarray) -> list:
+    """Flat cursor-order arena -> list of arrays with cfg.shapes()."""
+    res, off = [], 0
+    for sh in cfg.shapes():
+        n = int(np.prod(sh))
+        res.append(np.asarray(flat[off:off + n]).reshape(sh))
+        off += n
+    return res
+
+
+class Transformer:
+    """Batched single-block Post-Norm transformer (inference + training)."""
+
+    def __init__(self, cfg: TransformerConfig, max_batch: int = 1, stream=None):
+        self.cfg = cfg
+        self.max_batch = max_batch
+        if stream is None:
+            stream = torch.cuda.current_stream()
+        self._stream = stream
+        h = C.c_void_p()
+        spec = cfg.spec()
+        check(lib().oxf_transformer_create(C.byref(spec), max_batch, C.c_void_p(stream.cuda_stream),
+                                           C.byref(h)))
+        self._h = h
+        self.n = int(lib().oxf_transformer_param_count(h))
+        assert self.n == cfg.param_count(), (self.n, cfg.param_count())
+        self.params = device_view(lib().oxf_transformer_params(h), (self.n,), self)
+        self.grads = device_view(lib().oxf_transformer_grads(h), (self.n,), self)
+
+    # ---------------------------------------------------------------- params
+    def set_params(self, flat) -> None:
+        flat = np.ascontiguousarray(flat, np.float32)
+        assert flat.size == self.n
+        check(lib().oxf_transformer_set_params_host(self._h, flat.ctypes.data))
+
+    def get_params(self) -> np.ndarray:
+        out = np.empty(self.n, np.float32)
+        check(lib().oxf_transformer_get_params_host(self._h, out.ctypes.data))
+        return out
+
+    def bucket(self, stage: int) -> tuple[int, int]:
+        off, cnt = C.c_size_t(), C.c_size_t()
+        check(lib().oxf_transformer_bucket(self._h, stage, C.byref(off), C.byref(cnt)))
+        return off.value, cnt.value
+
+    # ---------------------------------------------------------------- compute
+    def _views(self, batch):
+        y, loss, dx = C.c_void_p(), C.c_void_p(), C.c_void_p()
+        check(lib().oxf_transformer_output(self._h, C.byref(y), C.byref(loss), C.byref(dx)))
+        rows = batch * self.cfg.seq
+        return (device_view(y.value, (rows, self.cfg.out), self),
+                device_view(loss.value, (rows,), self),
+                device_view(dx.value, (rows, self.cfg.hidden), self))
+
+    def forward(self, x: torch.Tensor, causal: bool = False) -> torch.Tensor:
+        batch = x.numel() // (self.cfg.seq * self.cfg.hidden)
+        check(lib().oxf_transformer_forward(self._h, x.data_ptr(), batch, int(causal), None))
+        return self._views(batch)[0]
+
+    def train_forward(self, x: torch.Tensor) -> torch.Tensor:
+        self._batch = x.numel() // (self.cfg.seq * self.cfg.hidden)
+        check(lib().oxf_transformer_train_forward(self._h, x.data_ptr(), self._batch))
+        return self._views(self._batch)[0]
+
+    def set_target(self, target: torch.Tensor) -> torch.Tensor:
+        check(lib().oxf_transformer_set_target(self._h, target.data_ptr()))
+        return self._views(self._batch)[1]
+
+    def set_output_gradient(self, dy: torch.Tensor) -> None:
+        check(lib().oxf_transformer_set_output_gradient(self._h, dy.data_ptr()))
+
+    def backward_stage(self, stage: int) -> None:
+        check(lib().oxf_transformer_backward_stage(self._h, stage))
+
+    def backward(self) -> torch.Tensor:
+        for s in range(3):
+            self.backward_stage(s)
+        return self._views(self._batch)[2]
+
+    def zero_grads(self) -> None:
+        check(lib().oxf_transformer_zero_grads(self._h))
+
+    def sgd(self, lr: float) -> None:
+        check(lib().oxf_transformer_sgd(self._h, float(lr)))
+
+    def train_step_host(self, x: np.ndarray, target: np.ndarray, lr: float) -> float:
+        """The e2e API: host arrays in, one SGD step, mean row loss out."""
+        x = np.ascontiguousarray(x, np.float32)
+        target = np.ascontiguousarray(target, np.float32)
+        batch = x.size // (self.cfg.seq * self.cfg.hidden)
+        loss = C.c_float()
+        check(lib().oxf_transformer_train_step_host(self._h, x.ctypes.data, target.ctypes.data,
+                                                    batch, float(lr), C.byref(loss)))
+        return loss.value
+
+    def set_timing(self, on: bool) -> None:
+        check(lib().oxf_transformer_set_timing(self._h, int(on)))
+
+    def read_timing(self) -> tuple[float, float, int]:
+        """(GEMM device ms, GEMM flops, GEMM launches) since the last read."""
+        ms, fl, n = C.c_double(), C.c_double(), C.c_int()
+        check(lib().oxf_transformer_read_timing(self._h, C.byref(ms), C.byref(fl), C.byref(n)))
+        return ms.value, fl.value, n.value
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().oxf_transformer_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Mlp:
+    """Batched MlpExecutor (forward, backward with deferred SGD)."""
+
+    def __init__(self, cfg: MlpConfig, max_rows: int, stream=None):
+        self.cfg = cfg
+        if stream is None:
+            stream = torch.cuda.current_stream()
+        h = C.c_void_p()
+        spec = cfg.spec()
+        check(lib().oxf_mlp_create(C.byref(spec), max_rows, C.c_void_p(stream.cuda_stream),
+                                   C.byref(h)))
+        self._h = h
+        self.n = int(lib().oxf_mlp_param_count(h))
+        self.params = device_view(lib().oxf_mlp_params(h), (self.n,), self)
+        self.grads = device_view(lib().oxf_mlp_grads(h), (self.n,), self)
+
+    def forward(self, x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+        check(lib().oxf_mlp_forward(self._h, x.data_ptr(), y.data_ptr(), x.shape[0]))
+        return y
+
+    def backward(self, dy: torch.Tensor, dx: torch.Tensor | None) -> None:
+        check(lib().oxf_mlp_backward(self._h, dy.data_ptr(),
+                                     dx.data_ptr() if dx is not None else None, dy.shape[0]))
+
+    def zero_grads(self) -> None:
+        check(lib().oxf_mlp_zero_grads(self._h))
+
+    def sgd(self, lr: float) -> None:
+        check(lib().oxf_mlp_sgd(self._h, float(lr)))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().oxf_mlp_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

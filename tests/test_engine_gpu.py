@@ -1,0 +1,219 @@
+"""GPU parity of the executors (transformer and MLP engines) against the
+oracle's single-sequence reference semantics, through the host C ABI.
+
+The GPU runs every product in TF32 (operands truncated to 10 mantissa bits);
+the oracle runs the same formulas with TF32 truncation emulated
+(GEMM_TF32_RZ), so what remains is summation order and the tensor core's
+internal accumulation. Tolerances: forward outputs 5e-3 (the north_star
+TF32 bound), gradients and updates 1e-2 of their own scale (errors of a
+whole backward pass compound through ~12 dependent products).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+FWD_TOL = 5e-3
+GRAD_TOL = 1e-2
+RZ = O.GEMM_TF32_RZ
+
+
+@pytest.fixture(scope="module")
+def M():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from oxf import _lib, kernels, models
+    yield models
+    assert kernels.device_error() == 0
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.detach().cpu().numpy().copy()
+
+
+def oracle_model(models, cfg, flat):
+    """oracle.TransformerParams from a flat cursor-order parameter array."""
+    parts = models.split_params(cfg, flat)
+    q, k, v, o = cfg.layers()
+    it = iter(parts)
+
+    def lin(spec):
+        w = next(it)
+        b = next(it) if spec.bias else None
+        return O.LinearParams(w, b, spec.act)
+
+    lq, lk, lv = lin(q), lin(k), lin(v)
+    pos = next(it)
+    ffn = O.MlpParams([lin(l) for l in cfg.ffn.layers], cfg.ffn.res_range)
+    lo = lin(o)
+    return O.TransformerParams(lq, lk, lv, pos, ffn, lo, cfg.norm, cfg.seq)
+
+
+CASES = [
+    # seq, hidden, ffn, norm, bias
+    (32, 64, 128, 1, False),
+    (32, 64, 128, 0, True),
+    (64, 128, 256, 1, True),
+]
+
+
+@pytest.mark.parametrize("seq,hidden,ffn,norm,bias", CASES)
+def test_training_step_single_sequence(M, seq, hidden, ffn, norm, bias):
+    """One reference training step (TrainingTransformer::forward + backward
+    with per-layer SGD, encoder.rs:114-186) on one sequence."""
+    cfg = M.transformer_config(seq, hidden, ffn, norm=norm, bias=bias)
+    flat = M.init_transformer_params(cfg, seed=11)
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((seq, hidden)).astype(np.float32)
+    t = rng.standard_normal((seq, hidden)).astype(np.float32)
+    lr = 0.05
+
+    ref = oracle_model(M, cfg, flat)
+    y_ref, loss_ref, dx_ref = O.transformer_train_step(ref, x, t, lr, rounding=RZ)
+
+    eng = M.Transformer(cfg, max_batch=1)
+    eng.set_params(flat)
+    eng.zero_grads()
+    y = host(eng.train_forward(dev(x)))
+    tt = dev(t)
+    loss = host(eng.set_target(tt))
+    dx = host(eng.backward())
+    eng.sgd(lr)
+    new = eng.get_params()
+    assert rel_err(y, y_ref) < FWD_TOL
+    assert rel_err(loss, loss_ref) < FWD_TOL
+    assert rel_err(dx, dx_ref) < GRAD_TOL
+    # compare the parameter update lr*grad, tensor by tensor
+    delta, delta_ref = flat - new, flat - ref.flat()
+    off = 0
+    for sh in cfg.shapes():
+        n = int(np.prod(sh))
+        assert rel_err(delta[off:off + n], delta_ref[off:off + n]) < GRAD_TOL, sh
+        off += n
+    eng.close()
+
+
+def test_batched_gradients_are_sums_of_sequences(M):
+    """B sequences in one call == the sum of B single-sequence gradients
+    (the data-parallel step relies on this)."""
+    seq, hidden, ffn, B = 32, 64, 128, 3
+    cfg = M.transformer_config(seq, hidden, ffn, norm=1)
+    flat = M.init_transformer_params(cfg, seed=3)
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal((B, seq, hidden)).astype(np.float32)
+    t = rng.standard_normal((B, seq, hidden)).astype(np.float32)
+    g_ref = np.zeros(flat.size, np.float32)
+    ys = []
+    for b in range(B):
+        ref = oracle_model(M, cfg, flat)
+        y, _, _ = O.transformer_train_step(ref, x[b], t[b], 0.0, grads=g_ref, rounding=RZ)
+        ys.append(y)
+    eng = M.Transformer(cfg, max_batch=4)
+    eng.set_params(flat)
+    eng.zero_grads()
+    y = host(eng.train_forward(dev(x.reshape(B * seq, hidden))))
+    eng.set_target(dev(t.reshape(B * seq, hidden)))
+    eng.backward()
+    g = host(eng.grads)
+    assert rel_err(y, np.concatenate(ys)) < FWD_TOL
+    off = 0
+    for sh in cfg.shapes():
+        n = int(np.prod(sh))
+        assert rel_err(g[off:off + n], g_ref[off:off + n]) < GRAD_TOL, sh
+        off += n
+    # buckets tile the arena in cursor order: attention+position, ffn, output
+    b2, b1, b0 = eng.bucket(2), eng.bucket(1), eng.bucket(0)
+    assert b2[0] == 0 and b2[0] + b2[1] == b1[0] and b1[0] + b1[1] == b0[0]
+    assert b0[0] + b0[1] == eng.n
+    eng.close()
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_inference_forward(M, causal):
+    """InferenceTransformer::forward (encoder) and the decoder's masked
+    forward (decoder.rs:50-52) with NormType::Rms."""
+    seq, hidden, ffn, B = 64, 128, 512, 2
+    cfg = M.transformer_config(seq, hidden, ffn, norm=0)
+    flat = M.init_transformer_params(cfg, seed=21)
+    x = np.random.default_rng(2).standard_normal((B, seq, hidden)).astype(np.float32)
+    eng = M.Transformer(cfg, max_batch=B)
+    eng.set_params(flat)
+    y = host(eng.forward(dev(x.reshape(B * seq, hidden)), causal=causal))
+    ref = oracle_model(M, cfg, flat)
+    for b in range(B):
+        want = O.transformer_forward(ref, x[b], causal=causal, rounding=RZ)
+        assert rel_err(y[b * seq:(b + 1) * seq], want) < FWD_TOL
+    eng.close()
+
+
+def test_train_step_host_api(M):
+    """The host-memory step (H2D, forward, loss, backward, SGD on the mean
+    gradient, loss D2H) equals the device-level calls."""
+    seq, hidden, ffn, B = 32, 64, 128, 2
+    cfg = M.transformer_config(seq, hidden, ffn, norm=1)
+    flat = M.init_transformer_params(cfg, seed=4)
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((B * seq, hidden)).astype(np.float32)
+    t = rng.standard_normal((B * seq, hidden)).astype(np.float32)
+    a = M.Transformer(cfg, max_batch=B)
+    a.set_params(flat)
+    loss = a.train_step_host(x, t, 0.1)
+    b = M.Transformer(cfg, max_batch=B)
+    b.set_params(flat)
+    b.zero_grads()
+    b.train_forward(dev(x))
+    rl = host(b.set_target(dev(t)))
+    b.backward()
+    b.sgd(0.1 / B)
+    assert abs(loss - rl.mean()) < 1e-5 * max(1.0, abs(loss))
+    assert rel_err(a.get_params() - flat, b.get_params() - flat) < 1e-6
+    a.close()
+    b.close()
+
+
+@pytest.mark.parametrize("res", [None, (0, 2)])
+def test_mlp_engine(M, res):
+    """MlpExecutor forward + backward + SGD (mlp.rs:53-168) with biases,
+    GELU and the residual range of config 3, scaled down."""
+    from oxf import _lib
+    rows, d, h = 96, 64, 256
+    cfg = M.MlpConfig([M.Layer(d, h, _lib.ACT_GELU, True), M.Layer(h, d, 0, True)], res)
+    rng = np.random.default_rng(8)
+    w1 = rng.uniform(-np.sqrt(6 / d), np.sqrt(6 / d), (d, h)).astype(np.float32)
+    b1 = (0.01 * rng.standard_normal(h)).astype(np.float32)
+    w2 = rng.uniform(-np.sqrt(6 / h), np.sqrt(6 / h), (h, d)).astype(np.float32)
+    b2 = (0.01 * rng.standard_normal(d)).astype(np.float32)
+    x = rng.standard_normal((rows, d)).astype(np.float32)
+    t = rng.standard_normal((rows, d)).astype(np.float32)
+    flat = np.concatenate([w1.ravel(), b1, w2.ravel(), b2])
+    lr = 0.05
+    ref = O.MlpParams([O.LinearParams(w1, b1, O.GELU), O.LinearParams(w2, b2)], res)
+    y_ref = O.mlp_forward(ref, x, rounding=RZ)
+    dy_ref = O.mse_grad(y_ref, t)
+    _, dx_ref = O.mlp_train_step(ref, x, dy_ref, lr, rounding=RZ)
+
+    eng = M.Mlp(cfg, rows)
+    eng.params.copy_(dev(flat))
+    eng.zero_grads()
+    xd = dev(x)
+    y = torch.empty((rows, d), device="cuda")
+    eng.forward(xd, y)
+    assert rel_err(host(y), y_ref) < FWD_TOL
+    dy = dev(dy_ref)
+    dx = torch.empty((rows, d), device="cuda")
+    eng.backward(dy, dx)
+    eng.sgd(lr)
+    assert rel_err(host(dx), dx_ref) < GRAD_TOL
+    new_ref = np.concatenate([p.ravel() for p in ref.params()])
+    assert rel_err(flat - host(eng.params), flat - new_ref) < GRAD_TOL
+    eng.close()
