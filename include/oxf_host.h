@@ -57,8 +57,8 @@ typedef struct oxf_mlp_s* oxf_mlp;
 
 /* ---------------------------------------------------------------- transformer */
 /* Builds an engine for up to max_batch sequences on the current device;
- * work runs on `stream` (NULL: a stream the engine creates). Parameters
- * start at zero. */
+ * all its work runs on `stream` (NULL: the legacy default stream).
+ * Parameters start at zero. */
 oxf_status oxf_transformer_create(const oxf_transformer_spec* spec, int max_batch,
                                   oxf_stream stream, oxf_transformer* out);
 oxf_status oxf_transformer_destroy(oxf_transformer t);

@@ -107,90 +107,123 @@ static inline float b_at(const float* B, size_t N, size_t K, int bt, size_t k, s
 }
 
 /* matrix_multiply_device, gemm.rs:202-373: each output is an f32 sum of
- * products of (optionally TF32-rounded) operands over k ascending. */
-static void gemm_rows(const float* A, const float* B, float* C, size_t M, size_t N, size_t K,
-                      int at, int bt, int rounding, float alpha, float beta, size_t r0,
-                      size_t r1) {
-    float* acc = (float*)malloc((N ? N : 1) * sizeof(float));
-    float* arow = (float*)malloc((K ? K : 1) * sizeof(float));
-    for (size_t m = r0; m < r1; ++m) {
-        for (size_t k = 0; k < K; ++k) arow[k] = round_op(a_at(A, M, K, at, m, k), rounding);
-        if (bt) {
-            /* B stored [N,K]: each output is a contiguous dot product. */
-            for (size_t n = 0; n < N; ++n) {
-                const float* brow = B + n * K;
-                float s = 0.0f;
-                if (rounding == OXO_GEMM_F32)
-                    for (size_t k = 0; k < K; ++k) s += arow[k] * brow[k];
-                else
-                    for (size_t k = 0; k < K; ++k) s += arow[k] * round_op(brow[k], rounding);
-                acc[n] = s;
-            }
-        } else {
-            for (size_t n = 0; n < N; ++n) acc[n] = 0.0f;
+ * products of (optionally TF32-rounded) operands over k ascending.
+ * Operands are first copied into row-major A[M,K] and B[K,N] with the
+ * rounding applied (so transposed inputs cost one O(MK + KN) pass), then
+ * rows are processed four at a time against 512-column panels of B: the
+ * same sums in the same order, with a quarter of the B traffic. */
+enum { RB = 4, NB = 512 };
+
+static void gemm_panel(const float* restrict A, const float* restrict B, float* restrict C,
+                       size_t N, size_t K, float alpha, float beta, size_t r0, size_t r1) {
+    float acc[RB][NB];
+    for (size_t m0 = r0; m0 < r1; m0 += RB) {
+        const size_t rb = (r1 - m0) < RB ? (r1 - m0) : RB;
+        for (size_t n0 = 0; n0 < N; n0 += NB) {
+            const size_t nb = (N - n0) < NB ? (N - n0) : NB;
+            for (size_t r = 0; r < RB; ++r)
+                for (size_t j = 0; j < NB; ++j) acc[r][j] = 0.0f;
             for (size_t k = 0; k < K; ++k) {
-                const float a = arow[k];
-                const float* brow = B + k * N;
-                if (rounding == OXO_GEMM_F32)
-                    for (size_t n = 0; n < N; ++n) acc[n] += a * brow[n];
-                else
-                    for (size_t n = 0; n < N; ++n) acc[n] += a * round_op(brow[n], rounding);
+                const float* restrict b = B + k * N + n0;
+                if (rb == RB && nb == NB) {
+                    const float a0 = A[(m0 + 0) * K + k], a1 = A[(m0 + 1) * K + k];
+                    const float a2 = A[(m0 + 2) * K + k], a3 = A[(m0 + 3) * K + k];
+                    for (size_t j = 0; j < NB; ++j) {
+                        const float bj = b[j];
+                        acc[0][j] += a0 * bj;
+                        acc[1][j] += a1 * bj;
+                        acc[2][j] += a2 * bj;
+                        acc[3][j] += a3 * bj;
+                    }
+                } else {
+                    for (size_t r = 0; r < rb; ++r) {
+                        const float a = A[(m0 + r) * K + k];
+                        for (size_t j = 0; j < nb; ++j) acc[r][j] += a * b[j];
+                    }
+                }
             }
-        }
-        for (size_t n = 0; n < N; ++n) {
-            float v = alpha * acc[n];
-            if (beta != 0.0f) v += beta * C[m * N + n];
-            C[m * N + n] = v;
+            for (size_t r = 0; r < rb; ++r)
+                for (size_t j = 0; j < nb; ++j) {
+                    float v = alpha * acc[r][j];
+                    float* c = C + (m0 + r) * N + n0 + j;
+                    if (beta != 0.0f) v += beta * *c;
+                    *c = v;
+                }
         }
     }
-    free(acc);
-    free(arow);
+}
+
+/* Row-major, rounded copies of the operands. */
+static float* prep_a(const float* A, size_t M, size_t K, int at, int rounding) {
+    const size_t na = M * K;
+    float* a = (float*)malloc((na ? na : 1) * sizeof(float));
+    for (size_t m = 0; m < M; ++m)
+        for (size_t k = 0; k < K; ++k) a[m * K + k] = round_op(a_at(A, M, K, at, m, k), rounding);
+    return a;
+}
+static float* prep_b(const float* B, size_t N, size_t K, int bt, int rounding) {
+    const size_t nbk = N * K;
+    float* b = (float*)malloc((nbk ? nbk : 1) * sizeof(float));
+    if (bt) {
+        for (size_t n = 0; n < N; ++n)
+            for (size_t k = 0; k < K; ++k) b[k * N + n] = round_op(B[n * K + k], rounding);
+    } else {
+        for (size_t i = 0; i < N * K; ++i) b[i] = round_op(B[i], rounding);
+    }
+    return b;
 }
 
 void oxo_gemm(const float* A, const float* B, float* C, size_t M, size_t N, size_t K,
               int a_trans, int b_trans, int rounding, float alpha, float beta) {
-    gemm_rows(A, B, C, M, N, K, a_trans, b_trans, rounding, alpha, beta, 0, M);
+    float* a = prep_a(A, M, K, a_trans, rounding);
+    float* b = prep_b(B, N, K, b_trans, rounding);
+    gemm_panel(a, b, C, N, K, alpha, beta, 0, M);
+    free(a);
+    free(b);
 }
 
 typedef struct {
     const float *A, *B;
     float* C;
-    size_t M, N, K;
-    int at, bt, rounding;
+    size_t N, K;
     float alpha, beta;
     size_t r0, r1;
 } gemm_job;
 
 static void* gemm_worker(void* p) {
     gemm_job* j = (gemm_job*)p;
-    gemm_rows(j->A, j->B, j->C, j->M, j->N, j->K, j->at, j->bt, j->rounding, j->alpha, j->beta,
-              j->r0, j->r1);
+    gemm_panel(j->A, j->B, j->C, j->N, j->K, j->alpha, j->beta, j->r0, j->r1);
     return NULL;
 }
 
 void oxo_gemm_mt(const float* A, const float* B, float* C, size_t M, size_t N, size_t K,
                  int a_trans, int b_trans, int rounding, float alpha, float beta) {
     int t = oxo_get_threads();
-    if (t <= 1 || M < 2) {
+    if (t <= 1 || M < 2 * RB) {
         oxo_gemm(A, B, C, M, N, K, a_trans, b_trans, rounding, alpha, beta);
         return;
     }
-    if ((size_t)t > M) t = (int)M;
+    float* a = prep_a(A, M, K, a_trans, rounding);
+    float* b = prep_b(B, N, K, b_trans, rounding);
+    size_t blocks = (M + RB - 1) / RB;
+    if ((size_t)t > blocks) t = (int)blocks;
     pthread_t* th = (pthread_t*)malloc(sizeof(pthread_t) * (size_t)t);
     gemm_job* jobs = (gemm_job*)malloc(sizeof(gemm_job) * (size_t)t);
-    size_t chunk = (M + (size_t)t - 1) / (size_t)t;
+    size_t per = (blocks + (size_t)t - 1) / (size_t)t * RB;
     int launched = 0;
     for (int i = 0; i < t; ++i) {
-        size_t r0 = (size_t)i * chunk, r1 = r0 + chunk;
+        size_t r0 = (size_t)i * per, r1 = r0 + per;
         if (r0 >= M) break;
         if (r1 > M) r1 = M;
-        jobs[i] = (gemm_job){A, B, C, M, N, K, a_trans, b_trans, rounding, alpha, beta, r0, r1};
+        jobs[i] = (gemm_job){a, b, C, N, K, alpha, beta, r0, r1};
         pthread_create(&th[i], NULL, gemm_worker, &jobs[i]);
         ++launched;
     }
     for (int i = 0; i < launched; ++i) pthread_join(th[i], NULL);
     free(th);
     free(jobs);
+    free(a);
+    free(b);
 }
 
 void oxo_gemm_f64(const float* A, const float* B, double* C, size_t M, size_t N, size_t K,

@@ -65,15 +65,11 @@ oxf::MlpSpec mlp_spec(const oxf_mlp_spec& m) {
   return s;
 }
 
+// NULL selects the legacy default stream, as everywhere in oxf.h; the
+// engines never create streams of their own.
 cudaStream_t make_stream(oxf_stream given, bool* own) {
-  if (given) {
-    *own = false;
-    return reinterpret_cast<cudaStream_t>(given);
-  }
-  cudaStream_t s;
-  oxf::check_cuda_call(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate");
-  *own = true;
-  return s;
+  *own = false;
+  return reinterpret_cast<cudaStream_t>(given);
 }
 
 }  // namespace
