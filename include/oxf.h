@@ -99,6 +99,10 @@ oxf_status oxf_sgd_update(oxf_slice target, oxf_cslice grad, float lr, oxf_strea
  * counterpart; loss_rows is linear.rs:325-333). */
 oxf_status oxf_mse_grad(oxf_cslice y, oxf_cslice target, oxf_slice out, size_t cols,
                         oxf_stream stream);
+/* loss_rows and its gradient in one pass: row_loss[r] = mean_j 0.5(y-t)^2
+ * and dy = (y - t)/cols. */
+oxf_status oxf_mse_loss_grad(oxf_cslice y, oxf_cslice target, oxf_slice row_loss, oxf_slice dy,
+                             size_t cols, oxf_stream stream);
 /* Linear::loss_rows (linear.rs:325-333) fused: row_loss[r] = mean_j 0.5(y-t)^2. */
 oxf_status oxf_loss_rows(oxf_cslice y, oxf_cslice target, oxf_slice row_loss, size_t cols,
                          oxf_stream stream);
@@ -205,6 +209,8 @@ typedef struct {
   int split_k;    /* 0/1 = none; >1 requires accumulate */
   int precision;  /* oxf_precision */
   void* workspace; size_t workspace_bytes;
+  int reduce_batch; /* 1: C = sum over the batch of op(A_b)·op(B_b) (one output,
+                       output strides 0); K then runs over batch x K */
 } oxf_gemm_desc;
 
 /* Fills a descriptor with defaults (batch 1, alpha 1, tight leading dims

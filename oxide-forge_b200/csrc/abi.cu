@@ -32,6 +32,8 @@ oxf_status rows_rmsnorm_bwd(const float*, const float*, float*, long long, long 
                             cudaStream_t);
 oxf_status rows_sum(const float*, float*, long long, long long, cudaStream_t);
 oxf_status rows_loss(const float*, const float*, float*, long long, long long, cudaStream_t);
+oxf_status rows_loss_grad(const float*, const float*, float*, float*, long long, long long,
+                          cudaStream_t);
 oxf_status ew_binary(const float*, const float*, float*, long long, int, cudaStream_t);
 oxf_status ew_binary_assign(float*, const float*, long long, int, cudaStream_t);
 oxf_status ew_unary(float*, long long, int, float, cudaStream_t);
@@ -168,6 +170,17 @@ oxf_status oxf_loss_rows(oxf_cslice y, oxf_cslice target, oxf_slice row_loss, si
   OXF_TRY(need(row_loss.len >= static_cast<size_t>(rows), "oxf_loss_rows: result too short"));
   return rows_loss(y.ptr, target.ptr, row_loss.ptr, rows, static_cast<long long>(cols),
                    S(stream));
+}
+
+oxf_status oxf_mse_loss_grad(oxf_cslice y, oxf_cslice target, oxf_slice row_loss, oxf_slice dy,
+                             size_t cols, oxf_stream stream) {
+  OXF_TRY(need(y.len == target.len && y.len == dy.len, "oxf_mse_loss_grad: length mismatch"));
+  long long rows = 0;
+  OXF_TRY(rows_of(y.len, cols, &rows, "oxf_mse_loss_grad"));
+  OXF_TRY(need(row_loss.len >= static_cast<size_t>(rows), "oxf_mse_loss_grad: result too short"));
+  if (rows == 0) return OXF_OK;
+  return rows_loss_grad(y.ptr, target.ptr, row_loss.ptr, dy.ptr, rows,
+                        static_cast<long long>(cols), S(stream));
 }
 
 // ---------------------------------------------------------------- reductions

@@ -12,8 +12,10 @@
 //   warp 1      TMEM allocator + MMA issuer: tcgen05.mma.kind::tf32,
 //               M=128 x N=BN x K=8 per instruction, accumulators in TMEM,
 //               tcgen05.commit frees ring slots and publishes accumulators
-//   warps 2..5  epilogue: tcgen05.ld, fused alpha/beta/bias/residual/
-//               pre-activation store/activation(-gradient), global stores
+//   warps 2..9  epilogue: tcgen05.ld, fused alpha/beta/bias/residual/
+//               pre-activation store/activation(-gradient), global stores;
+//               two warps per TMEM lane quarter take alternate 32-column
+//               chunks, so every SM sub-partition runs two epilogue warps
 // Two TMEM accumulators (2*BN columns) let the epilogue of tile i overlap
 // the main loop of tile i+1. No cluster multicast is used anywhere.
 #include <cuda.h>
@@ -33,7 +35,7 @@ namespace oxf {
 constexpr int BM = 128;       // tile rows (TMEM lanes)
 constexpr int BK = 32;        // K elements per ring slot: 32 x f32 = one 128-byte swizzle row
 constexpr int UMMA_K = 8;     // K per tcgen05.mma.kind::tf32
-constexpr int EPI_WARPS = 4;  // warps 2..5
+constexpr int EPI_WARPS = 8;  // warps 2..9: two per TMEM lane quarter, splitting columns
 constexpr int GEMM_THREADS = 64 + 32 * EPI_WARPS;
 constexpr int GROUP_M = 16;   // raster grouping for L2 reuse
 
@@ -42,7 +44,8 @@ struct GemmArgs {
   int a_mn, b_mn;  // operand stored MN-major (contiguous along M / N)
   int a3d, b3d;    // tensor map carries a batch coordinate
   int a_chunked, b_chunked;  // MN-major tile loaded by one (32, K, chunk) box
-  int tiles_m, tiles_n, splits, kblocks;
+  int tiles_m, tiles_n, splits, kblocks;  // kblocks: K blocks of the whole (reduced) K
+  int kblocks_item;                       // K blocks of one batch item
   long long units;
   uint32_t idesc;
   float* C; long long ldc, sc;
@@ -52,6 +55,7 @@ struct GemmArgs {
   float* P; long long ldp, sp;
   const float* X; long long ldx, sx;
   int act, grad_act, accumulate, vec_ok;
+  int reduce_batch;  // sum the batch into one output (K runs over batch x K)
 };
 
 template <int BN, int STAGES, bool SPLIT3>
@@ -82,10 +86,10 @@ struct GemmCtrl {
 __device__ __forceinline__ void decode_unit(const GemmArgs& a, long long u, int& b, int& tm,
                                             int& tn, int& kb0, int& kb1) {
   const long long tiles = static_cast<long long>(a.tiles_m) * a.tiles_n;
-  const long long per_split = tiles * a.batch;
+  const long long per_split = a.reduce_batch ? tiles : tiles * a.batch;
   const int s = static_cast<int>(u / per_split);
   const long long r = u - static_cast<long long>(s) * per_split;
-  b = static_cast<int>(r / tiles);
+  b = a.reduce_batch ? 0 : static_cast<int>(r / tiles);
   const long long t = r - static_cast<long long>(b) * tiles;
   const long long group_size = static_cast<long long>(GROUP_M) * a.tiles_n;
   const int g = static_cast<int>(t / group_size);
@@ -156,14 +160,14 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int b, int m, 
       if (prow) *reinterpret_cast<float4*>(prow + n0 + j) = acc;
       if (xrow) {
         const float4 x = *reinterpret_cast<const float4*>(xrow + n0 + j);
-        acc.x *= act_derivative(a.grad_act, x.x);
-        acc.y *= act_derivative(a.grad_act, x.y);
-        acc.z *= act_derivative(a.grad_act, x.z);
-        acc.w *= act_derivative(a.grad_act, x.w);
+        acc.x *= act_derivative_fast(a.grad_act, x.x);
+        acc.y *= act_derivative_fast(a.grad_act, x.y);
+        acc.z *= act_derivative_fast(a.grad_act, x.z);
+        acc.w *= act_derivative_fast(a.grad_act, x.w);
       }
       if (a.act != OXF_ACT_IDENTITY) {
-        acc.x = act_forward(a.act, acc.x); acc.y = act_forward(a.act, acc.y);
-        acc.z = act_forward(a.act, acc.z); acc.w = act_forward(a.act, acc.w);
+        acc.x = act_forward_fast(a.act, acc.x); acc.y = act_forward_fast(a.act, acc.y);
+        acc.z = act_forward_fast(a.act, acc.z); acc.w = act_forward_fast(a.act, acc.w);
       }
       if (a.accumulate) atomicAdd(reinterpret_cast<float4*>(crow + n0 + j), acc);
       else *reinterpret_cast<float4*>(crow + n0 + j) = acc;
@@ -178,8 +182,8 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int b, int m, 
       if (a.bias) acc += a.bias[n];
       if (rrow) acc += rrow[n];
       if (prow) prow[n] = acc;
-      if (xrow) acc *= act_derivative(a.grad_act, xrow[n]);
-      acc = act_forward(a.act, acc);
+      if (xrow) acc *= act_derivative_fast(a.grad_act, xrow[n]);
+      acc = act_forward_fast(a.act, acc);
       if (a.accumulate) atomicAdd(crow + n, acc);
       else crow[n] = acc;
     }
@@ -249,17 +253,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (ctrl->abort_flag) break;
           uint8_t* slot = ring + stage * Cfg::STAGE_BYTES;
           mbar_arrive_expect_tx(&ctrl->full[stage], Cfg::STAGE_BYTES);
-          const int k0 = kb * BK;
+          // batch-reduce GEMMs walk K over (batch item, k-block) pairs
+          const int bk = args.reduce_batch ? kb / args.kblocks_item : b;
+          const int k0 = (args.reduce_batch ? kb % args.kblocks_item : kb) * BK;
           load_operand<BM>(slot, &tmA, &ctrl->full[stage], args.a_mn, args.a3d, args.a_chunked,
-                           tm * BM, k0, b);
+                           tm * BM, k0, bk);
           load_operand<BN>(slot + Cfg::A_BYTES, &tmB, &ctrl->full[stage], args.b_mn, args.b3d,
-                           args.b_chunked, tn * BN, k0, b);
+                           args.b_chunked, tn * BN, k0, bk);
           if (SPLIT3) {
             uint8_t* lo = slot + Cfg::A_BYTES + Cfg::B_BYTES;
             load_operand<BM>(lo, &tmA_lo, &ctrl->full[stage], args.a_mn, args.a3d,
-                             args.a_chunked, tm * BM, k0, b);
+                             args.a_chunked, tm * BM, k0, bk);
             load_operand<BN>(lo + Cfg::A_BYTES, &tmB_lo, &ctrl->full[stage], args.b_mn,
-                             args.b3d, args.b_chunked, tn * BN, k0, b);
+                             args.b3d, args.b_chunked, tn * BN, k0, bk);
           }
           ++fills;
           if (++stage == STAGES) {
@@ -331,6 +337,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;  // which alternate 32-column chunks it takes
     const int row_local = quarter * 32 + lane;
     int local = 0;
     for (long long u = blockIdx.x; u < args.units; u += gridDim.x, ++local) {
@@ -347,7 +354,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(acc_slot * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = half; c < BN / 32; c += 2) {
         const int n0 = tn * BN + c * 32;
         if (n0 >= args.N) break;  // uniform across the warp
         float v[32];
@@ -699,6 +706,10 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
   a.X = d->aux; a.ldx = d->ldx; a.sx = d->stride_x;
   a.act = d->act; a.grad_act = d->aux ? d->grad_act : OXF_ACT_IDENTITY;
   a.accumulate = d->accumulate ? 1 : 0;
+  a.reduce_batch = (d->reduce_batch && d->batch > 1) ? 1 : 0;
+  if (a.reduce_batch && (d->stride_c || d->stride_r || d->stride_p || d->stride_x))
+    return set_error(OXF_ERR_INVALID_ARG,
+                     "oxf_gemm: reduce_batch writes one output (output strides must be 0)");
   auto vec = [](const void* p, long long ld, long long st) {
     return p == nullptr || (aligned16(p) && ld % 4 == 0 && st % 4 == 0);
   };
@@ -710,6 +721,9 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
   const bool tma_ok = d->K > 0 && tma_ok_ptr(d->A) && tma_ok_ptr(d->B) && d->lda % 4 == 0 &&
                       d->ldb % 4 == 0 && d->stride_a % 4 == 0 && d->stride_b % 4 == 0;
   if (!tma_ok) {
+    if (a.reduce_batch)
+      return set_error(OXF_ERR_UNSUPPORTED_SHAPE,
+                       "oxf_gemm: reduce_batch needs 16-byte aligned operands");
     a.splits = 1;
     if (d->K == 0) {
       // C = epilogue(0): run the SIMT kernel with an empty K loop.
@@ -776,8 +790,10 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
   }
   a.tiles_m = (d->M + BM - 1) / BM;
   a.tiles_n = (d->N + BN - 1) / BN;
-  a.kblocks = (d->K + BK - 1) / BK;
-  const long long tiles = static_cast<long long>(a.tiles_m) * a.tiles_n * d->batch;
+  a.kblocks_item = (d->K + BK - 1) / BK;
+  a.kblocks = a.kblocks_item * (a.reduce_batch ? d->batch : 1);
+  const long long tiles =
+      static_cast<long long>(a.tiles_m) * a.tiles_n * (a.reduce_batch ? 1 : d->batch);
   if (d->accumulate) {
     a.splits = split > 1 ? std::min(split, a.kblocks) : choose_splits(tiles, a.kblocks, sms);
   } else {

@@ -391,6 +391,33 @@ __global__ void loss_rows_kernel(const float* __restrict__ y, const float* __res
   if (t == 0) out[r] = s * (1.0f / static_cast<float>(cols));
 }
 
+// loss_rows and its gradient in one pass over y and t.
+template <int G, int NV>
+__global__ void loss_grad_rows_kernel(const float* __restrict__ y, const float* __restrict__ tg,
+                                      float* __restrict__ out, float* __restrict__ dy,
+                                      long long rows, int cols) {
+  __shared__ float red[G / 32];
+  long long r;
+  int t;
+  if (!row_index<G>(rows, r, t)) return;
+  const int cols4 = cols >> 2;
+  const float inv = 1.0f / static_cast<float>(cols);
+  Row<G, NV> a, b;
+  a.load(y + r * cols, t, cols4, 0.f);
+  b.load(tg + r * cols, t, cols4, 0.f);
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    float4& d = a.v[j];
+    d.x -= b.v[j].x; d.y -= b.v[j].y; d.z -= b.v[j].z; d.w -= b.v[j].w;
+    s += 0.5f * d.x * d.x + 0.5f * d.y * d.y + 0.5f * d.z * d.z + 0.5f * d.w * d.w;
+    d.x *= inv; d.y *= inv; d.z *= inv; d.w *= inv;
+  }
+  a.store(dy + r * cols, t, cols4);
+  s = GroupReduce<G>::sum(s, red);
+  if (t == 0) out[r] = s * inv;
+}
+
 // ------------------------------------------------------------------ looped (general) path
 // One block per row, any width and alignment, scalar accesses, several
 // passes over the row in global memory.
@@ -759,6 +786,9 @@ OXF_ROW_LAUNCHER(RmsBwdL, rmsnorm_bwd_kernel,
                  P_(x, dy, dx, rows, cols, eps))
 OXF_ROW_LAUNCHER(SumRowsL, sum_rows_kernel, P_(const float* m, float* out, int cols),
                  P_(m, out, rows, cols))
+OXF_ROW_LAUNCHER(LossGradL, loss_grad_rows_kernel,
+                 P_(const float* y, const float* t, float* out, float* dy, int cols),
+                 P_(y, t, out, dy, rows, cols))
 OXF_ROW_LAUNCHER(LossRowsL, loss_rows_kernel,
                  P_(const float* y, const float* t, float* out, int cols), P_(y, t, out, rows, cols))
 #undef P_
@@ -866,6 +896,19 @@ oxf_status rows_loss(const float* y, const float* t, float* out, long long rows,
   if (al(y) && al(t) && dispatch_row<LossRowsL>(rows, cols, s, y, t, out, static_cast<int>(cols)))
     return check_launch("loss_rows_kernel");
   return looped(LOOP_LOSS, out, y, t, rows, cols, 0.f, 0.f, 0, nullptr, nullptr, s);
+}
+
+oxf_status ew_mse_grad(const float*, const float*, float*, long long, long long, cudaStream_t);
+
+oxf_status rows_loss_grad(const float* y, const float* t, float* out, float* dy, long long rows,
+                          long long cols, cudaStream_t s) {
+  if (rows == 0) return OXF_OK;
+  if (al(y) && al(t) && al(dy) &&
+      dispatch_row<LossGradL>(rows, cols, s, y, t, out, dy, static_cast<int>(cols)))
+    return check_launch("loss_grad_rows_kernel");
+  oxf_status st = rows_loss(y, t, out, rows, cols, s);
+  if (st != OXF_OK) return st;
+  return ew_mse_grad(y, t, dy, rows * cols, cols, s);
 }
 
 oxf_status ew_binary(const float* a, const float* b, float* out, long long n, int op,

@@ -67,6 +67,7 @@ Gemm& Gemm::grad_act(int act, const float* aux, long long ldx, long long stride)
 }
 Gemm& Gemm::act(int a) { d_.act = a; return *this; }
 Gemm& Gemm::accumulate() { d_.accumulate = 1; return *this; }
+Gemm& Gemm::reduce_batch() { d_.reduce_batch = 1; return *this; }
 void Gemm::run(cudaStream_t s) const {
   GemmTimer* t = active_gemm_timer();
   if (t) t->begin(s, 2.0 * d_.M * d_.N * static_cast<double>(d_.K) * d_.batch);
@@ -417,8 +418,8 @@ void TransformerEngine::train_forward(const float* x, int batch) { forward(x, ba
 
 void TransformerEngine::set_target(const float* target) {
   const size_t T = static_cast<size_t>(batch_) * spec_.seq, O = spec_.o.out;
-  check(oxf_loss_rows(cs(y_, T * O), cs(target, T * O), ms(loss_, T), O, ST(stream_)));
-  check(oxf_mse_grad(cs(y_, T * O), cs(target, T * O), ms(dy_, T * O), O, ST(stream_)));
+  check(oxf_mse_loss_grad(cs(y_, T * O), cs(target, T * O), ms(loss_, T), ms(dy_, T * O), O,
+                          ST(stream_)));
 }
 
 void TransformerEngine::set_output_gradient(const float* dy) {
@@ -513,12 +514,22 @@ void TransformerEngine::backward_stage(int stage) {
                                     ls[j]->out, 1, ST(stream_)));
       }
     }
-    // d_positioned = dR + Σ_j dProj_j · W_jᵀ (attention.rs:127-131, 318-319)
-    for (int j = 0; j < 3; ++j) {
-      Gemm g(Ti, H, ls[j]->out, false, true, ds[j], params_ + offs[j], dpos_);
-      if (j == 0) g.residual(dr_, H);
-      else g.beta(1.0f);
-      g.run(stream_);
+    // d_positioned = dR + Σ_j dProj_j · W_jᵀ (attention.rs:127-131, 318-319):
+    // one batch-reduce GEMM over the three projections when they share a
+    // layout, otherwise three GEMMs accumulating through beta = 1.
+    if (uniform) {
+      Gemm g(Ti, H, D, false, true, dqkv_, params_ + off_q_, dpos_);
+      g.batch(3, static_cast<long long>(T) * D, static_cast<long long>(spec_.q.param_count()), 0)
+          .reduce_batch()
+          .residual(dr_, H)
+          .run(stream_);
+    } else {
+      for (int j = 0; j < 3; ++j) {
+        Gemm g(Ti, H, ls[j]->out, false, true, ds[j], params_ + offs[j], dpos_);
+        if (j == 0) g.residual(dr_, H);
+        else g.beta(1.0f);
+        g.run(stream_);
+      }
     }
     // position gradient: sum over the batch (encoder.rs:180-184)
     check(oxf_matrix_sum_cols(cs(dpos_, T * H), ms(grads_ + off_pos_, static_cast<size_t>(S) * H),

@@ -88,6 +88,7 @@ class Gemm {
   Gemm& grad_act(int act, const float* aux, long long ldx, long long stride = 0);
   Gemm& act(int a);
   Gemm& accumulate();
+  Gemm& reduce_batch();
   void run(cudaStream_t s) const;
 
  private:

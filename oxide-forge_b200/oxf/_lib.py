@@ -54,6 +54,7 @@ class GemmDesc(C.Structure):
         ("act", C.c_int), ("grad_act", C.c_int), ("accumulate", C.c_int),
         ("split_k", C.c_int), ("precision", C.c_int),
         ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
+        ("reduce_batch", C.c_int),
     ]
 
 
@@ -71,6 +72,7 @@ _SIGS = {
     "oxf_sgd_update": (C.c_int, [Slice, CSlice, C.c_float, C.c_void_p]),
     "oxf_mse_grad": (C.c_int, [CSlice, CSlice, Slice, C.c_size_t, C.c_void_p]),
     "oxf_loss_rows": (C.c_int, [CSlice, CSlice, Slice, C.c_size_t, C.c_void_p]),
+    "oxf_mse_loss_grad": (C.c_int, [CSlice, CSlice, Slice, Slice, C.c_size_t, C.c_void_p]),
     "oxf_slice_sum": (C.c_int, [CSlice, C.c_void_p, C.c_void_p]),
     "oxf_slice_max": (C.c_int, [CSlice, C.c_void_p, C.c_void_p]),
     "oxf_matrix_sum_rows": (C.c_int, [CSlice, Slice, C.c_size_t, C.c_void_p]),

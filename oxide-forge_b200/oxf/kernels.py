@@ -73,6 +73,12 @@ def loss_rows(y, t, out, stream=None):
     return out
 
 
+def mse_loss_grad(y, t, row_loss, dy, stream=None):
+    check(lib().oxf_mse_loss_grad(cs(y), cs(t), ms(row_loss), ms(dy), y.shape[-1],
+                                  _stream(stream)))
+    return row_loss, dy
+
+
 def slice_sum(x, out, stream=None):
     check(lib().oxf_slice_sum(cs(x), ptr(out), _stream(stream)))
     return out
@@ -184,7 +190,8 @@ def matrix_multiply_refalgo(a, b, out, stream=None):
 
 def gemm(a, b, out, *, a_trans=False, b_trans=False, alpha=1.0, beta=0.0, bias=None,
          residual=None, pre_out=None, aux=None, act=_lib.ACT_IDENTITY, grad_act=_lib.ACT_IDENTITY,
-         accumulate=False, split_k=0, precision=_lib.PREC_TF32, workspace=None, stream=None):
+         accumulate=False, split_k=0, precision=_lib.PREC_TF32, workspace=None, reduce_batch=False,
+         stream=None):
     """out = epilogue(alpha * op(a)·op(b)); 2-D or batched 3-D operands.
 
     a: [M,K] (or [K,M] with a_trans), b: [K,N] (or [N,K] with b_trans); a
@@ -217,6 +224,9 @@ def gemm(a, b, out, *, a_trans=False, b_trans=False, alpha=1.0, beta=0.0, bias=N
             setattr(d, sn, t.shape[-1] * t.shape[-2] if t.dim() == 3 else 0)
     d.act, d.grad_act = int(act), int(grad_act)
     d.accumulate, d.split_k, d.precision = int(accumulate), int(split_k), int(precision)
+    d.reduce_batch = int(reduce_batch)
+    if reduce_batch:
+        d.stride_c = 0
     if precision == _lib.PREC_TF32X3:
         need = lib().oxf_gemm_workspace_size(C.byref(d))
         if workspace is None or workspace.numel() * workspace.element_size() < need:

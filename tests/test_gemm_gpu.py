@@ -204,3 +204,16 @@ def test_large_square(K, rng):
     lhs = out.double() @ ones
     rhs = A.double() @ (B.double() @ ones)
     assert ((lhs - rhs).abs().max() / rhs.abs().max()).item() < TF32_TOL
+
+
+def test_batch_reduce(K, rng):
+    """C = R + Σ_b A_b·B_bᵀ in one GEMM (the input gradient of the three
+    projections, attention.rs:127-131)."""
+    batch, M, N, Kd = 3, 256, 192, 128
+    A = rng.uniform(-1, 1, (batch, M, Kd)).astype(np.float32)
+    B = rng.uniform(-1, 1, (batch, N, Kd)).astype(np.float32)
+    R = rng.standard_normal((M, N)).astype(np.float32)
+    out = torch.empty((M, N), device="cuda")
+    K.gemm(dev(A), dev(B), out, b_trans=True, residual=dev(R), reduce_batch=True)
+    want = R + sum(exact(A[b], B[b], 0, 1) for b in range(batch))
+    assert rel_err(host(out), want) < TF32_TOL

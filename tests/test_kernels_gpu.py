@@ -195,3 +195,14 @@ def test_shape_validation_matches_reference_asserts(K):
     # row vector length must equal cols (rows.rs:18)
     with pytest.raises(OxfError):
         K.binary_assign_by_rows(torch.zeros(3, 4, device="cuda"), torch.zeros(5, device="cuda"), 0)
+
+
+def test_mse_loss_grad_fused(K, rng):
+    for r, c in [(1, 1), (7, 36), (33, 1024), (5, 2048), (3, 20000)]:
+        y = rng.standard_normal((r, c)).astype(np.float32)
+        t = rng.standard_normal((r, c)).astype(np.float32)
+        loss = torch.empty(r, device="cuda")
+        dy = torch.empty((r, c), device="cuda")
+        K.mse_loss_grad(dev(y), dev(t), loss, dy)
+        assert rel_err(host(loss), O.loss_rows(y, t)) < TOL
+        assert rel_err(host(dy), O.mse_grad(y, t)) < TOL
