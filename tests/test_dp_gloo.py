@@ -1,0 +1,175 @@
+"""Data-parallel driver (oxf/dp.py) on CPU with world-size-2 gloo ranks.
+
+The engine is replaced by a host stand-in built on the oracle (test-only),
+so this checks the driver's own logic: batch sharding, the three bucketed
+all-reduces in cursor order, the global-mean SGD update, equality of the
+N-rank step with the 1-rank step on the same global batch, and that a rank
+which dies leaves the others with an error instead of a hang.
+"""
+from __future__ import annotations
+
+import os
+import socket
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+torch = pytest.importorskip("torch")
+SEQ, H, F = 8, 12, 20
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+class OracleModel:
+    """Host stand-in with the engine interface DataParallelTrainer uses."""
+
+    def __init__(self, flat: np.ndarray):
+        sys.path.insert(0, str(ROOT / "oracle"))
+        sys.path.insert(0, str(ROOT / "oxide-forge_b200"))
+        import oracle as O
+        self.O = O
+        self.flat = flat.astype(np.float32).copy()
+        self.params = torch.from_numpy(self.flat)
+        self.grads = torch.zeros_like(self.params)
+        # cursor order: wq, wk, wv, pos, w1, w2, wo
+        sizes = [H * H, H * H, H * H, SEQ * H, H * F, F * H, H * H]
+        self.offsets = np.cumsum([0] + sizes)
+
+    def _model(self):
+        O, f, o = self.O, self.flat, self.offsets
+        w = [f[o[i]:o[i + 1]] for i in range(7)]
+        lin = lambda a, shape, act=O.IDENTITY: O.LinearParams(a.reshape(shape), None, act)
+        return O.TransformerParams(lin(w[0], (H, H)), lin(w[1], (H, H)), lin(w[2], (H, H)),
+                                   w[3].reshape(SEQ, H),
+                                   O.MlpParams([lin(w[4], (H, F), O.GELU), lin(w[5], (F, H))]),
+                                   lin(w[6], (H, H)), O.NORM_LAYER, SEQ)
+
+    def zero_grads(self):
+        self.grads.zero_()
+
+    def train_forward(self, x):
+        self._x = x.numpy().reshape(-1, SEQ, H)
+
+    def set_target(self, t):
+        t = t.numpy().reshape(-1, SEQ, H)
+        g = np.zeros_like(self.flat)
+        losses = []
+        for b in range(self._x.shape[0]):
+            _, loss, _ = self.O.transformer_train_step(self._model(), self._x[b], t[b], 0.0,
+                                                       grads=g)
+            losses.append(loss)
+        self.grads += torch.from_numpy(g)
+        return torch.from_numpy(np.concatenate(losses))
+
+    def backward_stage(self, s):
+        pass  # gradients were produced in set_target
+
+    def bucket(self, s):
+        o = self.offsets
+        return {0: (int(o[6]), int(o[7] - o[6])), 1: (int(o[4]), int(o[6] - o[4])),
+                2: (0, int(o[4]))}[s]
+
+    def sgd(self, lr):
+        self.params -= lr * self.grads  # self.flat shares memory with params
+
+
+def _data(global_batch, seed):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((global_batch * SEQ, H)).astype(np.float32)
+    t = rng.standard_normal((global_batch * SEQ, H)).astype(np.float32)
+    return x, t
+
+
+def _flat0():
+    rng = np.random.default_rng(0)
+    sizes = [(H, H), (H, H), (H, H), (SEQ, H), (H, F), (F, H), (H, H)]
+    parts = [rng.uniform(-0.3, 0.3, s) for s in sizes]
+    parts[3] = 0.02 * rng.standard_normal((SEQ, H))
+    return np.concatenate([p.ravel() for p in parts]).astype(np.float32)
+
+
+def _worker(rank, world, port, global_batch, steps, out_dir, fail_rank):
+    import torch.distributed as dist
+    from datetime import timedelta
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=8))
+    sys.path.insert(0, str(ROOT / "oxide-forge_b200"))
+    from oxf.dp import DataParallelTrainer
+    model = OracleModel(_flat0() if rank == 0 else np.zeros_like(_flat0()))
+    tr = DataParallelTrainer(model, global_batch, lr=0.1, seq=SEQ)
+    tr.broadcast_params(model.params)
+    result = {"rank": rank}
+    try:
+        for step in range(steps):
+            if rank == fail_rank and step == 1:
+                os._exit(3)  # this rank dies between steps
+            x, t = _data(global_batch, seed=step)
+            lo, hi = tr.local
+            sl = slice(lo * SEQ, hi * SEQ)
+            loss = tr.step(torch.from_numpy(x[sl]), torch.from_numpy(t[sl]))
+            result[f"loss{step}"] = float(loss)
+        result["params"] = model.params.numpy().copy()
+    except Exception as ex:  # the surviving rank must see an error, not hang
+        result["error"] = type(ex).__name__
+    np.save(Path(out_dir) / f"rank{rank}.npy", result, allow_pickle=True)
+    try:
+        dist.destroy_process_group()
+    except Exception:
+        pass
+
+
+def _run(world, global_batch, steps, tmp_path, fail_rank=-1):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, global_batch, steps, str(tmp_path),
+                                               fail_rank)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+            raise AssertionError("a rank hung")
+    out = {}
+    for r in range(world):
+        f = tmp_path / f"rank{r}.npy"
+        if f.exists():
+            out[r] = np.load(f, allow_pickle=True).item()
+    return out
+
+
+def test_shard_arithmetic():
+    sys.path.insert(0, str(ROOT / "oxide-forge_b200"))
+    from oxf.dp import shard
+    assert [shard(128, r, 8) for r in range(8)][3] == (48, 64)
+    assert shard(6, 1, 2) == (3, 6)
+    with pytest.raises(ValueError):
+        shard(7, 0, 2)
+
+
+def test_two_ranks_match_one_rank(tmp_path):
+    (tmp_path / "one").mkdir()
+    (tmp_path / "two").mkdir()
+    one = _run(1, 4, 2, tmp_path / "one")
+    two = _run(2, 4, 2, tmp_path / "two")
+    p1, p20, p21 = one[0]["params"], two[0]["params"], two[1]["params"]
+    np.testing.assert_array_equal(p20, p21)          # ranks stay in lockstep
+    assert np.abs(p20 - p1).max() <= 1e-5 * np.abs(p1).max()
+    assert abs(two[0]["loss1"] - one[0]["loss1"]) < 1e-5
+    assert not np.array_equal(p1, _flat0())          # the steps did update
+
+
+def test_dead_rank_is_an_error_not_a_hang(tmp_path):
+    out = _run(2, 4, 3, tmp_path, fail_rank=1)
+    assert 1 not in out                               # rank 1 exited without a result
+    assert out[0].get("error"), out[0].keys()        # rank 0 got an error from its collective
