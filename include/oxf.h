@@ -221,6 +221,21 @@ void oxf_gemm_desc_init(oxf_gemm_desc* d, int M, int N, int K, int a_trans, int 
 size_t oxf_gemm_workspace_size(const oxf_gemm_desc* d);
 oxf_status oxf_gemm(const oxf_gemm_desc* d, oxf_stream stream);
 
+/* oxf_gemm in 3xTF32 precision without any allocation, for callers that
+ * cannot call cudaMalloc: plugin hosts that own the device memory budget
+ * through their own allocator, and latency-critical paths that must not
+ * pay for cudaMalloc's implicit synchronisation. No counterpart in the
+ * reference (it has no 3xTF32 mode and no scratch memory).
+ * The hi/lo operand splits live in a 16 MiB static device array that every
+ * GPU loading the library holds until exit; shapes needing more
+ * (oxf_gemm_workspace_size > 16 MiB) return OXF_ERR_UNSUPPORTED_SHAPE. The
+ * descriptor's precision and workspace fields are ignored. The first call on
+ * a device looks up the array's device address, so make it before any
+ * stream capture. All calls on a device share that device's array, which
+ * keeps the last call's contents: calls that can overlap on the GPU (issued
+ * on different streams of one device) race, so serialise them. */
+oxf_status oxf_gemm_tf32x3_noalloc(const oxf_gemm_desc* desc, oxf_stream stream);
+
 /* matrix_multiply (module.rs:179-191) with the reference's argument order:
  * result[rows,cols] = lhs[rows,len] · rhs[len,cols], TF32 operands, f32
  * accumulation. The reference asserts rows, cols, len % 16 == 0

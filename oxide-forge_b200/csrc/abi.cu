@@ -50,6 +50,7 @@ size_t gemm_workspace_bytes(const oxf_gemm_desc*);
 oxf_status gemm_refalgo(const float*, const float*, float*, size_t, size_t, size_t,
                         cudaStream_t);
 oxf_status gemm_read_device_error(uint32_t*);
+oxf_status gemm_tf32x3_noalloc(const oxf_gemm_desc*, cudaStream_t);
 
 namespace {
 thread_local char g_last_error[512] = "";
@@ -359,6 +360,12 @@ oxf_status oxf_gemm(const oxf_gemm_desc* d, oxf_stream stream) {
   if (d && (!valid_act(d->act) || !valid_act(d->grad_act)))
     return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: bad activation");
   return gemm_run(d, S(stream));
+}
+
+oxf_status oxf_gemm_tf32x3_noalloc(const oxf_gemm_desc* d, oxf_stream stream) {
+  if (d && (!valid_act(d->act) || !valid_act(d->grad_act)))
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm_tf32x3_noalloc: bad activation");
+  return gemm_tf32x3_noalloc(d, S(stream));
 }
 
 oxf_status oxf_matrix_multiply(oxf_cslice lhs, oxf_cslice rhs, oxf_slice result, size_t len,

@@ -832,6 +832,54 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
   return launch_tcgen05<64, 8, false>(ta, tb, ta, tb, a, stream, dev);
 }
 
+// ---------------------------------------------------------------- no-allocation variant
+// Some callers cannot call cudaMalloc: plugin hosts that own the whole device
+// memory budget through their own allocator and forbid allocations from
+// libraries, and latency-critical paths that must not pay for cudaMalloc's
+// implicit device synchronisation. For them the 3xTF32 GEMM can take its
+// hi/lo operand splits from this fixed array instead of a caller workspace.
+// It is a file-scope device array, so every GPU that loads this library
+// holds these 16 MiB until the process exits.
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+oxf_status gemm_tf32x3_noalloc(const oxf_gemm_desc* d, cudaStream_t stream) {
+  if (!d) return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm_tf32x3_noalloc: null descriptor");
+  oxf_gemm_desc desc = *d;
+  desc.precision = OXF_PREC_TF32X3;
+  const size_t need = gemm_workspace_bytes(&desc);
+  if (need > kNoAllocScratchBytes)
+    return set_error(OXF_ERR_UNSUPPORTED_SHAPE,
+                     "oxf_gemm_tf32x3_noalloc: this shape needs %zu bytes of operand splits, "
+                     "the static scratch holds %zu (16 MiB); use oxf_gemm with a workspace",
+                     need, kNoAllocScratchBytes);
+  int dev = 0;
+  oxf_status st = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  if (st != OXF_OK) return st;
+  if (dev < 0 || dev >= kMaxDevices)
+    return set_error(OXF_ERR_UNSUPPORTED_SHAPE, "oxf_gemm_tf32x3_noalloc: device ordinal %d", dev);
+  // In host code the array's name only stands in for it; its device address
+  // is looked up once per device, with that device current, on the first
+  // call there.
+  static std::mutex mu;
+  static void* scratch[kMaxDevices] = {nullptr};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!scratch[dev]) {
+      void* p = nullptr;
+      st = check_cuda(cudaGetSymbolAddress(&p, g_noalloc_scratch),
+                      "cudaGetSymbolAddress(no-alloc scratch)");
+      if (st != OXF_OK) return st;
+      scratch[dev] = p;
+    }
+  }
+  // Nothing in the scratch needs to start at zero: the split kernels write
+  // every element the GEMM then reads (TMA zero-fills reads past the edges).
+  desc.workspace = scratch[dev];
+  desc.workspace_bytes = kNoAllocScratchBytes;
+  return gemm_run(&desc, stream);
+}
+
 oxf_status gemm_refalgo(const float* A, const float* B, float* C, size_t len, size_t rows,
                         size_t cols, cudaStream_t stream) {
   if (rows % 16 || cols % 16 || len % 16)

@@ -101,6 +101,7 @@ _SIGS = {
                                   C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
     "oxf_gemm_workspace_size": (C.c_size_t, [C.POINTER(GemmDesc)]),
     "oxf_gemm": (C.c_int, [C.POINTER(GemmDesc), C.c_void_p]),
+    "oxf_gemm_tf32x3_noalloc": (C.c_int, [C.POINTER(GemmDesc), C.c_void_p]),
     "oxf_matrix_multiply": (C.c_int, [CSlice, CSlice, Slice, C.c_size_t, C.c_size_t, C.c_size_t,
                                       C.c_void_p]),
     "oxf_matrix_multiply_refalgo": (C.c_int, [CSlice, CSlice, Slice, C.c_size_t, C.c_size_t,
