@@ -55,6 +55,13 @@ def parse():
     ap.add_argument("--ffn", type=int, default=FFN)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--workload", default="train",
+                    choices=["train", "gemm", "rows", "mlp", "infer"],
+                    help="train: the contract line (config 5). The others are supplementary "
+                         "single-GPU measurements of configs 1-4: gemm (square sweep / one "
+                         "shape), rows (config 2 row suite), mlp (config 3), infer (config 4)")
+    ap.add_argument("--shape", default=None, help="gemm: M,N,K (default: the 512..8192 sweep)")
+    ap.add_argument("--mode", default="nn", help="gemm: nn, nt, tn or tt")
     return ap.parse_args()
 
 
@@ -175,9 +182,12 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ GPU side
-def cublas_tf32_peak(torch) -> float:
-    """TF32 dense GEMM throughput of cuBLAS (torch.matmul) at 8192^3,
-    best of 10 after warm-up: the roofline denominator for TF32 kernels."""
+def cublas_tf32_peak(torch, sustained_s: float = 0.0):
+    """TF32 dense GEMM throughput of cuBLAS (torch.matmul) at 8192^3, the
+    roofline denominator for TF32 kernels. Returns the burst figure (best
+    of 10 single launches) or, with sustained_s > 0, the mean over
+    back-to-back launches for that many seconds (the power-capped rate a
+    kernel inside a long step sees)."""
     n = 8192
     a = torch.randn(n, n, device="cuda")
     b = torch.randn(n, n, device="cuda")
@@ -186,23 +196,137 @@ def cublas_tf32_peak(torch) -> float:
     torch.backends.cuda.matmul.allow_tf32 = True
     for _ in range(3):
         torch.matmul(a, b, out=c)
-    best = float("inf")
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    for _ in range(10):
+    if sustained_s > 0:
+        torch.cuda.synchronize()
         s.record()
-        torch.matmul(a, b, out=c)
+        t0, iters = time.perf_counter(), 0
+        while time.perf_counter() - t0 < sustained_s:
+            for _ in range(10):
+                torch.matmul(a, b, out=c)
+            iters += 10
+            torch.cuda.current_stream().synchronize()
         e.record()
         e.synchronize()
-        best = min(best, s.elapsed_time(e))
+        ms = s.elapsed_time(e) / iters
+    else:
+        ms = float("inf")
+        for _ in range(10):
+            s.record()
+            torch.matmul(a, b, out=c)
+            e.record()
+            e.synchronize()
+            ms = min(ms, s.elapsed_time(e))
     torch.backends.cuda.matmul.allow_tf32 = prev
     del a, b, c
-    return 2 * n ** 3 / (best * 1e-3) / 1e12
+    return 2 * n ** 3 / (ms * 1e-3) / 1e12
+
+
+def _events(torch):
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def _time(torch, fn, steps, warmup):
+    """Mean device ms per call over `steps` after `warmup` calls."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = _events(torch)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_gemm(a, torch):
+    """Config 3's square sweep (or one shape): TF32 GEMM TFLOP/s against
+    cuBLAS TF32 on the same GPU; inputs U(-1,1), 3 x 256 MiB operands at
+    8192 (larger than L2)."""
+    from oxf import kernels as K
+    peak = cublas_tf32_peak(torch)
+    shapes = [tuple(int(v) for v in a.shape.split(","))] if a.shape else \
+        [(n, n, n) for n in (512, 1024, 2048, 4096, 8192)]
+    at, bt = a.mode[0] == "t", a.mode[1] == "t"
+    res = []
+    for M, N, Kd in shapes:
+        A = torch.empty((Kd, M) if at else (M, Kd), device="cuda").uniform_(-1, 1)
+        B = torch.empty((N, Kd) if bt else (Kd, N), device="cuda").uniform_(-1, 1)
+        Cm = torch.empty((M, N), device="cuda")
+        ms = _time(torch, lambda: K.gemm(A, B, Cm, a_trans=at, b_trans=bt), a.steps, a.warmup)
+        torch.backends.cuda.matmul.allow_tf32 = True
+        ref = _time(torch, lambda: torch.matmul(A.T if at else A, B.T if bt else B, out=Cm),
+                    a.steps, a.warmup)
+        fl = 2.0 * M * N * Kd
+        res.append({"shape": [M, N, Kd], "mode": a.mode, "ms": ms, "tflops": fl / ms / 1e9,
+                    "cublas_tflops": fl / ref / 1e9, "frac_of_peak": fl / ms / 1e9 / peak})
+        del A, B, Cm
+    print(json.dumps({"metric": "GEMM TF32 TFLOP/s", "unit": "TFLOP/s", "workload": "gemm",
+                      "peak_cublas_tf32_8192": peak, "results": res}), flush=True)
+
+
+def run_rows(a, torch):
+    """Config 2 row suite on [4096,1024] f32: GB/s of algorithmic bytes per
+    kernel (read + write of whole matrices, vectors ignored). The matrices
+    (16 MiB each) fit in L2, so a 256 MiB buffer is written after each
+    input is prepared and before the timed launch; only the kernel is
+    timed."""
+    from oxf import kernels as K
+    R, Cc = 4096, 1024
+    g = torch.Generator(device="cuda").manual_seed(2)
+    x = torch.randn(R, Cc, device="cuda", generator=g)
+    dy = torch.randn(R, Cc, device="cuda", generator=g)
+    gamma = 1 + 0.1 * torch.randn(Cc, device="cuda", generator=g)
+    beta = 0.1 * torch.randn(Cc, device="cuda", generator=g)
+    work = torch.empty_like(x)
+    out = torch.empty_like(x)
+    p = torch.softmax(x, dim=1).contiguous()
+    flush = torch.empty(64 << 20, device="cuda")
+    mat = R * Cc * 4
+    reset = lambda src: (lambda: work.copy_(src))
+    nothing = lambda: None
+    ops = {  # name: (prepare, kernel, algorithmic bytes)
+        "softmax_fwd": (reset(x), lambda: K.softmax_rows(work), 2 * mat),
+        "softmax_bwd": (nothing, lambda: K.softmax_backward(p, dy, out), 3 * mat),
+        "layernorm_fwd": (nothing, lambda: K.norm_rows(x, out, 1), 2 * mat),
+        "layernorm_fwd_affine": (nothing, lambda: K.norm_rows(x, out, 1, 1e-5, gamma, beta),
+                                 2 * mat),
+        "layernorm_bwd": (nothing, lambda: K.layer_norm_backward(x, dy, out), 3 * mat),
+        "rmsnorm_fwd": (nothing, lambda: K.norm_rows(x, out, 0), 2 * mat),
+        "rmsnorm_bwd": (nothing, lambda: K.rms_norm_backward(x, dy, out), 3 * mat),
+        "gelu_fwd": (reset(x), lambda: K.unary(work, 2, 1), 2 * mat),
+        "gelu_bwd": (reset(dy), lambda: K.mul_act_derivative(work, x, 1), 3 * mat),
+        "row_broadcast_add": (reset(x), lambda: K.binary_assign_by_rows(work, beta, 0), 2 * mat),
+    }
+    res = {}
+    for name, (prep, fn, nbytes) in ops.items():
+        times = []
+        for _ in range(a.warmup + a.steps):
+            prep()
+            flush.fill_(1.0)
+            e0, e1 = _events(torch)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+        ms = statistics.median(times[a.warmup:])
+        res[name] = {"ms": ms, "gbs": nbytes / ms / 1e6}
+    print(json.dumps({"metric": "row kernels GB/s", "unit": "GB/s", "workload": "rows",
+                      "shape": [R, Cc], "l2": "256 MiB flush before every timed launch",
+                      "results": res}), flush=True)
 
 
 def main():
     a = parse()
     if a.impl == "reference":
         run_reference(a)
+        return
+    if a.workload in ("gemm", "rows"):
+        import torch
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        (run_gemm if a.workload == "gemm" else run_rows)(a, torch)
         return
     import numpy as np
     import torch
@@ -233,7 +357,8 @@ def main():
     x = torch.randn(rows, a.hidden, device="cuda", generator=g)
     t = torch.randn(rows, a.hidden, device="cuda", generator=g)
 
-    peak = cublas_tf32_peak(torch)
+    peak_burst = cublas_tf32_peak(torch)
+    peak = cublas_tf32_peak(torch, sustained_s=3.0)
 
     # ---------------- device-resident timing
     for _ in range(a.warmup):
@@ -333,7 +458,10 @@ def main():
                          "traffic": None, "kernel": "gemm_tf32_tcgen05 (all GEMMs of a step)",
                          "gemm_launches_per_step": gemm_launches // max(1, a.steps),
                          "gemm_share_of_step": gemm_ms / elapsed_ms if elapsed_ms else None,
-                         "peak_source": "cuBLAS TF32 8192^3 (torch.matmul) measured in this run"},
+                         "peak_source": "cuBLAS TF32 8192^3 (torch.matmul), back to back for "
+                                        "3 s in this run (sustained: the GEMMs run inside a "
+                                        "long power-capped step)",
+                         "peak_burst": peak_burst},
             "model_tflops": value * fpt / 1e12,
             "cpu_baseline": cpu,
             "clocks": clk,

@@ -211,6 +211,8 @@ typedef struct {
   void* workspace; size_t workspace_bytes;
   int reduce_batch; /* 1: C = sum over the batch of op(A_b)·op(B_b) (one output,
                        output strides 0); K then runs over batch x K */
+  int variant;      /* kernel choice: 0 automatic, 1 one CTA per 128-row tile,
+                       2 a CTA pair per 256-row tile (tcgen05 cta_group::2) */
 } oxf_gemm_desc;
 
 /* Fills a descriptor with defaults (batch 1, alpha 1, tight leading dims

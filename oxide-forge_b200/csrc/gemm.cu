@@ -56,6 +56,7 @@ struct GemmArgs {
   const float* X; long long ldx, sx;
   int act, grad_act, accumulate, vec_ok;
   int reduce_batch;  // sum the batch into one output (K runs over batch x K)
+  int bm;            // rows per output tile: 128 (one CTA) or 256 (a CTA pair)
 };
 
 template <int BN, int STAGES, bool SPLIT3>
@@ -374,6 +375,213 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   }
 }
 
+// ---------------------------------------------------------------- CTA-pair kernel
+// The same pipeline on a cluster of two CTAs computing a 256 x BN tile with
+// tcgen05.mma.cta_group::2: each CTA loads its 128 rows of A and its BN/2
+// columns of B (so each SM moves 32 KB instead of 48 KB per K block at
+// BN = 256, leaving room for 6 stages), both halves complete on the leader
+// CTA's full barrier, the leader alone issues the MMAs and multicast-commits
+// to both CTAs' barriers, and each CTA's epilogue drains its own 128 TMEM
+// lanes and releases the accumulator to the leader with a remote arrive.
+template <int BN, int STAGES>
+struct GemmPairCfg {
+  static constexpr int A_BYTES = BM * BK * 4;
+  static constexpr int B_BYTES = (BN / 2) * BK * 4;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int CTRL_BYTES = 1024;
+  static constexpr int SMEM_BYTES = 1024 + CTRL_BYTES + STAGES * STAGE_BYTES;
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+  static_assert(TMEM_COLS <= 512 && BN % 64 == 0, "tile shape");
+};
+
+template <int ROWS>
+__device__ __forceinline__ void load_operand_pair(uint8_t* dst, const CUtensorMap* map,
+                                                  uint32_t bar, int mn_major, int is3d,
+                                                  int chunked, int row0, int k0, int b) {
+  if (!mn_major) {
+    if (is3d) tma_load_3d_pair(dst, map, bar, k0, row0, b);
+    else tma_load_2d_pair(dst, map, bar, k0, row0);
+  } else if (chunked) {
+    if (is3d) tma_load_4d_pair(dst, map, bar, 0, k0, row0 / 32, b);
+    else tma_load_3d_pair(dst, map, bar, 0, k0, row0 / 32);
+  } else {
+#pragma unroll
+    for (int c = 0; c < ROWS / 32; ++c) {
+      if (is3d) tma_load_3d_pair(dst + c * 4096, map, bar, row0 + 32 * c, k0, b);
+      else tma_load_2d_pair(dst + c * 4096, map, bar, row0 + 32 * c, k0);
+    }
+  }
+}
+
+template <int BN, int STAGES>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
+    gemm_tf32_tcgen05_pair(const __grid_constant__ CUtensorMap tmA,
+                           const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
+  using Cfg = GemmPairCfg<BN, STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  auto* ctrl = reinterpret_cast<GemmCtrl<STAGES>*>(base);
+  uint8_t* ring = base + Cfg::CTRL_BYTES;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&ctrl->full[s], 1);   // used in the leader: its producer's arrive + both halves' bytes
+      mbar_init(&ctrl->empty[s], 1);  // the leader's multicast commit
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ctrl->tfull[i], 1);               // the leader's multicast commit
+      mbar_init(&ctrl->tempty[i], 2 * EPI_WARPS);  // leader: one arrive per epilogue warp of the pair
+    }
+    ctrl->abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&ctrl->tmem_base, Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = ctrl->tmem_base;
+  const uint32_t full0 = map_to_rank(&ctrl->full[0], 0);
+  const uint32_t tempty0 = map_to_rank(&ctrl->tempty[0], 0);
+  const long long cluster_id = blockIdx.x >> 1;
+  const long long nclusters = gridDim.x >> 1;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      long long fills = 0;
+      for (long long u = cluster_id; u < args.units && !ctrl->abort_flag; u += nclusters) {
+        int b, tm, tn, kb0, kb1;
+        decode_unit(args, u, b, tm, tn, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&ctrl->empty[stage], phase ^ 1u, DEVERR_GEMM_WAIT_EMPTY)) {
+            ctrl->abort_flag = 1;
+            break;
+          }
+          if (ctrl->abort_flag) break;
+          if (leader) mbar_arrive_expect_tx(&ctrl->full[stage], 2 * Cfg::STAGE_BYTES);
+          uint8_t* slot = ring + stage * Cfg::STAGE_BYTES;
+          const uint32_t bar = full0 + 8u * stage;
+          const int bk = args.reduce_batch ? kb / args.kblocks_item : b;
+          const int k0 = (args.reduce_batch ? kb % args.kblocks_item : kb) * BK;
+          load_operand_pair<BM>(slot, &tmA, bar, args.a_mn, args.a3d, args.a_chunked,
+                                tm * 2 * BM + static_cast<int>(rank) * BM, k0, bk);
+          load_operand_pair<BN / 2>(slot + Cfg::A_BYTES, &tmB, bar, args.b_mn, args.b3d,
+                                    args.b_chunked, tn * BN + static_cast<int>(rank) * (BN / 2),
+                                    k0, bk);
+          ++fills;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // The leader's full barriers count both halves: once they complete,
+      // no copy is still landing in either CTA.
+      if (leader) {
+        const long long first = fills > STAGES ? fills - STAGES : 0;
+        for (long long j = first; j < fills; ++j)
+          mbar_wait(&ctrl->full[j % STAGES], static_cast<uint32_t>((j / STAGES) & 1),
+                    DEVERR_GEMM_DRAIN);
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      int local = 0;
+      for (long long u = cluster_id; u < args.units && !ctrl->abort_flag;
+           u += nclusters, ++local) {
+        int b, tm, tn, kb0, kb1;
+        decode_unit(args, u, b, tm, tn, kb0, kb1);
+        const int acc_slot = local & 1;
+        const uint32_t use = static_cast<uint32_t>(local >> 1);
+        if (!mbar_wait(&ctrl->tempty[acc_slot], (use & 1u) ^ 1u, DEVERR_GEMM_WAIT_TMEM_EMPTY)) {
+          ctrl->abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc_slot * BN);
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&ctrl->full[stage], phase, DEVERR_GEMM_WAIT_FULL)) {
+            ctrl->abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(ring + stage * Cfg::STAGE_BYTES);
+          const uint32_t b_base = a_base + Cfg::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / UMMA_K; ++kk)
+            umma_tf32_pair(d_tmem, operand_desc(a_base, args.a_mn, kk),
+                           operand_desc(b_base, args.b_mn, kk), args.idesc,
+                           (kb > kb0 || kk > 0) ? 1u : 0u);
+          umma_commit_pair(&ctrl->empty[stage], 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&ctrl->tfull[acc_slot], 0x3);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row_local = quarter * 32 + lane;
+    int local = 0;
+    for (long long u = cluster_id; u < args.units; u += nclusters, ++local) {
+      int b, tm, tn, kb0, kb1;
+      decode_unit(args, u, b, tm, tn, kb0, kb1);
+      const int acc_slot = local & 1;
+      const uint32_t use = static_cast<uint32_t>(local >> 1);
+      if (!mbar_wait(&ctrl->tfull[acc_slot], use & 1u, DEVERR_GEMM_WAIT_TMEM_FULL)) {
+        ctrl->abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int m = tm * 2 * BM + static_cast<int>(rank) * BM + row_local;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                             static_cast<uint32_t>(acc_slot * BN);
+#pragma unroll 1
+      for (int c = half; c < BN / 32; c += 2) {
+        const int n0 = tn * BN + c * 32;
+        if (n0 >= args.N) break;
+        float v[32];
+        tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), v);
+        if (m < args.M) epilogue_chunk(args, b, m, n0, v);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(tempty0 + 8u * static_cast<uint32_t>(acc_slot));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its partner may still signal it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
 // ---------------------------------------------------------------- 3xTF32 split
 // hi = TF32 (round to nearest, ties away) of x, lo = x - hi; both f32.
 __global__ void split_tf32_kernel(const float* __restrict__ src, long long ld, long long stride,
@@ -633,6 +841,25 @@ oxf_status launch_tcgen05(const CUtensorMap& ta, const CUtensorMap& tb, const CU
   return check_launch("gemm_tf32_tcgen05");
 }
 
+template <int BN, int STAGES>
+oxf_status launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& args,
+                       cudaStream_t stream, int dev) {
+  using Cfg = GemmPairCfg<BN, STAGES>;
+  static bool configured[kMaxDevices] = {false};
+  if (dev >= 0 && dev < kMaxDevices && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tf32_tcgen05_pair<BN, STAGES>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(gemm pair)");
+    configured[dev] = true;
+  }
+  args.idesc = make_idesc_tf32(2 * BM, BN, args.a_mn != 0, args.b_mn != 0);
+  const long long clusters = std::min<long long>(args.units, sm_count(dev) / 2);
+  gemm_tf32_tcgen05_pair<BN, STAGES><<<static_cast<unsigned>(2 * clusters), GEMM_THREADS,
+                                       Cfg::SMEM_BYTES, stream>>>(ta, tb, args);
+  return check_launch("gemm_tf32_tcgen05_pair");
+}
+
 // Chooses how many K splits an accumulating GEMM uses: minimises
 // waves * k-blocks-per-unit plus a per-split epilogue cost.
 int choose_splits(long long tiles, int kblocks, int sms) {
@@ -788,7 +1015,17 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
                            d->batch;
     if (t256 < sms && !d->accumulate) BN = 128;  // more, smaller tiles when the grid is thin
   }
-  a.tiles_m = (d->M + BM - 1) / BM;
+  // CTA pairs (256-row tiles) for plain TF32 GEMMs with enough 256 x 256
+  // tiles to occupy every SM pair; variant 1 forces one CTA, 2 forces pairs.
+  bool pair = false;
+  if (!split3) {
+    const long long tiles2 = static_cast<long long>((d->M + 2 * BM - 1) / (2 * BM)) *
+                             ((d->N + 255) / 256) * (d->reduce_batch ? 1 : d->batch);
+    pair = d->variant == 2 || (d->variant == 0 && d->M >= 2 * BM && tiles2 >= sms / 2);
+    if (pair) BN = 256;
+  }
+  a.bm = pair ? 2 * BM : BM;
+  a.tiles_m = (d->M + a.bm - 1) / a.bm;
   a.tiles_n = (d->N + BN - 1) / BN;
   a.kblocks_item = (d->K + BK - 1) / BK;
   a.kblocks = a.kblocks_item * (a.reduce_batch ? d->batch : 1);
@@ -811,8 +1048,9 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
   // (box_outer carries the tile rows); otherwise one 32x32 box per chunk.
   a.a_chunked = a.a_mn && (a_inner % 32 == 0) ? 1 : 0;
   a.b_chunked = a.b_mn && (b_inner % 32 == 0) ? 1 : 0;
+  const int b_rows = pair ? BN / 2 : BN;  // a CTA of a pair loads half of B
   const int a_box_outer = a.a_mn ? (a.a_chunked ? BM : 32) : BM;
-  const int b_box_outer = a.b_mn ? (a.b_chunked ? BN : 32) : BN;
+  const int b_box_outer = a.b_mn ? (a.b_chunked ? b_rows : 32) : b_rows;
   const bool amn = a.a_mn != 0, bmn = a.b_mn != 0;
   bool ok =
       encode_map(&ta, A, a_inner, a_outer, lda, d->batch, sa, 32, a_box_outer, amn, &a3d) &&
@@ -827,6 +1065,7 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
   a.b3d = b3d;
 
   if (split3) return launch_tcgen05<128, 3, true>(ta, tb, ta_lo, tb_lo, a, stream, dev);
+  if (pair) return launch_pair<256, 6>(ta, tb, a, stream, dev);
   if (BN == 256) return launch_tcgen05<256, 4, false>(ta, tb, ta, tb, a, stream, dev);
   if (BN == 128) return launch_tcgen05<128, 6, false>(ta, tb, ta, tb, a, stream, dev);
   return launch_tcgen05<64, 8, false>(ta, tb, ta, tb, a, stream, dev);

@@ -54,7 +54,7 @@ class GemmDesc(C.Structure):
         ("act", C.c_int), ("grad_act", C.c_int), ("accumulate", C.c_int),
         ("split_k", C.c_int), ("precision", C.c_int),
         ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
-        ("reduce_batch", C.c_int),
+        ("reduce_batch", C.c_int), ("variant", C.c_int),
     ]
 
 

@@ -191,7 +191,7 @@ def matrix_multiply_refalgo(a, b, out, stream=None):
 def gemm(a, b, out, *, a_trans=False, b_trans=False, alpha=1.0, beta=0.0, bias=None,
          residual=None, pre_out=None, aux=None, act=_lib.ACT_IDENTITY, grad_act=_lib.ACT_IDENTITY,
          accumulate=False, split_k=0, precision=_lib.PREC_TF32, workspace=None, reduce_batch=False,
-         stream=None):
+         variant=0, stream=None):
     """out = epilogue(alpha * op(a)·op(b)); 2-D or batched 3-D operands.
 
     a: [M,K] (or [K,M] with a_trans), b: [K,N] (or [N,K] with b_trans); a
@@ -225,6 +225,7 @@ def gemm(a, b, out, *, a_trans=False, b_trans=False, alpha=1.0, beta=0.0, bias=N
     d.act, d.grad_act = int(act), int(grad_act)
     d.accumulate, d.split_k, d.precision = int(accumulate), int(split_k), int(precision)
     d.reduce_batch = int(reduce_batch)
+    d.variant = int(variant)
     if reduce_batch:
         d.stride_c = 0
     if precision == _lib.PREC_TF32X3:

@@ -217,3 +217,49 @@ def test_batch_reduce(K, rng):
     K.gemm(dev(A), dev(B), out, b_trans=True, residual=dev(R), reduce_batch=True)
     want = R + sum(exact(A[b], B[b], 0, 1) for b in range(batch))
     assert rel_err(host(out), want) < TF32_TOL
+
+
+@pytest.mark.parametrize("variant", [1, 2])
+@pytest.mark.parametrize("at,bt", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("M,N,Kd", [(256, 256, 64), (300, 520, 72), (1024, 768, 256)])
+def test_cta_pair_and_single_variants(K, rng, M, N, Kd, at, bt, variant):
+    """variant 1: one CTA per 128-row tile; variant 2: a CTA pair per
+    256-row tile (tcgen05.mma.cta_group::2, half of B in each CTA)."""
+    A, B = operands(rng, M, N, Kd, at, bt)
+    out = torch.empty((M, N), device="cuda")
+    K.gemm(dev(A), dev(B), out, a_trans=bool(at), b_trans=bool(bt), variant=variant)
+    assert rel_err(host(out), exact(A, B, at, bt)) < TF32_TOL
+
+
+def test_cta_pair_features(K, rng):
+    """Batched operands, fused epilogue, split-K accumulation and
+    batch-reduce on the CTA-pair kernel."""
+    batch, M, N, Kd = 3, 256, 384, 128
+    A, B = operands(rng, M, N, Kd, 0, 0, batch=batch)
+    out = torch.empty((batch, M, N), device="cuda")
+    K.gemm(dev(A), dev(B), out, variant=2)
+    got = host(out)
+    for b in range(batch):
+        assert rel_err(got[b], exact(A[b], B[b], 0, 0)) < TF32_TOL
+    X, W = operands(rng, 512, 256, 256, 0, 0)
+    bias = (0.1 * rng.standard_normal(256)).astype(np.float32)
+    R = rng.standard_normal((512, 256)).astype(np.float32)
+    y = torch.empty((512, 256), device="cuda")
+    pre = torch.empty((512, 256), device="cuda")
+    K.gemm(dev(X), dev(W), y, bias=dev(bias), residual=dev(R), pre_out=pre, act=1, variant=2)
+    z = exact(X, W, 0, 0) + bias + R
+    assert rel_err(host(pre), z) < TF32_TOL
+    assert rel_err(host(y), O.act_forward(O.GELU, z.astype(np.float32))) < TF32_TOL
+    Xt = rng.standard_normal((2048, 256)).astype(np.float32)
+    G = rng.standard_normal((2048, 512)).astype(np.float32)
+    G0 = rng.standard_normal((256, 512)).astype(np.float32)
+    acc = dev(G0)
+    K.gemm(dev(Xt), dev(G), acc, a_trans=True, accumulate=True, split_k=4, variant=2)
+    assert rel_err(host(acc), G0 + exact(Xt, G, 1, 0)) < TF32_TOL
+    Ab = rng.uniform(-1, 1, (3, 256, 128)).astype(np.float32)
+    Bb = rng.uniform(-1, 1, (3, 256, 128)).astype(np.float32)
+    Rb = rng.standard_normal((256, 256)).astype(np.float32)
+    red = torch.empty((256, 256), device="cuda")
+    K.gemm(dev(Ab), dev(Bb), red, b_trans=True, residual=dev(Rb), reduce_batch=True, variant=2)
+    want = Rb + sum(exact(Ab[b], Bb[b], 0, 1) for b in range(3))
+    assert rel_err(host(red), want) < TF32_TOL
