@@ -35,6 +35,7 @@ enum DeviceErrorCode : uint32_t {
   DEVERR_GEMM_WAIT_TMEM_EMPTY = 0x103,
   DEVERR_GEMM_WAIT_TMEM_FULL = 0x104,
   DEVERR_GEMM_DRAIN = 0x105,
+  DEVERR_GEMM_EPI_LOAD = 0x106,
 };
 
 }  // namespace oxf
