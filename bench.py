@@ -318,15 +318,121 @@ def run_rows(a, torch):
                       "results": res}), flush=True)
 
 
+def run_mlp(a, torch):
+    """Config 3: MLP 1024 -> 4096 (GELU) -> 1024 with biases and a residual
+    from the MLP input to its output, X [8192,1024] N(0,1), Kaiming-uniform
+    weights, biases 0.01*N(0,1), MSE loss against N(0,1) targets. A step is
+    forward, loss + gradient, backward (dX of layer 0 included, as
+    mlp.rs:142-143 always computes it) and SGD; 412.3 GFLOP of products."""
+    import numpy as np
+    from oxf import _lib, models
+    from oxf import kernels as K
+    rows, d, h = 8192, 1024, 4096
+    cfg = models.MlpConfig([models.Layer(d, h, _lib.ACT_GELU, True),
+                            models.Layer(h, d, _lib.ACT_IDENTITY, True)], (0, 2))
+    rng = np.random.default_rng(3000)
+    w1 = rng.uniform(-np.sqrt(6 / d), np.sqrt(6 / d), (d, h)).astype(np.float32)
+    w2 = rng.uniform(-np.sqrt(6 / h), np.sqrt(6 / h), (h, d)).astype(np.float32)
+    b1 = (0.01 * rng.standard_normal(h)).astype(np.float32)
+    b2 = (0.01 * rng.standard_normal(d)).astype(np.float32)
+    stream = torch.cuda.current_stream()
+    eng = models.Mlp(cfg, rows, stream=stream)
+    eng.params.copy_(torch.from_numpy(np.concatenate([w1.ravel(), b1, w2.ravel(), b2])))
+    g = torch.Generator(device="cuda").manual_seed(3001)
+    x = torch.randn(rows, d, device="cuda", generator=g)
+    t = torch.randn(rows, d, device="cuda", generator=g)
+    y, dy, dx = torch.empty_like(x), torch.empty_like(x), torch.empty_like(x)
+    row_loss = torch.empty(rows, device="cuda")
+    lr = 1e-3
+
+    def step():
+        eng.zero_grads()
+        eng.forward(x, y)
+        K.mse_loss_grad(y, t, row_loss, dy)
+        eng.backward(dy, dx)
+        eng.sgd(lr / rows)
+
+    ms = _time(torch, step, a.steps, a.warmup)
+    flops = 3 * 2 * (2.0 * rows * d * h)
+    peak = cublas_tf32_peak(torch)
+    print(json.dumps({"metric": "MLP fwd+bwd+SGD rows/s", "value": rows / ms * 1e3,
+                      "unit": "rows/s", "workload": "mlp", "ms_per_step": ms,
+                      "tflops": flops / ms / 1e9, "peak_cublas_tf32_8192": peak,
+                      "frac_of_peak": flops / ms / 1e9 / peak,
+                      "config": {"workload": "C3 MLP 1024->4096(GELU)->1024, biases, "
+                                             "residual range (0,2), MSE",
+                                 "rows": rows, "flops_per_step": flops}}), flush=True)
+    eng.close()
+
+
+def run_infer(a, torch):
+    """Config 4: single-head Post-Norm transformer inference, NormType::Rms,
+    per sequence [2048,1024], FFN 1024->4096->1024 GELU, Xavier-uniform
+    projections, position table N(0,0.02); 64 independent sequences
+    batch-sharded over the ranks (no collective; each rank runs its share).
+    value = tokens of all 64 sequences / max-over-ranks device time."""
+    import torch.distributed as dist
+    from oxf import _lib, models
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    seq, hidden, ffn, nseq = 2048, 1024, 4096, 64
+    if nseq % world:
+        raise SystemExit(f"64 sequences do not divide over {world} ranks")
+    local = nseq // world
+    cfg = models.transformer_config(seq, hidden, ffn, norm=_lib.NORM_RMS)
+    stream = torch.cuda.current_stream()
+    model = models.Transformer(cfg, max_batch=local, stream=stream)
+    model.set_params(models.init_transformer_params(cfg, seed=4000))
+    g = torch.Generator(device="cuda").manual_seed(4001 + rank)
+    x = torch.randn(local * seq, hidden, device="cuda", generator=g)
+    for _ in range(a.warmup):
+        model.forward(x)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = _events(torch)
+    e0.record(stream)
+    for _ in range(a.steps):
+        model.forward(x)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.steps
+    if world > 1:
+        tt = torch.tensor([ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = tt.item()
+    fpt = 2 * (3 * hidden * hidden + 2 * seq * hidden + 2 * hidden * ffn + hidden * hidden)
+    tokens = nseq * seq
+    if rank == 0:
+        print(json.dumps({"metric": "Transformer inference tokens/s",
+                          "value": tokens / ms * 1e3, "unit": "tokens/s", "workload": "infer",
+                          "n_gpus": world, "ms_per_batch": ms, "scaling": "strong",
+                          "model_tflops": tokens / ms * 1e3 * fpt / 1e12,
+                          "config": {"workload": "C4 single-head Post-Norm transformer "
+                                                 "inference, NormType::Rms",
+                                     "seq_len": seq, "hidden": hidden, "ffn": ffn,
+                                     "sequences": nseq, "parallelism": f"batch-shard {world}"}}),
+              flush=True)
+    model.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     a = parse()
     if a.impl == "reference":
         run_reference(a)
         return
-    if a.workload in ("gemm", "rows"):
+    if a.workload != "train":
         import torch
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
-        (run_gemm if a.workload == "gemm" else run_rows)(a, torch)
+        {"gemm": run_gemm, "rows": run_rows, "mlp": run_mlp, "infer": run_infer}[a.workload](
+            a, torch)
         return
     import numpy as np
     import torch
@@ -398,26 +504,12 @@ def main():
     if not a.no_e2e:
         xh = torch.randn(rows, a.hidden, generator=torch.Generator().manual_seed(7 + rank)).pin_memory()
         th = torch.randn(rows, a.hidden, generator=torch.Generator().manual_seed(9 + rank)).pin_memory()
-        xd = torch.empty_like(x)
-        td = torch.empty_like(t)
-        lh = torch.empty(1).pin_memory()
-
-        def e2e_step():
-            xd.copy_(xh, non_blocking=True)
-            td.copy_(th, non_blocking=True)
-            l = trainer.step(xd, td)
-            lh.copy_(l, non_blocking=True)
-            torch.cuda.current_stream().synchronize()
-            return float(lh.item())
-
-        for _ in range(max(1, a.warmup)):
-            e2e_step()
+        trainer.run_host([(xh, th)] * max(1, a.warmup), stream=stream)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
         w0 = time.perf_counter()
-        for _ in range(a.steps):
-            e2e_step()
+        trainer.run_host([(xh, th)] * a.steps, stream=stream)
         e2e_s = time.perf_counter() - w0
         if world > 1:
             tt = torch.tensor([e2e_s], device="cuda")
@@ -426,8 +518,10 @@ def main():
         e2e = {"value": tokens / e2e_s, "unit": UNIT,
                "h2d_bytes_per_step": int(xh.numel() * 4 + th.numel() * 4),
                "d2h_bytes_per_step": 4,
-               "api": "oxf.dp.DataParallelTrainer.step (liboxf.so engine) with pinned host "
-                      "inputs/targets copied every step; wall clock, max over ranks"}
+               "api": "oxf.dp.DataParallelTrainer.run_host (liboxf.so engine): every step "
+                      "copies its pinned host inputs/targets to the device (on a side stream, "
+                      "overlapping the previous step) and reads its loss back; wall clock, "
+                      "max over ranks"}
 
     # ---------------- CPU baseline (rank 0, N = 1)
     cpu = None

@@ -90,3 +90,61 @@ class DataParallelTrainer:
                     w.wait()
         m.sgd(self.lr / self.global_batch)
         return loss / (self.global_batch * self.seq)
+
+    def run_host(self, batches, stream: torch.cuda.Stream | None = None) -> list[float]:
+        """Steps over host-resident batches, one step per (x, target) pair
+        of pinned CPU tensors ([local_batch*seq, width] each). The inputs of
+        step i+1 are copied host->device on a side stream while step i
+        computes (two device buffer pairs), and each step's mean loss is
+        copied back and read when the following step has been queued.
+        Returns the losses in step order."""
+        compute = stream or torch.cuda.current_stream()
+        copy = torch.cuda.Stream(device=compute.device)
+        bufs, ready, free = [], [], []
+        losses, pending = [], []
+        lh = [torch.empty(1, pin_memory=True) for _ in range(2)]
+        lev = [torch.cuda.Event() for _ in range(2)]
+
+        def stage(i, xh, th):
+            k = i % 2
+            if len(bufs) <= k:
+                bufs.append((torch.empty(xh.shape, device=compute.device),
+                             torch.empty(th.shape, device=compute.device)))
+                ready.append(torch.cuda.Event())
+                free.append(None)
+            with torch.cuda.stream(copy):
+                if free[k] is not None:
+                    copy.wait_event(free[k])  # step i-2 is done with this pair
+                bufs[k][0].copy_(xh, non_blocking=True)
+                bufs[k][1].copy_(th, non_blocking=True)
+                ready[k].record(copy)
+
+        it = iter(batches)
+        nxt = next(it, None)
+        if nxt is None:
+            return losses
+        stage(0, *nxt)
+        i = 0
+        while nxt is not None:
+            k = i % 2
+            compute.wait_event(ready[k])
+            with torch.cuda.stream(compute):
+                loss = self.step(*bufs[k])
+                ev = torch.cuda.Event()
+                ev.record(compute)
+                free[k] = ev
+                lh[k].copy_(loss, non_blocking=True)
+                lev[k].record(compute)
+            nxt = next(it, None)
+            if nxt is not None:
+                stage(i + 1, *nxt)
+            if pending:
+                j, kk = pending.pop()
+                lev[kk].synchronize()
+                losses.append(float(lh[kk].item()))
+            pending.append((i, k))
+            i += 1
+        for j, kk in pending:
+            lev[kk].synchronize()
+            losses.append(float(lh[kk].item()))
+        return losses
