@@ -62,6 +62,10 @@ def parse():
                          "shape), rows (config 2 row suite), mlp (config 3), infer (config 4)")
     ap.add_argument("--shape", default=None, help="gemm: M,N,K (default: the 512..8192 sweep)")
     ap.add_argument("--mode", default="nn", help="gemm: nn, nt, tn or tt")
+    ap.add_argument("--epi", default="none",
+                    choices=["none", "bias_gelu_pre", "gelu_grad_aux", "bias_residual"],
+                    help="gemm: fused epilogue (FFN1 forward, FFN1 input gradient, FFN2 "
+                         "forward); the cuBLAS comparison stays a plain product")
     return ap.parse_args()
 
 
@@ -244,6 +248,7 @@ def run_gemm(a, torch):
     """Config 3's square sweep (or one shape): TF32 GEMM TFLOP/s against
     cuBLAS TF32 on the same GPU; inputs U(-1,1), 3 x 256 MiB operands at
     8192 (larger than L2)."""
+    from oxf import _lib
     from oxf import kernels as K
     peak = cublas_tf32_peak(torch)
     shapes = [tuple(int(v) for v in a.shape.split(","))] if a.shape else \
@@ -254,12 +259,22 @@ def run_gemm(a, torch):
         A = torch.empty((Kd, M) if at else (M, Kd), device="cuda").uniform_(-1, 1)
         B = torch.empty((N, Kd) if bt else (Kd, N), device="cuda").uniform_(-1, 1)
         Cm = torch.empty((M, N), device="cuda")
-        ms = _time(torch, lambda: K.gemm(A, B, Cm, a_trans=at, b_trans=bt), a.steps, a.warmup)
+        kw = {}
+        if a.epi == "bias_gelu_pre":
+            kw = dict(bias=torch.randn(N, device="cuda"), act=_lib.ACT_GELU,
+                      pre_out=torch.empty((M, N), device="cuda"))
+        elif a.epi == "gelu_grad_aux":
+            kw = dict(aux=torch.randn(M, N, device="cuda"), grad_act=_lib.ACT_GELU)
+        elif a.epi == "bias_residual":
+            kw = dict(bias=torch.randn(N, device="cuda"), residual=torch.randn(M, N, device="cuda"))
+        ms = _time(torch, lambda: K.gemm(A, B, Cm, a_trans=at, b_trans=bt, **kw), a.steps,
+                   a.warmup)
         torch.backends.cuda.matmul.allow_tf32 = True
         ref = _time(torch, lambda: torch.matmul(A.T if at else A, B.T if bt else B, out=Cm),
                     a.steps, a.warmup)
         fl = 2.0 * M * N * Kd
-        res.append({"shape": [M, N, Kd], "mode": a.mode, "ms": ms, "tflops": fl / ms / 1e9,
+        res.append({"shape": [M, N, Kd], "mode": a.mode, "epilogue": a.epi, "ms": ms,
+                    "tflops": fl / ms / 1e9,
                     "cublas_tflops": fl / ref / 1e9, "frac_of_peak": fl / ms / 1e9 / peak})
         del A, B, Cm
     print(json.dumps({"metric": "GEMM TF32 TFLOP/s", "unit": "TFLOP/s", "workload": "gemm",

@@ -54,12 +54,19 @@ __device__ __forceinline__ float act_derivative(int act, float x) {
 
 // Activation forms for GEMM epilogues, where each element costs issue slots
 // of the few epilogue warps: tanh(u) = 1 - 2 / (exp(2u) + 1) from the
-// hardware exp2-based __expf and an IEEE reciprocal (saturates to +-1 for
-// large |u| without NaNs). Absolute error in tanh is ~1e-7, far inside the
-// TF32 error of the product feeding it.
+// hardware exp2-based __expf and the hardware reciprocal (rcp.approx, within
+// 1 ulp). It saturates to +-1 for large |u| (1/inf = 0) without NaNs.
+// Absolute error in tanh is ~2e-7, far inside the TF32 error of the
+// product feeding it.
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 __device__ __forceinline__ float tanh_fast(float u) {
   const float e = __expf(2.0f * u);
-  return 1.0f - 2.0f * __frcp_rn(e + 1.0f);
+  return 1.0f - 2.0f * rcp_approx(e + 1.0f);
 }
 
 __device__ __forceinline__ float act_forward_fast(int act, float x) {
@@ -69,7 +76,7 @@ __device__ __forceinline__ float act_forward_fast(int act, float x) {
       return 0.5f * x * (1.0f + tanh_fast(inner));
     }
     case OXF_ACT_RELU: return x > 0.0f ? x : 0.0f;
-    case OXF_ACT_SILU: return x * __frcp_rn(1.0f + __expf(-x));
+    case OXF_ACT_SILU: return x * rcp_approx(1.0f + __expf(-x));
     default: return x;
   }
 }
@@ -85,10 +92,45 @@ __device__ __forceinline__ float act_derivative_fast(int act, float x) {
     }
     case OXF_ACT_RELU: return x > 0.0f ? 1.0f : 0.0f;
     case OXF_ACT_SILU: {
-      const float sg = __frcp_rn(1.0f + __expf(-x));
+      const float sg = rcp_approx(1.0f + __expf(-x));
       return sg + x * sg * (1.0f - sg);
     }
     default: return 1.0f;
+  }
+}
+
+// Whole-chunk forms: the activation is a template constant inside the
+// element loop, so the per-element switch folds away.
+template <int ACT, int N>
+__device__ __forceinline__ void act_forward_chunk(float (&v)[N]) {
+#pragma unroll
+  for (int j = 0; j < N; ++j) v[j] = act_forward_fast(ACT, v[j]);
+}
+
+template <int N>
+__device__ __forceinline__ void act_forward_chunk(int act, float (&v)[N]) {
+  switch (act) {
+    case OXF_ACT_GELU: act_forward_chunk<OXF_ACT_GELU>(v); break;
+    case OXF_ACT_RELU: act_forward_chunk<OXF_ACT_RELU>(v); break;
+    case OXF_ACT_SILU: act_forward_chunk<OXF_ACT_SILU>(v); break;
+    default: break;
+  }
+}
+
+// v[j] *= act'(x[j])
+template <int ACT, int N>
+__device__ __forceinline__ void act_grad_chunk(float (&v)[N], const float (&x)[N]) {
+#pragma unroll
+  for (int j = 0; j < N; ++j) v[j] *= act_derivative_fast(ACT, x[j]);
+}
+
+template <int N>
+__device__ __forceinline__ void act_grad_chunk(int act, float (&v)[N], const float (&x)[N]) {
+  switch (act) {
+    case OXF_ACT_GELU: act_grad_chunk<OXF_ACT_GELU>(v, x); break;
+    case OXF_ACT_RELU: act_grad_chunk<OXF_ACT_RELU>(v, x); break;
+    case OXF_ACT_SILU: act_grad_chunk<OXF_ACT_SILU>(v, x); break;
+    default: break;
   }
 }
 

@@ -284,8 +284,10 @@ __device__ __forceinline__ bool epilogue_chunk_tma(const GemmArgs& a, const EpiM
   uint8_t* buf1 = bufs + (NBUF - 1) * EPI_TILE_BYTES;  // buf0 again when NBUF == 1
   epi_buffers_free(lane);  // the previous chunk's stores are done with both buffers
   bool busy0 = false;      // buf0 holds a store still in flight
+  if (a.alpha != 1.0f) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] *= a.alpha;
+    for (int j = 0; j < 32; ++j) v[j] *= a.alpha;
+  }
   float t[32];
   if (a.beta != 0.0f) {
     if (!epi_load(buf0, &em.c, a.c3d, bar, phase, n0, m0, b, lane)) return false;
@@ -331,13 +333,9 @@ __device__ __forceinline__ bool epilogue_chunk_tma(const GemmArgs& a, const EpiM
   if (a.X) {
     if (!epi_load(out, &em.x, a.x3d, bar, phase, n0, m0, b, lane)) return false;
     stage_read_row(out, lane, t);
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] *= act_derivative_fast(a.grad_act, t[j]);
+    act_grad_chunk(a.grad_act, v, t);
   }
-  if (a.act != OXF_ACT_IDENTITY) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = act_forward_fast(a.act, v[j]);
-  }
+  act_forward_chunk(a.act, v);
   stage_write_row(out, lane, v);
   epi_store(out, &em.c, a.c3d, n0, m0, b, lane, a.accumulate != 0);
   return true;
