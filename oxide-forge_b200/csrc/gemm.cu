@@ -229,12 +229,11 @@ __device__ __forceinline__ void stage_read_row(uint8_t* buf, int lane, float (&t
   }
 }
 
-// Loads the 32 x 32 tile at (column n0, row m0[, batch b]) into buf and
-// waits for it (bounded). Prior generic accesses of buf by the warp are
-// ordered before the asynchronous write.
-__device__ __forceinline__ bool epi_load(uint8_t* buf, const CUtensorMap* map, int is3d,
-                                         uint64_t* bar, uint32_t& phase, int n0, int m0, int b,
-                                         int lane) {
+// Starts loading the 32 x 32 tile at (column n0, row m0[, batch b]) into
+// buf. Prior generic accesses of buf by the warp are ordered before the
+// asynchronous write.
+__device__ __forceinline__ void epi_issue(uint8_t* buf, const CUtensorMap* map, int is3d,
+                                          uint64_t* bar, int n0, int m0, int b, int lane) {
   fence_proxy_async_smem();
   __syncwarp();
   if (lane == 0) {
@@ -243,6 +242,10 @@ __device__ __forceinline__ bool epi_load(uint8_t* buf, const CUtensorMap* map, i
     if (is3d) tma_load_3d(buf, map, bar, n0, m0, b, pol);
     else tma_load_2d(buf, map, bar, n0, m0, pol);
   }
+}
+
+// Waits (bounded) for the load issued last on bar.
+__device__ __forceinline__ bool epi_wait(uint64_t* bar, uint32_t& phase) {
   const bool ok = mbar_wait(bar, phase, DEVERR_GEMM_EPI_LOAD);
   phase ^= 1u;
   return ok;
@@ -272,25 +275,55 @@ __device__ __forceinline__ void epi_buffers_free(int lane) {
   __syncwarp();
 }
 
+// The epilogue input read first into buffer 0, before any store of the
+// chunk: C (when beta != 0), else the residual, else aux when there is no
+// pre-activation output. That one can be loaded ahead, while the warp is
+// still busy with its previous chunk.
+__device__ __forceinline__ const CUtensorMap* epi_first_input(const GemmArgs& a,
+                                                              const EpiMaps& em, int& is3d) {
+  if (a.beta != 0.0f) { is3d = a.c3d; return &em.c; }
+  if (a.R) { is3d = a.r3d; return &em.r; }
+  if (a.X && !a.P) { is3d = a.x3d; return &em.x; }
+  return nullptr;
+}
+
+// Issues the first input of a later chunk into buffer 0 once the stores in
+// flight have read it. Returns whether a load was issued.
+__device__ __forceinline__ bool epi_prefetch(const GemmArgs& a, const EpiMaps& em, uint8_t* bufs,
+                                             uint64_t* bar, int b, int m0, int n0, int lane) {
+  int is3d = 0;
+  const CUtensorMap* map = epi_first_input(a, em, is3d);
+  if (!map || m0 >= a.M || n0 >= a.N) return false;
+  epi_buffers_free(lane);
+  epi_issue(bufs, map, is3d, bar, n0, m0, b, lane);
+  return true;
+}
+
 // The fused epilogue of one warp's 32 x 32 chunk (rows m0.., columns n0..),
-// in the same arithmetic order as epilogue_chunk. Returns false if a staged
-// load timed out.
+// in the same arithmetic order as epilogue_chunk. `prefetched`: the first
+// input (epi_first_input) is already on its way into buffer 0. Returns false
+// if a staged load timed out.
 template <int NBUF>
 __device__ __forceinline__ bool epilogue_chunk_tma(const GemmArgs& a, const EpiMaps& em, int b,
                                                    int m0, int n0, float (&v)[32], uint8_t* bufs,
-                                                   uint64_t* bar, uint32_t& phase, int lane) {
+                                                   uint64_t* bar, uint32_t& phase, int lane,
+                                                   bool prefetched) {
   if (m0 >= a.M) return true;  // rows past the matrix (last tile): nothing to move
   uint8_t* buf0 = bufs;
   uint8_t* buf1 = bufs + (NBUF - 1) * EPI_TILE_BYTES;  // buf0 again when NBUF == 1
-  epi_buffers_free(lane);  // the previous chunk's stores are done with both buffers
-  bool busy0 = false;      // buf0 holds a store still in flight
+  // The previous chunk's stores must be done with the buffers (a prefetch
+  // already waited for that before it was issued).
+  if (!prefetched) epi_buffers_free(lane);
+  bool busy0 = false;  // buf0 holds a store still in flight
   if (a.alpha != 1.0f) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] *= a.alpha;
   }
   float t[32];
   if (a.beta != 0.0f) {
-    if (!epi_load(buf0, &em.c, a.c3d, bar, phase, n0, m0, b, lane)) return false;
+    if (!prefetched) epi_issue(buf0, &em.c, a.c3d, bar, n0, m0, b, lane);
+    prefetched = false;
+    if (!epi_wait(bar, phase)) return false;
     stage_read_row(buf0, lane, t);
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] += a.beta * t[j];
@@ -311,7 +344,9 @@ __device__ __forceinline__ bool epilogue_chunk_tma(const GemmArgs& a, const EpiM
     for (int j = 0; j < 32; ++j) v[j] += t[j];
   }
   if (a.R) {
-    if (!epi_load(buf0, &em.r, a.r3d, bar, phase, n0, m0, b, lane)) return false;
+    if (!prefetched) epi_issue(buf0, &em.r, a.r3d, bar, n0, m0, b, lane);
+    prefetched = false;
+    if (!epi_wait(bar, phase)) return false;
     stage_read_row(buf0, lane, t);
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] += t[j];
@@ -331,7 +366,8 @@ __device__ __forceinline__ bool epilogue_chunk_tma(const GemmArgs& a, const EpiM
     }
   }
   if (a.X) {
-    if (!epi_load(out, &em.x, a.x3d, bar, phase, n0, m0, b, lane)) return false;
+    if (!prefetched) epi_issue(out, &em.x, a.x3d, bar, n0, m0, b, lane);
+    if (!epi_wait(bar, phase)) return false;
     stage_read_row(out, lane, t);
     act_grad_chunk(a.grad_act, v, t);
   }
@@ -339,6 +375,28 @@ __device__ __forceinline__ bool epilogue_chunk_tma(const GemmArgs& a, const EpiM
   stage_write_row(out, lane, v);
   epi_store(out, &em.c, a.c3d, n0, m0, b, lane, a.accumulate != 0);
   return true;
+}
+
+// The chunk an epilogue warp takes after chunk c of unit u: the next
+// alternate column chunk of the same tile, else its first chunk of the next
+// unit its CTA (pair) owns. Rows of a unit start at tm * a.bm + row_off.
+template <int BN>
+__device__ __forceinline__ bool epi_next_chunk(const GemmArgs& a, long long u, long long stride,
+                                               int c, int half, int row_off, int b, int tn,
+                                               int m0, int& nb, int& nm0, int& nn0) {
+  if (c + 2 < BN / 32 && tn * BN + (c + 2) * 32 < a.N) {
+    nb = b;
+    nm0 = m0;
+    nn0 = tn * BN + (c + 2) * 32;
+    return true;
+  }
+  const long long u2 = u + stride;
+  if (u2 >= a.units) return false;
+  int tm2, tn2, kb0, kb1;
+  decode_unit(a, u2, nb, tm2, tn2, kb0, kb1);
+  nm0 = tm2 * a.bm + row_off;
+  nn0 = tn2 * BN + half * 32;
+  return nn0 < a.N;
 }
 
 template <int BN, int STAGES, bool SPLIT3, int NBUF>
@@ -497,7 +555,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     uint8_t* bufs = ring + STAGES * Cfg::STAGE_BYTES + (warp - 2) * NBUF * EPI_TILE_BYTES;
     uint64_t* ebar = &ctrl->epi[warp - 2];
     uint32_t ephase = 0;
-    bool ok = true;
+    bool ok = true, pf = false;  // pf: the next chunk's first input is being loaded
     int local = 0;
     for (long long u = blockIdx.x; u < args.units && ok; u += gridDim.x, ++local) {
       int b, tm, tn, kb0, kb1;
@@ -519,12 +577,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         float v[32];
         tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), v);
         if (args.epi_tma) {
-          if (!epilogue_chunk_tma<NBUF>(args, em, b, tm * BM + quarter * 32, n0, v, bufs, ebar,
-                                        ephase, lane)) {
+          const int m0 = tm * BM + quarter * 32;
+          if (!epilogue_chunk_tma<NBUF>(args, em, b, m0, n0, v, bufs, ebar, ephase, lane,
+                                        pf)) {
             ctrl->abort_flag = 1;
-            ok = false;
+            ok = pf = false;
             break;
           }
+          int nb, nm0, nn0;
+          pf = epi_next_chunk<BN>(args, u, gridDim.x, c, half, quarter * 32, b, tn, m0, nb, nm0,
+                                  nn0) &&
+               epi_prefetch(args, em, bufs, ebar, nb, nm0, nn0, lane);
         } else if (m < args.M) {
           epilogue_chunk(args, b, m, n0, v);
         }
@@ -532,6 +595,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tc_fence_before();
       mbar_arrive(&ctrl->tempty[acc_slot]);
     }
+    if (pf) epi_wait(ebar, ephase);  // an abandoned prefetch must land before exit
     if (lane == 0) bulk_wait_group0();  // no store may outlive the CTA's shared memory
     __syncwarp();
   }
@@ -723,7 +787,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     uint8_t* bufs = ring + STAGES * Cfg::STAGE_BYTES + (warp - 2) * NBUF * EPI_TILE_BYTES;
     uint64_t* ebar = &ctrl->epi[warp - 2];
     uint32_t ephase = 0;
-    bool ok = true;
+    bool ok = true, pf = false;  // pf: the next chunk's first input is being loaded
     int local = 0;
     for (long long u = cluster_id; u < args.units && ok; u += nclusters, ++local) {
       int b, tm, tn, kb0, kb1;
@@ -746,12 +810,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
         float v[32];
         tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), v);
         if (args.epi_tma) {
-          if (!epilogue_chunk_tma<NBUF>(args, em, b, m_base + quarter * 32, n0, v, bufs, ebar,
-                                        ephase, lane)) {
+          const int m0 = m_base + quarter * 32;
+          if (!epilogue_chunk_tma<NBUF>(args, em, b, m0, n0, v, bufs, ebar, ephase, lane, pf)) {
             ctrl->abort_flag = 1;
-            ok = false;
+            ok = pf = false;
             break;
           }
+          int nb, nm0, nn0;
+          pf = epi_next_chunk<BN>(args, u, nclusters, c, half,
+                                  static_cast<int>(rank) * BM + quarter * 32, b, tn, m0, nb, nm0,
+                                  nn0) &&
+               epi_prefetch(args, em, bufs, ebar, nb, nm0, nn0, lane);
         } else if (m < args.M) {
           epilogue_chunk(args, b, m, n0, v);
         }
@@ -760,6 +829,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(tempty0 + 8u * static_cast<uint32_t>(acc_slot));
     }
+    if (pf) epi_wait(ebar, ephase);  // an abandoned prefetch must land before exit
     if (lane == 0) bulk_wait_group0();  // no store may outlive the CTA's shared memory
     __syncwarp();
   }
@@ -1130,6 +1200,9 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
     return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: aux given without grad_act");
   if (d->accumulate && (d->pre_out || d->act != OXF_ACT_IDENTITY) && split > 1)
     return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: split_k cannot fuse activation");
+  if (d->accumulate && (d->bias || d->residual) && split > 1)
+    return set_error(OXF_ERR_INVALID_ARG,
+                     "oxf_gemm: split_k would add bias / residual once per split");
 
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1252,7 +1325,11 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
   const long long tiles =
       static_cast<long long>(a.tiles_m) * a.tiles_n * (a.reduce_batch ? 1 : d->batch);
   if (d->accumulate) {
-    a.splits = split > 1 ? std::min(split, a.kblocks) : choose_splits(tiles, a.kblocks, sms);
+    // Each K split adds its partial product into C, so terms added once per
+    // output (bias, residual) rule splitting out.
+    const bool additive = d->bias != nullptr || d->residual != nullptr;
+    a.splits = split > 1 ? std::min(split, a.kblocks)
+                         : (additive ? 1 : choose_splits(tiles, a.kblocks, sms));
   } else {
     a.splits = 1;
   }
