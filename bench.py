@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--ffn", type=int, default=FFN)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-peak", action="store_true",
+                    help="skip the cuBLAS denominator (profiling runs: keeps the launch list "
+                         "to the step's own kernels); roofline.peak is then null")
     ap.add_argument("--workload", default="train",
                     choices=["train", "gemm", "rows", "mlp", "infer"],
                     help="train: the contract line (config 5). The others are supplementary "
@@ -226,6 +229,16 @@ def cublas_tf32_peak(torch, sustained_s: float = 0.0):
     return 2 * n ** 3 / (ms * 1e-3) / 1e12
 
 
+def hbm_peak():
+    """Measured HBM copy bandwidth of this pool's B200s (MEASURED_PEAKS.json),
+    else the earlier measurement 6650 GB/s."""
+    try:
+        return {"gbs": json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["hbm_gbs"],
+                "source": "MEASURED_PEAKS.json"}
+    except (OSError, KeyError, ValueError):
+        return {"gbs": 6650.0, "source": "fallback"}
+
+
 def _events(torch):
     return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
@@ -328,9 +341,62 @@ def run_rows(a, torch):
             times.append(e0.elapsed_time(e1))
         ms = statistics.median(times[a.warmup:])
         res[name] = {"ms": ms, "gbs": nbytes / ms / 1e6}
+    del work, out, flush
+    # Back to back: a ring of 16 independent input/output sets (16 x 3
+    # matrices = 805 MB, far above L2), each launch on the next set, so
+    # every launch reads its inputs from HBM and launch gaps overlap.
+    ring = 16
+    xs = torch.randn(ring, R, Cc, device="cuda", generator=g)
+    dys = torch.randn(ring, R, Cc, device="cuda", generator=g)
+    outs = torch.empty(ring, R, Cc, device="cuda")
+    ps = torch.softmax(xs, dim=2).contiguous()
+    ring_ops = {
+        "softmax_fwd": (lambda i: K.softmax_rows(outs[i]), 2 * mat),
+        "softmax_bwd": (lambda i: K.softmax_backward(ps[i], dys[i], outs[i]), 3 * mat),
+        "layernorm_fwd": (lambda i: K.norm_rows(xs[i], outs[i], 1), 2 * mat),
+        "layernorm_fwd_affine": (lambda i: K.norm_rows(xs[i], outs[i], 1, 1e-5, gamma, beta),
+                                 2 * mat),
+        "layernorm_bwd": (lambda i: K.layer_norm_backward(xs[i], dys[i], outs[i]), 3 * mat),
+        "rmsnorm_fwd": (lambda i: K.norm_rows(xs[i], outs[i], 0), 2 * mat),
+        "rmsnorm_bwd": (lambda i: K.rms_norm_backward(xs[i], dys[i], outs[i]), 3 * mat),
+        "gelu_fwd": (lambda i: K.unary(outs[i], 2, 1), 2 * mat),
+        "gelu_bwd": (lambda i: K.mul_act_derivative(outs[i], xs[i], 1), 3 * mat),
+        "row_broadcast_add": (lambda i: K.binary_assign_by_rows(outs[i], beta, 0), 2 * mat),
+    }
+    # The ring's launches are captured once into a CUDA graph and replayed,
+    # so host launch overhead (Python + ctypes per call) does not starve
+    # the GPU between 10 us kernels.
+    res_ring = {}
+    side = torch.cuda.Stream()
+    reps = max(1, a.steps // 4)
+    for name, (fn, nbytes) in ring_ops.items():
+        outs.copy_(xs)  # in-place kernels start from N(0,1) data
+        for i in range(ring):
+            fn(i)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side), torch.cuda.graph(graph, stream=side):
+            for i in range(ring):
+                fn(i)
+        torch.cuda.synchronize()
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = _events(torch)
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / (reps * ring)
+        res_ring[name] = {"ms": ms, "gbs": nbytes / ms / 1e6}
+        del graph
     print(json.dumps({"metric": "row kernels GB/s", "unit": "GB/s", "workload": "rows",
-                      "shape": [R, Cc], "l2": "256 MiB flush before every timed launch",
-                      "results": res}), flush=True)
+                      "shape": [R, Cc], "hbm_copy_gbs": hbm_peak(),
+                      "l2": "single: 256 MiB flush before every timed launch; back_to_back: "
+                            "a 16-set ring of inputs (805 MB) cycled, one launch per set, "
+                            "the 16 launches replayed as one CUDA graph",
+                      "results": res, "back_to_back": res_ring}), flush=True)
 
 
 def run_mlp(a, torch):
@@ -478,8 +544,10 @@ def main():
     x = torch.randn(rows, a.hidden, device="cuda", generator=g)
     t = torch.randn(rows, a.hidden, device="cuda", generator=g)
 
-    peak_burst = cublas_tf32_peak(torch)
-    peak = cublas_tf32_peak(torch, sustained_s=3.0)
+    peak_burst = peak = None
+    if not a.no_peak:
+        peak_burst = cublas_tf32_peak(torch)
+        peak = cublas_tf32_peak(torch, sustained_s=3.0)
 
     # ---------------- device-resident timing
     for _ in range(a.warmup):
@@ -563,7 +631,8 @@ def main():
             "e2e": e2e,
             "gpu_launches": int(launches),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
-                         "unit": "TFLOP/s", "frac": (achieved / peak) if achieved else None,
+                         "unit": "TFLOP/s",
+                         "frac": (achieved / peak) if achieved and peak else None,
                          "traffic": None, "kernel": "gemm_tf32_tcgen05 (all GEMMs of a step)",
                          "gemm_launches_per_step": gemm_launches // max(1, a.steps),
                          "gemm_share_of_step": gemm_ms / elapsed_ms if elapsed_ms else None,
