@@ -39,6 +39,10 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "oxide-forge_b200"))
 
 SEQ, HIDDEN, FFN, GLOBAL_BATCH, LR = 1024, 2048, 8192, 128, 1e-3
+# DRAM bytes (read + write) of the 18 GEMM launches of one C5 step at N=1,
+# from the ncu launch list in profiles/launches_train_step_c5.md (105.8 GB
+# read + 29.1 GB written); their compulsory traffic is about 74 GB.
+GEMM_DRAM_BYTES_PER_STEP = 134.9e9
 METRIC = "Transformer fwd+bwd tokens/s"
 UNIT = "tokens/s"
 
@@ -633,7 +637,11 @@ def main():
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
                          "unit": "TFLOP/s",
                          "frac": (achieved / peak) if achieved and peak else None,
-                         "traffic": None, "kernel": "gemm_tf32_tcgen05 (all GEMMs of a step)",
+                         "traffic": GEMM_DRAM_BYTES_PER_STEP / 18 if world == 1 else None,
+                         "traffic_note": "DRAM bytes per GEMM launch, mean over the 18 GEMMs "
+                                         "of a step (ncu launch list, profiles/); compulsory "
+                                         "≈74 GB per step = 4.1 GB per launch",
+                         "kernel": "gemm_tf32_tcgen05 (all GEMMs of a step)",
                          "gemm_launches_per_step": gemm_launches // max(1, a.steps),
                          "gemm_share_of_step": gemm_ms / elapsed_ms if elapsed_ms else None,
                          "peak_source": "cuBLAS TF32 8192^3 (torch.matmul), back to back for "
