@@ -127,6 +127,45 @@ oxf_status oxf_mlp_backward(oxf_mlp m, const float* dy, float* dx, size_t rows);
 oxf_status oxf_mlp_zero_grads(oxf_mlp m);
 oxf_status oxf_mlp_sgd(oxf_mlp m, float lr);
 
+/* ---------------------------------------------------------------- checkpoints (v1) */
+/* The reference's checkpoint format (src/net/checkpoint/model.rs:17-21,
+ * io.rs:14-181): <name>.toml holds format_version = 1, model_type
+ * ("linear" | "mlp" | "transformer"), scalar_type = "f32_le", data_file,
+ * data_bytes and the model's metadata (Linear neuron counts, activation,
+ * weight/bias shapes and [byte_start, byte_end) ranges; MLP layer_count,
+ * loss, residual; transformer block_count, residual flags, normalization,
+ * position); <name>.bin holds the parameters as little-endian f32 in cursor
+ * order. `path` without an extension gets ".toml"; any extension other
+ * than .toml is refused (io.rs:20-29). Loading validates what the
+ * reference validates (model.rs:350-537): version, model type, scalar
+ * encoding, contiguous ranges, shapes, Linear connectivity, residual and
+ * transformer dimensions, and the data file's size.
+ *
+ * Host-array forms (no GPU needed); parameters in cursor order: */
+/* dump_linear / dump_mlp / dump_transformer with the parameters given. */
+oxf_status oxf_checkpoint_write_linear(const char* path, const oxf_layer_spec* spec,
+                                       const float* params_host, size_t count);
+oxf_status oxf_checkpoint_write_mlp(const char* path, const oxf_mlp_spec* spec,
+                                    const float* params_host, size_t count);
+oxf_status oxf_checkpoint_write_transformer(const char* path, const oxf_transformer_spec* spec,
+                                            const float* params_host, size_t count);
+/* load_*: validates, fills *spec (may be NULL) and *count, and copies the
+ * parameters when params_host != NULL (capacity >= *count). */
+oxf_status oxf_checkpoint_read_linear(const char* path, oxf_layer_spec* spec, float* params_host,
+                                      size_t capacity, size_t* count);
+oxf_status oxf_checkpoint_read_mlp(const char* path, oxf_mlp_spec* spec, float* params_host,
+                                   size_t capacity, size_t* count);
+oxf_status oxf_checkpoint_read_transformer(const char* path, oxf_transformer_spec* spec,
+                                           float* params_host, size_t capacity, size_t* count);
+/* Engine forms: dump_transformer / load_transformer and dump_mlp / load_mlp
+ * (model.rs:78-208) on an engine's parameter arena. Loading creates the
+ * engine (as oxf_*_create) with the checkpoint's parameters. */
+oxf_status oxf_transformer_dump(oxf_transformer t, const char* path);
+oxf_status oxf_transformer_load(const char* path, int max_batch, oxf_stream stream,
+                                oxf_transformer* out);
+oxf_status oxf_mlp_dump(oxf_mlp m, const char* path);
+oxf_status oxf_mlp_load(const char* path, size_t max_rows, oxf_stream stream, oxf_mlp* out);
+
 #ifdef __cplusplus
 }
 #endif

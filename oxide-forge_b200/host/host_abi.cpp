@@ -3,15 +3,18 @@
 // oxf_status plus oxf_last_error_string().
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <exception>
 #include <new>
 #include <vector>
 
+#include "checkpoint.hpp"
 #include "engine.hpp"
 #include "errors.hpp"
 #include "oxf_host.h"
 
 struct oxf_transformer_s {
+  oxf_transformer_spec spec{};  // as created (checkpoint metadata)
   oxf::TransformerEngine* engine = nullptr;
   cudaStream_t stream = nullptr;
   bool own_stream = false;
@@ -21,6 +24,7 @@ struct oxf_transformer_s {
 };
 
 struct oxf_mlp_s {
+  oxf_mlp_spec spec{};  // as created (checkpoint metadata)
   oxf::MlpEngine* engine = nullptr;
   cudaStream_t stream = nullptr;
   bool own_stream = false;
@@ -74,6 +78,42 @@ cudaStream_t make_stream(oxf_stream given, bool* own) {
 
 }  // namespace
 
+// Checkpoint entry points: copy between a checkpoint and host arrays.
+namespace {
+
+template <typename Spec>
+oxf_status write_ckpt(const char* path, oxf::ckpt::ModelType type, const Spec* spec,
+                      const float* params_host, size_t count,
+                      void (*put)(oxf::ckpt::Model&, const Spec&)) {
+  if (!path || !spec || (!params_host && count)) {
+    return oxf::set_error(OXF_ERR_INVALID_ARG, "null argument");
+  }
+  return guard([&] {
+    oxf::ckpt::Model m;
+    m.type = type;
+    put(m, *spec);
+    m.params.assign(params_host, params_host + count);
+    oxf::ckpt::write(path, m);
+  });
+}
+
+template <typename Spec>
+oxf_status read_ckpt(const char* path, oxf::ckpt::ModelType type, Spec* spec, float* params_host,
+                     size_t capacity, size_t* count, Spec (*get)(const oxf::ckpt::Model&)) {
+  if (!path || !count) return oxf::set_error(OXF_ERR_INVALID_ARG, "null argument");
+  return guard([&] {
+    const oxf::ckpt::Model m = oxf::ckpt::read(path, type);
+    *count = m.params.size();
+    if (spec) *spec = get(m);
+    if (params_host) {
+      oxf::require(capacity >= m.params.size(), "parameter buffer smaller than the checkpoint");
+      std::copy(m.params.begin(), m.params.end(), params_host);
+    }
+  });
+}
+
+}  // namespace
+
 extern "C" {
 
 // ---------------------------------------------------------------- transformer
@@ -92,6 +132,7 @@ oxf_status oxf_transformer_create(const oxf_transformer_spec* spec, int max_batc
     s.ffn = mlp_spec(spec->ffn);
     s.o = layer(spec->out);
     auto* h = new oxf_transformer_s();
+    h->spec = *spec;
     try {
       h->stream = make_stream(stream, &h->own_stream);
       h->engine = new oxf::TransformerEngine(s, max_batch, h->stream);
@@ -261,6 +302,7 @@ oxf_status oxf_mlp_create(const oxf_mlp_spec* spec, size_t max_rows, oxf_stream 
   return guard([&] {
     oxf::MlpSpec s = mlp_spec(*spec);
     auto* h = new oxf_mlp_s();
+    h->spec = *spec;
     try {
       h->stream = make_stream(stream, &h->own_stream);
       h->engine = new oxf::MlpEngine(s, max_rows);
@@ -330,6 +372,109 @@ oxf_status oxf_mlp_sgd(oxf_mlp m, float lr) {
   return guard([&] {
     oxf::check(oxf_sgd_update({m->params, m->nparams}, {m->grads, m->nparams}, lr,
                               reinterpret_cast<oxf_stream>(m->stream)));
+  });
+}
+
+// ---------------------------------------------------------------- checkpoints (v1)
+oxf_status oxf_checkpoint_write_linear(const char* path, const oxf_layer_spec* spec,
+                                       const float* params_host, size_t count) {
+  return write_ckpt<oxf_layer_spec>(
+      path, oxf::ckpt::ModelType::Linear, spec, params_host, count,
+      [](oxf::ckpt::Model& m, const oxf_layer_spec& s) { m.linear = s; });
+}
+
+oxf_status oxf_checkpoint_write_mlp(const char* path, const oxf_mlp_spec* spec,
+                                    const float* params_host, size_t count) {
+  return write_ckpt<oxf_mlp_spec>(path, oxf::ckpt::ModelType::Mlp, spec, params_host, count,
+                                  [](oxf::ckpt::Model& m, const oxf_mlp_spec& s) { m.mlp = s; });
+}
+
+oxf_status oxf_checkpoint_write_transformer(const char* path, const oxf_transformer_spec* spec,
+                                            const float* params_host, size_t count) {
+  return write_ckpt<oxf_transformer_spec>(
+      path, oxf::ckpt::ModelType::Transformer, spec, params_host, count,
+      [](oxf::ckpt::Model& m, const oxf_transformer_spec& s) { m.transformer = s; });
+}
+
+oxf_status oxf_checkpoint_read_linear(const char* path, oxf_layer_spec* spec, float* params_host,
+                                      size_t capacity, size_t* count) {
+  return read_ckpt<oxf_layer_spec>(path, oxf::ckpt::ModelType::Linear, spec, params_host,
+                                   capacity, count,
+                                   [](const oxf::ckpt::Model& m) { return m.linear; });
+}
+
+oxf_status oxf_checkpoint_read_mlp(const char* path, oxf_mlp_spec* spec, float* params_host,
+                                   size_t capacity, size_t* count) {
+  return read_ckpt<oxf_mlp_spec>(path, oxf::ckpt::ModelType::Mlp, spec, params_host, capacity,
+                                 count, [](const oxf::ckpt::Model& m) { return m.mlp; });
+}
+
+oxf_status oxf_checkpoint_read_transformer(const char* path, oxf_transformer_spec* spec,
+                                           float* params_host, size_t capacity, size_t* count) {
+  return read_ckpt<oxf_transformer_spec>(
+      path, oxf::ckpt::ModelType::Transformer, spec, params_host, capacity, count,
+      [](const oxf::ckpt::Model& m) { return m.transformer; });
+}
+
+oxf_status oxf_transformer_dump(oxf_transformer t, const char* path) {
+  if (!t || !path) return oxf::set_error(OXF_ERR_INVALID_ARG, "null argument");
+  return guard([&] {
+    oxf::ckpt::Model m;
+    m.type = oxf::ckpt::ModelType::Transformer;
+    m.transformer = t->spec;
+    m.params.resize(t->engine->param_count());
+    oxf::check(oxf_transformer_get_params_host(t, m.params.data()));
+    oxf::ckpt::write(path, m);
+  });
+}
+
+oxf_status oxf_transformer_load(const char* path, int max_batch, oxf_stream stream,
+                                oxf_transformer* out) {
+  if (!path || !out) return oxf::set_error(OXF_ERR_INVALID_ARG, "null argument");
+  *out = nullptr;
+  return guard([&] {
+    const oxf::ckpt::Model m = oxf::ckpt::read(path, oxf::ckpt::ModelType::Transformer);
+    oxf_transformer t = nullptr;
+    oxf::check(oxf_transformer_create(&m.transformer, max_batch, stream, &t));
+    const oxf_status st = oxf_transformer_set_params_host(t, m.params.data());
+    if (st != OXF_OK) {
+      oxf_transformer_destroy(t);
+      oxf::check(st);
+    }
+    *out = t;
+  });
+}
+
+oxf_status oxf_mlp_dump(oxf_mlp m, const char* path) {
+  if (!m || !path) return oxf::set_error(OXF_ERR_INVALID_ARG, "null argument");
+  return guard([&] {
+    oxf::ckpt::Model c;
+    c.type = oxf::ckpt::ModelType::Mlp;
+    c.mlp = m->spec;
+    c.params.resize(m->nparams);
+    oxf::check_cuda_call(cudaMemcpyAsync(c.params.data(), m->params, m->nparams * 4,
+                                         cudaMemcpyDeviceToHost, m->stream),
+                         "D2H params");
+    oxf::check_cuda_call(cudaStreamSynchronize(m->stream), "sync");
+    oxf::ckpt::write(path, c);
+  });
+}
+
+oxf_status oxf_mlp_load(const char* path, size_t max_rows, oxf_stream stream, oxf_mlp* out) {
+  if (!path || !out) return oxf::set_error(OXF_ERR_INVALID_ARG, "null argument");
+  *out = nullptr;
+  return guard([&] {
+    const oxf::ckpt::Model c = oxf::ckpt::read(path, oxf::ckpt::ModelType::Mlp);
+    oxf_mlp m = nullptr;
+    oxf::check(oxf_mlp_create(&c.mlp, max_rows, stream, &m));
+    cudaError_t e = cudaMemcpyAsync(m->params, c.params.data(), c.params.size() * 4,
+                                    cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) {
+      oxf_mlp_destroy(m);
+      oxf::check_cuda_call(e, "H2D params");
+    }
+    *out = m;
   });
 }
 

@@ -57,6 +57,21 @@ SIGS: dict = {
     "oxf_mlp_backward": (C.c_int, [_h, _fp, _fp, _sz]),
     "oxf_mlp_zero_grads": (C.c_int, [_h]),
     "oxf_mlp_sgd": (C.c_int, [_h, C.c_float]),
+    "oxf_checkpoint_write_linear": (C.c_int, [C.c_char_p, C.POINTER(LayerSpec), _fp, _sz]),
+    "oxf_checkpoint_write_mlp": (C.c_int, [C.c_char_p, C.POINTER(MlpSpec), _fp, _sz]),
+    "oxf_checkpoint_write_transformer": (C.c_int, [C.c_char_p, C.POINTER(TransformerSpec), _fp,
+                                                   _sz]),
+    "oxf_checkpoint_read_linear": (C.c_int, [C.c_char_p, C.POINTER(LayerSpec), _fp, _sz,
+                                             C.POINTER(_sz)]),
+    "oxf_checkpoint_read_mlp": (C.c_int, [C.c_char_p, C.POINTER(MlpSpec), _fp, _sz,
+                                          C.POINTER(_sz)]),
+    "oxf_checkpoint_read_transformer": (C.c_int, [C.c_char_p, C.POINTER(TransformerSpec), _fp,
+                                                  _sz, C.POINTER(_sz)]),
+    "oxf_transformer_dump": (C.c_int, [_h, C.c_char_p]),
+    "oxf_transformer_load": (C.c_int, [C.c_char_p, C.c_int, C.c_void_p,
+                                       C.POINTER(C.c_void_p)]),
+    "oxf_mlp_dump": (C.c_int, [_h, C.c_char_p]),
+    "oxf_mlp_load": (C.c_int, [C.c_char_p, _sz, C.c_void_p, C.POINTER(C.c_void_p)]),
 }
 
 

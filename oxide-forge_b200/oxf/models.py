@@ -147,16 +147,18 @@ def split_params(cfg, flat: np.ndarray) -> list:
 class Transformer:
     """Batched single-block Post-Norm transformer (inference + training)."""
 
-    def __init__(self, cfg: TransformerConfig, max_batch: int = 1, stream=None):
+    def __init__(self, cfg: TransformerConfig, max_batch: int = 1, stream=None, _handle=None):
         self.cfg = cfg
         self.max_batch = max_batch
         if stream is None:
             stream = torch.cuda.current_stream()
         self._stream = stream
-        h = C.c_void_p()
-        spec = cfg.spec()
-        check(lib().oxf_transformer_create(C.byref(spec), max_batch, C.c_void_p(stream.cuda_stream),
-                                           C.byref(h)))
+        h = _handle
+        if h is None:
+            h = C.c_void_p()
+            spec = cfg.spec()
+            check(lib().oxf_transformer_create(C.byref(spec), max_batch,
+                                               C.c_void_p(stream.cuda_stream), C.byref(h)))
         self._h = h
         self.n = int(lib().oxf_transformer_param_count(h))
         assert self.n == cfg.param_count(), (self.n, cfg.param_count())
@@ -253,14 +255,16 @@ class Transformer:
 class Mlp:
     """Batched MlpExecutor (forward, backward with deferred SGD)."""
 
-    def __init__(self, cfg: MlpConfig, max_rows: int, stream=None):
+    def __init__(self, cfg: MlpConfig, max_rows: int, stream=None, _handle=None):
         self.cfg = cfg
         if stream is None:
             stream = torch.cuda.current_stream()
-        h = C.c_void_p()
-        spec = cfg.spec()
-        check(lib().oxf_mlp_create(C.byref(spec), max_rows, C.c_void_p(stream.cuda_stream),
-                                   C.byref(h)))
+        h = _handle
+        if h is None:
+            h = C.c_void_p()
+            spec = cfg.spec()
+            check(lib().oxf_mlp_create(C.byref(spec), max_rows, C.c_void_p(stream.cuda_stream),
+                                       C.byref(h)))
         self._h = h
         self.n = int(lib().oxf_mlp_param_count(h))
         self.params = device_view(lib().oxf_mlp_params(h), (self.n,), self)

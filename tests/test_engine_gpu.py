@@ -255,3 +255,37 @@ def test_pipelined_host_steps_match_device_steps(M):
     assert rel_err(a.get_params() - flat, b.get_params() - flat) < 1e-4
     a.close()
     b.close()
+
+
+def test_checkpoint_engine_round_trip(M, tmp_path):
+    """dump_transformer / load_transformer and dump_mlp / load_mlp on the
+    engines' device arenas: the loaded engines hold the same parameters and
+    compute the same outputs."""
+    from oxf import _lib
+    from oxf import checkpoint as ck
+    seq, hidden, ffn, B = 32, 64, 128, 2
+    cfg = M.transformer_config(seq, hidden, ffn, norm=0, bias=True)
+    flat = M.init_transformer_params(cfg, seed=9)
+    a = M.Transformer(cfg, max_batch=B)
+    a.set_params(flat)
+    ck.dump_transformer(a, tmp_path / "model")
+    b = ck.load_transformer(tmp_path / "model.toml", max_batch=B)
+    assert b.cfg == cfg
+    np.testing.assert_array_equal(b.get_params(), flat)
+    x = dev(np.random.default_rng(4).standard_normal((B * seq, hidden)))
+    ya = host(a.forward(x))
+    yb = host(b.forward(x))
+    np.testing.assert_array_equal(ya, yb)
+    a.close()
+    b.close()
+
+    mcfg = M.MlpConfig([M.Layer(64, 256, _lib.ACT_GELU, True), M.Layer(256, 64, 0, True)], (0, 2))
+    m = M.Mlp(mcfg, 96)
+    mflat = np.random.default_rng(5).standard_normal(m.n).astype(np.float32)
+    m.params.copy_(dev(mflat))
+    ck.dump_mlp_engine(m, tmp_path / "mlp")
+    m2 = ck.load_mlp_engine(tmp_path / "mlp", 96)
+    assert m2.cfg == mcfg
+    np.testing.assert_array_equal(host(m2.params), mflat)
+    m.close()
+    m2.close()
