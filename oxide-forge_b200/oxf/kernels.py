@@ -196,9 +196,22 @@ def gemm(a, b, out, *, a_trans=False, b_trans=False, alpha=1.0, beta=0.0, bias=N
 
     a: [M,K] (or [K,M] with a_trans), b: [K,N] (or [N,K] with b_trans); a
     leading batch dimension on any operand makes it per-batch (a 2-D operand
-    is shared across the batch)."""
+    is shared across the batch). Matrices may be row-strided views (unit
+    stride along rows); leading dimensions and batch strides come from the
+    tensors' strides."""
     def dims(t):
         return (t.shape[0], t.shape[1], t.shape[2]) if t.dim() == 3 else (1, t.shape[0], t.shape[1])
+
+    def lds(t, name):
+        """(leading dimension, batch stride) in elements."""
+        if not (t.is_cuda and t.dtype == torch.float32) or t.dim() not in (2, 3):
+            raise ValueError(f"{name} must be a 2-D or 3-D float32 CUDA tensor")
+        if t.numel() == 0:
+            return t.shape[-1], 0
+        if t.shape[-1] > 1 and t.stride(-1) != 1:
+            raise ValueError(f"{name} must have unit stride along its rows")
+        ld = t.stride(-2) if t.shape[-2] > 1 else t.shape[-1]
+        return ld, (t.stride(0) if t.dim() == 3 else 0)
 
     ba, ar, ac = dims(a)
     bb, br, bc = dims(b)
@@ -209,9 +222,9 @@ def gemm(a, b, out, *, a_trans=False, b_trans=False, alpha=1.0, beta=0.0, bias=N
     lib().oxf_gemm_desc_init(C.byref(d), M, N, K, int(a_trans), int(b_trans), a.data_ptr(),
                              b.data_ptr(), out.data_ptr())
     d.batch = batch
-    d.lda, d.stride_a = ac, (ar * ac if a.dim() == 3 else 0)
-    d.ldb, d.stride_b = bc, (br * bc if b.dim() == 3 else 0)
-    d.ldc, d.stride_c = N, (M * N if out.dim() == 3 else 0)
+    d.lda, d.stride_a = lds(a, "a")
+    d.ldb, d.stride_b = lds(b, "b")
+    d.ldc, d.stride_c = lds(out, "out")
     d.alpha, d.beta = float(alpha), float(beta)
     if bias is not None:
         d.bias = _f32(bias).data_ptr()
@@ -219,9 +232,10 @@ def gemm(a, b, out, *, a_trans=False, b_trans=False, alpha=1.0, beta=0.0, bias=N
                              ("pre_out", pre_out, "ldp", "stride_p"),
                              ("aux", aux, "ldx", "stride_x")):
         if t is not None:
-            setattr(d, name, _f32(t).data_ptr())
-            setattr(d, ldn, t.shape[-1])
-            setattr(d, sn, t.shape[-1] * t.shape[-2] if t.dim() == 3 else 0)
+            setattr(d, name, t.data_ptr())
+            ld, st = lds(t, name)
+            setattr(d, ldn, ld)
+            setattr(d, sn, st)
     d.act, d.grad_act = int(act), int(grad_act)
     d.accumulate, d.split_k, d.precision = int(accumulate), int(split_k), int(precision)
     d.reduce_batch = int(reduce_batch)

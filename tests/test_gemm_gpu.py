@@ -263,3 +263,57 @@ def test_cta_pair_features(K, rng):
     K.gemm(dev(Ab), dev(Bb), red, b_trans=True, residual=dev(Rb), reduce_batch=True, variant=2)
     want = Rb + sum(exact(Ab[b], Bb[b], 0, 1) for b in range(3))
     assert rel_err(host(red), want) < TF32_TOL
+
+
+@pytest.mark.parametrize("variant", [1, 2])
+@pytest.mark.parametrize("M,N,Kd", [(300, 200, 72), (512, 384, 128)])
+def test_epilogue_tiles_batched_and_shared(K, rng, M, N, Kd, variant):
+    """The TMA-staged epilogue on batched outputs: a residual shared by the
+    batch (stride 0, a 2-D tensor map), per-item aux and pre-activation
+    outputs (3-D maps), beta * C read back through TMA, ragged M and N
+    (partial 32x32 tiles clipped by the map), and the bias tail."""
+    batch = 2
+    A, B = operands(rng, M, N, Kd, 0, 0, batch=batch)
+    bias = (0.1 * rng.standard_normal(N)).astype(np.float32)
+    R = rng.standard_normal((M, N)).astype(np.float32)
+    C0 = rng.standard_normal((batch, M, N)).astype(np.float32)
+    out = dev(C0)
+    pre = torch.empty((batch, M, N), device="cuda")
+    K.gemm(dev(A), dev(B), out, alpha=0.5, beta=0.25, bias=dev(bias), residual=dev(R),
+           pre_out=pre, act=1, variant=variant)
+    for b in range(batch):
+        z = 0.5 * exact(A[b], B[b], 0, 0) + 0.25 * C0[b] + bias + R
+        assert rel_err(host(pre)[b], z) < TF32_TOL
+        assert rel_err(host(out)[b], O.act_forward(O.GELU, z.astype(np.float32))) < TF32_TOL
+    X = rng.standard_normal((batch, M, N)).astype(np.float32)
+    g = torch.empty((batch, M, N), device="cuda")
+    K.gemm(dev(A), dev(B), g, aux=dev(X), grad_act=1, variant=variant)
+    for b in range(batch):
+        want = exact(A[b], B[b], 0, 0) * O.act_derivative(O.GELU, X[b]).astype(np.float64)
+        assert rel_err(host(g)[b], want) < TF32_TOL
+
+
+def test_epilogue_unaligned_output_falls_back(K, rng):
+    """Aligned operands but an output leading dimension that TMA cannot
+    describe (201 floats): the tcgen05 kernel keeps per-thread stores."""
+    M, N, Kd = 256, 200, 128
+    A, B = operands(rng, M, N, Kd, 0, 0)
+    big = torch.zeros((M, 201), device="cuda")
+    view = big[:, :N]
+    R = rng.standard_normal((M, N)).astype(np.float32)
+    K.gemm(dev(A), dev(B), view, residual=dev(R))
+    assert rel_err(host(big)[:, :N], exact(A, B, 0, 0) + R) < TF32_TOL
+    assert not host(big)[:, N:].any()
+
+
+def test_accumulate_rejects_split_with_bias(K, rng):
+    """Split-K adds each partial product into C, so a bias or residual would
+    be added once per split: refused when asked for, avoided when automatic."""
+    M, N, Kd = 256, 256, 4096
+    A, B = operands(rng, M, N, Kd, 1, 0)
+    bias = rng.standard_normal(N).astype(np.float32)
+    acc = torch.zeros((M, N), device="cuda")
+    with pytest.raises(Exception, match="split_k"):
+        K.gemm(dev(A), dev(B), acc, a_trans=True, bias=dev(bias), accumulate=True, split_k=4)
+    K.gemm(dev(A), dev(B), acc, a_trans=True, bias=dev(bias), accumulate=True)
+    assert rel_err(host(acc), exact(A, B, 1, 0) + bias) < TF32_TOL
