@@ -128,6 +128,16 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int mn_major, in
                   : make_smem_desc(base + kk * 32, 16, 1024, kLayoutSW128);
 }
 
+// Byte step between the K=8 slices of an operand tile (see operand_desc).
+__device__ __forceinline__ uint32_t operand_kstep(int mn_major) { return mn_major ? 1024u : 32u; }
+
+// A descriptor moved by `bytes` within shared memory: only the start
+// address field (bits [0,14), in 16-byte units) changes, and shared memory
+// addresses stay below 2^18, so the add never carries out of the field.
+__device__ __forceinline__ uint64_t desc_advance(uint64_t desc, uint32_t bytes) {
+  return desc + (bytes >> 4);
+}
+
 template <int ROWS>
 __device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* map, uint64_t* bar,
                                              int mn_major, int is3d, int chunked, int row0, int k0,
@@ -458,27 +468,32 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       for (long long u = blockIdx.x; u < args.units && !ctrl->abort_flag; u += gridDim.x) {
         int b, tm, tn, kb0, kb1;
         decode_unit(args, u, b, tm, tn, kb0, kb1);
+        // Batch-reduce GEMMs walk K over (batch item, k-block) pairs; the
+        // pair advances incrementally (no division in the per-block loop).
+        int bk = args.reduce_batch ? kb0 / args.kblocks_item : b;
+        int kin = args.reduce_batch ? kb0 - bk * args.kblocks_item : kb0;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&ctrl->empty[stage], phase ^ 1u, DEVERR_GEMM_WAIT_EMPTY)) {
             ctrl->abort_flag = 1;
             break;
           }
-          if (ctrl->abort_flag) break;
           uint8_t* slot = ring + stage * Cfg::STAGE_BYTES;
           mbar_arrive_expect_tx(&ctrl->full[stage], Cfg::STAGE_BYTES);
-          // batch-reduce GEMMs walk K over (batch item, k-block) pairs
-          const int bk = args.reduce_batch ? kb / args.kblocks_item : b;
-          const int k0 = (args.reduce_batch ? kb % args.kblocks_item : kb) * BK;
+          const int k0 = kin * BK, item = bk;
+          if (++kin == args.kblocks_item && args.reduce_batch) {
+            kin = 0;
+            ++bk;
+          }
           load_operand<BM>(slot, &tmA, &ctrl->full[stage], args.a_mn, args.a3d, args.a_chunked,
-                           tm * BM, k0, bk, pol_a);
+                           tm * BM, k0, item, pol_a);
           load_operand<BN>(slot + Cfg::A_BYTES, &tmB, &ctrl->full[stage], args.b_mn, args.b3d,
-                           args.b_chunked, tn * BN, k0, bk, pol_b);
+                           args.b_chunked, tn * BN, k0, item, pol_b);
           if (SPLIT3) {
             uint8_t* lo = slot + Cfg::A_BYTES + Cfg::B_BYTES;
             load_operand<BM>(lo, &tmA_lo, &ctrl->full[stage], args.a_mn, args.a3d,
-                             args.a_chunked, tm * BM, k0, bk, pol_a);
+                             args.a_chunked, tm * BM, k0, item, pol_a);
             load_operand<BN>(lo + Cfg::A_BYTES, &tmB_lo, &ctrl->full[stage], args.b_mn,
-                             args.b3d, args.b_chunked, tn * BN, k0, bk, pol_b);
+                             args.b3d, args.b_chunked, tn * BN, k0, item, pol_b);
           }
           ++fills;
           if (++stage == STAGES) {
@@ -499,6 +514,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (lane == 0) {
       uint32_t stage = 0, phase = 0;
       int local = 0;
+      // Descriptors of stage 0, K slice 0; every other (stage, slice) is an
+      // address offset from these.
+      const uint64_t a_desc0 = operand_desc(smem_u32(ring), args.a_mn, 0);
+      const uint64_t b_desc0 = operand_desc(smem_u32(ring) + Cfg::A_BYTES, args.b_mn, 0);
+      const uint32_t a_step = operand_kstep(args.a_mn), b_step = operand_kstep(args.b_mn);
       for (long long u = blockIdx.x; u < args.units && !ctrl->abort_flag;
            u += gridDim.x, ++local) {
         int b, tm, tn, kb0, kb1;
@@ -519,17 +539,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(ring + stage * Cfg::STAGE_BYTES);
-          const uint32_t b_base = a_base + Cfg::A_BYTES;
+          const uint32_t off = stage * Cfg::STAGE_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-            const uint64_t da = operand_desc(a_base, args.a_mn, kk);
-            const uint64_t db = operand_desc(b_base, args.b_mn, kk);
+            const uint64_t da = desc_advance(a_desc0, off + kk * a_step);
+            const uint64_t db = desc_advance(b_desc0, off + kk * b_step);
             const uint32_t accumulate = (kb > kb0 || kk > 0) ? 1u : 0u;
             if (SPLIT3) {
-              const uint32_t lo_base = b_base + Cfg::B_BYTES;
-              const uint64_t da_lo = operand_desc(lo_base, args.a_mn, kk);
-              const uint64_t db_lo = operand_desc(lo_base + Cfg::A_BYTES, args.b_mn, kk);
+              const uint32_t lo = Cfg::A_BYTES + Cfg::B_BYTES;
+              const uint64_t da_lo = desc_advance(a_desc0, off + lo + kk * a_step);
+              const uint64_t db_lo = desc_advance(b_desc0, off + lo + kk * b_step);
               umma_tf32(d_tmem, da_lo, db, args.idesc, accumulate);
               umma_tf32(d_tmem, da, db_lo, args.idesc, 1u);
               umma_tf32(d_tmem, da, db, args.idesc, 1u);
@@ -707,22 +726,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
       for (long long u = cluster_id; u < args.units && !ctrl->abort_flag; u += nclusters) {
         int b, tm, tn, kb0, kb1;
         decode_unit(args, u, b, tm, tn, kb0, kb1);
+        int bk = args.reduce_batch ? kb0 / args.kblocks_item : b;  // as in the single-CTA kernel
+        int kin = args.reduce_batch ? kb0 - bk * args.kblocks_item : kb0;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&ctrl->empty[stage], phase ^ 1u, DEVERR_GEMM_WAIT_EMPTY)) {
             ctrl->abort_flag = 1;
             break;
           }
-          if (ctrl->abort_flag) break;
           if (leader) mbar_arrive_expect_tx(&ctrl->full[stage], 2 * Cfg::STAGE_BYTES);
           uint8_t* slot = ring + stage * Cfg::STAGE_BYTES;
           const uint32_t bar = full0 + 8u * stage;
-          const int bk = args.reduce_batch ? kb / args.kblocks_item : b;
-          const int k0 = (args.reduce_batch ? kb % args.kblocks_item : kb) * BK;
+          const int k0 = kin * BK, item = bk;
+          if (++kin == args.kblocks_item && args.reduce_batch) {
+            kin = 0;
+            ++bk;
+          }
           load_operand_pair<BM>(slot, &tmA, bar, args.a_mn, args.a3d, args.a_chunked,
-                                tm * 2 * BM + static_cast<int>(rank) * BM, k0, bk, pol_a);
+                                tm * 2 * BM + static_cast<int>(rank) * BM, k0, item, pol_a);
           load_operand_pair<BN / 2>(slot + Cfg::A_BYTES, &tmB, bar, args.b_mn, args.b3d,
                                     args.b_chunked, tn * BN + static_cast<int>(rank) * (BN / 2),
-                                    k0, bk, pol_b);
+                                    k0, item, pol_b);
           ++fills;
           if (++stage == STAGES) {
             stage = 0;
@@ -743,6 +766,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     if (leader && lane == 0) {
       uint32_t stage = 0, phase = 0;
       int local = 0;
+      const uint64_t a_desc0 = operand_desc(smem_u32(ring), args.a_mn, 0);
+      const uint64_t b_desc0 = operand_desc(smem_u32(ring) + Cfg::A_BYTES, args.b_mn, 0);
+      const uint32_t a_step = operand_kstep(args.a_mn), b_step = operand_kstep(args.b_mn);
       for (long long u = cluster_id; u < args.units && !ctrl->abort_flag;
            u += nclusters, ++local) {
         int b, tm, tn, kb0, kb1;
@@ -763,12 +789,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(ring + stage * Cfg::STAGE_BYTES);
-          const uint32_t b_base = a_base + Cfg::A_BYTES;
+          const uint32_t off = stage * Cfg::STAGE_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / UMMA_K; ++kk)
-            umma_tf32_pair(d_tmem, operand_desc(a_base, args.a_mn, kk),
-                           operand_desc(b_base, args.b_mn, kk), args.idesc,
+            umma_tf32_pair(d_tmem, desc_advance(a_desc0, off + kk * a_step),
+                           desc_advance(b_desc0, off + kk * b_step), args.idesc,
                            (kb > kb0 || kk > 0) ? 1u : 0u);
           umma_commit_pair(&ctrl->empty[stage], 0x3);
           if (++stage == STAGES) {
