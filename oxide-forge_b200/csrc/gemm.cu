@@ -71,7 +71,7 @@ struct EpiMaps {
 
 constexpr int EPI_TILE_BYTES = 32 * 32 * 4;  // one staging tile per warp and buffer
 
-template <int BN, int STAGES, bool SPLIT3, int NBUF>
+template <int BN, int STAGES, bool SPLIT3>
 struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 4;
   static constexpr int B_BYTES = BN * BK * 4;
@@ -79,7 +79,7 @@ struct GemmCfg {
   static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * OPS;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int CTRL_BYTES = 1024;
-  static constexpr int EPI_BYTES = EPI_WARPS * NBUF * EPI_TILE_BYTES;
+  static constexpr int EPI_BYTES = EPI_WARPS * EPI_TILE_BYTES;  // one staging tile per epilogue warp
   static constexpr int SMEM_BYTES = 1024 + CTRL_BYTES + STAGES * STAGE_BYTES + EPI_BYTES;
   static_assert(TMEM_COLS >= 32 && TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0,
                 "TMEM allocation must be a power of two in [32, 512]");
@@ -216,7 +216,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int b, int m, 
 }
 
 // ---------------------------------------------------------------- TMA epilogue
-// Each epilogue warp owns NBUF staging tiles of 32 rows x 128 B in the TMA
+// Each epilogue warp owns one staging tile of 32 rows x 128 B in the TMA
 // 128B-swizzle layout: 16-byte unit j of row r sits at unit j ^ (r & 7), so
 // the 32 lanes (lane = row) touching unit j of their rows hit every bank
 // once per 8 lanes. A lane only ever reads and writes its own row; the TMA
@@ -310,31 +310,37 @@ __device__ __forceinline__ bool epi_prefetch(const GemmArgs& a, const EpiMaps& e
 }
 
 // The fused epilogue of one warp's 32 x 32 chunk (rows m0.., columns n0..),
-// in the same arithmetic order as epilogue_chunk. `prefetched`: the first
-// input (epi_first_input) is already on its way into buffer 0. Returns false
-// if a staged load timed out.
-template <int NBUF>
+// in the same arithmetic order as epilogue_chunk, through the warp's one
+// staging tile. `prefetched`: the first input (epi_first_input) is already
+// on its way into the tile. Stores issued earlier may still be reading the
+// tile; the warp waits for them only right before it next writes the tile,
+// so the arithmetic in between overlaps those reads. Returns false if a
+// staged load timed out.
 __device__ __forceinline__ bool epilogue_chunk_tma(const GemmArgs& a, const EpiMaps& em, int b,
-                                                   int m0, int n0, float (&v)[32], uint8_t* bufs,
+                                                   int m0, int n0, float (&v)[32], uint8_t* buf,
                                                    uint64_t* bar, uint32_t& phase, int lane,
                                                    bool prefetched) {
   if (m0 >= a.M) return true;  // rows past the matrix (last tile): nothing to move
-  uint8_t* buf0 = bufs;
-  uint8_t* buf1 = bufs + (NBUF - 1) * EPI_TILE_BYTES;  // buf0 again when NBUF == 1
-  // The previous chunk's stores must be done with the buffers (a prefetch
-  // already waited for that before it was issued).
-  if (!prefetched) epi_buffers_free(lane);
-  bool busy0 = false;  // buf0 holds a store still in flight
+  bool in_use = !prefetched;   // a store may still be reading the tile
+  auto claim = [&] {
+    if (in_use) {
+      epi_buffers_free(lane);
+      in_use = false;
+    }
+  };
   if (a.alpha != 1.0f) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] *= a.alpha;
   }
   float t[32];
   if (a.beta != 0.0f) {
-    if (!prefetched) epi_issue(buf0, &em.c, a.c3d, bar, n0, m0, b, lane);
+    if (!prefetched) {
+      claim();
+      epi_issue(buf, &em.c, a.c3d, bar, n0, m0, b, lane);
+    }
     prefetched = false;
     if (!epi_wait(bar, phase)) return false;
-    stage_read_row(buf0, lane, t);
+    stage_read_row(buf, lane, t);
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] += a.beta * t[j];
   }
@@ -354,36 +360,35 @@ __device__ __forceinline__ bool epilogue_chunk_tma(const GemmArgs& a, const EpiM
     for (int j = 0; j < 32; ++j) v[j] += t[j];
   }
   if (a.R) {
-    if (!prefetched) epi_issue(buf0, &em.r, a.r3d, bar, n0, m0, b, lane);
+    if (!prefetched) {
+      claim();
+      epi_issue(buf, &em.r, a.r3d, bar, n0, m0, b, lane);
+    }
     prefetched = false;
     if (!epi_wait(bar, phase)) return false;
-    stage_read_row(buf0, lane, t);
+    stage_read_row(buf, lane, t);
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] += t[j];
   }
   if (a.P) {
-    stage_write_row(buf0, lane, v);
-    epi_store(buf0, &em.p, a.p3d, n0, m0, b, lane, false);
-    busy0 = true;
-  }
-  uint8_t* out = buf0;
-  if (busy0) {
-    if (NBUF == 1) {
-      epi_buffers_free(lane);
-      busy0 = false;
-    } else {
-      out = buf1;
-    }
+    claim();
+    stage_write_row(buf, lane, v);
+    epi_store(buf, &em.p, a.p3d, n0, m0, b, lane, false);
+    in_use = true;
   }
   if (a.X) {
-    if (!prefetched) epi_issue(out, &em.x, a.x3d, bar, n0, m0, b, lane);
+    if (!prefetched) {  // aux is prefetched only when there is no pre-activation store
+      claim();
+      epi_issue(buf, &em.x, a.x3d, bar, n0, m0, b, lane);
+    }
     if (!epi_wait(bar, phase)) return false;
-    stage_read_row(out, lane, t);
+    stage_read_row(buf, lane, t);
     act_grad_chunk(a.grad_act, v, t);
   }
   act_forward_chunk(a.act, v);
-  stage_write_row(out, lane, v);
-  epi_store(out, &em.c, a.c3d, n0, m0, b, lane, a.accumulate != 0);
+  claim();
+  stage_write_row(buf, lane, v);
+  epi_store(buf, &em.c, a.c3d, n0, m0, b, lane, a.accumulate != 0);
   return true;
 }
 
@@ -409,14 +414,14 @@ __device__ __forceinline__ bool epi_next_chunk(const GemmArgs& a, long long u, l
   return nn0 < a.N;
 }
 
-template <int BN, int STAGES, bool SPLIT3, int NBUF>
+template <int BN, int STAGES, bool SPLIT3>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tf32_tcgen05(const __grid_constant__ CUtensorMap tmA,
                       const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmA_lo,
                       const __grid_constant__ CUtensorMap tmB_lo,
                       const __grid_constant__ EpiMaps em, const GemmArgs args) {
-  using Cfg = GemmCfg<BN, STAGES, SPLIT3, NBUF>;
+  using Cfg = GemmCfg<BN, STAGES, SPLIT3>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -571,7 +576,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;  // which alternate 32-column chunks it takes
     const int row_local = quarter * 32 + lane;
-    uint8_t* bufs = ring + STAGES * Cfg::STAGE_BYTES + (warp - 2) * NBUF * EPI_TILE_BYTES;
+    uint8_t* bufs = ring + STAGES * Cfg::STAGE_BYTES + (warp - 2) * EPI_TILE_BYTES;
     uint64_t* ebar = &ctrl->epi[warp - 2];
     uint32_t ephase = 0;
     bool ok = true, pf = false;  // pf: the next chunk's first input is being loaded
@@ -597,7 +602,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), v);
         if (args.epi_tma) {
           const int m0 = tm * BM + quarter * 32;
-          if (!epilogue_chunk_tma<NBUF>(args, em, b, m0, n0, v, bufs, ebar, ephase, lane,
+          if (!epilogue_chunk_tma(args, em, b, m0, n0, v, bufs, ebar, ephase, lane,
                                         pf)) {
             ctrl->abort_flag = 1;
             ok = pf = false;
@@ -635,14 +640,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 // CTA's full barrier, the leader alone issues the MMAs and multicast-commits
 // to both CTAs' barriers, and each CTA's epilogue drains its own 128 TMEM
 // lanes and releases the accumulator to the leader with a remote arrive.
-template <int BN, int STAGES, int NBUF>
+template <int BN, int STAGES>
 struct GemmPairCfg {
   static constexpr int A_BYTES = BM * BK * 4;
   static constexpr int B_BYTES = (BN / 2) * BK * 4;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int CTRL_BYTES = 1024;
-  static constexpr int EPI_BYTES = EPI_WARPS * NBUF * EPI_TILE_BYTES;
+  static constexpr int EPI_BYTES = EPI_WARPS * EPI_TILE_BYTES;  // one staging tile per epilogue warp
   static constexpr int SMEM_BYTES = 1024 + CTRL_BYTES + STAGES * STAGE_BYTES + EPI_BYTES;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
   static_assert(TMEM_COLS <= 512 && BN % 64 == 0, "tile shape");
@@ -668,12 +673,12 @@ __device__ __forceinline__ void load_operand_pair(uint8_t* dst, const CUtensorMa
   }
 }
 
-template <int BN, int STAGES, int NBUF>
+template <int BN, int STAGES>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     gemm_tf32_tcgen05_pair(const __grid_constant__ CUtensorMap tmA,
                            const __grid_constant__ CUtensorMap tmB,
                            const __grid_constant__ EpiMaps em, const GemmArgs args) {
-  using Cfg = GemmPairCfg<BN, STAGES, NBUF>;
+  using Cfg = GemmPairCfg<BN, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -809,7 +814,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row_local = quarter * 32 + lane;
-    uint8_t* bufs = ring + STAGES * Cfg::STAGE_BYTES + (warp - 2) * NBUF * EPI_TILE_BYTES;
+    uint8_t* bufs = ring + STAGES * Cfg::STAGE_BYTES + (warp - 2) * EPI_TILE_BYTES;
     uint64_t* ebar = &ctrl->epi[warp - 2];
     uint32_t ephase = 0;
     bool ok = true, pf = false;  // pf: the next chunk's first input is being loaded
@@ -836,7 +841,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
         tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), v);
         if (args.epi_tma) {
           const int m0 = m_base + quarter * 32;
-          if (!epilogue_chunk_tma<NBUF>(args, em, b, m0, n0, v, bufs, ebar, ephase, lane, pf)) {
+          if (!epilogue_chunk_tma(args, em, b, m0, n0, v, bufs, ebar, ephase, lane, pf)) {
             ctrl->abort_flag = 1;
             ok = pf = false;
             break;
@@ -1107,14 +1112,14 @@ bool encode_map(CUtensorMap* map, const float* ptr, long long inner, long long o
   return r == CUDA_SUCCESS;
 }
 
-template <int BN, int STAGES, bool SPLIT3, int NBUF>
+template <int BN, int STAGES, bool SPLIT3>
 oxf_status launch_tcgen05(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta_lo,
                           const CUtensorMap& tb_lo, const EpiMaps& em, GemmArgs& args,
                           cudaStream_t stream, int dev) {
-  using Cfg = GemmCfg<BN, STAGES, SPLIT3, NBUF>;
+  using Cfg = GemmCfg<BN, STAGES, SPLIT3>;
   static bool configured[kMaxDevices] = {false};
   if (dev >= 0 && dev < kMaxDevices && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tf32_tcgen05<BN, STAGES, SPLIT3, NBUF>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_tf32_tcgen05<BN, STAGES, SPLIT3>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg::SMEM_BYTES);
     if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(gemm)");
@@ -1122,19 +1127,19 @@ oxf_status launch_tcgen05(const CUtensorMap& ta, const CUtensorMap& tb, const CU
   }
   args.idesc = make_idesc_tf32(BM, BN, args.a_mn != 0, args.b_mn != 0);
   const long long grid = std::min<long long>(args.units, sm_count(dev));
-  gemm_tf32_tcgen05<BN, STAGES, SPLIT3, NBUF>
+  gemm_tf32_tcgen05<BN, STAGES, SPLIT3>
       <<<static_cast<unsigned>(grid), GEMM_THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, ta_lo,
                                                                               tb_lo, em, args);
   return check_launch("gemm_tf32_tcgen05");
 }
 
-template <int BN, int STAGES, int NBUF>
+template <int BN, int STAGES>
 oxf_status launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const EpiMaps& em,
                        GemmArgs& args, cudaStream_t stream, int dev) {
-  using Cfg = GemmPairCfg<BN, STAGES, NBUF>;
+  using Cfg = GemmPairCfg<BN, STAGES>;
   static bool configured[kMaxDevices] = {false};
   if (dev >= 0 && dev < kMaxDevices && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tf32_tcgen05_pair<BN, STAGES, NBUF>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_tf32_tcgen05_pair<BN, STAGES>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg::SMEM_BYTES);
     if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(gemm pair)");
@@ -1142,7 +1147,7 @@ oxf_status launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const EpiMa
   }
   args.idesc = make_idesc_tf32(2 * BM, BN, args.a_mn != 0, args.b_mn != 0);
   const long long clusters = std::min<long long>(args.units, sm_count(dev) / 2);
-  gemm_tf32_tcgen05_pair<BN, STAGES, NBUF><<<static_cast<unsigned>(2 * clusters), GEMM_THREADS,
+  gemm_tf32_tcgen05_pair<BN, STAGES><<<static_cast<unsigned>(2 * clusters), GEMM_THREADS,
                                              Cfg::SMEM_BYTES, stream>>>(ta, tb, em, args);
   return check_launch("gemm_tf32_tcgen05_pair");
 }
@@ -1405,11 +1410,11 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
     a.epi_tma = eok ? 1 : 0;
   }
 
-  if (split3) return launch_tcgen05<128, 3, true, 1>(ta, tb, ta_lo, tb_lo, em, a, stream, dev);
-  if (pair) return launch_pair<256, 6, 1>(ta, tb, em, a, stream, dev);
-  if (BN == 256) return launch_tcgen05<256, 4, false, 1>(ta, tb, ta, tb, em, a, stream, dev);
-  if (BN == 128) return launch_tcgen05<128, 6, false, 1>(ta, tb, ta, tb, em, a, stream, dev);
-  return launch_tcgen05<64, 8, false, 1>(ta, tb, ta, tb, em, a, stream, dev);
+  if (split3) return launch_tcgen05<128, 3, true>(ta, tb, ta_lo, tb_lo, em, a, stream, dev);
+  if (pair) return launch_pair<256, 6>(ta, tb, em, a, stream, dev);
+  if (BN == 256) return launch_tcgen05<256, 4, false>(ta, tb, ta, tb, em, a, stream, dev);
+  if (BN == 128) return launch_tcgen05<128, 6, false>(ta, tb, ta, tb, em, a, stream, dev);
+  return launch_tcgen05<64, 8, false>(ta, tb, ta, tb, em, a, stream, dev);
 }
 
 // ---------------------------------------------------------------- no-allocation variant
