@@ -39,6 +39,7 @@ constexpr int BM = 128;       // tile rows (TMEM lanes)
 constexpr int BK = 32;        // K elements per ring slot: 32 x f32 = one 128-byte swizzle row
 constexpr int UMMA_K = 8;     // K per tcgen05.mma.kind::tf32
 constexpr int EPI_WARPS = 8;  // warps 2..9: two per TMEM lane quarter, splitting columns
+constexpr int EPI_GROUPS = EPI_WARPS / 4;  // warps per lane quarter (take alternate chunks)
 constexpr int GEMM_THREADS = 64 + 32 * EPI_WARPS;
 
 struct GemmArgs {
@@ -397,12 +398,13 @@ __device__ __forceinline__ bool epilogue_chunk_tma(const GemmArgs& a, const EpiM
 // unit its CTA (pair) owns. Rows of a unit start at tm * a.bm + row_off.
 template <int BN>
 __device__ __forceinline__ bool epi_next_chunk(const GemmArgs& a, long long u, long long stride,
-                                               int c, int half, int row_off, int b, int tn,
+                                               int c, int group, int row_off, int b, int tn,
                                                int m0, int& nb, int& nm0, int& nn0) {
-  if (c + 2 < BN / 32 && tn * BN + (c + 2) * 32 < a.N) {
+  const int c2 = c + EPI_GROUPS;
+  if (c2 < BN / 32 && tn * BN + c2 * 32 < a.N) {
     nb = b;
     nm0 = m0;
-    nn0 = tn * BN + (c + 2) * 32;
+    nn0 = tn * BN + c2 * 32;
     return true;
   }
   const long long u2 = u + stride;
@@ -410,7 +412,7 @@ __device__ __forceinline__ bool epi_next_chunk(const GemmArgs& a, long long u, l
   int tm2, tn2, kb0, kb1;
   decode_unit(a, u2, nb, tm2, tn2, kb0, kb1);
   nm0 = tm2 * a.bm + row_off;
-  nn0 = tn2 * BN + half * 32;
+  nn0 = tn2 * BN + group * 32;
   return nn0 < a.N;
 }
 
@@ -574,7 +576,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const int half = (warp - 2) >> 2;  // which alternate 32-column chunks it takes
+    const int group = (warp - 2) / 4;  // which alternate 32-column chunks it takes
     const int row_local = quarter * 32 + lane;
     uint8_t* bufs = ring + STAGES * Cfg::STAGE_BYTES + (warp - 2) * EPI_TILE_BYTES;
     uint64_t* ebar = &ctrl->epi[warp - 2];
@@ -595,7 +597,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(acc_slot * BN);
 #pragma unroll 1
-      for (int c = half; c < BN / 32; c += 2) {
+      for (int c = group; c < BN / 32; c += EPI_GROUPS) {
         const int n0 = tn * BN + c * 32;
         if (n0 >= args.N) break;  // uniform across the warp
         float v[32];
@@ -609,7 +611,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             break;
           }
           int nb, nm0, nn0;
-          pf = epi_next_chunk<BN>(args, u, gridDim.x, c, half, quarter * 32, b, tn, m0, nb, nm0,
+          pf = epi_next_chunk<BN>(args, u, gridDim.x, c, group, quarter * 32, b, tn, m0, nb, nm0,
                                   nn0) &&
                epi_prefetch(args, em, bufs, ebar, nb, nm0, nn0, lane);
         } else if (m < args.M) {
@@ -812,7 +814,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     }
   } else {
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int group = (warp - 2) / 4;
     const int row_local = quarter * 32 + lane;
     uint8_t* bufs = ring + STAGES * Cfg::STAGE_BYTES + (warp - 2) * EPI_TILE_BYTES;
     uint64_t* ebar = &ctrl->epi[warp - 2];
@@ -834,7 +836,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(acc_slot * BN);
 #pragma unroll 1
-      for (int c = half; c < BN / 32; c += 2) {
+      for (int c = group; c < BN / 32; c += EPI_GROUPS) {
         const int n0 = tn * BN + c * 32;
         if (n0 >= args.N) break;
         float v[32];
@@ -847,7 +849,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
             break;
           }
           int nb, nm0, nn0;
-          pf = epi_next_chunk<BN>(args, u, nclusters, c, half,
+          pf = epi_next_chunk<BN>(args, u, nclusters, c, group,
                                   static_cast<int>(rank) * BM + quarter * 32, b, tn, m0, nb, nm0,
                                   nn0) &&
                epi_prefetch(args, em, bufs, ebar, nb, nm0, nn0, lane);
