@@ -113,6 +113,23 @@ oxf_status oxf_loss_rows(oxf_cslice y, oxf_cslice target, oxf_slice row_loss, si
 oxf_status oxf_slice_sum(oxf_cslice span, float* result, oxf_stream stream);
 /* slice_max (module.rs:92-97, span.rs:318-333); empty -> f32::MIN. */
 oxf_status oxf_slice_max(oxf_cslice span, float* result, oxf_stream stream);
+/* slice_map_sum (module.rs:79-90, reduction.rs:44-80, span.rs:335-359):
+ * *result = sum_i f(span[i]), the closure given as an oxf_unary_op with
+ * its parameter (as oxf_slice_unary). */
+oxf_status oxf_slice_map_sum(oxf_cslice span, oxf_unary_op op, float param, float* result,
+                             oxf_stream stream);
+
+/* ---------------------------------------------------------------- fills */
+/* slice_set (module.rs:15-20): every element = value. */
+oxf_status oxf_slice_set(oxf_slice target, float value, oxf_stream stream);
+/* slice_set_seq (module.rs:22-27, elementwise.rs:24-35): element i = i
+ * (dir != 0) or len - i, as f32. */
+oxf_status oxf_slice_set_seq(oxf_slice target, int dir, oxf_stream stream);
+/* slice_set_random (module.rs:29-34, elementwise.rs:37-43): element i =
+ * h(seed + i) / (float)UINT32_MAX with the reference's hash h
+ * (common.rs:3-9: x += x<<13; x -= x>>17; x *= x<<5, wrapping 32-bit), so
+ * the same seed fills the same values as the reference. */
+oxf_status oxf_slice_set_random(oxf_slice target, uint32_t seed, oxf_stream stream);
 /* matrix_sum_rows (module.rs:102-108): result[r] = sum_j M[r,j]. */
 oxf_status oxf_matrix_sum_rows(oxf_cslice matrix, oxf_slice result, size_t cols,
                                oxf_stream stream);
@@ -168,6 +185,14 @@ oxf_status oxf_matrix_binary_assign_by_rows(oxf_slice matrix, oxf_cslice row, si
                                             oxf_binary_op op, oxf_stream stream);
 /* matrix_causal_mask (module.rs:245-250): M[i,j] = -inf for j > i. */
 oxf_status oxf_matrix_causal_mask(oxf_slice matrix, size_t cols, oxf_stream stream);
+/* matrix_slice (module.rs:208-227, layout.rs:58-86, container/convert.rs:
+ * 105-130): cuts a matrix with input_cols columns into tile_rows x
+ * tile_cols tiles, tiles_per_row of them per row of tiles, and writes them
+ * one after another (each row-major) into output; output.len / (tile_rows *
+ * tile_cols) tiles are taken. Tiles reaching past the input are refused. */
+oxf_status oxf_matrix_slice(oxf_cslice input, oxf_slice output, size_t input_cols,
+                            size_t tile_rows, size_t tile_cols, size_t tiles_per_row,
+                            oxf_stream stream);
 /* matrix_transpose (module.rs:193-203): out[cols,rows] = in[rows,cols]^T. */
 oxf_status oxf_matrix_transpose(oxf_cslice input, oxf_slice result, size_t rows, size_t cols,
                                 oxf_stream stream);

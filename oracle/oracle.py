@@ -60,6 +60,11 @@ def lib() -> C.CDLL:
             "oxo_sum_rows": (None, [fp, fp, sz, sz]),
             "oxo_sum_cols": (None, [fp, fp, sz, sz]),
             "oxo_transpose": (None, [fp, fp, sz, sz]),
+            "oxo_fill_seq": (None, [fp, sz, C.c_int]),
+            "oxo_fill_random": (None, [fp, sz, C.c_uint32]),
+            "oxo_unary": (C.c_float, [C.c_int, C.c_float, C.c_float]),
+            "oxo_map_sum": (C.c_float, [fp, sz, C.c_int, C.c_float]),
+            "oxo_matrix_slice": (None, [fp, fp, sz, sz, sz, sz, sz]),
             "oxo_causal_mask": (None, [fp, sz, sz, sz]),
             "oxo_softmax_rows": (None, [fp, sz, sz, C.c_float, sz]),
             "oxo_layer_norm_rows": (None, [fp, sz, sz, C.c_float, fp, fp]),
@@ -170,6 +175,31 @@ def transpose(m):
     m = _c(m)
     out = np.empty((m.shape[1], m.shape[0]), F32)
     lib().oxo_transpose(_p(m), _p(out), m.shape[0], m.shape[1])
+    return out
+
+
+def fill_seq(n, ascending=True):
+    out = np.empty(n, F32)
+    lib().oxo_fill_seq(_p(out), n, int(bool(ascending)))
+    return out
+
+
+def fill_random(n, seed):
+    out = np.empty(n, F32)
+    lib().oxo_fill_random(_p(out), n, int(seed) & 0xFFFFFFFF)
+    return out
+
+
+def map_sum(x, op, param=0.0):
+    x = _c(x)
+    return float(lib().oxo_map_sum(_p(x), x.size, op, param))
+
+
+def matrix_slice(m, tile_rows, tile_cols, tiles_per_row, n_tiles):
+    m = _c(m)
+    out = np.empty(n_tiles * tile_rows * tile_cols, F32)
+    lib().oxo_matrix_slice(_p(m), _p(out), out.size, m.shape[1], tile_rows, tile_cols,
+                           tiles_per_row)
     return out
 
 

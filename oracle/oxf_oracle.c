@@ -307,6 +307,63 @@ void oxo_activate(float* x, size_t n, int act) {
 /* ------------------------------------------------------------------------ */
 /* row kernels                                                               */
 
+/* slice_set_device, slice_set_seq_device, slice_set_random_device
+ * (elementwise.rs:15-43) with the hash of common.rs:3-9 (wrapping u32). */
+void oxo_fill(float* out, size_t n, float value) {
+    for (size_t i = 0; i < n; ++i) out[i] = value;
+}
+
+void oxo_fill_seq(float* out, size_t n, int dir) {
+    for (size_t i = 0; i < n; ++i) out[i] = dir ? (float)i : (float)(n - i);
+}
+
+static uint32_t ref_hash(uint32_t x) {
+    x += x << 13;
+    x -= x >> 17;
+    x *= x << 5;
+    return x;
+}
+
+void oxo_fill_random(float* out, size_t n, uint32_t seed) {
+    const float denom = (float)UINT32_MAX;  /* u32::MAX as f32 = 2^32 */
+    for (size_t i = 0; i < n; ++i) out[i] = (float)ref_hash(seed + (uint32_t)i) / denom;
+}
+
+float oxo_unary(int op, float x, float p) {
+    switch (op) {
+        case 0: return x * p;
+        case 1: return x + p;
+        case 2: return oxo_act_forward((int)p, x);
+        case 3: return oxo_act_derivative((int)p, x);
+        default: return 0.5f * x * x;
+    }
+}
+
+/* slice_map_sum_device, reduction.rs:44-80 (a shuffle tree per block; the
+ * pairwise sum restates the tree's order of magnitude of rounding). */
+float oxo_map_sum(const float* x, size_t n, int op, float p) {
+    if (n == 0) return 0.0f;
+    float* t = (float*)malloc(n * sizeof(float));
+    if (!t) return 0.0f;
+    for (size_t i = 0; i < n; ++i) t[i] = oxo_unary(op, x[i], p);
+    const float s = psum(t, n);
+    free(t);
+    return s;
+}
+
+/* matrix_slice_device, layout.rs:58-86. */
+void oxo_matrix_slice(const float* in, float* out, size_t out_len, size_t input_cols,
+                      size_t tile_rows, size_t tile_cols, size_t tiles_per_row) {
+    const size_t tile = tile_rows * tile_cols;
+    for (size_t l = 0; l < out_len; ++l) {
+        const size_t ti = l / tile, local = l % tile;
+        const size_t ty = ti / tiles_per_row, tx = ti % tiles_per_row;
+        const size_t r = ty * tile_rows + local / tile_cols;
+        const size_t c = tx * tile_cols + local % tile_cols;
+        out[l] = in[r * input_cols + c];
+    }
+}
+
 /* matrix_sum_rows_device, row.rs:16-53. */
 void oxo_sum_rows(const float* m, float* out, size_t rows, size_t cols) {
     for (size_t r = 0; r < rows; ++r) out[r] = psum(m + r * cols, cols);

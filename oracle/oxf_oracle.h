@@ -70,6 +70,24 @@ float oxo_act_forward(int act, float x);
 float oxo_act_derivative(int act, float x);
 void oxo_activate(float* x, size_t n, int act);
 
+/* Fills, elementwise.rs:15-43: slice_set, slice_set_seq (element i = i, or
+ * len - i), slice_set_random (hash of seed + i, common.rs:3-9, scaled by
+ * 1 / (float)UINT32_MAX). */
+void oxo_fill(float* out, size_t n, float value);
+void oxo_fill_seq(float* out, size_t n, int dir);
+void oxo_fill_random(float* out, size_t n, uint32_t seed);
+/* The closures the reference passes to slice_for_each / slice_map_sum, as
+ * the enumerated oxf_unary_op set: 0 x*p, 1 x+p, 2 act(x) (p = activation),
+ * 3 act'(x), 4 0.5*x*x. */
+float oxo_unary(int op, float x, float p);
+/* slice_map_sum, reduction.rs:44-80: sum of f(x_i) (pairwise). */
+float oxo_map_sum(const float* x, size_t n, int op, float p);
+/* matrix_slice, layout.rs:58-86: output element l belongs to tile l / (tr*tc)
+ * (tile row = tile / tiles_per_row, tile column = tile % tiles_per_row) at
+ * local row (l % (tr*tc)) / tc, local column (l % (tr*tc)) % tc. */
+void oxo_matrix_slice(const float* in, float* out, size_t out_len, size_t input_cols,
+                      size_t tile_rows, size_t tile_cols, size_t tiles_per_row);
+
 /* row.rs:16-53 (per-row sum). */
 void oxo_sum_rows(const float* m, float* out, size_t rows, size_t cols);
 /* Column sum = sum_rows(transpose(G)), linear.rs:267-270. */

@@ -43,7 +43,11 @@ oxf_status ew_by_rows(float*, const float*, long long, long long, int, cudaStrea
 oxf_status causal_mask(float*, long long, long long, cudaStream_t);
 oxf_status cols_sum(const float*, float*, long long, long long, int, cudaStream_t);
 oxf_status transpose(const float*, float*, long long, long long, cudaStream_t);
-oxf_status slice_reduce(const float*, long long, float*, int, cudaStream_t);
+oxf_status slice_reduce(const float*, long long, float*, int, cudaStream_t, int map_op = -1,
+                        float map_p = 0.f);
+oxf_status fill_slice(float*, long long, int, float, int, uint32_t, cudaStream_t);
+oxf_status matrix_slice(const float*, float*, long long, long long, long long, long long,
+                        long long, cudaStream_t);
 // gemm.cu
 oxf_status gemm_run(const oxf_gemm_desc*, cudaStream_t);
 size_t gemm_workspace_bytes(const oxf_gemm_desc*);
@@ -195,6 +199,36 @@ oxf_status oxf_slice_max(oxf_cslice span, float* result, oxf_stream stream) {
   return slice_reduce(span.ptr, static_cast<long long>(span.len), result, 1, S(stream));
 }
 
+oxf_status oxf_slice_map_sum(oxf_cslice span, oxf_unary_op op, float param, float* result,
+                             oxf_stream stream) {
+  OXF_TRY(need(result != nullptr, "oxf_slice_map_sum: null result"));
+  if (op < OXF_UNARY_SCALE || op > OXF_UNARY_HALF_SQUARE)
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_slice_map_sum: bad op");
+  if ((op == OXF_UNARY_ACT_FORWARD || op == OXF_UNARY_ACT_DERIV) &&
+      !valid_act(static_cast<int>(param)))
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_slice_map_sum: bad activation");
+  if (span.len && !span.ptr) return set_error(OXF_ERR_INVALID_ARG, "oxf_slice_map_sum: null");
+  return slice_reduce(span.ptr, static_cast<long long>(span.len), result, 0, S(stream),
+                      static_cast<int>(op), param);
+}
+
+oxf_status oxf_slice_set(oxf_slice target, float value, oxf_stream stream) {
+  if (target.len && !target.ptr) return set_error(OXF_ERR_INVALID_ARG, "oxf_slice_set: null");
+  return fill_slice(target.ptr, static_cast<long long>(target.len), 0, value, 0, 0, S(stream));
+}
+
+oxf_status oxf_slice_set_seq(oxf_slice target, int dir, oxf_stream stream) {
+  if (target.len && !target.ptr) return set_error(OXF_ERR_INVALID_ARG, "oxf_slice_set_seq: null");
+  return fill_slice(target.ptr, static_cast<long long>(target.len), 1, 0.f, dir != 0, 0,
+                    S(stream));
+}
+
+oxf_status oxf_slice_set_random(oxf_slice target, uint32_t seed, oxf_stream stream) {
+  if (target.len && !target.ptr)
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_slice_set_random: null");
+  return fill_slice(target.ptr, static_cast<long long>(target.len), 2, 0.f, 0, seed, S(stream));
+}
+
 oxf_status oxf_matrix_sum_rows(oxf_cslice matrix, oxf_slice result, size_t cols,
                                oxf_stream stream) {
   long long rows = 0;
@@ -329,6 +363,28 @@ oxf_status oxf_matrix_causal_mask(oxf_slice matrix, size_t cols, oxf_stream stre
   long long rows = 0;
   OXF_TRY(rows_of(matrix.len, cols, &rows, "oxf_matrix_causal_mask"));
   return causal_mask(matrix.ptr, rows, static_cast<long long>(cols), S(stream));
+}
+
+oxf_status oxf_matrix_slice(oxf_cslice input, oxf_slice output, size_t input_cols,
+                            size_t tile_rows, size_t tile_cols, size_t tiles_per_row,
+                            oxf_stream stream) {
+  OXF_TRY(need(tile_rows > 0 && tile_cols > 0 && tiles_per_row > 0,
+               "oxf_matrix_slice: tile sizes must be positive"));
+  const size_t tile = tile_rows * tile_cols;
+  OXF_TRY(need(output.len % tile == 0, "oxf_matrix_slice: output is not a whole number of tiles"));
+  OXF_TRY(need(tiles_per_row * tile_cols <= input_cols,
+               "oxf_matrix_slice: tiles_per_row * tile_cols exceeds input_cols"));
+  if (output.len) {
+    const size_t tiles = output.len / tile;
+    const size_t last_row = ((tiles - 1) / tiles_per_row + 1) * tile_rows - 1;
+    OXF_TRY(need((last_row + 1) * input_cols <= input.len,
+                 "oxf_matrix_slice: tiles reach past the input matrix"));
+    if (!input.ptr || !output.ptr) return set_error(OXF_ERR_INVALID_ARG, "oxf_matrix_slice: null");
+  }
+  return matrix_slice(input.ptr, output.ptr, static_cast<long long>(output.len),
+                      static_cast<long long>(input_cols), static_cast<long long>(tile_rows),
+                      static_cast<long long>(tile_cols), static_cast<long long>(tiles_per_row),
+                      S(stream));
 }
 
 oxf_status oxf_matrix_transpose(oxf_cslice input, oxf_slice result, size_t rows, size_t cols,

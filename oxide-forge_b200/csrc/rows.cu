@@ -696,18 +696,62 @@ __device__ __forceinline__ void atomic_max_float(float* addr, float v) {
 __global__ void fill_kernel(float* p, float v) { *p = v; }
 
 // One-launch reductions (the reference re-launches slice_sum from the host
-// until one element is left, span.rs:361-385).
+// until one element is left, span.rs:361-385). map_op >= 0 sums
+// unary_apply(map_op, x, map_p) instead of x (slice_map_sum).
 __global__ void slice_reduce_kernel(const float* __restrict__ x, long long n, float* result,
-                                    int is_max) {
+                                    int is_max, int map_op, float map_p) {
   __shared__ float red[32];
   float acc = is_max ? -FLT_MAX : 0.f;
   for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-       i += static_cast<long long>(gridDim.x) * blockDim.x)
-    acc = is_max ? fmaxf(acc, x[i]) : acc + x[i];
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float v = map_op >= 0 ? unary_apply(map_op, x[i], map_p) : x[i];
+    acc = is_max ? fmaxf(acc, v) : acc + v;
+  }
   acc = is_max ? block_max(acc, red) : block_sum(acc, red);
   if (threadIdx.x == 0) {
     if (is_max) atomic_max_float(result, acc);
     else atomicAdd(result, acc);
+  }
+}
+
+// slice_set / slice_set_seq / slice_set_random (elementwise.rs:15-43).
+enum FillKind { FILL_VALUE, FILL_SEQ, FILL_RANDOM };
+
+// The reference's integer hash (common.rs:3-9), wrapping 32-bit arithmetic.
+__device__ __forceinline__ uint32_t ref_hash(uint32_t x) {
+  x += x << 13;
+  x -= x >> 17;
+  x *= x << 5;
+  return x;
+}
+
+__global__ void fill_slice_kernel(float* __restrict__ out, long long n, int kind, float value,
+                                  int dir, uint32_t seed) {
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    float v = value;
+    if (kind == FILL_SEQ) {
+      v = dir ? static_cast<float>(i) : static_cast<float>(n - i);
+    } else if (kind == FILL_RANDOM) {
+      // (hash as f32) / (u32::MAX as f32); u32::MAX rounds to 2^32 in f32.
+      v = static_cast<float>(ref_hash(seed + static_cast<uint32_t>(i))) / 4294967296.0f;
+    }
+    out[i] = v;
+  }
+}
+
+// matrix_slice (layout.rs:58-86): output element l of tile l / (tr*tc).
+__global__ void matrix_slice_kernel(const float* __restrict__ in, float* __restrict__ out,
+                                    long long n, long long input_cols, long long tile_rows,
+                                    long long tile_cols, long long tiles_per_row) {
+  const long long tile = tile_rows * tile_cols;
+  for (long long l = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; l < n;
+       l += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long ti = l / tile, local = l - ti * tile;
+    const long long ty = ti / tiles_per_row, tx = ti - ty * tiles_per_row;
+    const long long r = ty * tile_rows + local / tile_cols;
+    const long long c = tx * tile_cols + local % tile_cols;
+    out[l] = in[r * input_cols + c];
   }
 }
 
@@ -976,14 +1020,31 @@ oxf_status transpose(const float* in, float* out, long long rows, long long cols
   return check_launch("transpose_kernel");
 }
 
-oxf_status slice_reduce(const float* x, long long n, float* result, int is_max, cudaStream_t s) {
+oxf_status slice_reduce(const float* x, long long n, float* result, int is_max, cudaStream_t s,
+                        int map_op, float map_p) {
   fill_kernel<<<1, 1, 0, s>>>(result, is_max ? -FLT_MAX : 0.f);
   count_launch();
   if (n > 0) {
     const unsigned blocks = ew_blocks((n + 3) / 4);
-    slice_reduce_kernel<<<blocks, 256, 0, s>>>(x, n, result, is_max);
+    slice_reduce_kernel<<<blocks, 256, 0, s>>>(x, n, result, is_max, map_op, map_p);
   }
   return check_launch("slice_reduce_kernel");
+}
+
+oxf_status fill_slice(float* out, long long n, int kind, float value, int dir, uint32_t seed,
+                      cudaStream_t s) {
+  if (n <= 0) return OXF_OK;
+  fill_slice_kernel<<<ew_blocks(n), 256, 0, s>>>(out, n, kind, value, dir, seed);
+  return check_launch("fill_slice_kernel");
+}
+
+oxf_status matrix_slice(const float* in, float* out, long long n, long long input_cols,
+                        long long tile_rows, long long tile_cols, long long tiles_per_row,
+                        cudaStream_t s) {
+  if (n <= 0) return OXF_OK;
+  matrix_slice_kernel<<<ew_blocks(n), 256, 0, s>>>(in, out, n, input_cols, tile_rows, tile_cols,
+                                                  tiles_per_row);
+  return check_launch("matrix_slice_kernel");
 }
 
 }  // namespace oxf

@@ -75,6 +75,12 @@ _SIGS = {
     "oxf_mse_loss_grad": (C.c_int, [CSlice, CSlice, Slice, Slice, C.c_size_t, C.c_void_p]),
     "oxf_slice_sum": (C.c_int, [CSlice, C.c_void_p, C.c_void_p]),
     "oxf_slice_max": (C.c_int, [CSlice, C.c_void_p, C.c_void_p]),
+    "oxf_slice_map_sum": (C.c_int, [CSlice, C.c_int, C.c_float, C.c_void_p, C.c_void_p]),
+    "oxf_slice_set": (C.c_int, [Slice, C.c_float, C.c_void_p]),
+    "oxf_slice_set_seq": (C.c_int, [Slice, C.c_int, C.c_void_p]),
+    "oxf_slice_set_random": (C.c_int, [Slice, C.c_uint32, C.c_void_p]),
+    "oxf_matrix_slice": (C.c_int, [CSlice, Slice, C.c_size_t, C.c_size_t, C.c_size_t, C.c_size_t,
+                                   C.c_void_p]),
     "oxf_matrix_sum_rows": (C.c_int, [CSlice, Slice, C.c_size_t, C.c_void_p]),
     "oxf_matrix_sum_cols": (C.c_int, [CSlice, Slice, C.c_size_t, C.c_int, C.c_void_p]),
     "oxf_matrix_softmax_rows": (C.c_int, [Slice, C.c_size_t, C.c_float, C.c_size_t, C.c_void_p]),

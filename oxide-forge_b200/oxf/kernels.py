@@ -89,6 +89,35 @@ def slice_max(x, out, stream=None):
     return out
 
 
+def map_sum(x, op, param, out, stream=None):
+    """slice_map_sum: out[0] = sum of the unary op applied to x."""
+    check(lib().oxf_slice_map_sum(cs(x), op, float(param), ptr(out), _stream(stream)))
+    return out
+
+
+def fill(x, value, stream=None):
+    check(lib().oxf_slice_set(ms(x), float(value), _stream(stream)))
+    return x
+
+
+def fill_seq(x, ascending=True, stream=None):
+    check(lib().oxf_slice_set_seq(ms(x), int(bool(ascending)), _stream(stream)))
+    return x
+
+
+def fill_random(x, seed, stream=None):
+    check(lib().oxf_slice_set_random(ms(x), int(seed) & 0xFFFFFFFF, _stream(stream)))
+    return x
+
+
+def matrix_slice(m, out, tile_rows, tile_cols, tiles_per_row, stream=None):
+    """matrix_slice: tiles of m (2-D) concatenated into out (1-D or any
+    contiguous shape holding a whole number of tiles)."""
+    check(lib().oxf_matrix_slice(cs(m), ms(out), m.shape[-1], tile_rows, tile_cols, tiles_per_row,
+                                 _stream(stream)))
+    return out
+
+
 def sum_rows(m, out, stream=None):
     check(lib().oxf_matrix_sum_rows(cs(m), ms(out), m.shape[-1], _stream(stream)))
     return out

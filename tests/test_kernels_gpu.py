@@ -206,3 +206,43 @@ def test_mse_loss_grad_fused(K, rng):
         K.mse_loss_grad(dev(y), dev(t), loss, dy)
         assert rel_err(host(loss), O.loss_rows(y, t)) < TOL
         assert rel_err(host(dy), O.mse_grad(y, t)) < TOL
+
+
+@pytest.mark.parametrize("n", [0, 1, 1000, (1 << 25) + 3])
+def test_fills_match_reference_bitwise(K, n):
+    """slice_set / slice_set_seq / slice_set_random: identical values to the
+    oracle's restatement of elementwise.rs:15-43 (seq rounds large indices
+    to f32 the same way)."""
+    x = torch.empty(n, device="cuda")
+    K.fill(x, 2.5)
+    assert (host(x) == 2.5).all()
+    for asc in (True, False):
+        K.fill_seq(x, asc)
+        np.testing.assert_array_equal(host(x), O.fill_seq(n, asc))
+    for seed in (0, 12345, 0xFFFFFFF0):
+        K.fill_random(x, seed)
+        np.testing.assert_array_equal(host(x), O.fill_random(n, seed))
+
+
+def test_map_sum(K, rng):
+    x = rng.standard_normal(123457).astype(np.float32)
+    out = torch.empty(1, device="cuda")
+    for op, p in ((4, 0.0), (0, 0.5), (1, 1.0), (2, 1.0), (3, 1.0)):
+        K.map_sum(dev(x), op, p, out)
+        want = O.map_sum(x, op, p)
+        scale = O.map_sum(np.abs(x), 0, 1.0) if op in (0, 1) else abs(want)
+        assert abs(host(out)[0] - want) <= 1e-5 * max(scale, 1.0), (op, host(out)[0], want)
+    with pytest.raises(Exception):
+        K.map_sum(dev(x), 9, 0.0, out)
+
+
+def test_matrix_slice(K, rng):
+    m = rng.standard_normal((96, 160)).astype(np.float32)
+    for tr, tc, tpr, nt in ((32, 40, 4, 12), (96, 160, 1, 1), (1, 1, 160, 160 * 96), (8, 16, 5, 3)):
+        out = torch.empty(nt * tr * tc, device="cuda")
+        K.matrix_slice(dev(m), out, tr, tc, tpr)
+        np.testing.assert_array_equal(host(out), O.matrix_slice(m, tr, tc, tpr, nt))
+    with pytest.raises(Exception, match="past the input"):
+        K.matrix_slice(dev(m), torch.empty(13 * 32 * 40, device="cuda"), 32, 40, 4)
+    with pytest.raises(Exception, match="exceeds input_cols"):
+        K.matrix_slice(dev(m), torch.empty(32 * 40, device="cuda"), 32, 40, 5)

@@ -194,3 +194,36 @@ def test_grads_accumulate_equals_immediate_update():
     g = np.zeros(t2.flat().size, np.float32)
     O.transformer_train_step(t2, x, tg, 0.0, grads=g)
     assert rel_err(t2.flat() - 0.05 * g, t1.flat()) < 1e-6
+
+
+def _ref_hash(x):
+    """common.rs:3-9 in numpy uint32 arithmetic (wrapping)."""
+    x = np.asarray(x, np.uint32)
+    with np.errstate(over="ignore"):
+        x = x + (x << np.uint32(13))
+        x = x - (x >> np.uint32(17))
+        x = x * (x << np.uint32(5))
+    return x
+
+
+def test_fills_known_answers():
+    """slice_set_seq (elementwise.rs:24-35) and slice_set_random
+    (elementwise.rs:37-43) against independent numpy restatements."""
+    np.testing.assert_array_equal(O.fill_seq(5), [0, 1, 2, 3, 4])
+    np.testing.assert_array_equal(O.fill_seq(5, ascending=False), [5, 4, 3, 2, 1])
+    n, seed = 4099, 0xFFFFFF00  # seed + index wraps past 2^32
+    idx = np.arange(n, dtype=np.uint64)
+    h = _ref_hash(((np.uint64(seed) + idx) & np.uint64(0xFFFFFFFF)).astype(np.uint32))
+    want = h.astype(np.float32) / np.float32(4294967296.0)
+    np.testing.assert_array_equal(O.fill_random(n, seed), want)
+    assert O.fill_random(1, 0)[0] == 0.0  # hash(0) == 0
+
+
+def test_map_sum_and_matrix_slice_known_answers(rng):
+    x = rng.standard_normal(10000).astype(np.float32)
+    assert abs(O.map_sum(x, 4) - 0.5 * np.sum(x.astype(np.float64) ** 2)) < 1e-5 * np.sum(x ** 2)
+    assert abs(O.map_sum(x, 0, 2.0) - 2 * np.sum(x.astype(np.float64))) < 1e-3
+    m = np.arange(6 * 8, dtype=np.float32).reshape(6, 8)
+    got = O.matrix_slice(m, 3, 4, 2, 4)
+    want = np.concatenate([m[r:r + 3, c:c + 4].ravel() for r in (0, 3) for c in (0, 4)])
+    np.testing.assert_array_equal(got, want)
