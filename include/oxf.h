@@ -198,7 +198,9 @@ oxf_status oxf_matrix_transpose(oxf_cslice input, oxf_slice result, size_t rows,
                                 oxf_stream stream);
 
 /* ---------------------------------------------------------------- GEMM */
-typedef enum { OXF_PREC_TF32 = 0, OXF_PREC_TF32X3 = 1 } oxf_precision;
+/* TF32: tensor cores, TF32 operands. TF32X3: tensor cores, hi+lo splits (f32-faithful).
+ * F32: CUDA cores, f32 products and sums (the reference's matrix_multiply_fp32). */
+typedef enum { OXF_PREC_TF32 = 0, OXF_PREC_TF32X3 = 1, OXF_PREC_F32 = 2 } oxf_precision;
 
 /* One (batched) GEMM with a fused epilogue:
  *   acc = alpha * op(A)·op(B)                         [M,N] per batch item
@@ -269,6 +271,12 @@ oxf_status oxf_gemm_tf32x3_noalloc(const oxf_gemm_desc* desc, oxf_stream stream)
  * (matrix.rs:147-149); this entry point accepts any sizes. */
 oxf_status oxf_matrix_multiply(oxf_cslice lhs, oxf_cslice rhs, oxf_slice result, size_t len,
                                size_t rows, size_t cols, oxf_stream stream);
+
+/* matrix_multiply_fp32 (module.rs:165-177, gemm.rs:16-113): the same
+ * product with f32 operands and f32 fused multiply-adds on the CUDA cores
+ * (no TF32 rounding), tiled 32 x 32 as the reference does. Any sizes. */
+oxf_status oxf_matrix_multiply_fp32(oxf_cslice lhs, oxf_cslice rhs, oxf_slice result, size_t len,
+                                    size_t rows, size_t cols, oxf_stream stream);
 
 /* Reference-algorithm restatement, for measurement only: the reference's
  * 32x32-tile, 128-thread, mma.sync.m16n8k8 TF32, 2-stage cp.async GEMM

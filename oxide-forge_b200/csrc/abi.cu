@@ -436,6 +436,19 @@ oxf_status oxf_matrix_multiply(oxf_cslice lhs, oxf_cslice rhs, oxf_slice result,
   return gemm_run(&d, S(stream));
 }
 
+oxf_status oxf_matrix_multiply_fp32(oxf_cslice lhs, oxf_cslice rhs, oxf_slice result,
+                                    size_t len, size_t rows, size_t cols, oxf_stream stream) {
+  OXF_TRY(need(lhs.len >= rows * len && rhs.len >= len * cols && result.len >= rows * cols,
+               "oxf_matrix_multiply_fp32: slice shorter than its shape"));
+  if (rows > 0x7fffffffu || cols > 0x7fffffffu || len > 0x7fffffffu)
+    return set_error(OXF_ERR_UNSUPPORTED_SHAPE, "oxf_matrix_multiply_fp32: dimension too large");
+  oxf_gemm_desc d;
+  oxf_gemm_desc_init(&d, static_cast<int>(rows), static_cast<int>(cols), static_cast<int>(len), 0,
+                     0, lhs.ptr, rhs.ptr, result.ptr);
+  d.precision = OXF_PREC_F32;
+  return gemm_run(&d, S(stream));
+}
+
 oxf_status oxf_matrix_multiply_refalgo(oxf_cslice lhs, oxf_cslice rhs, oxf_slice result,
                                        size_t len, size_t rows, size_t cols, oxf_stream stream) {
   OXF_TRY(need(lhs.len >= rows * len && rhs.len >= len * cols && result.len >= rows * cols,

@@ -1219,7 +1219,8 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
     return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: split_k > 1 requires accumulate");
   if (d->accumulate && d->beta != 0.0f)
     return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: beta must be 0 with accumulate");
-  if (d->precision != OXF_PREC_TF32 && d->precision != OXF_PREC_TF32X3)
+  if (d->precision != OXF_PREC_TF32 && d->precision != OXF_PREC_TF32X3 &&
+      d->precision != OXF_PREC_F32)
     return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: unknown precision %d", d->precision);
   const long long min_lda = d->a_trans ? d->M : d->K;
   const long long min_ldb = d->b_trans ? d->K : d->N;
@@ -1263,12 +1264,15 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
              (d->bias == nullptr || aligned16(d->bias));
 
   // TMA needs 16-byte aligned bases, leading dimensions and batch strides.
+  // OXF_PREC_F32 asks for f32 products on the CUDA cores: the SIMT kernel.
   const bool tma_ok = d->K > 0 && tma_ok_ptr(d->A) && tma_ok_ptr(d->B) && d->lda % 4 == 0 &&
-                      d->ldb % 4 == 0 && d->stride_a % 4 == 0 && d->stride_b % 4 == 0;
+                      d->ldb % 4 == 0 && d->stride_a % 4 == 0 && d->stride_b % 4 == 0 &&
+                      d->precision != OXF_PREC_F32;
   if (!tma_ok) {
     if (a.reduce_batch)
       return set_error(OXF_ERR_UNSUPPORTED_SHAPE,
-                       "oxf_gemm: reduce_batch needs 16-byte aligned operands");
+                       "oxf_gemm: reduce_batch runs on the tensor cores only (16-byte aligned "
+                       "operands, TF32 or TF32X3 precision)");
     a.splits = 1;
     if (d->K == 0) {
       // C = epilogue(0): run the SIMT kernel with an empty K loop.
@@ -1276,7 +1280,7 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
     dim3 grid((d->N + 31) / 32, (d->M + 31) / 32, d->batch);
     gemm_simt_kernel<<<grid, dim3(32, 8), 0, stream>>>(a, d->A, d->lda, d->stride_a, d->B,
                                                         d->ldb, d->stride_b,
-                                                        d->precision == OXF_PREC_TF32X3);
+                                                        d->precision != OXF_PREC_TF32);
     return check_launch("gemm_simt_kernel");
   }
 

@@ -21,7 +21,7 @@ STATUS_NAMES = {0: "OK", 1: "INVALID_ARG", 2: "UNSUPPORTED_SHAPE", 3: "CUDA_ERRO
 ADD, SUB, MUL, DIV = 0, 1, 2, 3
 ACT_IDENTITY, ACT_GELU, ACT_RELU, ACT_SILU = 0, 1, 2, 3
 UNARY_SCALE, UNARY_ADD_SCALAR, UNARY_ACT_FORWARD, UNARY_ACT_DERIV, UNARY_HALF_SQUARE = range(5)
-PREC_TF32, PREC_TF32X3 = 0, 1
+PREC_TF32, PREC_TF32X3, PREC_F32 = 0, 1, 2
 NORM_RMS, NORM_LAYER = 0, 1
 
 
@@ -110,6 +110,8 @@ _SIGS = {
     "oxf_gemm_tf32x3_noalloc": (C.c_int, [C.POINTER(GemmDesc), C.c_void_p]),
     "oxf_matrix_multiply": (C.c_int, [CSlice, CSlice, Slice, C.c_size_t, C.c_size_t, C.c_size_t,
                                       C.c_void_p]),
+    "oxf_matrix_multiply_fp32": (C.c_int, [CSlice, CSlice, Slice, C.c_size_t, C.c_size_t,
+                                          C.c_size_t, C.c_void_p]),
     "oxf_matrix_multiply_refalgo": (C.c_int, [CSlice, CSlice, Slice, C.c_size_t, C.c_size_t,
                                               C.c_size_t, C.c_void_p]),
 }

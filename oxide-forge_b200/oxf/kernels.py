@@ -211,6 +211,13 @@ def matrix_multiply(a, b, out, stream=None):
     return out
 
 
+def matrix_multiply_fp32(a, b, out, stream=None):
+    """module.rs:165-177 argument order; f32 products on the CUDA cores."""
+    check(lib().oxf_matrix_multiply_fp32(cs(a), cs(b), ms(out), a.shape[1], a.shape[0], b.shape[1],
+                                         _stream(stream)))
+    return out
+
+
 def matrix_multiply_refalgo(a, b, out, stream=None):
     check(lib().oxf_matrix_multiply_refalgo(cs(a), cs(b), ms(out), a.shape[1], a.shape[0],
                                             b.shape[1], _stream(stream)))

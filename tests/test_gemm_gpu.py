@@ -317,3 +317,16 @@ def test_accumulate_rejects_split_with_bias(K, rng):
         K.gemm(dev(A), dev(B), acc, a_trans=True, bias=dev(bias), accumulate=True, split_k=4)
     K.gemm(dev(A), dev(B), acc, a_trans=True, bias=dev(bias), accumulate=True)
     assert rel_err(host(acc), exact(A, B, 1, 0) + bias) < TF32_TOL
+
+
+@pytest.mark.parametrize("M,N,Kd", [(256, 64, 128), (300, 200, 72), (1024, 512, 2048)])
+def test_matrix_multiply_fp32_is_f32_exact(K, rng, M, N, Kd):
+    """matrix_multiply_fp32 (gemm.rs:16-113): f32 products, no TF32
+    rounding, so it agrees with the float64 product to f32 summation error
+    (far tighter than TF32's 5e-3) and matches the oracle's f32 GEMM."""
+    A, B = operands(rng, M, N, Kd, 0, 0)
+    out = torch.empty((M, N), device="cuda")
+    K.matrix_multiply_fp32(dev(A), dev(B), out)
+    got = host(out)
+    assert rel_err(got, exact(A, B, 0, 0)) < 1e-5
+    assert rel_err(got, O.gemm(A, B)) < 1e-5
