@@ -289,3 +289,39 @@ def test_checkpoint_engine_round_trip(M, tmp_path):
     np.testing.assert_array_equal(host(m2.params), mflat)
     m.close()
     m2.close()
+
+
+def test_full_size_c5_sequence_matches_oracle(M):
+    """Config 5 at its full per-sequence size ([1024, 2048], FFN 8192,
+    LayerNorm): one sequence's training step (output, loss, input gradient
+    and the per-tensor SGD update) against the oracle's multithreaded C
+    restatement, inside a batch of 2 so the batched paths are exercised.
+    The second sequence's contribution is taken out by running it alone."""
+    seq, hidden, ffn = 1024, 2048, 8192
+    cfg = M.transformer_config(seq, hidden, ffn, norm=1)
+    flat = M.init_transformer_params(cfg, seed=0)
+    rng = np.random.default_rng(21)
+    x = rng.standard_normal((2, seq, hidden)).astype(np.float32)
+    t = rng.standard_normal((2, seq, hidden)).astype(np.float32)
+    lr = 1e-3
+
+    ref = oracle_model(M, cfg, flat)
+    y_ref, loss_ref, dx_ref = O.transformer_train_step(ref, x[0], t[0], lr, rounding=RZ)
+
+    eng = M.Transformer(cfg, max_batch=2)
+    eng.set_params(flat)
+    eng.zero_grads()
+    y = host(eng.train_forward(dev(x.reshape(2 * seq, hidden))))
+    loss = host(eng.set_target(dev(t.reshape(2 * seq, hidden))))
+    dx = host(eng.backward())
+    g2 = host(eng.grads).copy()
+    assert rel_err(y[:seq], y_ref) < FWD_TOL
+    assert rel_err(loss[:seq], loss_ref) < FWD_TOL
+    assert rel_err(dx[:seq], dx_ref) < GRAD_TOL
+    eng.zero_grads()
+    eng.train_forward(dev(x[1]))
+    eng.set_target(dev(t[1]))
+    eng.backward()
+    g1 = host(eng.grads)
+    check_per_tensor(cfg, lr * (g2 - g1), flat - ref.flat())
+    eng.close()
