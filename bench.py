@@ -63,10 +63,11 @@ def parse():
                     help="skip the cuBLAS denominator (profiling runs: keeps the launch list "
                          "to the step's own kernels); roofline.peak is then null")
     ap.add_argument("--workload", default="train",
-                    choices=["train", "gemm", "rows", "mlp", "infer"],
+                    choices=["train", "linear", "gemm", "rows", "mlp", "infer"],
                     help="train: the contract line (config 5). The others are supplementary "
-                         "single-GPU measurements of configs 1-4: gemm (square sweep / one "
-                         "shape), rows (config 2 row suite), mlp (config 3), infer (config 4)")
+                         "single-GPU measurements of configs 1-4: linear (config 1), gemm "
+                         "(square sweep / one shape), rows (config 2 row suite), mlp "
+                         "(config 3), infer (config 4)")
     ap.add_argument("--shape", default=None, help="gemm: M,N,K (default: the 512..8192 sweep)")
     ap.add_argument("--mode", default="nn", help="gemm: nn, nt, tn or tt")
     ap.add_argument("--epi", default="none",
@@ -403,6 +404,65 @@ def run_rows(a, torch):
                       "results": res, "back_to_back": res_ring}), flush=True)
 
 
+def run_linear(a, torch):
+    """Config 1: Linear forward exactly as the repository example (X [256,128]
+    U(-1,1) from seed 0, W [128,64] U(-1/sqrt(128), 1/sqrt(128)), no bias,
+    Identity) through matrix_multiply's argument order (module.rs:179-191):
+    device time per call, against the C oracle (TF32 RNA operands, as the
+    reference's kernel rounds) and the reference-algorithm restatement."""
+    import numpy as np
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+    from oxf import kernels as K
+    rng = np.random.default_rng(0)
+    x = rng.uniform(-1, 1, (256, 128)).astype(np.float32)
+    b = 1 / np.sqrt(128)
+    w = rng.uniform(-b, b, (128, 64)).astype(np.float32)
+    xd, wd = torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda()
+    y = torch.empty(256, 64, device="cuda")
+    def graph_ms(fn, reps=200):
+        """Device time per call: `reps` calls captured once in a CUDA graph
+        and replayed, so host call overhead does not separate the kernels."""
+        fn()
+        torch.cuda.synchronize()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side), torch.cuda.graph(g, stream=side):
+            for _ in range(reps):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = _events(torch)
+        e0.record()
+        for _ in range(max(1, a.steps)):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / (reps * max(1, a.steps))
+
+    ms = graph_ms(lambda: K.matrix_multiply(xd, wd, y))
+    host_ms = _time(torch, lambda: K.matrix_multiply(xd, wd, y), a.steps * 20, a.warmup)
+    got = y.cpu().numpy()
+    want = O.gemm(x, w, rounding=O.GEMM_TF32_RNA)
+    ms_ref = graph_ms(lambda: K.matrix_multiply_refalgo(xd, wd, y))
+    t0 = time.perf_counter()
+    for _ in range(20):
+        O.gemm(x, w, rounding=O.GEMM_TF32_RNA)
+    cpu_ms = (time.perf_counter() - t0) / 20 * 1e3
+    fl = 2 * 256 * 64 * 128
+    print(json.dumps({"metric": "Linear [256,128]x[128,64] forward latency", "value": ms * 1e3,
+                      "unit": "us", "workload": "linear", "higher_is_better": False,
+                      "gflops": fl / ms / 1e6, "refalgo_us": ms_ref * 1e3,
+                      "host_call_us": host_ms * 1e3, "cpu_oracle_us": cpu_ms * 1e3,
+                      "max_rel_err_vs_oracle": float(np.abs(got - want).max() / np.abs(want).max()),
+                      "config": {"workload": "C1 Linear forward, repository example shape",
+                                 "timing": "value/refalgo_us: device time per call (200 calls "
+                                           "replayed as a CUDA graph); host_call_us: calls "
+                                           "issued one by one from Python"}}),
+          flush=True)
+
+
 def run_mlp(a, torch):
     """Config 3: MLP 1024 -> 4096 (GELU) -> 1024 with biases and a residual
     from the MLP input to its output, X [8192,1024] N(0,1), Kaiming-uniform
@@ -516,7 +576,8 @@ def main():
     if a.workload != "train":
         import torch
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
-        {"gemm": run_gemm, "rows": run_rows, "mlp": run_mlp, "infer": run_infer}[a.workload](
+        {"gemm": run_gemm, "rows": run_rows, "mlp": run_mlp, "infer": run_infer,
+         "linear": run_linear}[a.workload](
             a, torch)
         return
     import numpy as np
