@@ -367,6 +367,8 @@ def run_rows(a, torch):
         "gelu_fwd": (lambda i: K.unary(outs[i], 2, 1), 2 * mat),
         "gelu_bwd": (lambda i: K.mul_act_derivative(outs[i], xs[i], 1), 3 * mat),
         "row_broadcast_add": (lambda i: K.binary_assign_by_rows(outs[i], beta, 0), 2 * mat),
+        # the same-size copy (torch), for the bandwidth a 16 MiB read+write reaches at all
+        "torch_copy_same_size": (lambda i: outs[i].copy_(xs[i]), 2 * mat),
     }
     # The ring's launches are captured once into a CUDA graph and replayed,
     # so host launch overhead (Python + ctypes per call) does not starve

@@ -100,6 +100,17 @@ struct Row {
   }
 };
 
+// Programmatic dependent launch: every kernel here is launched with
+// programmatic stream serialisation (launch_pdl below). It lets the next
+// kernel of the stream be scheduled as soon as all of this grid's blocks
+// are running, then waits, before touching memory, until the previous
+// kernel of the stream has completed and its writes are visible. Launched
+// without the attribute, both instructions have no effect.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 __device__ __forceinline__ float hsum(float4 a) { return (a.x + a.y) + (a.z + a.w); }
 __device__ __forceinline__ float hmax(float4 a) { return fmaxf(fmaxf(a.x, a.y), fmaxf(a.z, a.w)); }
 
@@ -121,6 +132,7 @@ __device__ __forceinline__ bool row_index(long long rows, long long& r, int& t) 
 template <int G, int NV>
 __global__ void softmax_fwd_kernel(float* __restrict__ m, long long rows, int cols, float scale,
                                    long long period) {
+  pdl_enter();
   __shared__ float red[2 * (G / 32)];
   long long r;
   int t;
@@ -164,6 +176,7 @@ __global__ void softmax_fwd_kernel(float* __restrict__ m, long long rows, int co
 template <int G, int NV>
 __global__ void softmax_bwd_kernel(const float* __restrict__ p, const float* __restrict__ dy,
                                    float* __restrict__ dx, long long rows, int cols, float scale) {
+  pdl_enter();
   __shared__ float red[G / 32];
   long long r;
   int t;
@@ -194,13 +207,29 @@ template <int G, int NV>
 __global__ void layernorm_fwd_kernel(const float* in, float* out, long long rows, int cols,
                                      float eps, const float* __restrict__ gamma,
                                      const float* __restrict__ beta) {
+  pdl_enter();
   __shared__ float red[2 * (G / 32)];
+  // Warp-per-row blocks hold several rows: gamma and beta are staged in
+  // shared memory once per block, while the rows' loads are in flight, so
+  // they are not an L2 round trip on each row's critical path.
+  constexpr int STAGE = G == 32 ? 32 * NV : 1;
+  __shared__ float4 sg[STAGE], sb[STAGE];
   long long r;
   int t;
-  if (!row_index<G>(rows, r, t)) return;
+  const bool live = row_index<G>(rows, r, t);
   const int cols4 = cols >> 2;
   Row<G, NV> x;
-  x.load(in + r * cols, t, cols4, 0.f);
+  if (live) x.load(in + r * cols, t, cols4, 0.f);
+  if constexpr (G == 32) {
+    if (gamma || beta) {
+      for (int i = threadIdx.x; i < cols4; i += blockDim.x) {
+        if (gamma) sg[i] = reinterpret_cast<const float4*>(gamma)[i];
+        if (beta) sb[i] = reinterpret_cast<const float4*>(beta)[i];
+      }
+      __syncthreads();
+    }
+  }
+  if (!live) return;
   float s = 0.f;
 #pragma unroll
   for (int j = 0; j < NV; ++j) s += hsum(x.v[j]);
@@ -221,11 +250,11 @@ __global__ void layernorm_fwd_kernel(const float* in, float* out, long long rows
     float4& a = x.v[j];
     a.x *= inv_std; a.y *= inv_std; a.z *= inv_std; a.w *= inv_std;
     if (gamma) {
-      const float4 g = reinterpret_cast<const float4*>(gamma)[t + j * G];
+      const float4 g = G == 32 ? sg[t + j * G] : reinterpret_cast<const float4*>(gamma)[t + j * G];
       a.x *= g.x; a.y *= g.y; a.z *= g.z; a.w *= g.w;
     }
     if (beta) {
-      const float4 b = reinterpret_cast<const float4*>(beta)[t + j * G];
+      const float4 b = G == 32 ? sb[t + j * G] : reinterpret_cast<const float4*>(beta)[t + j * G];
       a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
     }
   }
@@ -236,6 +265,7 @@ __global__ void layernorm_fwd_kernel(const float* in, float* out, long long rows
 template <int G, int NV>
 __global__ void layernorm_bwd_kernel(const float* __restrict__ xin, const float* __restrict__ dy,
                                      float* __restrict__ dx, long long rows, int cols, float eps) {
+  pdl_enter();
   __shared__ float red[4 * (G / 32)];
   long long r;
   int t;
@@ -287,6 +317,7 @@ __global__ void layernorm_bwd_kernel(const float* __restrict__ xin, const float*
 template <int G, int NV>
 __global__ void rmsnorm_fwd_kernel(const float* in, float* out, long long rows, int cols,
                                    float eps, const float* __restrict__ gamma) {
+  pdl_enter();
   __shared__ float red[G / 32];
   long long r;
   int t;
@@ -319,6 +350,7 @@ __global__ void rmsnorm_fwd_kernel(const float* in, float* out, long long rows, 
 template <int G, int NV>
 __global__ void rmsnorm_bwd_kernel(const float* __restrict__ xin, const float* __restrict__ dy,
                                    float* __restrict__ dx, long long rows, int cols, float eps) {
+  pdl_enter();
   __shared__ float red[2 * (G / 32)];
   long long r;
   int t;
@@ -354,6 +386,7 @@ __global__ void rmsnorm_bwd_kernel(const float* __restrict__ xin, const float* _
 template <int G, int NV>
 __global__ void sum_rows_kernel(const float* __restrict__ m, float* __restrict__ out,
                                 long long rows, int cols) {
+  pdl_enter();
   __shared__ float red[G / 32];
   long long r;
   int t;
@@ -372,6 +405,7 @@ __global__ void sum_rows_kernel(const float* __restrict__ m, float* __restrict__
 template <int G, int NV>
 __global__ void loss_rows_kernel(const float* __restrict__ y, const float* __restrict__ tg,
                                  float* __restrict__ out, long long rows, int cols) {
+  pdl_enter();
   __shared__ float red[G / 32];
   long long r;
   int t;
@@ -396,6 +430,7 @@ template <int G, int NV>
 __global__ void loss_grad_rows_kernel(const float* __restrict__ y, const float* __restrict__ tg,
                                       float* __restrict__ out, float* __restrict__ dy,
                                       long long rows, int cols) {
+  pdl_enter();
   __shared__ float red[G / 32];
   long long r;
   int t;
@@ -450,6 +485,7 @@ __global__ void row_looped_kernel(int op, float* __restrict__ out, const float* 
                                   const float* __restrict__ b, long long cols, float p0, float p1,
                                   long long period, const float* __restrict__ gamma,
                                   const float* __restrict__ beta) {
+  pdl_enter();
   __shared__ float red[32];
   const long long r = blockIdx.x;
   const float n = static_cast<float>(cols);
@@ -584,6 +620,7 @@ template <bool VEC>
 __global__ void elementwise_kernel(int kind, int op, float* __restrict__ out,
                                    const float* __restrict__ a, const float* __restrict__ b,
                                    long long n, float p, long long cols) {
+  pdl_enter();
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
   long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if constexpr (VEC) {
@@ -646,6 +683,7 @@ __global__ void elementwise_kernel(int kind, int op, float* __restrict__ out,
 
 // row.rs:5-14 (standalone): M[i,j] = -inf for j > i; one block per row.
 __global__ void causal_mask_kernel(float* __restrict__ m, long long rows, long long cols) {
+  pdl_enter();
   const long long r = blockIdx.x;
   for (long long c = r + 1 + threadIdx.x; c < cols; c += blockDim.x) m[r * cols + c] = -INFINITY;
 }
@@ -654,6 +692,7 @@ __global__ void causal_mask_kernel(float* __restrict__ m, long long rows, long l
 // are combined with atomics into a zeroed (or accumulating) result.
 __global__ void sum_cols_kernel(const float* __restrict__ m, float* __restrict__ out,
                                 long long rows, long long cols, long long rows_per_block) {
+  pdl_enter();
   __shared__ float part[8][33];
   const long long c = static_cast<long long>(blockIdx.x) * 32 + threadIdx.x;
   const long long r0 = static_cast<long long>(blockIdx.y) * rows_per_block;
@@ -674,6 +713,7 @@ __global__ void sum_cols_kernel(const float* __restrict__ m, float* __restrict__
 // layout.rs:9-55: 32x32 tiles through padded shared memory.
 __global__ void transpose_kernel(const float* __restrict__ in, float* __restrict__ out,
                                  long long rows, long long cols) {
+  pdl_enter();
   __shared__ float tile[32][33];
   const long long c = static_cast<long long>(blockIdx.x) * 32 + threadIdx.x;
   for (int i = threadIdx.y; i < 32; i += 8) {
@@ -693,13 +733,17 @@ __device__ __forceinline__ void atomic_max_float(float* addr, float v) {
   else atomicMin(reinterpret_cast<unsigned int*>(addr), __float_as_uint(v));
 }
 
-__global__ void fill_kernel(float* p, float v) { *p = v; }
+__global__ void fill_kernel(float* p, float v) {
+  pdl_enter();
+  *p = v;
+}
 
 // One-launch reductions (the reference re-launches slice_sum from the host
 // until one element is left, span.rs:361-385). map_op >= 0 sums
 // unary_apply(map_op, x, map_p) instead of x (slice_map_sum).
 __global__ void slice_reduce_kernel(const float* __restrict__ x, long long n, float* result,
                                     int is_max, int map_op, float map_p) {
+  pdl_enter();
   __shared__ float red[32];
   float acc = is_max ? -FLT_MAX : 0.f;
   for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
@@ -727,6 +771,7 @@ __device__ __forceinline__ uint32_t ref_hash(uint32_t x) {
 
 __global__ void fill_slice_kernel(float* __restrict__ out, long long n, int kind, float value,
                                   int dir, uint32_t seed) {
+  pdl_enter();
   for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     float v = value;
@@ -744,6 +789,7 @@ __global__ void fill_slice_kernel(float* __restrict__ out, long long n, int kind
 __global__ void matrix_slice_kernel(const float* __restrict__ in, float* __restrict__ out,
                                     long long n, long long input_cols, long long tile_rows,
                                     long long tile_cols, long long tiles_per_row) {
+  pdl_enter();
   const long long tile = tile_rows * tile_cols;
   for (long long l = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; l < n;
        l += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -757,6 +803,26 @@ __global__ void matrix_slice_kernel(const float* __restrict__ in, float* __restr
 
 // ================================================================== host side
 namespace {
+
+// Launches `kernel` with programmatic stream serialisation (see pdl_enter)
+// and counts it; returns the launch status.
+template <typename... KArgs, typename... Args>
+oxf_status launch_pdl(const char* name, void (*kernel)(KArgs...), dim3 grid, dim3 block,
+                      cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+  count_launch();
+  return check_cuda(e != cudaSuccess ? e : cudaGetLastError(), name);
+}
 
 int sm_count_rows() {
   static int c = 0;
@@ -774,17 +840,18 @@ bool fits_int(long long v) { return v >= 0 && v <= 0x7fffffffll; }
 // Launches `K<G,NV>` for the smallest register footprint that holds the
 // row, or returns false if the row needs the looped path.
 template <template <int, int> class Launcher, typename... Args>
-bool dispatch_row(long long rows, long long cols, cudaStream_t s, Args... args) {
+bool dispatch_row(long long rows, long long cols, cudaStream_t s, oxf_status* st,
+                  Args... args) {
   if (cols % 4 != 0 || cols > 16384 || !fits_int(cols)) return false;
   const long long c4 = cols / 4;
-  if (c4 <= 32) return Launcher<32, 1>::go(rows, s, args...);
-  if (c4 <= 64) return Launcher<32, 2>::go(rows, s, args...);
-  if (c4 <= 128) return Launcher<32, 4>::go(rows, s, args...);
-  if (c4 <= 256) return Launcher<32, 8>::go(rows, s, args...);
-  if (c4 <= 512) return Launcher<32, 16>::go(rows, s, args...);
-  if (c4 <= 1024) return Launcher<128, 8>::go(rows, s, args...);
-  if (c4 <= 2048) return Launcher<256, 8>::go(rows, s, args...);
-  return Launcher<256, 16>::go(rows, s, args...);
+  if (c4 <= 32) return Launcher<32, 1>::go(rows, s, st, args...);
+  if (c4 <= 64) return Launcher<32, 2>::go(rows, s, st, args...);
+  if (c4 <= 128) return Launcher<32, 4>::go(rows, s, st, args...);
+  if (c4 <= 256) return Launcher<32, 8>::go(rows, s, st, args...);
+  if (c4 <= 512) return Launcher<32, 16>::go(rows, s, st, args...);
+  if (c4 <= 1024) return Launcher<128, 8>::go(rows, s, st, args...);
+  if (c4 <= 2048) return Launcher<256, 8>::go(rows, s, st, args...);
+  return Launcher<256, 16>::go(rows, s, st, args...);
 }
 
 template <int G>
@@ -797,13 +864,15 @@ dim3 row_grid(long long rows, int& threads) {
   return dim3(static_cast<unsigned>(rows));
 }
 
+// go() launches the kernel (its status goes to *st) and returns true;
+// dispatch_row returns false instead when no instantiation fits the row.
 #define OXF_ROW_LAUNCHER(NAME, KERNEL, PARAMS, ARGS)                         \
   template <int G, int NV>                                                   \
   struct NAME {                                                              \
-    static bool go(long long rows, cudaStream_t s, PARAMS) {                 \
+    static bool go(long long rows, cudaStream_t s, oxf_status* st, PARAMS) { \
       int threads;                                                           \
       dim3 grid = row_grid<G>(rows, threads);                                \
-      KERNEL<G, NV><<<grid, threads, 0, s>>>(ARGS);                          \
+      *st = launch_pdl(#KERNEL, KERNEL<G, NV>, grid, dim3(threads), s, ARGS); \
       return true;                                                           \
     }                                                                        \
   };
@@ -843,9 +912,8 @@ oxf_status looped(int op, float* out, const float* a, const float* b, long long 
                   long long cols, float p0, float p1, long long period, const float* g,
                   const float* be, cudaStream_t s) {
   if (rows > 0x7fffffffll) return set_error(OXF_ERR_UNSUPPORTED_SHAPE, "too many rows");
-  row_looped_kernel<<<static_cast<unsigned>(rows), 256, 0, s>>>(op, out, a, b, cols, p0, p1,
-                                                               period, g, be);
-  return check_launch("row_looped_kernel");
+  return launch_pdl("row_looped_kernel", row_looped_kernel, dim3(static_cast<unsigned>(rows)),
+                    dim3(256), s, op, out, a, b, cols, p0, p1, period, g, be);
 }
 
 unsigned ew_blocks(long long work) {
@@ -863,10 +931,10 @@ oxf_status elementwise(int kind, int op, float* out, const float* a, const float
   bool vec = al(out) && al(a) && al(b) && (n % 4 == 0);
   if (kind == EW_BY_ROWS || kind == EW_BINARY_BCAST) vec = vec && (cols % 4 == 0);
   if (vec)
-    elementwise_kernel<true><<<ew_blocks(n / 4), 256, 0, s>>>(kind, op, out, a, b, n, p, cols);
-  else
-    elementwise_kernel<false><<<ew_blocks(n), 256, 0, s>>>(kind, op, out, a, b, n, p, cols);
-  return check_launch("elementwise_kernel");
+    return launch_pdl("elementwise_kernel", elementwise_kernel<true>, dim3(ew_blocks(n / 4)),
+                      dim3(256), s, kind, op, out, a, b, n, p, cols);
+  return launch_pdl("elementwise_kernel", elementwise_kernel<false>, dim3(ew_blocks(n)),
+                    dim3(256), s, kind, op, out, a, b, n, p, cols);
 }
 
 }  // namespace
@@ -875,61 +943,68 @@ oxf_status elementwise(int kind, int op, float* out, const float* a, const float
 oxf_status rows_softmax(float* m, long long rows, long long cols, float scale, long long period,
                         cudaStream_t s) {
   if (rows == 0 || cols == 0) return OXF_OK;
-  if (al(m) && dispatch_row<SoftmaxFwdL>(rows, cols, s, m, static_cast<int>(cols), scale, period))
-    return check_launch("softmax_fwd_kernel");
+  oxf_status st = OXF_OK;
+  if (al(m) && dispatch_row<SoftmaxFwdL>(rows, cols, s, &st, m, static_cast<int>(cols), scale, period))
+    return st;
   return looped(LOOP_SOFTMAX, m, m, nullptr, rows, cols, scale, 0.f, period, nullptr, nullptr, s);
 }
 
 oxf_status rows_softmax_bwd(const float* p, const float* dy, float* dx, long long rows,
                             long long cols, float scale, cudaStream_t s) {
   if (rows == 0 || cols == 0) return OXF_OK;
+  oxf_status st = OXF_OK;
   if (al(p) && al(dy) && al(dx) &&
-      dispatch_row<SoftmaxBwdL>(rows, cols, s, p, dy, dx, static_cast<int>(cols), scale))
-    return check_launch("softmax_bwd_kernel");
+      dispatch_row<SoftmaxBwdL>(rows, cols, s, &st, p, dy, dx, static_cast<int>(cols), scale))
+    return st;
   return looped(LOOP_SOFTMAX_BWD, dx, p, dy, rows, cols, scale, 0.f, 0, nullptr, nullptr, s);
 }
 
 oxf_status rows_layernorm(const float* in, float* out, long long rows, long long cols, float eps,
                           const float* g, const float* b, cudaStream_t s) {
   if (rows == 0 || cols == 0) return OXF_OK;
+  oxf_status st = OXF_OK;
   if (al(in) && al(out) && al(g) && al(b) &&
-      dispatch_row<LnFwdL>(rows, cols, s, in, out, static_cast<int>(cols), eps, g, b))
-    return check_launch("layernorm_fwd_kernel");
+      dispatch_row<LnFwdL>(rows, cols, s, &st, in, out, static_cast<int>(cols), eps, g, b))
+    return st;
   return looped(LOOP_LN, out, in, nullptr, rows, cols, eps, 0.f, 0, g, b, s);
 }
 
 oxf_status rows_layernorm_bwd(const float* x, const float* dy, float* dx, long long rows,
                               long long cols, float eps, cudaStream_t s) {
   if (rows == 0 || cols == 0) return OXF_OK;
+  oxf_status st = OXF_OK;
   if (al(x) && al(dy) && al(dx) &&
-      dispatch_row<LnBwdL>(rows, cols, s, x, dy, dx, static_cast<int>(cols), eps))
-    return check_launch("layernorm_bwd_kernel");
+      dispatch_row<LnBwdL>(rows, cols, s, &st, x, dy, dx, static_cast<int>(cols), eps))
+    return st;
   return looped(LOOP_LN_BWD, dx, x, dy, rows, cols, eps, 0.f, 0, nullptr, nullptr, s);
 }
 
 oxf_status rows_rmsnorm(const float* in, float* out, long long rows, long long cols, float eps,
                         const float* g, cudaStream_t s) {
   if (rows == 0 || cols == 0) return OXF_OK;
+  oxf_status st = OXF_OK;
   if (al(in) && al(out) && al(g) &&
-      dispatch_row<RmsFwdL>(rows, cols, s, in, out, static_cast<int>(cols), eps, g))
-    return check_launch("rmsnorm_fwd_kernel");
+      dispatch_row<RmsFwdL>(rows, cols, s, &st, in, out, static_cast<int>(cols), eps, g))
+    return st;
   return looped(LOOP_RMS, out, in, nullptr, rows, cols, eps, 0.f, 0, g, nullptr, s);
 }
 
 oxf_status rows_rmsnorm_bwd(const float* x, const float* dy, float* dx, long long rows,
                             long long cols, float eps, cudaStream_t s) {
   if (rows == 0 || cols == 0) return OXF_OK;
+  oxf_status st = OXF_OK;
   if (al(x) && al(dy) && al(dx) &&
-      dispatch_row<RmsBwdL>(rows, cols, s, x, dy, dx, static_cast<int>(cols), eps))
-    return check_launch("rmsnorm_bwd_kernel");
+      dispatch_row<RmsBwdL>(rows, cols, s, &st, x, dy, dx, static_cast<int>(cols), eps))
+    return st;
   return looped(LOOP_RMS_BWD, dx, x, dy, rows, cols, eps, 0.f, 0, nullptr, nullptr, s);
 }
 
 oxf_status rows_sum(const float* m, float* out, long long rows, long long cols, cudaStream_t s) {
   if (rows == 0) return OXF_OK;
   if (cols == 0) return check_cuda(cudaMemsetAsync(out, 0, rows * 4, s), "memset");
-  if (al(m) && dispatch_row<SumRowsL>(rows, cols, s, m, out, static_cast<int>(cols)))
-    return check_launch("sum_rows_kernel");
+  oxf_status st = OXF_OK;
+  if (al(m) && dispatch_row<SumRowsL>(rows, cols, s, &st, m, out, static_cast<int>(cols)))
+    return st;
   return looped(LOOP_SUM, out, m, nullptr, rows, cols, 0.f, 0.f, 0, nullptr, nullptr, s);
 }
 
@@ -937,8 +1012,9 @@ oxf_status rows_loss(const float* y, const float* t, float* out, long long rows,
                      cudaStream_t s) {
   if (rows == 0) return OXF_OK;
   if (cols == 0) return check_cuda(cudaMemsetAsync(out, 0, rows * 4, s), "memset");
-  if (al(y) && al(t) && dispatch_row<LossRowsL>(rows, cols, s, y, t, out, static_cast<int>(cols)))
-    return check_launch("loss_rows_kernel");
+  oxf_status st = OXF_OK;
+  if (al(y) && al(t) && dispatch_row<LossRowsL>(rows, cols, s, &st, y, t, out, static_cast<int>(cols)))
+    return st;
   return looped(LOOP_LOSS, out, y, t, rows, cols, 0.f, 0.f, 0, nullptr, nullptr, s);
 }
 
@@ -947,10 +1023,11 @@ oxf_status ew_mse_grad(const float*, const float*, float*, long long, long long,
 oxf_status rows_loss_grad(const float* y, const float* t, float* out, float* dy, long long rows,
                           long long cols, cudaStream_t s) {
   if (rows == 0) return OXF_OK;
+  oxf_status st = OXF_OK;
   if (al(y) && al(t) && al(dy) &&
-      dispatch_row<LossGradL>(rows, cols, s, y, t, out, dy, static_cast<int>(cols)))
-    return check_launch("loss_grad_rows_kernel");
-  oxf_status st = rows_loss(y, t, out, rows, cols, s);
+      dispatch_row<LossGradL>(rows, cols, s, &st, y, t, out, dy, static_cast<int>(cols)))
+    return st;
+  st = rows_loss(y, t, out, rows, cols, s);
   if (st != OXF_OK) return st;
   return ew_mse_grad(y, t, dy, rows * cols, cols, s);
 }
@@ -987,8 +1064,8 @@ oxf_status ew_mul_act_deriv(float* g, const float* pre, long long n, int act, cu
 oxf_status causal_mask(float* m, long long rows, long long cols, cudaStream_t s) {
   if (rows == 0 || cols == 0) return OXF_OK;
   if (rows > 0x7fffffffll) return set_error(OXF_ERR_UNSUPPORTED_SHAPE, "causal mask: rows");
-  causal_mask_kernel<<<static_cast<unsigned>(rows), 256, 0, s>>>(m, rows, cols);
-  return check_launch("causal_mask_kernel");
+  return launch_pdl("causal_mask_kernel", causal_mask_kernel, dim3(static_cast<unsigned>(rows)),
+                    dim3(256), s, m, rows, cols);
 }
 
 oxf_status cols_sum(const float* m, float* out, long long rows, long long cols, int accumulate,
@@ -1006,9 +1083,9 @@ oxf_status cols_sum(const float* m, float* out, long long rows, long long cols, 
   const long long per = (rows + slices - 1) / slices;
   slices = (rows + per - 1) / per;
   if (strips > 0x7fffffffll) return set_error(OXF_ERR_UNSUPPORTED_SHAPE, "too many columns");
-  sum_cols_kernel<<<dim3(static_cast<unsigned>(strips), static_cast<unsigned>(slices)),
-                    dim3(32, 8), 0, s>>>(m, out, rows, cols, per);
-  return check_launch("sum_cols_kernel");
+  return launch_pdl("sum_cols_kernel", sum_cols_kernel,
+                    dim3(static_cast<unsigned>(strips), static_cast<unsigned>(slices)),
+                    dim3(32, 8), s, m, out, rows, cols, per);
 }
 
 oxf_status transpose(const float* in, float* out, long long rows, long long cols,
@@ -1016,35 +1093,32 @@ oxf_status transpose(const float* in, float* out, long long rows, long long cols
   if (rows == 0 || cols == 0) return OXF_OK;
   if ((rows + 31) / 32 > 65535) return set_error(OXF_ERR_UNSUPPORTED_SHAPE, "transpose: rows");
   dim3 grid(static_cast<unsigned>((cols + 31) / 32), static_cast<unsigned>((rows + 31) / 32));
-  transpose_kernel<<<grid, dim3(32, 8), 0, s>>>(in, out, rows, cols);
-  return check_launch("transpose_kernel");
+  return launch_pdl("transpose_kernel", transpose_kernel, grid, dim3(32, 8), s, in, out, rows,
+                    cols);
 }
 
 oxf_status slice_reduce(const float* x, long long n, float* result, int is_max, cudaStream_t s,
                         int map_op, float map_p) {
-  fill_kernel<<<1, 1, 0, s>>>(result, is_max ? -FLT_MAX : 0.f);
-  count_launch();
-  if (n > 0) {
-    const unsigned blocks = ew_blocks((n + 3) / 4);
-    slice_reduce_kernel<<<blocks, 256, 0, s>>>(x, n, result, is_max, map_op, map_p);
-  }
-  return check_launch("slice_reduce_kernel");
+  const oxf_status st = launch_pdl("fill_kernel", fill_kernel, dim3(1), dim3(1), s, result,
+                                   is_max ? -FLT_MAX : 0.f);
+  if (st != OXF_OK || n <= 0) return st;
+  return launch_pdl("slice_reduce_kernel", slice_reduce_kernel, dim3(ew_blocks((n + 3) / 4)),
+                    dim3(256), s, x, n, result, is_max, map_op, map_p);
 }
 
 oxf_status fill_slice(float* out, long long n, int kind, float value, int dir, uint32_t seed,
                       cudaStream_t s) {
   if (n <= 0) return OXF_OK;
-  fill_slice_kernel<<<ew_blocks(n), 256, 0, s>>>(out, n, kind, value, dir, seed);
-  return check_launch("fill_slice_kernel");
+  return launch_pdl("fill_slice_kernel", fill_slice_kernel, dim3(ew_blocks(n)), dim3(256), s, out,
+                    n, kind, value, dir, seed);
 }
 
 oxf_status matrix_slice(const float* in, float* out, long long n, long long input_cols,
                         long long tile_rows, long long tile_cols, long long tiles_per_row,
                         cudaStream_t s) {
   if (n <= 0) return OXF_OK;
-  matrix_slice_kernel<<<ew_blocks(n), 256, 0, s>>>(in, out, n, input_cols, tile_rows, tile_cols,
-                                                  tiles_per_row);
-  return check_launch("matrix_slice_kernel");
+  return launch_pdl("matrix_slice_kernel", matrix_slice_kernel, dim3(ew_blocks(n)), dim3(256), s,
+                    in, out, n, input_cols, tile_rows, tile_cols, tiles_per_row);
 }
 
 }  // namespace oxf
