@@ -78,6 +78,13 @@ const char* oxf_last_error_string(void);
 /* Reads and clears the device error word that bounded in-kernel waits set
  * (0 = none). Synchronises the current device. */
 oxf_status oxf_device_error(uint32_t* code);
+/* Failure-detection self-test: a one-thread kernel waits on an mbarrier
+ * that nothing completes, bounded by limit_us (1..1e6), exactly as every
+ * pipeline wait in this library is bounded. On expiry it writes 1 to the
+ * device int *expired, records 0x1FF in the device error word and returns:
+ * no hang, no fault, the context stays usable. No counterpart in the
+ * reference (its waits are unbounded). */
+oxf_status oxf_wait_timeout_selftest(uint32_t limit_us, int* expired, oxf_stream stream);
 /* Library version string. */
 const char* oxf_version(void);
 /* Kernels this library has launched in this process (all devices). */

@@ -54,6 +54,7 @@ size_t gemm_workspace_bytes(const oxf_gemm_desc*);
 oxf_status gemm_refalgo(const float*, const float*, float*, size_t, size_t, size_t,
                         cudaStream_t);
 oxf_status gemm_read_device_error(uint32_t*);
+oxf_status wait_selftest(unsigned long long, int*, cudaStream_t);
 oxf_status gemm_tf32x3_noalloc(const oxf_gemm_desc*, cudaStream_t);
 
 namespace {
@@ -119,6 +120,13 @@ oxf_status oxf_device_error(uint32_t* code) {
   if (!code) return set_error(OXF_ERR_INVALID_ARG, "oxf_device_error: null code");
   OXF_TRY(check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize"));
   return gemm_read_device_error(code);
+}
+
+oxf_status oxf_wait_timeout_selftest(uint32_t limit_us, int* expired, oxf_stream stream) {
+  if (!expired) return set_error(OXF_ERR_INVALID_ARG, "oxf_wait_timeout_selftest: null flag");
+  if (limit_us == 0 || limit_us > 1000000)
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_wait_timeout_selftest: limit must be 1..1e6 us");
+  return wait_selftest(static_cast<unsigned long long>(limit_us) * 1000ull, expired, S(stream));
 }
 
 // ---------------------------------------------------------------- elementwise

@@ -1483,6 +1483,25 @@ oxf_status gemm_refalgo(const float* A, const float* B, float* C, size_t len, si
   return check_launch("gemm_refalgo_kernel");
 }
 
+// Failure-detection self-test: one thread waits on an mbarrier that nothing
+// arrives at, with a short bound, so the wait expires exactly as a stalled
+// pipeline's would: it records DEVERR_WAIT_SELFTEST in the device error
+// word and returns. Nothing hangs and nothing faults; the context stays
+// usable.
+__global__ void wait_selftest_kernel(unsigned long long limit_ns, int* waited) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  fence_barrier_init();
+  const bool ok = mbar_wait(&bar, 0, DEVERR_WAIT_SELFTEST, limit_ns);
+  *waited = ok ? 0 : 1;
+}
+
+oxf_status wait_selftest(unsigned long long limit_ns, int* waited, cudaStream_t stream) {
+  wait_selftest_kernel<<<1, 32, 0, stream>>>(limit_ns, waited);
+  return check_launch("wait_selftest_kernel");
+}
+
 oxf_status gemm_read_device_error(uint32_t* code) {
   uint32_t v = 0;
   cudaError_t e = cudaMemcpyFromSymbol(&v, g_oxf_device_error, sizeof(v));

@@ -73,12 +73,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait for the phase with the given parity. Returns false (and
 // records `code` in the device error word) if the limit is exceeded.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t code) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t code,
+                                          unsigned long long limit_ns = OXF_WAIT_LIMIT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long start = global_timer_ns();
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, parity)) {
-    if ((++spins & 1023u) == 0 && global_timer_ns() - start > OXF_WAIT_LIMIT_NS) {
+    if ((++spins & 1023u) == 0 && global_timer_ns() - start > limit_ns) {
       report_device_error(code);
       return false;
     }

@@ -77,6 +77,7 @@ _SIGS = {
     "oxf_slice_max": (C.c_int, [CSlice, C.c_void_p, C.c_void_p]),
     "oxf_slice_map_sum": (C.c_int, [CSlice, C.c_int, C.c_float, C.c_void_p, C.c_void_p]),
     "oxf_slice_set": (C.c_int, [Slice, C.c_float, C.c_void_p]),
+    "oxf_wait_timeout_selftest": (C.c_int, [C.c_uint32, C.c_void_p, C.c_void_p]),
     "oxf_slice_set_seq": (C.c_int, [Slice, C.c_int, C.c_void_p]),
     "oxf_slice_set_random": (C.c_int, [Slice, C.c_uint32, C.c_void_p]),
     "oxf_matrix_slice": (C.c_int, [CSlice, Slice, C.c_size_t, C.c_size_t, C.c_size_t, C.c_size_t,

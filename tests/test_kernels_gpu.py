@@ -246,3 +246,25 @@ def test_matrix_slice(K, rng):
         K.matrix_slice(dev(m), torch.empty(13 * 32 * 40, device="cuda"), 32, 40, 4)
     with pytest.raises(Exception, match="exceeds input_cols"):
         K.matrix_slice(dev(m), torch.empty(32 * 40, device="cuda"), 32, 40, 5)
+
+
+def test_bounded_wait_expires_and_context_survives(K):
+    """Failure detection without a GPU fault: a wait that nothing completes
+    expires after its bound (20 ms here; 4 s in the pipelines), sets the
+    device error word and returns; the next kernels run normally."""
+    import ctypes
+    from oxf import _lib
+    expired = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _lib.check(_lib.lib().oxf_wait_timeout_selftest(20000, ctypes.c_void_p(expired.data_ptr()),
+                                                   K._stream(None)))
+    torch.cuda.synchronize()
+    assert int(expired.item()) == 1
+    assert K.device_error() == 0x1FF
+    assert K.device_error() == 0  # reading clears the word
+    a = torch.randn(256, 128, device="cuda")
+    b = torch.randn(128, 64, device="cuda")
+    y = torch.empty(256, 64, device="cuda")
+    K.matrix_multiply(a, b, y)
+    ref = a.double() @ b.double()
+    assert ((y.double() - ref).abs().max() / ref.abs().max()).item() < 5e-3
+    assert K.device_error() == 0
