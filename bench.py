@@ -74,6 +74,9 @@ def parse():
                     choices=["none", "bias_gelu_pre", "gelu_grad_aux", "bias_residual"],
                     help="gemm: fused epilogue (FFN1 forward, FFN1 input gradient, FFN2 "
                          "forward); the cuBLAS comparison stays a plain product")
+    ap.add_argument("--precision", default="tf32", choices=["tf32", "tf32x3", "f32"],
+                    help="gemm: tensor-core TF32, 3xTF32 (f32-faithful splits, three MMAs "
+                         "per step) or f32 on the CUDA cores")
     return ap.parse_args()
 
 
@@ -285,13 +288,19 @@ def run_gemm(a, torch):
             kw = dict(aux=torch.randn(M, N, device="cuda"), grad_act=_lib.ACT_GELU)
         elif a.epi == "bias_residual":
             kw = dict(bias=torch.randn(N, device="cuda"), residual=torch.randn(M, N, device="cuda"))
-        ms = _time(torch, lambda: K.gemm(A, B, Cm, a_trans=at, b_trans=bt, **kw), a.steps,
-                   a.warmup)
+        prec = {"tf32": _lib.PREC_TF32, "tf32x3": _lib.PREC_TF32X3, "f32": _lib.PREC_F32}[
+            a.precision]
+        if prec == _lib.PREC_TF32X3:
+            kw["workspace"] = torch.empty(
+                K.gemm_workspace_bytes(M, N, Kd, at, bt) // 4 + 64, device="cuda")
+        ms = _time(torch, lambda: K.gemm(A, B, Cm, a_trans=at, b_trans=bt, precision=prec, **kw),
+                   a.steps, a.warmup)
         torch.backends.cuda.matmul.allow_tf32 = True
         ref = _time(torch, lambda: torch.matmul(A.T if at else A, B.T if bt else B, out=Cm),
                     a.steps, a.warmup)
         fl = 2.0 * M * N * Kd
-        res.append({"shape": [M, N, Kd], "mode": a.mode, "epilogue": a.epi, "ms": ms,
+        res.append({"shape": [M, N, Kd], "mode": a.mode, "epilogue": a.epi,
+                    "precision": a.precision, "ms": ms,
                     "tflops": fl / ms / 1e9,
                     "cublas_tflops": fl / ref / 1e9, "frac_of_peak": fl / ms / 1e9 / peak})
         del A, B, Cm
@@ -448,6 +457,7 @@ def run_linear(a, torch):
     got = y.cpu().numpy()
     want = O.gemm(x, w, rounding=O.GEMM_TF32_RNA)
     ms_ref = graph_ms(lambda: K.matrix_multiply_refalgo(xd, wd, y))
+    ms_f32 = graph_ms(lambda: K.matrix_multiply_fp32(xd, wd, y))
     t0 = time.perf_counter()
     for _ in range(20):
         O.gemm(x, w, rounding=O.GEMM_TF32_RNA)
@@ -456,6 +466,7 @@ def run_linear(a, torch):
     print(json.dumps({"metric": "Linear [256,128]x[128,64] forward latency", "value": ms * 1e3,
                       "unit": "us", "workload": "linear", "higher_is_better": False,
                       "gflops": fl / ms / 1e6, "refalgo_us": ms_ref * 1e3,
+                      "fp32_cuda_core_us": ms_f32 * 1e3,
                       "host_call_us": host_ms * 1e3, "cpu_oracle_us": cpu_ms * 1e3,
                       "max_rel_err_vs_oracle": float(np.abs(got - want).max() / np.abs(want).max()),
                       "config": {"workload": "C1 Linear forward, repository example shape",
