@@ -642,11 +642,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 // CTA's full barrier, the leader alone issues the MMAs and multicast-commits
 // to both CTAs' barriers, and each CTA's epilogue drains its own 128 TMEM
 // lanes and releases the accumulator to the leader with a remote arrive.
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool SPLIT3>
 struct GemmPairCfg {
   static constexpr int A_BYTES = BM * BK * 4;
   static constexpr int B_BYTES = (BN / 2) * BK * 4;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int OPS = SPLIT3 ? 2 : 1;  // hi (+ lo) copies of each operand
+  static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * OPS;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int CTRL_BYTES = 1024;
   static constexpr int EPI_BYTES = EPI_WARPS * EPI_TILE_BYTES;  // one staging tile per epilogue warp
@@ -675,12 +676,14 @@ __device__ __forceinline__ void load_operand_pair(uint8_t* dst, const CUtensorMa
   }
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool SPLIT3>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     gemm_tf32_tcgen05_pair(const __grid_constant__ CUtensorMap tmA,
                            const __grid_constant__ CUtensorMap tmB,
+                           const __grid_constant__ CUtensorMap tmA_lo,
+                           const __grid_constant__ CUtensorMap tmB_lo,
                            const __grid_constant__ EpiMaps em, const GemmArgs args) {
-  using Cfg = GemmPairCfg<BN, STAGES>;
+  using Cfg = GemmPairCfg<BN, STAGES, SPLIT3>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -711,6 +714,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (SPLIT3) {
+      tma_prefetch_desc(&tmA_lo);
+      tma_prefetch_desc(&tmB_lo);
+    }
   }
   if (warp == 1) {
     tmem_alloc_pair(&ctrl->tmem_base, Cfg::TMEM_COLS);
@@ -748,11 +755,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
             kin = 0;
             ++bk;
           }
-          load_operand_pair<BM>(slot, &tmA, bar, args.a_mn, args.a3d, args.a_chunked,
-                                tm * 2 * BM + static_cast<int>(rank) * BM, k0, item, pol_a);
+          const int arow = tm * 2 * BM + static_cast<int>(rank) * BM;
+          const int brow = tn * BN + static_cast<int>(rank) * (BN / 2);
+          load_operand_pair<BM>(slot, &tmA, bar, args.a_mn, args.a3d, args.a_chunked, arow, k0,
+                                item, pol_a);
           load_operand_pair<BN / 2>(slot + Cfg::A_BYTES, &tmB, bar, args.b_mn, args.b3d,
-                                    args.b_chunked, tn * BN + static_cast<int>(rank) * (BN / 2),
-                                    k0, item, pol_b);
+                                    args.b_chunked, brow, k0, item, pol_b);
+          if (SPLIT3) {
+            uint8_t* lo = slot + Cfg::A_BYTES + Cfg::B_BYTES;
+            load_operand_pair<BM>(lo, &tmA_lo, bar, args.a_mn, args.a3d, args.a_chunked, arow,
+                                  k0, item, pol_a);
+            load_operand_pair<BN / 2>(lo + Cfg::A_BYTES, &tmB_lo, bar, args.b_mn, args.b3d,
+                                      args.b_chunked, brow, k0, item, pol_b);
+          }
           ++fills;
           if (++stage == STAGES) {
             stage = 0;
@@ -798,10 +813,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
           tc_fence_after();
           const uint32_t off = stage * Cfg::STAGE_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < BK / UMMA_K; ++kk)
-            umma_tf32_pair(d_tmem, desc_advance(a_desc0, off + kk * a_step),
-                           desc_advance(b_desc0, off + kk * b_step), args.idesc,
-                           (kb > kb0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+            const uint64_t da = desc_advance(a_desc0, off + kk * a_step);
+            const uint64_t db = desc_advance(b_desc0, off + kk * b_step);
+            const uint32_t accumulate = (kb > kb0 || kk > 0) ? 1u : 0u;
+            if (SPLIT3) {
+              // lo·hi + hi·lo + hi·hi, as in the one-CTA kernel
+              const uint32_t lo = Cfg::A_BYTES + Cfg::B_BYTES;
+              umma_tf32_pair(d_tmem, desc_advance(a_desc0, off + lo + kk * a_step), db,
+                             args.idesc, accumulate);
+              umma_tf32_pair(d_tmem, da, desc_advance(b_desc0, off + lo + kk * b_step),
+                             args.idesc, 1u);
+              umma_tf32_pair(d_tmem, da, db, args.idesc, 1u);
+            } else {
+              umma_tf32_pair(d_tmem, da, db, args.idesc, accumulate);
+            }
+          }
           umma_commit_pair(&ctrl->empty[stage], 0x3);
           if (++stage == STAGES) {
             stage = 0;
@@ -1135,13 +1162,14 @@ oxf_status launch_tcgen05(const CUtensorMap& ta, const CUtensorMap& tb, const CU
   return check_launch("gemm_tf32_tcgen05");
 }
 
-template <int BN, int STAGES>
-oxf_status launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const EpiMaps& em,
-                       GemmArgs& args, cudaStream_t stream, int dev) {
-  using Cfg = GemmPairCfg<BN, STAGES>;
+template <int BN, int STAGES, bool SPLIT3>
+oxf_status launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta_lo,
+                       const CUtensorMap& tb_lo, const EpiMaps& em, GemmArgs& args,
+                       cudaStream_t stream, int dev) {
+  using Cfg = GemmPairCfg<BN, STAGES, SPLIT3>;
   static bool configured[kMaxDevices] = {false};
   if (dev >= 0 && dev < kMaxDevices && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tf32_tcgen05_pair<BN, STAGES>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_tf32_tcgen05_pair<BN, STAGES, SPLIT3>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg::SMEM_BYTES);
     if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(gemm pair)");
@@ -1149,8 +1177,9 @@ oxf_status launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const EpiMa
   }
   args.idesc = make_idesc_tf32(2 * BM, BN, args.a_mn != 0, args.b_mn != 0);
   const long long clusters = std::min<long long>(args.units, sm_count(dev) / 2);
-  gemm_tf32_tcgen05_pair<BN, STAGES><<<static_cast<unsigned>(2 * clusters), GEMM_THREADS,
-                                             Cfg::SMEM_BYTES, stream>>>(ta, tb, em, args);
+  gemm_tf32_tcgen05_pair<BN, STAGES, SPLIT3>
+      <<<static_cast<unsigned>(2 * clusters), GEMM_THREADS, Cfg::SMEM_BYTES, stream>>>(
+          ta, tb, ta_lo, tb_lo, em, args);
   return check_launch("gemm_tf32_tcgen05_pair");
 }
 
@@ -1328,7 +1357,7 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
 
   // Tile width along N.
   const int sms = sm_count(dev);
-  // The 3xTF32 kernel is instantiated for BN = 128 only.
+  // The one-CTA 3xTF32 kernel is instantiated for BN = 128 only.
   int BN = 256;
   if (split3 || d->N <= 128) BN = 128;
   if (!split3 && d->N <= 64) BN = 64;
@@ -1337,10 +1366,11 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
                            d->batch;
     if (t256 < sms && !d->accumulate) BN = 128;  // more, smaller tiles when the grid is thin
   }
-  // CTA pairs (256-row tiles) for plain TF32 GEMMs with enough 256 x 256
-  // tiles to occupy every SM pair; variant 1 forces one CTA, 2 forces pairs.
+  // CTA pairs (256 x 256 tiles, half the L2->SM bytes per flop of a one-CTA
+  // tile) whenever there are enough of them to occupy every SM pair;
+  // variant 1 forces one CTA, 2 forces pairs.
   bool pair = false;
-  if (!split3) {
+  {
     const long long tiles2 = static_cast<long long>((d->M + 2 * BM - 1) / (2 * BM)) *
                              ((d->N + 255) / 256) * (d->reduce_batch ? 1 : d->batch);
     pair = d->variant == 2 || (d->variant == 0 && d->M >= 2 * BM && tiles2 >= sms / 2);
@@ -1416,8 +1446,9 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
     a.epi_tma = eok ? 1 : 0;
   }
 
+  if (split3 && pair) return launch_pair<256, 3, true>(ta, tb, ta_lo, tb_lo, em, a, stream, dev);
   if (split3) return launch_tcgen05<128, 3, true>(ta, tb, ta_lo, tb_lo, em, a, stream, dev);
-  if (pair) return launch_pair<256, 6>(ta, tb, em, a, stream, dev);
+  if (pair) return launch_pair<256, 6, false>(ta, tb, ta, tb, em, a, stream, dev);
   if (BN == 256) return launch_tcgen05<256, 4, false>(ta, tb, ta, tb, em, a, stream, dev);
   if (BN == 128) return launch_tcgen05<128, 6, false>(ta, tb, ta, tb, em, a, stream, dev);
   return launch_tcgen05<64, 8, false>(ta, tb, ta, tb, em, a, stream, dev);

@@ -77,13 +77,18 @@ def test_gemm_modes_tf32(K, rng, M, N, Kd, at, bt):
 
 
 @pytest.mark.parametrize("at,bt", [(0, 0), (1, 0), (0, 1)])
-@pytest.mark.parametrize("M,N,Kd", [(256, 64, 128), (300, 200, 72), (512, 384, 1024)])
-def test_gemm_tf32x3(K, rng, M, N, Kd, at, bt):
+@pytest.mark.parametrize("M,N,Kd,variant", [
+    (256, 64, 128, 0), (300, 200, 72, 0), (512, 384, 1024, 0),
+    (300, 520, 96, 2),      # CTA pair, ragged
+    (2048, 2560, 256, 0),   # enough 256 x 256 tiles for the CTA pair automatically
+])
+def test_gemm_tf32x3(K, rng, M, N, Kd, variant, at, bt):
     A, B = operands(rng, M, N, Kd, at, bt, dist="normal")
     out = torch.empty((M, N), device="cuda")
     ws = torch.empty(K.gemm_workspace_bytes(M, N, Kd, bool(at), bool(bt)) // 4 + 64,
                      device="cuda")
-    K.gemm(dev(A), dev(B), out, a_trans=bool(at), b_trans=bool(bt), precision=1, workspace=ws)
+    K.gemm(dev(A), dev(B), out, a_trans=bool(at), b_trans=bool(bt), precision=1, workspace=ws,
+           variant=variant)
     assert rel_err(host(out), exact(A, B, at, bt)) < TF32X3_TOL
 
 
