@@ -64,13 +64,17 @@ class DataParallelTrainer:
         if self.world > 1:
             dist.broadcast(params, 0, group=self.group)
 
-    def step(self, x: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
+    def step(self, x: torch.Tensor, target: torch.Tensor, _before_target=None) -> torch.Tensor:
         """One step on this rank's shard (x, target already on the device,
         [local_batch*seq, width]). Returns the global mean row loss as a
-        one-element tensor on the model's device (not synchronised)."""
+        one-element tensor on the model's device (not synchronised).
+        _before_target (internal) runs between the forward pass and the use
+        of `target`, e.g. to make the compute stream wait for its copy."""
         m = self.model
         m.zero_grads()
         m.train_forward(x)
+        if _before_target is not None:
+            _before_target()
         row_loss = m.set_target(target)
         works = []
         for s in self.STAGES:
@@ -95,12 +99,13 @@ class DataParallelTrainer:
         """Steps over host-resident batches, one step per (x, target) pair
         of pinned CPU tensors ([local_batch*seq, width] each). The inputs of
         step i+1 are copied host->device on a side stream while step i
-        computes (two device buffer pairs), and each step's mean loss is
-        copied back and read when the following step has been queued.
-        Returns the losses in step order."""
+        computes (two device buffer pairs); within a step the forward pass
+        waits only for x, and the target's copy overlaps it. Each step's
+        mean loss is copied back and read when the following step has been
+        queued. Returns the losses in step order."""
         compute = stream or torch.cuda.current_stream()
         copy = torch.cuda.Stream(device=compute.device)
-        bufs, ready, free = [], [], []
+        bufs, ready, ready_t, free = [], [], [], []
         losses, pending = [], []
         lh = [torch.empty(1, pin_memory=True) for _ in range(2)]
         lev = [torch.cuda.Event() for _ in range(2)]
@@ -111,13 +116,15 @@ class DataParallelTrainer:
                 bufs.append((torch.empty(xh.shape, device=compute.device),
                              torch.empty(th.shape, device=compute.device)))
                 ready.append(torch.cuda.Event())
+                ready_t.append(torch.cuda.Event())
                 free.append(None)
             with torch.cuda.stream(copy):
                 if free[k] is not None:
                     copy.wait_event(free[k])  # step i-2 is done with this pair
                 bufs[k][0].copy_(xh, non_blocking=True)
-                bufs[k][1].copy_(th, non_blocking=True)
                 ready[k].record(copy)
+                bufs[k][1].copy_(th, non_blocking=True)
+                ready_t[k].record(copy)
 
         it = iter(batches)
         nxt = next(it, None)
@@ -129,7 +136,8 @@ class DataParallelTrainer:
             k = i % 2
             compute.wait_event(ready[k])
             with torch.cuda.stream(compute):
-                loss = self.step(*bufs[k])
+                loss = self.step(*bufs[k],
+                                 _before_target=lambda k=k: compute.wait_event(ready_t[k]))
                 ev = torch.cuda.Event()
                 ev.record(compute)
                 free[k] = ev
