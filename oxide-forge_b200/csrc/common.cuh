@@ -19,15 +19,24 @@ __device__ __forceinline__ float apply_binary(float lhs, float rhs, int op) {
 
 // Activation::forward / derivative, src/net/linear.rs:21-70 (tanh GELU with
 // GELU_SCALE = 0.7978846, GELU_CUBIC = 0.044715).
+//
+// The reference's 0.5·x·(1 + tanh(u)) is evaluated through the identity
+// 1 + tanh(u) = 2·sigmoid(2u): GELU(x) = x / (1 + e^(-2u)), and with
+// s = sigmoid(2u), 1 - tanh(u)^2 = 4·s·(1 - s) and 1 - s = e^(-2u)·s. This
+// is the same function without the cancellation of 1 + tanh(u) for
+// negative u, and one exponential replaces tanh. The exponent is capped at
+// 80 (e^80 is finite in f32), where the sigmoid is already below 1e-34.
 constexpr float kGeluScale = 0.7978846f;
 constexpr float kGeluCubic = 0.044715f;
 
+__device__ __forceinline__ float gelu_exp(float x) {
+  const float inner = kGeluScale * (x + kGeluCubic * x * x * x);
+  return fminf(-2.0f * inner, 80.0f);
+}
+
 __device__ __forceinline__ float act_forward(int act, float x) {
   switch (act) {
-    case OXF_ACT_GELU: {
-      const float inner = kGeluScale * (x + kGeluCubic * x * x * x);
-      return 0.5f * x * (1.0f + tanhf(inner));
-    }
+    case OXF_ACT_GELU: return x / (1.0f + expf(gelu_exp(x)));
     case OXF_ACT_RELU: return x > 0.0f ? x : 0.0f;
     case OXF_ACT_SILU: return x / (1.0f + expf(-x));
     default: return x;
@@ -38,10 +47,10 @@ __device__ __forceinline__ float act_derivative(int act, float x) {
   switch (act) {
     case OXF_ACT_GELU: {
       const float quad = kGeluScale * 3.0f * kGeluCubic;
-      const float inner = kGeluScale * (x + kGeluCubic * x * x * x);
-      const float th = tanhf(inner);
+      const float e = expf(gelu_exp(x));
+      const float sg = 1.0f / (1.0f + e);  // (1 + tanh(u)) / 2
       const float dinner = kGeluScale + quad * x * x;
-      return 0.5f * (1.0f + th) + 0.5f * x * (1.0f - th * th) * dinner;
+      return sg * (1.0f + 2.0f * x * (e * sg) * dinner);
     }
     case OXF_ACT_RELU: return x > 0.0f ? 1.0f : 0.0f;
     case OXF_ACT_SILU: {
@@ -53,28 +62,19 @@ __device__ __forceinline__ float act_derivative(int act, float x) {
 }
 
 // Activation forms for GEMM epilogues, where each element costs issue slots
-// of the few epilogue warps: tanh(u) = 1 - 2 / (exp(2u) + 1) from the
+// of the few epilogue warps: the same sigmoid forms as above from the
 // hardware exp2-based __expf and the hardware reciprocal (rcp.approx, within
-// 1 ulp). It saturates to +-1 for large |u| (1/inf = 0) without NaNs.
-// Absolute error in tanh is ~2e-7, far inside the TF32 error of the
-// product feeding it.
+// 1 ulp), relative error ~3e-7, far inside the TF32 error of the product
+// feeding them.
 __device__ __forceinline__ float rcp_approx(float x) {
   float r;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
   return r;
 }
 
-__device__ __forceinline__ float tanh_fast(float u) {
-  const float e = __expf(2.0f * u);
-  return 1.0f - 2.0f * rcp_approx(e + 1.0f);
-}
-
 __device__ __forceinline__ float act_forward_fast(int act, float x) {
   switch (act) {
-    case OXF_ACT_GELU: {
-      const float inner = kGeluScale * (x + kGeluCubic * x * x * x);
-      return 0.5f * x * (1.0f + tanh_fast(inner));
-    }
+    case OXF_ACT_GELU: return x * rcp_approx(1.0f + __expf(gelu_exp(x)));
     case OXF_ACT_RELU: return x > 0.0f ? x : 0.0f;
     case OXF_ACT_SILU: return x * rcp_approx(1.0f + __expf(-x));
     default: return x;
@@ -85,10 +85,10 @@ __device__ __forceinline__ float act_derivative_fast(int act, float x) {
   switch (act) {
     case OXF_ACT_GELU: {
       const float quad = kGeluScale * 3.0f * kGeluCubic;
-      const float inner = kGeluScale * (x + kGeluCubic * x * x * x);
-      const float th = tanh_fast(inner);
+      const float e = __expf(gelu_exp(x));
+      const float sg = rcp_approx(1.0f + e);
       const float dinner = kGeluScale + quad * x * x;
-      return 0.5f * (1.0f + th) + 0.5f * x * (1.0f - th * th) * dinner;
+      return sg * (1.0f + 2.0f * x * (e * sg) * dinner);
     }
     case OXF_ACT_RELU: return x > 0.0f ? 1.0f : 0.0f;
     case OXF_ACT_SILU: {
