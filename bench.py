@@ -57,6 +57,9 @@ def parse():
     ap.add_argument("--seq", type=int, default=SEQ)
     ap.add_argument("--hidden", type=int, default=HIDDEN)
     ap.add_argument("--ffn", type=int, default=FFN)
+    ap.add_argument("--exchange", default="nccl", choices=["nccl", "peer"],
+                    help="train at N>1: gradient exchange = NCCL all-reduce buckets + SGD, or "
+                         "the fused peer-memory exchange + SGD kernel (oxf/exchange.py)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-peak", action="store_true",
@@ -85,7 +88,8 @@ def config_dict(a, world, l2_note=True):
             "model": "oxide-forge transformer block", "seq_len": a.seq, "hidden": a.hidden,
             "ffn": a.ffn, "out": a.hidden, "norm": "layer", "global_batch": a.global_batch,
             "tokens_per_step": a.global_batch * a.seq, "parallelism": f"dp{world}",
-            "lr": LR, "l2": "inputs larger than L2 (1 GiB activations); no flush needed"}
+            "lr": LR, "l2": "inputs larger than L2 (1 GiB activations); no flush needed",
+            **({"gradient_exchange": getattr(a, "exchange", "nccl")} if world > 1 else {})}
 
 
 def flops_per_token(a) -> float:
@@ -614,7 +618,7 @@ def main():
     stream = torch.cuda.current_stream()
     model = models.Transformer(cfg, max_batch=local_batch, stream=stream)
     model.set_params(models.init_transformer_params(cfg, seed=0))
-    trainer = DataParallelTrainer(model, a.global_batch, LR, a.seq)
+    trainer = DataParallelTrainer(model, a.global_batch, LR, a.seq, exchange=a.exchange)
     trainer.broadcast_params(model.params)
 
     rows = local_batch * a.seq
@@ -728,6 +732,7 @@ def main():
             "final_loss": final_loss,
         }
         print(json.dumps(line), flush=True)
+    trainer.close()
     model.close()
     if world > 1:
         dist.destroy_process_group()

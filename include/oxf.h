@@ -292,6 +292,68 @@ oxf_status oxf_matrix_multiply_fp32(oxf_cslice lhs, oxf_cslice rhs, oxf_slice re
 oxf_status oxf_matrix_multiply_refalgo(oxf_cslice lhs, oxf_cslice rhs, oxf_slice result,
                                        size_t len, size_t rows, size_t cols, oxf_stream stream);
 
+/* ---------------------------------------------------------------- peer exchange
+ * Data-parallel SGD over the GPUs of one node in one kernel per rank, over
+ * NVLink peer memory instead of a library all-reduce followed by an update.
+ * No reference counterpart: the reference trains on one GPU
+ * (src/cuda/runtime.rs:34-45) and its update is Linear::learn's
+ * W -= lr * dW (src/net/linear.rs:373-391).
+ *
+ * Every process maps every other rank's parameter arena, gradient arena and
+ * signal pad (CUDA IPC handles, exchanged by the caller). One call of
+ * oxf_exchange_sgd on every rank, with the same offset, count, lr, epoch and
+ * blocks, computes for each element i of [offset, offset + count)
+ *     p_i = p_i - lr * (g0_i + g1_i + ... + g{world-1}_i)
+ * (rank order, left to right) with each rank owning 1/world of the range:
+ * it reads that shard's gradients from every rank, updates its own copy of
+ * the parameters and stores the result into every rank's parameter arena.
+ * All ranks therefore hold bit-identical parameters afterwards; with
+ * world == 1 the result equals oxf_sgd_update bit for bit.
+ *
+ * Two cross-GPU barriers per CTA bracket the data movement: the start barrier
+ * (every rank's kernel has begun, so the gradients its stream produced
+ * before it are complete) and the end barrier (every rank has finished
+ * reading this rank's gradients and writing its parameters). Each barrier
+ * wait is bounded by timeout_us; on expiry the kernel records
+ * OXF_DEVERR_EXCHANGE_START / _END in the device error word (read by
+ * oxf_device_error), skips the rest of its work and returns. */
+#define OXF_EXCHANGE_MAX_RANKS 8
+#define OXF_EXCHANGE_MAX_BLOCKS 1024
+/* Bytes of one rank's signal pad; zero it once before the first call. */
+#define OXF_EXCHANGE_SIGNAL_BYTES (2u * OXF_EXCHANGE_MAX_BLOCKS * OXF_EXCHANGE_MAX_RANKS * 4u)
+#define OXF_DEVERR_EXCHANGE_START 0x201u
+#define OXF_DEVERR_EXCHANGE_END 0x202u
+
+typedef struct {
+  int rank;  /* this process's rank, 0 <= rank < world */
+  int world; /* 1..OXF_EXCHANGE_MAX_RANKS */
+  /* Indexed by rank, each as mapped into this process (its own entry is
+   * local memory). All 16-byte aligned. */
+  float* params[OXF_EXCHANGE_MAX_RANKS];
+  const float* grads[OXF_EXCHANGE_MAX_RANKS];
+  uint32_t* signals[OXF_EXCHANGE_MAX_RANKS];
+  uint32_t epoch;      /* nonzero, larger than every earlier call's on these pads */
+  int blocks;          /* CTAs per rank, equal on all ranks; 0 = one per SM */
+  uint32_t timeout_us; /* bound of each barrier wait; 0 = 4 s */
+} oxf_exchange_desc;
+
+oxf_status oxf_exchange_sgd(const oxf_exchange_desc* desc, size_t offset, size_t count, float lr,
+                            oxf_stream stream);
+
+/* CUDA IPC for the exchange: a handle names the cudaMalloc allocation that
+ * holds `ptr` plus ptr's offset inside it. oxf_ipc_open maps another
+ * process's allocation (peer access over NVLink) and returns the pointer at
+ * the same offset; oxf_ipc_close unmaps it. A process does not open its own
+ * handles. */
+typedef struct {
+  unsigned char handle[64]; /* cudaIpcMemHandle_t */
+  uint64_t offset;
+} oxf_ipc_handle;
+
+oxf_status oxf_ipc_export(const void* ptr, oxf_ipc_handle* out);
+oxf_status oxf_ipc_open(const oxf_ipc_handle* handle, void** ptr);
+oxf_status oxf_ipc_close(const oxf_ipc_handle* handle, void* ptr);
+
 #ifdef __cplusplus
 }
 #endif

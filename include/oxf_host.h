@@ -166,6 +166,35 @@ oxf_status oxf_transformer_load(const char* path, int max_batch, oxf_stream stre
 oxf_status oxf_mlp_dump(oxf_mlp m, const char* path);
 oxf_status oxf_mlp_load(const char* path, size_t max_rows, oxf_stream stream, oxf_mlp* out);
 
+/* ---------------------------------------------------------------- peer exchange */
+/* One rank's side of the fused gradient exchange + SGD (oxf_exchange_sgd in
+ * oxf.h) over a parameter and a gradient arena of `count` floats each,
+ * e.g. oxf_transformer_params / _grads. Usage, on every rank of one node
+ * (one process per GPU): create; send the three handles of
+ * oxf_exchange_handles to every rank (any host transport); connect with all
+ * ranks' handles; then oxf_exchange_step once per gradient bucket, in the
+ * same order on every rank. No reference counterpart (single-GPU
+ * reference, src/cuda/runtime.rs:34-45). */
+typedef struct oxf_exchange_s* oxf_exchange;
+
+/* Allocates and zeroes this rank's signal pad on the current device. */
+oxf_status oxf_exchange_create(int rank, int world, float* params, float* grads, size_t count,
+                               oxf_exchange* out);
+/* This rank's handles: out[0] params, out[1] grads, out[2] signal pad. */
+oxf_status oxf_exchange_handles(oxf_exchange ex, oxf_ipc_handle out[3]);
+/* Maps every other rank's memory: all[3*q + 0..2] are rank q's handles
+ * (this rank's entries are not opened). Once per exchange. */
+oxf_status oxf_exchange_connect(oxf_exchange ex, const oxf_ipc_handle* all);
+/* oxf_exchange_sgd over [offset, offset + count) of the arenas with the
+ * next epoch; blocks = CTAs per rank (0: one per SM), equal on all ranks. */
+oxf_status oxf_exchange_step(oxf_exchange ex, size_t offset, size_t count, float lr, int blocks,
+                             oxf_stream stream);
+/* Bound of each barrier wait in later steps (0: 4 s). */
+oxf_status oxf_exchange_set_timeout(oxf_exchange ex, uint32_t timeout_us);
+/* Unmaps the peers' memory and frees the pad. Every rank must have finished
+ * its last step first (synchronise, then a host barrier). */
+oxf_status oxf_exchange_destroy(oxf_exchange ex);
+
 #ifdef __cplusplus
 }
 #endif

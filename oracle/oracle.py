@@ -65,6 +65,7 @@ def lib() -> C.CDLL:
             "oxo_unary": (C.c_float, [C.c_int, C.c_float, C.c_float]),
             "oxo_map_sum": (C.c_float, [fp, sz, C.c_int, C.c_float]),
             "oxo_matrix_slice": (None, [fp, fp, sz, sz, sz, sz, sz]),
+            "oxo_exchange_sgd": (None, [C.c_void_p, C.c_void_p, C.c_int, sz, sz, C.c_float]),
             "oxo_causal_mask": (None, [fp, sz, sz, sz]),
             "oxo_softmax_rows": (None, [fp, sz, sz, C.c_float, sz]),
             "oxo_layer_norm_rows": (None, [fp, sz, sz, C.c_float, fp, fp]),
@@ -193,6 +194,18 @@ def fill_random(n, seed):
 def map_sum(x, op, param=0.0):
     x = _c(x)
     return float(lib().oxo_map_sum(_p(x), x.size, op, param))
+
+
+def exchange_sgd(params: list, grads: list, offset: int, count: int, lr: float) -> list:
+    """Every rank's parameters after the data-parallel update of
+    [offset, offset+count) (oxo_exchange_sgd); inputs are not modified."""
+    ps = [_c(p).copy() for p in params]
+    gs = [_c(g) for g in grads]
+    W = len(ps)
+    pp = (C.c_void_p * W)(*[p.ctypes.data for p in ps])
+    gp = (C.c_void_p * W)(*[g.ctypes.data for g in gs])
+    lib().oxo_exchange_sgd(pp, gp, W, offset, count, lr)
+    return ps
 
 
 def matrix_slice(m, tile_rows, tile_cols, tiles_per_row, n_tiles):

@@ -351,6 +351,17 @@ float oxo_map_sum(const float* x, size_t n, int op, float p) {
     return s;
 }
 
+/* Data-parallel update across ranks; contract in oxf_oracle.h. */
+void oxo_exchange_sgd(float* const* params, const float* const* grads, int world, size_t offset,
+                      size_t count, float lr) {
+    for (size_t i = offset; i < offset + count; ++i) {
+        float s = grads[0][i];
+        for (int q = 1; q < world; ++q) s += grads[q][i];
+        const float r = fmaf(-s, lr, params[0][i]);
+        for (int q = 0; q < world; ++q) params[q][i] = r;
+    }
+}
+
 /* matrix_slice_device, layout.rs:58-86. */
 void oxo_matrix_slice(const float* in, float* out, size_t out_len, size_t input_cols,
                       size_t tile_rows, size_t tile_cols, size_t tiles_per_row) {

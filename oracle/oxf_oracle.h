@@ -88,6 +88,16 @@ float oxo_map_sum(const float* x, size_t n, int op, float p);
 void oxo_matrix_slice(const float* in, float* out, size_t out_len, size_t input_cols,
                       size_t tile_rows, size_t tile_cols, size_t tiles_per_row);
 
+/* The data-parallel update over `world` ranks' arenas (the per-rank update
+ * is Linear::learn's W -= lr * dW, linear.rs:373-391; the reference itself
+ * is single-GPU): for i in [offset, offset + count),
+ *   p_i = p_i - lr * (g0_i + g1_i + ... + g{world-1}_i)
+ * with the gradients summed left to right in f32 and the update rounded
+ * once (fmaf), then written to every rank's parameters. The source value
+ * is params[0][i] (all ranks hold equal parameters before the step). */
+void oxo_exchange_sgd(float* const* params, const float* const* grads, int world, size_t offset,
+                      size_t count, float lr);
+
 /* row.rs:16-53 (per-row sum). */
 void oxo_sum_rows(const float* m, float* out, size_t rows, size_t cols);
 /* Column sum = sum_rows(transpose(G)), linear.rs:267-270. */

@@ -56,6 +56,12 @@ oxf_status gemm_refalgo(const float*, const float*, float*, size_t, size_t, size
 oxf_status gemm_read_device_error(uint32_t*);
 oxf_status wait_selftest(unsigned long long, int*, cudaStream_t);
 oxf_status gemm_tf32x3_noalloc(const oxf_gemm_desc*, cudaStream_t);
+// exchange.cu
+oxf_status exchange_sgd(const oxf_exchange_desc*, size_t, size_t, float, cudaStream_t);
+oxf_status exchange_read_device_error(uint32_t*);
+oxf_status ipc_export(const void*, oxf_ipc_handle*);
+oxf_status ipc_open(const oxf_ipc_handle*, void**);
+oxf_status ipc_close(const oxf_ipc_handle*, void*);
 
 namespace {
 thread_local char g_last_error[512] = "";
@@ -119,7 +125,24 @@ unsigned long long oxf_kernel_launches(void) { return g_launches.load(); }
 oxf_status oxf_device_error(uint32_t* code) {
   if (!code) return set_error(OXF_ERR_INVALID_ARG, "oxf_device_error: null code");
   OXF_TRY(check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize"));
-  return gemm_read_device_error(code);
+  // Each translation unit with bounded waits has its own word; report the
+  // first nonzero one and clear both.
+  uint32_t g = 0, x = 0;
+  OXF_TRY(gemm_read_device_error(&g));
+  OXF_TRY(exchange_read_device_error(&x));
+  *code = g ? g : x;
+  return OXF_OK;
+}
+
+oxf_status oxf_exchange_sgd(const oxf_exchange_desc* desc, size_t offset, size_t count, float lr,
+                            oxf_stream stream) {
+  return exchange_sgd(desc, offset, count, lr, S(stream));
+}
+
+oxf_status oxf_ipc_export(const void* ptr, oxf_ipc_handle* out) { return ipc_export(ptr, out); }
+oxf_status oxf_ipc_open(const oxf_ipc_handle* handle, void** ptr) { return ipc_open(handle, ptr); }
+oxf_status oxf_ipc_close(const oxf_ipc_handle* handle, void* ptr) {
+  return ipc_close(handle, ptr);
 }
 
 oxf_status oxf_wait_timeout_selftest(uint32_t limit_us, int* expired, oxf_stream stream) {

@@ -72,6 +72,12 @@ SIGS: dict = {
                                        C.POINTER(C.c_void_p)]),
     "oxf_mlp_dump": (C.c_int, [_h, C.c_char_p]),
     "oxf_mlp_load": (C.c_int, [C.c_char_p, _sz, C.c_void_p, C.POINTER(C.c_void_p)]),
+    "oxf_exchange_create": (C.c_int, [C.c_int, C.c_int, _fp, _fp, _sz, C.POINTER(C.c_void_p)]),
+    "oxf_exchange_handles": (C.c_int, [_h, C.c_void_p]),
+    "oxf_exchange_connect": (C.c_int, [_h, C.c_void_p]),
+    "oxf_exchange_step": (C.c_int, [_h, _sz, _sz, C.c_float, C.c_int, C.c_void_p]),
+    "oxf_exchange_set_timeout": (C.c_int, [_h, C.c_uint32]),
+    "oxf_exchange_destroy": (C.c_int, [_h]),
 }
 
 

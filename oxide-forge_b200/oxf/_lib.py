@@ -58,6 +58,27 @@ class GemmDesc(C.Structure):
     ]
 
 
+# Peer exchange (oxf.h): limits, device error codes, descriptor and handle.
+EXCHANGE_MAX_RANKS = 8
+EXCHANGE_MAX_BLOCKS = 1024
+EXCHANGE_SIGNAL_BYTES = 2 * EXCHANGE_MAX_BLOCKS * EXCHANGE_MAX_RANKS * 4
+DEVERR_EXCHANGE_START, DEVERR_EXCHANGE_END = 0x201, 0x202
+
+
+class IpcHandle(C.Structure):
+    _fields_ = [("handle", C.c_ubyte * 64), ("offset", C.c_uint64)]
+
+
+class ExchangeDesc(C.Structure):
+    _fields_ = [
+        ("rank", C.c_int), ("world", C.c_int),
+        ("params", C.c_void_p * EXCHANGE_MAX_RANKS),
+        ("grads", C.c_void_p * EXCHANGE_MAX_RANKS),
+        ("signals", C.c_void_p * EXCHANGE_MAX_RANKS),
+        ("epoch", C.c_uint32), ("blocks", C.c_int), ("timeout_us", C.c_uint32),
+    ]
+
+
 _lib = None
 
 # name -> (restype, argtypes)
@@ -115,6 +136,11 @@ _SIGS = {
                                           C.c_size_t, C.c_void_p]),
     "oxf_matrix_multiply_refalgo": (C.c_int, [CSlice, CSlice, Slice, C.c_size_t, C.c_size_t,
                                               C.c_size_t, C.c_void_p]),
+    "oxf_exchange_sgd": (C.c_int, [C.POINTER(ExchangeDesc), C.c_size_t, C.c_size_t, C.c_float,
+                                   C.c_void_p]),
+    "oxf_ipc_export": (C.c_int, [C.c_void_p, C.POINTER(IpcHandle)]),
+    "oxf_ipc_open": (C.c_int, [C.POINTER(IpcHandle), C.POINTER(C.c_void_p)]),
+    "oxf_ipc_close": (C.c_int, [C.POINTER(IpcHandle), C.c_void_p]),
 }
 
 

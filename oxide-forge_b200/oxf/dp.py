@@ -11,6 +11,14 @@ averaged over the global batch:  W -= lr * (1/B) * sum_b grad_b.
 For one sequence this is exactly the reference's update (every weight is
 used for dX before it is updated, so deferring the update changes nothing).
 
+With exchange="peer" the bucket all-reduces and the final update are
+replaced by the fused peer-memory exchange (oxf/exchange.py): after each
+backward stage one kernel per rank pulls its shard of the bucket's
+gradients from every GPU over NVLink, updates that shard and pushes it to
+every GPU's parameters. The update of each bucket then happens as soon as
+its gradients are complete (no later stage reads that bucket's weights;
+the next forward pass waits for all of them).
+
 The model object only needs the engine interface used below, so the same
 driver runs over `gloo` on CPU in tests with a host stand-in model.
 """
@@ -46,9 +54,20 @@ class DataParallelTrainer:
 
     STAGES = (0, 1, 2)
 
+    EXCHANGES = ("nccl", "peer")
+
     def __init__(self, model, global_batch: int, lr: float, seq: int, group=None,
-                 overlap: bool = True):
+                 overlap: bool = True, exchange: str = "nccl", overlap_blocks: int = 32):
+        if exchange not in self.EXCHANGES:
+            raise ValueError(f"exchange must be one of {self.EXCHANGES}")
+        if exchange == "peer" and not (torch.cuda.is_available()
+                                       and getattr(model.params, "is_cuda", False)):
+            raise ValueError("exchange='peer' needs a CUDA engine (peer memory over NVLink)")
         self.model = model
+        self.exchange = exchange
+        self.overlap_blocks = overlap_blocks
+        self._peer = None
+        self._xstream = None
         self.rank, self.world = world()
         self.global_batch = global_batch
         self.local = shard(global_batch, self.rank, self.world)
@@ -70,6 +89,8 @@ class DataParallelTrainer:
         one-element tensor on the model's device (not synchronised).
         _before_target (internal) runs between the forward pass and the use
         of `target`, e.g. to make the compute stream wait for its copy."""
+        if self.exchange == "peer":
+            return self._step_peer(x, target, _before_target)
         m = self.model
         m.zero_grads()
         m.train_forward(x)
@@ -94,6 +115,45 @@ class DataParallelTrainer:
                     w.wait()
         m.sgd(self.lr / self.global_batch)
         return loss / (self.global_batch * self.seq)
+
+    def _step_peer(self, x, target, _before_target):
+        """step() with the fused exchange: every bucket's kernel runs on one
+        side stream (so a rank's exchanges never overlap one another), each
+        after its backward stage; the compute stream waits for the last."""
+        from .exchange import PeerExchange
+
+        m = self.model
+        compute = torch.cuda.current_stream()
+        if self._peer is None:
+            self._peer = PeerExchange(m.params, m.grads, group=self.group)
+            self._xstream = torch.cuda.Stream(device=compute.device)
+        xs = self._xstream
+        lr = self.lr / self.global_batch
+        m.zero_grads()
+        m.train_forward(x)
+        if _before_target is not None:
+            _before_target()
+        row_loss = m.set_target(target)
+        last = self.STAGES[-1]
+        for s in self.STAGES:
+            m.backward_stage(s)
+            off, cnt = m.bucket(s)
+            xs.wait_stream(compute)
+            # Buckets that overlap later backward stages use few CTAs; the
+            # last one has the GPU to itself.
+            self._peer.step(off, cnt, lr, blocks=0 if s == last else self.overlap_blocks,
+                            stream=xs)
+        loss = row_loss.sum().reshape(1)
+        if self.world > 1:
+            dist.all_reduce(loss, group=self.group)
+        compute.wait_stream(xs)
+        return loss / (self.global_batch * self.seq)
+
+    def close(self) -> None:
+        """Releases the peer exchange (collective when exchange='peer')."""
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
 
     def run_host(self, batches, stream: torch.cuda.Stream | None = None) -> list[float]:
         """Steps over host-resident batches, one step per (x, target) pair

@@ -173,3 +173,13 @@ def test_dead_rank_is_an_error_not_a_hang(tmp_path):
     out = _run(2, 4, 3, tmp_path, fail_rank=1)
     assert 1 not in out                               # rank 1 exited without a result
     assert out[0].get("error"), out[0].keys()        # rank 0 got an error from its collective
+
+
+def test_peer_exchange_needs_cuda_arenas():
+    sys.path.insert(0, str(ROOT / "oxide-forge_b200"))
+    from oxf.dp import DataParallelTrainer
+    model = OracleModel(_flat0())
+    with pytest.raises(ValueError):
+        DataParallelTrainer(model, 4, lr=0.1, seq=SEQ, exchange="peer")
+    with pytest.raises(ValueError):
+        DataParallelTrainer(model, 4, lr=0.1, seq=SEQ, exchange="allgather")

@@ -227,3 +227,26 @@ def test_map_sum_and_matrix_slice_known_answers(rng):
     got = O.matrix_slice(m, 3, 4, 2, 4)
     want = np.concatenate([m[r:r + 3, c:c + 4].ravel() for r in (0, 3) for c in (0, 4)])
     np.testing.assert_array_equal(got, want)
+
+
+def test_exchange_sgd_known_answers():
+    """The data-parallel update: rank-order f32 sum, one rounding, every
+    rank written, nothing outside [offset, offset+count) touched."""
+    n = 11
+    p = np.arange(n, dtype=np.float32)
+    g = [np.full(n, v, np.float32) for v in (1.0, 2.0, 3.0)]
+    out = O.exchange_sgd([p, p, p], g, 2, 7, 0.5)
+    for q in range(3):
+        want = p.copy()
+        want[2:9] -= np.float32(3.0)  # 0.5 * (1 + 2 + 3)
+        np.testing.assert_array_equal(out[q], want)
+    np.testing.assert_array_equal(p, np.arange(n, dtype=np.float32))  # inputs untouched
+    # left-to-right order: (1e8 + 1) rounds to 1e8 in f32, then - 1e8 = 0
+    g = [np.float32([1e8]), np.float32([1.0]), np.float32([-1e8])]
+    out = O.exchange_sgd([np.float32([5.0])] * 3, g, 0, 1, 1.0)
+    assert out[0][0] == 5.0 and out[2][0] == 5.0
+    # one rounding: p - s*lr with s*lr not representable
+    p1, g1 = np.float32([1.0]), np.float32([1.0 + 2.0 ** -23])
+    lr = np.float32(1.0 - 2.0 ** -24)
+    want = np.float32(np.float64(p1[0]) - np.float64(g1[0]) * np.float64(lr))
+    assert O.exchange_sgd([p1], [g1], 0, 1, float(lr))[0][0] == want
