@@ -60,17 +60,21 @@ def parse():
     ap.add_argument("--exchange", default="nccl", choices=["nccl", "peer"],
                     help="train at N>1: gradient exchange = NCCL all-reduce buckets + SGD, or "
                          "the fused peer-memory exchange + SGD kernel (oxf/exchange.py)")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="train at N>1: exchange gradients after the whole backward pass "
+                         "instead of per bucket during it")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-peak", action="store_true",
                     help="skip the cuBLAS denominator (profiling runs: keeps the launch list "
                          "to the step's own kernels); roofline.peak is then null")
     ap.add_argument("--workload", default="train",
-                    choices=["train", "linear", "gemm", "rows", "mlp", "infer"],
+                    choices=["train", "linear", "gemm", "rows", "mlp", "infer", "exchange"],
                     help="train: the contract line (config 5). The others are supplementary "
                          "single-GPU measurements of configs 1-4: linear (config 1), gemm "
                          "(square sweep / one shape), rows (config 2 row suite), mlp "
-                         "(config 3), infer (config 4)")
+                         "(config 3), infer (config 4); exchange: gradient exchange + SGD over the "
+                         "config-5 arena at N GPUs, fused peer kernel vs NCCL + SGD")
     ap.add_argument("--shape", default=None, help="gemm: M,N,K (default: the 512..8192 sweep)")
     ap.add_argument("--mode", default="nn", help="gemm: nn, nt, tn or tt")
     ap.add_argument("--epi", default="none",
@@ -89,7 +93,8 @@ def config_dict(a, world, l2_note=True):
             "ffn": a.ffn, "out": a.hidden, "norm": "layer", "global_batch": a.global_batch,
             "tokens_per_step": a.global_batch * a.seq, "parallelism": f"dp{world}",
             "lr": LR, "l2": "inputs larger than L2 (1 GiB activations); no flush needed",
-            **({"gradient_exchange": getattr(a, "exchange", "nccl")} if world > 1 else {})}
+            **({"gradient_exchange": getattr(a, "exchange", "nccl"),
+                "exchange_overlap": not getattr(a, "no_overlap", False)} if world > 1 else {})}
 
 
 def flops_per_token(a) -> float:
@@ -527,6 +532,88 @@ def run_mlp(a, torch):
     eng.close()
 
 
+def run_exchange(a, torch):
+    """Gradient exchange + SGD over a parameter arena the size of config 5's
+    (seq, hidden, ffn as given; 52.4 M f32 at the defaults) on N GPUs: the
+    fused peer-memory kernel (oxf/exchange.py, one launch per call) against
+    NCCL all-reduce followed by the SGD kernel. Device time per call (CUDA
+    events around `steps` back-to-back calls, after `warmup`, max over
+    ranks). Roofline of the fused kernel: per rank, (N-1)/N of the arena
+    (4 B per element) crosses NVLink in each direction (gradients in,
+    parameters out), against the measured 770 GB/s peer-copy bandwidth per
+    direction."""
+    import torch.distributed as dist
+    from datetime import timedelta
+    from oxf import kernels as K
+    from oxf import models
+    from oxf.exchange import PeerExchange
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    cfg = models.transformer_config(a.seq, a.hidden, a.ffn)
+    n = cfg.param_count()
+    g = torch.Generator(device="cuda").manual_seed(5)
+    params = torch.empty(n, device="cuda").uniform_(-0.05, 0.05, generator=g)
+    g.manual_seed(100 + rank)
+    grads = torch.randn(n, device="cuda", generator=g)
+    gbuf = grads.clone()
+    lr = 1e-6
+    x = PeerExchange(params, grads)
+    stream = torch.cuda.current_stream()
+
+    def timed(fn):
+        for _ in range(a.warmup):
+            fn()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = _events(torch)
+        e0.record(stream)
+        for _ in range(a.steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / a.steps
+        if world > 1:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = t.item()
+        return ms
+
+    res = {}
+    sms = torch.cuda.get_device_properties(local_rank).multi_processor_count
+    for blocks in (sms, 2 * sms, 4 * sms):
+        res[f"peer_blocks_{blocks}"] = timed(lambda: x.step(0, n, lr, blocks=blocks))
+
+    def nccl_then_sgd():
+        if world > 1:
+            dist.all_reduce(gbuf)
+        K.sgd_update(params, gbuf, lr)
+
+    res["nccl_allreduce_then_sgd"] = timed(nccl_then_sgd)
+    if world > 1:
+        res["nccl_allreduce_only"] = timed(lambda: dist.all_reduce(gbuf))
+    x.close()
+    if rank == 0:
+        remote = (world - 1) / world * 4 * n
+        best = min(v for k, v in res.items() if k.startswith("peer"))
+        line = {"metric": "gradient exchange + SGD", "unit": "ms per call", "n_gpus": world,
+                "elements": n, "arena_bytes": 4 * n, "steps": a.steps, "warmup": a.warmup,
+                "ms": res,
+                "roofline": {"bound": "nvlink", "bytes_per_direction_per_rank": remote,
+                             "achieved_gbs": remote / (best * 1e-3) / 1e9 if remote else None,
+                             "peak_gbs": 770.0, "peak_source": "measured peer copy per "
+                             "direction on this pool",
+                             "frac": remote / (best * 1e-3) / 770e9 if remote else None}}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def run_infer(a, torch):
     """Config 4: single-head Post-Norm transformer inference, NormType::Rms,
     per sequence [2048,1024], FFN 1024->4096->1024 GELU, Xavier-uniform
@@ -594,7 +681,7 @@ def main():
         import torch
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
         {"gemm": run_gemm, "rows": run_rows, "mlp": run_mlp, "infer": run_infer,
-         "linear": run_linear}[a.workload](
+         "linear": run_linear, "exchange": run_exchange}[a.workload](
             a, torch)
         return
     import numpy as np
@@ -618,7 +705,8 @@ def main():
     stream = torch.cuda.current_stream()
     model = models.Transformer(cfg, max_batch=local_batch, stream=stream)
     model.set_params(models.init_transformer_params(cfg, seed=0))
-    trainer = DataParallelTrainer(model, a.global_batch, LR, a.seq, exchange=a.exchange)
+    trainer = DataParallelTrainer(model, a.global_batch, LR, a.seq, exchange=a.exchange,
+                                  overlap=not a.no_overlap)
     trainer.broadcast_params(model.params)
 
     rows = local_batch * a.seq

@@ -137,12 +137,19 @@ class DataParallelTrainer:
         last = self.STAGES[-1]
         for s in self.STAGES:
             m.backward_stage(s)
+            if not self.overlap:
+                continue
             off, cnt = m.bucket(s)
             xs.wait_stream(compute)
             # Buckets that overlap later backward stages use few CTAs; the
             # last one has the GPU to itself.
             self._peer.step(off, cnt, lr, blocks=0 if s == last else self.overlap_blocks,
                             stream=xs)
+        if not self.overlap:
+            # One exchange over the whole arena once backward is done: no
+            # exchange CTA shares the GPU with a backward GEMM.
+            xs.wait_stream(compute)
+            self._peer.step(0, m.grads.numel(), lr, blocks=0, stream=xs)
         loss = row_loss.sum().reshape(1)
         if self.world > 1:
             dist.all_reduce(loss, group=self.group)
