@@ -538,9 +538,11 @@ def run_exchange(a, torch):
     fused peer-memory kernel (oxf/exchange.py, one launch per call) against
     NCCL all-reduce followed by the SGD kernel. Device time per call (CUDA
     events around `steps` back-to-back calls, after `warmup`, max over
-    ranks). Roofline of the fused kernel: per rank, (N-1)/N of the arena
-    (4 B per element) crosses NVLink in each direction (gradients in,
-    parameters out), against the measured 770 GB/s peer-copy bandwidth per
+    ranks). Roofline of the fused kernel: each direction of a rank's NVLink
+    carries 2*(N-1)/N of the arena (4 B per element): out, the parameters it
+    pushes and the gradients peers pull from it; in, the gradients it pulls
+    and the parameters peers push to it. The same volume as a ring
+    all-reduce, against the measured 770 GB/s peer-copy bandwidth per
     direction."""
     import torch.distributed as dist
     from datetime import timedelta
@@ -599,7 +601,7 @@ def run_exchange(a, torch):
         res["nccl_allreduce_only"] = timed(lambda: dist.all_reduce(gbuf))
     x.close()
     if rank == 0:
-        remote = (world - 1) / world * 4 * n
+        remote = 2 * (world - 1) / world * 4 * n
         best = min(v for k, v in res.items() if k.startswith("peer"))
         line = {"metric": "gradient exchange + SGD", "unit": "ms per call", "n_gpus": world,
                 "elements": n, "arena_bytes": 4 * n, "steps": a.steps, "warmup": a.warmup,
