@@ -27,7 +27,9 @@
 #include <algorithm>
 #include <cstdint>
 #include <cstring>
+#include <cstdlib>
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "ptx.cuh"
@@ -63,6 +65,11 @@ struct GemmArgs {
   int group_m;       // raster: tiles walk N within groups of group_m row tiles
   int epi_tma;       // epilogue moves tiles by TMA (else per-thread global accesses)
   int c3d, p3d, r3d, x3d;  // epilogue tensor maps carry a batch coordinate
+  // Dynamic schedule: units are claimed from *sched_next (zero at launch);
+  // the last CTA to finish resets it and *sched_done. Null: static schedule
+  // (CTA c takes units c, c + grid, c + 2 grid, ...).
+  unsigned long long* sched_next;
+  unsigned int* sched_done;
 };
 
 // Tensor maps of the epilogue operands: 32 x 32 f32 boxes, 128B swizzle.
@@ -88,6 +95,10 @@ struct GemmCfg {
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
+// Depth of the tile queue through which the producer publishes the units it
+// claims under the dynamic schedule.
+constexpr int TQ = 4;
+
 template <int STAGES>
 struct GemmCtrl {
   uint64_t full[STAGES];
@@ -95,6 +106,9 @@ struct GemmCtrl {
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint64_t epi[EPI_WARPS];  // one per epilogue warp: its staged operand loads
+  uint64_t qfull[TQ];       // tile queue: entry published (one arrive, the leader's producer)
+  uint64_t qempty[TQ];      // tile queue (leader CTA): entry read by every consumer
+  long long qunit[TQ];      // the published unit, -1 = no more work
   uint32_t tmem_base;
   volatile uint32_t abort_flag;
 };
@@ -116,6 +130,80 @@ __device__ __forceinline__ void decode_unit(const GemmArgs& a, long long u, int&
   tn = inner / gm;
   kb0 = static_cast<int>((static_cast<long long>(s) * a.kblocks) / a.splits);
   kb1 = static_cast<int>((static_cast<long long>(s + 1) * a.kblocks) / a.splits);
+}
+
+// ---------------------------------------------------------------- unit schedule
+// A persistent CTA (or CTA pair) processes the units of its sequence i = 0,
+// 1, 2, ... Static: unit first + i * stride. Dynamic: the leader CTA's
+// producer claims each unit from a global counter and publishes it through
+// the tile queue (qunit/qfull, and the partner CTA's copy for a pair); every
+// other role takes it from there. A CTA that starts late, because other
+// kernels occupy SMs, then simply claims fewer units instead of delaying the
+// whole grid with a fixed share. Units are claimed in increasing order, so
+// the tiles in flight stay a contiguous window of the raster, as with the
+// static order.
+
+__device__ __forceinline__ long long static_unit(const GemmArgs& a, long long first,
+                                                 long long stride, int i) {
+  const long long u = first + static_cast<long long>(i) * stride;
+  return u < a.units ? u : -1;
+}
+
+// Producer of the leader CTA: claims the i-th unit and publishes it to this
+// CTA's queue and, for a pair, to the partner's. False on a wait expiry.
+template <int STAGES, bool PAIR>
+__device__ __forceinline__ bool queue_publish(GemmCtrl<STAGES>* ctrl, const GemmArgs& a, int i,
+                                              long long* u_out) {
+  const int slot = i % TQ;
+  const uint32_t par = static_cast<uint32_t>(i / TQ) & 1u;
+  if (!mbar_wait(&ctrl->qempty[slot], par ^ 1u, DEVERR_GEMM_QUEUE)) return false;
+  long long u = static_cast<long long>(atomicAdd(a.sched_next, 1ull));
+  if (u >= a.units) u = -1;
+  ctrl->qunit[slot] = u;
+  if (PAIR) {
+    st_cluster_s64(map_to_rank(&ctrl->qunit[slot], 1), u);
+    mbar_arrive_remote(map_to_rank(&ctrl->qfull[slot], 1));
+  }
+  mbar_arrive(&ctrl->qfull[slot]);
+  *u_out = u;
+  return true;
+}
+
+// Any other role: reads the i-th published unit. `release` (one thread per
+// consumer) frees the entry on the leader CTA's qempty (cluster address of
+// qempty[0]; entries are 8 bytes apart). False on a wait expiry.
+template <int STAGES>
+__device__ __forceinline__ bool queue_take(GemmCtrl<STAGES>* ctrl, int i, uint32_t qempty0,
+                                           bool release, long long* u_out) {
+  const int slot = i % TQ;
+  const uint32_t par = static_cast<uint32_t>(i / TQ) & 1u;
+  if (!mbar_wait_cluster(&ctrl->qfull[slot], par, DEVERR_GEMM_QUEUE)) return false;
+  *u_out = ctrl->qunit[slot];
+  if (release) mbar_arrive_remote(qempty0 + 8u * static_cast<uint32_t>(slot));
+  return true;
+}
+
+// The i-th unit if it is already published (-2 if not yet), without taking
+// it: the epilogue's look-ahead for its next tile's first input.
+template <int STAGES>
+__device__ __forceinline__ long long queue_peek(GemmCtrl<STAGES>* ctrl, int i) {
+  const int slot = i % TQ;
+  const uint32_t par = static_cast<uint32_t>(i / TQ) & 1u;
+  if (!mbar_test_wait_cluster(&ctrl->qfull[slot], par)) return -2;
+  return ctrl->qunit[slot];
+}
+
+// Dynamic schedule only: the last CTA of the grid to finish resets the
+// counter for the next launch on this slot (every CTA reaches this point,
+// aborted ones included, after its producer stopped claiming).
+__device__ __forceinline__ void schedule_release(const GemmArgs& a) {
+  if (a.sched_next == nullptr || threadIdx.x != 0) return;
+  __threadfence();
+  if (atomicAdd(a.sched_done, 1u) == gridDim.x - 1) {
+    *a.sched_next = 0ull;
+    *a.sched_done = 0u;
+    __threadfence();
+  }
 }
 
 // Shared-memory descriptor of one K=8 slice of an operand tile.
@@ -397,9 +485,9 @@ __device__ __forceinline__ bool epilogue_chunk_tma(const GemmArgs& a, const EpiM
 // alternate column chunk of the same tile, else its first chunk of the next
 // unit its CTA (pair) owns. Rows of a unit start at tm * a.bm + row_off.
 template <int BN>
-__device__ __forceinline__ bool epi_next_chunk(const GemmArgs& a, long long u, long long stride,
-                                               int c, int group, int row_off, int b, int tn,
-                                               int m0, int& nb, int& nm0, int& nn0) {
+__device__ __forceinline__ bool epi_next_chunk(const GemmArgs& a, long long u2, int c, int group,
+                                               int row_off, int b, int tn, int m0, int& nb,
+                                               int& nm0, int& nn0) {
   const int c2 = c + EPI_GROUPS;
   if (c2 < BN / 32 && tn * BN + c2 * 32 < a.N) {
     nb = b;
@@ -407,8 +495,7 @@ __device__ __forceinline__ bool epi_next_chunk(const GemmArgs& a, long long u, l
     nn0 = tn * BN + c2 * 32;
     return true;
   }
-  const long long u2 = u + stride;
-  if (u2 >= a.units) return false;
+  if (u2 < 0 || u2 >= a.units) return false;  // no next unit, or not yet known
   int tm2, tn2, kb0, kb1;
   decode_unit(a, u2, nb, tm2, tn2, kb0, kb1);
   nm0 = tm2 * a.bm + row_off;
@@ -446,6 +533,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
 #pragma unroll
     for (int w = 0; w < EPI_WARPS; ++w) mbar_init(&ctrl->epi[w], 1);
+#pragma unroll
+    for (int q = 0; q < TQ; ++q) {
+      mbar_init(&ctrl->qfull[q], 1);                // the producer's publish
+      mbar_init(&ctrl->qempty[q], 1 + EPI_WARPS);  // the MMA issuer and every epilogue warp
+    }
     ctrl->abort_flag = 0;
     fence_barrier_init();
   }
@@ -465,6 +557,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = ctrl->tmem_base;
+  const bool dyn = args.sched_next != nullptr;
+  const uint32_t qempty0 = map_to_rank(&ctrl->qempty[0], 0);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -472,7 +566,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       uint32_t stage = 0, phase = 0;
       long long fills = 0;
       const uint64_t pol_a = make_l2_policy(L2_NORMAL), pol_b = pol_a;
-      for (long long u = blockIdx.x; u < args.units && !ctrl->abort_flag; u += gridDim.x) {
+      for (int i = 0; !ctrl->abort_flag; ++i) {
+        long long u;
+        if (dyn) {
+          if (!queue_publish<STAGES, false>(ctrl, args, i, &u)) {
+            ctrl->abort_flag = 1;
+            break;
+          }
+        } else {
+          u = static_unit(args, blockIdx.x, gridDim.x, i);
+        }
+        if (u < 0) break;
         int b, tm, tn, kb0, kb1;
         decode_unit(args, u, b, tm, tn, kb0, kb1);
         // Batch-reduce GEMMs walk K over (batch item, k-block) pairs; the
@@ -520,14 +624,22 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       uint32_t stage = 0, phase = 0;
-      int local = 0;
       // Descriptors of stage 0, K slice 0; every other (stage, slice) is an
       // address offset from these.
       const uint64_t a_desc0 = operand_desc(smem_u32(ring), args.a_mn, 0);
       const uint64_t b_desc0 = operand_desc(smem_u32(ring) + Cfg::A_BYTES, args.b_mn, 0);
       const uint32_t a_step = operand_kstep(args.a_mn), b_step = operand_kstep(args.b_mn);
-      for (long long u = blockIdx.x; u < args.units && !ctrl->abort_flag;
-           u += gridDim.x, ++local) {
+      for (int local = 0; !ctrl->abort_flag; ++local) {
+        long long u;
+        if (dyn) {
+          if (!queue_take(ctrl, local, qempty0, true, &u)) {
+            ctrl->abort_flag = 1;
+            break;
+          }
+        } else {
+          u = static_unit(args, blockIdx.x, gridDim.x, local);
+        }
+        if (u < 0) break;
         int b, tm, tn, kb0, kb1;
         decode_unit(args, u, b, tm, tn, kb0, kb1);
         const int acc_slot = local & 1;
@@ -582,8 +694,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     uint64_t* ebar = &ctrl->epi[warp - 2];
     uint32_t ephase = 0;
     bool ok = true, pf = false;  // pf: the next chunk's first input is being loaded
-    int local = 0;
-    for (long long u = blockIdx.x; u < args.units && ok; u += gridDim.x, ++local) {
+    for (int local = 0; ok; ++local) {
+      long long u;
+      if (dyn) {
+        if (!queue_take(ctrl, local, qempty0, false, &u)) {
+          ctrl->abort_flag = 1;
+          break;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(qempty0 + 8u * static_cast<uint32_t>(local % TQ));
+      } else {
+        u = static_unit(args, blockIdx.x, gridDim.x, local);
+      }
+      if (u < 0) break;
       int b, tm, tn, kb0, kb1;
       decode_unit(args, u, b, tm, tn, kb0, kb1);
       const int acc_slot = local & 1;
@@ -611,8 +734,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             break;
           }
           int nb, nm0, nn0;
-          pf = epi_next_chunk<BN>(args, u, gridDim.x, c, group, quarter * 32, b, tn, m0, nb, nm0,
-                                  nn0) &&
+          long long u2 = -2;  // the next unit, for its first chunk's input
+          if (dyn) {
+            if (lane == 0) u2 = queue_peek(ctrl, local + 1);
+            u2 = __shfl_sync(0xffffffffu, u2, 0);
+          } else {
+            u2 = static_unit(args, blockIdx.x, gridDim.x, local + 1);
+          }
+          pf = epi_next_chunk<BN>(args, u2, c, group, quarter * 32, b, tn, m0, nb, nm0, nn0) &&
                epi_prefetch(args, em, bufs, ebar, nb, nm0, nn0, lane);
         } else if (m < args.M) {
           epilogue_chunk(args, b, m, n0, v);
@@ -632,6 +761,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
+  schedule_release(args);
 }
 
 // ---------------------------------------------------------------- CTA-pair kernel
@@ -708,6 +838,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     }
 #pragma unroll
     for (int w = 0; w < EPI_WARPS; ++w) mbar_init(&ctrl->epi[w], 1);
+#pragma unroll
+    for (int q = 0; q < TQ; ++q) {
+      mbar_init(&ctrl->qfull[q], 1);  // the leader producer's publish (local or remote)
+      // leader: its MMA issuer, the partner's producer and both CTAs' epilogue warps
+      mbar_init(&ctrl->qempty[q], 2 + 2 * EPI_WARPS);
+    }
     ctrl->abort_flag = 0;
     fence_barrier_init();
   }
@@ -731,13 +867,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
   const uint32_t tempty0 = map_to_rank(&ctrl->tempty[0], 0);
   const long long cluster_id = blockIdx.x >> 1;
   const long long nclusters = gridDim.x >> 1;
+  const bool dyn = args.sched_next != nullptr;
+  const uint32_t qempty0 = map_to_rank(&ctrl->qempty[0], 0);
 
   if (warp == 0) {
     if (lane == 0) {
       uint32_t stage = 0, phase = 0;
       long long fills = 0;
       const uint64_t pol_a = make_l2_policy(L2_NORMAL), pol_b = pol_a;
-      for (long long u = cluster_id; u < args.units && !ctrl->abort_flag; u += nclusters) {
+      for (int i = 0; !ctrl->abort_flag; ++i) {
+        long long u;
+        if (dyn) {
+          // the leader claims and publishes; the partner's producer follows
+          const bool got = leader ? queue_publish<STAGES, true>(ctrl, args, i, &u)
+                                  : queue_take(ctrl, i, qempty0, true, &u);
+          if (!got) {
+            ctrl->abort_flag = 1;
+            break;
+          }
+        } else {
+          u = static_unit(args, cluster_id, nclusters, i);
+        }
+        if (u < 0) break;
         int b, tm, tn, kb0, kb1;
         decode_unit(args, u, b, tm, tn, kb0, kb1);
         int bk = args.reduce_batch ? kb0 / args.kblocks_item : b;  // as in the single-CTA kernel
@@ -787,12 +938,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
   } else if (warp == 1) {
     if (leader && lane == 0) {
       uint32_t stage = 0, phase = 0;
-      int local = 0;
       const uint64_t a_desc0 = operand_desc(smem_u32(ring), args.a_mn, 0);
       const uint64_t b_desc0 = operand_desc(smem_u32(ring) + Cfg::A_BYTES, args.b_mn, 0);
       const uint32_t a_step = operand_kstep(args.a_mn), b_step = operand_kstep(args.b_mn);
-      for (long long u = cluster_id; u < args.units && !ctrl->abort_flag;
-           u += nclusters, ++local) {
+      for (int local = 0; !ctrl->abort_flag; ++local) {
+        long long u;
+        if (dyn) {
+          if (!queue_take(ctrl, local, qempty0, true, &u)) {
+            ctrl->abort_flag = 1;
+            break;
+          }
+        } else {
+          u = static_unit(args, cluster_id, nclusters, local);
+        }
+        if (u < 0) break;
         int b, tm, tn, kb0, kb1;
         decode_unit(args, u, b, tm, tn, kb0, kb1);
         const int acc_slot = local & 1;
@@ -847,8 +1006,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     uint64_t* ebar = &ctrl->epi[warp - 2];
     uint32_t ephase = 0;
     bool ok = true, pf = false;  // pf: the next chunk's first input is being loaded
-    int local = 0;
-    for (long long u = cluster_id; u < args.units && ok; u += nclusters, ++local) {
+    for (int local = 0; ok; ++local) {
+      long long u;
+      if (dyn) {
+        if (!queue_take(ctrl, local, qempty0, false, &u)) {
+          ctrl->abort_flag = 1;
+          break;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(qempty0 + 8u * static_cast<uint32_t>(local % TQ));
+      } else {
+        u = static_unit(args, cluster_id, nclusters, local);
+      }
+      if (u < 0) break;
       int b, tm, tn, kb0, kb1;
       decode_unit(args, u, b, tm, tn, kb0, kb1);
       const int acc_slot = local & 1;
@@ -876,9 +1046,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
             break;
           }
           int nb, nm0, nn0;
-          pf = epi_next_chunk<BN>(args, u, nclusters, c, group,
-                                  static_cast<int>(rank) * BM + quarter * 32, b, tn, m0, nb, nm0,
-                                  nn0) &&
+          long long u2 = -2;  // the next unit, for its first chunk's input
+          if (dyn) {
+            if (lane == 0) u2 = queue_peek(ctrl, local + 1);
+            u2 = __shfl_sync(0xffffffffu, u2, 0);
+          } else {
+            u2 = static_unit(args, cluster_id, nclusters, local + 1);
+          }
+          pf = epi_next_chunk<BN>(args, u2, c, group, static_cast<int>(rank) * BM + quarter * 32,
+                                  b, tn, m0, nb, nm0, nn0) &&
                epi_prefetch(args, em, bufs, ebar, nb, nm0, nn0, lane);
         } else if (m < args.M) {
           epilogue_chunk(args, b, m, n0, v);
@@ -900,6 +1076,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
   }
+  schedule_release(args);
 }
 
 // ---------------------------------------------------------------- 3xTF32 split
@@ -1091,6 +1268,54 @@ EncodeTiledFn get_encode_fn() {
 
 constexpr int kMaxDevices = 64;
 
+// ---------------------------------------------------------------- schedule slots
+constexpr int kSchedSlots = 64;
+__device__ unsigned long long g_sched_next[kSchedSlots];
+__device__ unsigned int g_sched_done[kSchedSlots];
+
+// The dynamic schedule's counter slot for `stream` on device `dev`: one slot
+// per stream, so GEMMs that may run concurrently never share a counter;
+// launches on one stream are ordered, and each launch's last CTA resets the
+// slot before the next launch starts. Static schedule (false) under graph
+// capture (a replay could overlap other work of the capturing stream), for
+// the per-thread default stream, once every slot is taken, or when the
+// environment sets OXF_GEMM_SCHEDULE=static.
+bool schedule_slot(cudaStream_t stream, int dev, unsigned long long** next, unsigned int** done) {
+  const char* env = std::getenv("OXF_GEMM_SCHEDULE");
+  if (env && std::strcmp(env, "static") == 0) return false;
+  if (dev < 0 || dev >= kMaxDevices || stream == cudaStreamPerThread) return false;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  if (cs != cudaStreamCaptureStatusNone) return false;
+  static std::mutex mu;
+  static std::vector<cudaStream_t> streams[kMaxDevices];
+  static unsigned long long* next_base[kMaxDevices];
+  static unsigned int* done_base[kMaxDevices];
+  std::lock_guard<std::mutex> lock(mu);
+  if (!next_base[dev]) {
+    void *p = nullptr, *q = nullptr;
+    if (cudaGetSymbolAddress(&p, g_sched_next) != cudaSuccess ||
+        cudaGetSymbolAddress(&q, g_sched_done) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    next_base[dev] = static_cast<unsigned long long*>(p);
+    done_base[dev] = static_cast<unsigned int*>(q);
+  }
+  auto& v = streams[dev];
+  const size_t k = static_cast<size_t>(std::find(v.begin(), v.end(), stream) - v.begin());
+  if (k == v.size()) {
+    if (v.size() >= static_cast<size_t>(kSchedSlots)) return false;
+    v.push_back(stream);
+  }
+  *next = next_base[dev] + k;
+  *done = done_base[dev] + k;
+  return true;
+}
+
 int sm_count(int dev) {
   static int counts[kMaxDevices] = {0};
   if (dev < 0 || dev >= kMaxDevices) return 148;
@@ -1156,6 +1381,9 @@ oxf_status launch_tcgen05(const CUtensorMap& ta, const CUtensorMap& tb, const CU
   }
   args.idesc = make_idesc_tf32(BM, BN, args.a_mn != 0, args.b_mn != 0);
   const long long grid = std::min<long long>(args.units, sm_count(dev));
+  args.sched_next = nullptr;
+  args.sched_done = nullptr;
+  if (args.units > grid) schedule_slot(stream, dev, &args.sched_next, &args.sched_done);
   gemm_tf32_tcgen05<BN, STAGES, SPLIT3>
       <<<static_cast<unsigned>(grid), GEMM_THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, ta_lo,
                                                                               tb_lo, em, args);
@@ -1177,6 +1405,9 @@ oxf_status launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
   }
   args.idesc = make_idesc_tf32(2 * BM, BN, args.a_mn != 0, args.b_mn != 0);
   const long long clusters = std::min<long long>(args.units, sm_count(dev) / 2);
+  args.sched_next = nullptr;
+  args.sched_done = nullptr;
+  if (args.units > clusters) schedule_slot(stream, dev, &args.sched_next, &args.sched_done);
   gemm_tf32_tcgen05_pair<BN, STAGES, SPLIT3>
       <<<static_cast<unsigned>(2 * clusters), GEMM_THREADS, Cfg::SMEM_BYTES, stream>>>(
           ta, tb, ta_lo, tb_lo, em, args);

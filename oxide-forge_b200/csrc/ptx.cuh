@@ -285,6 +285,54 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
                : "memory");
 }
 
+// 64-bit store into another CTA's shared memory (cluster address).
+__device__ __forceinline__ void st_cluster_s64(uint32_t cluster_addr, long long v) {
+  asm volatile("st.shared::cluster.s64 [%0], %1;" ::"r"(cluster_addr), "l"(v) : "memory");
+}
+
+// Waits on a local mbarrier whose phase another CTA of the cluster may
+// complete (remote release): acquire at cluster scope, so data that CTA
+// stored into this CTA's shared memory before arriving is visible.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Non-blocking test of the same (no suspension).
+__device__ __forceinline__ bool mbar_test_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait with cluster-scope acquire (see mbar_wait).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint32_t code,
+                                                  unsigned long long limit_ns = OXF_WAIT_LIMIT_NS) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const unsigned long long start = global_timer_ns();
+  uint32_t spins = 0;
+  while (!mbar_try_wait_cluster(bar, parity)) {
+    if ((++spins & 1023u) == 0 && global_timer_ns() - start > limit_ns) {
+      report_device_error(code);
+      return false;
+    }
+  }
+  return true;
+}
+
 // Tiled loads into this CTA's shared memory whose transaction bytes are
 // counted on an mbarrier of the leader CTA (cluster address). No multicast.
 __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const void* tmap,

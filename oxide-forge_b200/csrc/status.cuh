@@ -36,6 +36,7 @@ enum DeviceErrorCode : uint32_t {
   DEVERR_GEMM_WAIT_TMEM_FULL = 0x104,
   DEVERR_GEMM_DRAIN = 0x105,
   DEVERR_GEMM_EPI_LOAD = 0x106,
+  DEVERR_GEMM_QUEUE = 0x107,  // tile queue (dynamic schedule): entry never published / freed
   DEVERR_WAIT_SELFTEST = 0x1FF,  // oxf_wait_timeout_selftest: the expected expiry
 };
 
