@@ -57,7 +57,7 @@ def parse():
     ap.add_argument("--seq", type=int, default=SEQ)
     ap.add_argument("--hidden", type=int, default=HIDDEN)
     ap.add_argument("--ffn", type=int, default=FFN)
-    ap.add_argument("--exchange", default="nccl", choices=["nccl", "peer"],
+    ap.add_argument("--exchange", default="peer", choices=["nccl", "peer"],
                     help="train at N>1: gradient exchange = NCCL all-reduce buckets + SGD, or "
                          "the fused peer-memory exchange + SGD kernel (oxf/exchange.py)")
     ap.add_argument("--no-overlap", action="store_true",
