@@ -707,7 +707,9 @@ def main():
     stream = torch.cuda.current_stream()
     model = models.Transformer(cfg, max_batch=local_batch, stream=stream)
     model.set_params(models.init_transformer_params(cfg, seed=0))
-    trainer = DataParallelTrainer(model, a.global_batch, LR, a.seq, exchange=a.exchange,
+    # One GPU has nothing to exchange: the step ends with the plain SGD kernel.
+    trainer = DataParallelTrainer(model, a.global_batch, LR, a.seq,
+                                  exchange=a.exchange if world > 1 else "nccl",
                                   overlap=not a.no_overlap)
     trainer.broadcast_params(model.params)
 
