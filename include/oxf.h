@@ -246,7 +246,8 @@ typedef struct {
   int reduce_batch; /* 1: C = sum over the batch of op(A_b)·op(B_b) (one output,
                        output strides 0); K then runs over batch x K */
   int variant;      /* kernel choice: 0 automatic, 1 one CTA per 128-row tile,
-                       2 a CTA pair per 256-row tile (tcgen05 cta_group::2) */
+                       2 a CTA pair per 256 x 256 tile (tcgen05 cta_group::2),
+                       3 a CTA pair per 256 x 512 tile (TF32 only) */
 } oxf_gemm_desc;
 
 /* Fills a descriptor with defaults (batch 1, alpha 1, tight leading dims

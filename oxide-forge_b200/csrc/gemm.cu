@@ -778,13 +778,32 @@ struct GemmPairCfg {
   static constexpr int B_BYTES = (BN / 2) * BK * 4;
   static constexpr int OPS = SPLIT3 ? 2 : 1;  // hi (+ lo) copies of each operand
   static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * OPS;
-  static constexpr int TMEM_COLS = 2 * BN;
+  // One MMA covers N = 256 (128 columns from each CTA's half of B). A wider
+  // tile issues NSUB of them per K step into consecutive 256-column TMEM
+  // ranges, all reading the same A: fewer operand bytes per flop.
+  static constexpr int MMA_N = 256;
+  static constexpr int NSUB = BN / MMA_N;
+  static constexpr int B_SUB_BYTES = 128 * BK * 4;  // one MMA's 128 columns in one CTA
+  // Accumulators are double-buffered (the epilogue drains one while the MMA
+  // fills the other) unless one tile already fills TMEM's 512 columns.
+  static constexpr int ACC_BUFS = 2 * BN <= 512 ? 2 : 1;
+  static constexpr int TMEM_COLS = ACC_BUFS * BN;
   static constexpr int CTRL_BYTES = 1024;
   static constexpr int EPI_BYTES = EPI_WARPS * EPI_TILE_BYTES;  // one staging tile per epilogue warp
   static constexpr int SMEM_BYTES = 1024 + CTRL_BYTES + STAGES * STAGE_BYTES + EPI_BYTES;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
-  static_assert(TMEM_COLS <= 512 && BN % 64 == 0, "tile shape");
+  static_assert(BN % MMA_N == 0 && TMEM_COLS <= 512, "tile shape");
 };
+
+// TMEM column of a pair tile's 32-column output chunk c. CTA r of the pair
+// loads tile columns [r*BN/2, (r+1)*BN/2) as 128-column sub-tiles, and MMA h
+// reads sub-tile h of both CTAs, so accumulator h (columns h*256..) holds CTA
+// 0's sub-tile h, then CTA 1's. For BN = 256 this is the identity.
+template <int BN>
+__device__ __forceinline__ uint32_t pair_chunk_tmem_col(int c) {
+  const int x = c * 32;
+  return static_cast<uint32_t>(((x % (BN / 2)) / 128) * 256 + (x / (BN / 2)) * 128 + x % 128);
+}
 
 template <int ROWS>
 __device__ __forceinline__ void load_operand_pair(uint8_t* dst, const CUtensorMap* map,
@@ -954,8 +973,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
         if (u < 0) break;
         int b, tm, tn, kb0, kb1;
         decode_unit(args, u, b, tm, tn, kb0, kb1);
-        const int acc_slot = local & 1;
-        const uint32_t use = static_cast<uint32_t>(local >> 1);
+        const int acc_slot = local % Cfg::ACC_BUFS;
+        const uint32_t use = static_cast<uint32_t>(local / Cfg::ACC_BUFS);
         if (!mbar_wait(&ctrl->tempty[acc_slot], (use & 1u) ^ 1u, DEVERR_GEMM_WAIT_TMEM_EMPTY)) {
           ctrl->abort_flag = 1;
           break;
@@ -974,18 +993,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
           for (int kk = 0; kk < BK / UMMA_K; ++kk) {
             const uint64_t da = desc_advance(a_desc0, off + kk * a_step);
-            const uint64_t db = desc_advance(b_desc0, off + kk * b_step);
             const uint32_t accumulate = (kb > kb0 || kk > 0) ? 1u : 0u;
-            if (SPLIT3) {
-              // lo·hi + hi·lo + hi·hi, as in the one-CTA kernel
-              const uint32_t lo = Cfg::A_BYTES + Cfg::B_BYTES;
-              umma_tf32_pair(d_tmem, desc_advance(a_desc0, off + lo + kk * a_step), db,
-                             args.idesc, accumulate);
-              umma_tf32_pair(d_tmem, da, desc_advance(b_desc0, off + lo + kk * b_step),
-                             args.idesc, 1u);
-              umma_tf32_pair(d_tmem, da, db, args.idesc, 1u);
-            } else {
-              umma_tf32_pair(d_tmem, da, db, args.idesc, accumulate);
+#pragma unroll
+            for (int h = 0; h < Cfg::NSUB; ++h) {
+              const uint32_t dh = d_tmem + static_cast<uint32_t>(h * Cfg::MMA_N);
+              const uint32_t bo = off + static_cast<uint32_t>(h * Cfg::B_SUB_BYTES);
+              const uint64_t db = desc_advance(b_desc0, bo + kk * b_step);
+              if (SPLIT3) {
+                // lo·hi + hi·lo + hi·hi, as in the one-CTA kernel
+                const uint32_t lo = Cfg::A_BYTES + Cfg::B_BYTES;
+                umma_tf32_pair(dh, desc_advance(a_desc0, off + lo + kk * a_step), db,
+                               args.idesc, accumulate);
+                umma_tf32_pair(dh, da, desc_advance(b_desc0, bo + lo + kk * b_step),
+                               args.idesc, 1u);
+                umma_tf32_pair(dh, da, db, args.idesc, 1u);
+              } else {
+                umma_tf32_pair(dh, da, db, args.idesc, accumulate);
+              }
             }
           }
           umma_commit_pair(&ctrl->empty[stage], 0x3);
@@ -1021,8 +1045,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
       if (u < 0) break;
       int b, tm, tn, kb0, kb1;
       decode_unit(args, u, b, tm, tn, kb0, kb1);
-      const int acc_slot = local & 1;
-      const uint32_t use = static_cast<uint32_t>(local >> 1);
+      const int acc_slot = local % Cfg::ACC_BUFS;
+      const uint32_t use = static_cast<uint32_t>(local / Cfg::ACC_BUFS);
       if (!mbar_wait(&ctrl->tfull[acc_slot], use & 1u, DEVERR_GEMM_WAIT_TMEM_FULL)) {
         ctrl->abort_flag = 1;
         break;
@@ -1037,7 +1061,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
         const int n0 = tn * BN + c * 32;
         if (n0 >= args.N) break;
         float v[32];
-        tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), v);
+        tmem_ld_32x32b_x32(taddr + pair_chunk_tmem_col<BN>(c), v);
         if (args.epi_tma) {
           const int m0 = m_base + quarter * 32;
           if (!epilogue_chunk_tma(args, em, b, m0, n0, v, bufs, ebar, ephase, lane, pf)) {
@@ -1267,6 +1291,8 @@ EncodeTiledFn get_encode_fn() {
 }
 
 constexpr int kMaxDevices = 64;
+// Wide (256 x 512) pair tiles from this many K blocks of 32 up (K >= 4096).
+constexpr long long kWideMinKBlocks = 128;
 
 // ---------------------------------------------------------------- schedule slots
 constexpr int kSchedSlots = 64;
@@ -1403,7 +1429,7 @@ oxf_status launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(gemm pair)");
     configured[dev] = true;
   }
-  args.idesc = make_idesc_tf32(2 * BM, BN, args.a_mn != 0, args.b_mn != 0);
+  args.idesc = make_idesc_tf32(2 * BM, Cfg::MMA_N, args.a_mn != 0, args.b_mn != 0);
   const long long clusters = std::min<long long>(args.units, sm_count(dev) / 2);
   args.sched_next = nullptr;
   args.sched_done = nullptr;
@@ -1604,8 +1630,34 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
   {
     const long long tiles2 = static_cast<long long>((d->M + 2 * BM - 1) / (2 * BM)) *
                              ((d->N + 255) / 256) * (d->reduce_batch ? 1 : d->batch);
-    pair = d->variant == 2 || (d->variant == 0 && d->M >= 2 * BM && tiles2 >= sms / 2);
+    pair = d->variant == 2 || d->variant == 3 ||
+           (d->variant == 0 && d->M >= 2 * BM && tiles2 >= sms / 2);
     if (pair) BN = 256;
+  }
+  // Wide pair tiles (256 x 512): a quarter fewer operand bytes per flop
+  // through L2, but a tile fills TMEM, so its epilogue no longer overlaps the
+  // next tile's MMAs. Chosen for long K, where the MMA time per tile dwarfs
+  // the epilogue, and only if the fewer, larger tiles fill the last wave of
+  // CTA pairs about as well. OXF_GEMM_TILE=256 / 512 overrides the choice.
+  if (pair && !split3) {
+    const long long kbl = static_cast<long long>((d->K + BK - 1) / BK) *
+                          (d->reduce_batch ? d->batch : 1);
+    const long long mt = (d->M + 2 * BM - 1) / (2 * BM), nb = d->reduce_batch ? 1 : d->batch;
+    const long long tiles_w = mt * ((d->N + 511) / 512) * nb;
+    const long long tiles_n = mt * ((d->N + 255) / 256) * nb;
+    const long long pairs = sms / 2;
+    auto fill = [pairs](long long t) {
+      return static_cast<double>(t) / static_cast<double>(((t + pairs - 1) / pairs) * pairs);
+    };
+    bool wide = d->variant == 3 ||
+                (d->variant == 0 && d->N >= 512 && kbl >= kWideMinKBlocks && tiles_w >= pairs &&
+                 fill(tiles_w) >= fill(tiles_n) - 0.02);
+    const char* env = std::getenv("OXF_GEMM_TILE");
+    if (env && d->variant == 0) {
+      if (std::strcmp(env, "256") == 0) wide = false;
+      if (std::strcmp(env, "512") == 0) wide = d->N >= 512;
+    }
+    if (wide) BN = 512;
   }
   a.bm = pair ? 2 * BM : BM;
   a.tiles_m = (d->M + a.bm - 1) / a.bm;
@@ -1679,6 +1731,7 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
 
   if (split3 && pair) return launch_pair<256, 3, true>(ta, tb, ta_lo, tb_lo, em, a, stream, dev);
   if (split3) return launch_tcgen05<128, 3, true>(ta, tb, ta_lo, tb_lo, em, a, stream, dev);
+  if (pair && BN == 512) return launch_pair<512, 4, false>(ta, tb, ta, tb, em, a, stream, dev);
   if (pair) return launch_pair<256, 6, false>(ta, tb, ta, tb, em, a, stream, dev);
   if (BN == 256) return launch_tcgen05<256, 4, false>(ta, tb, ta, tb, em, a, stream, dev);
   if (BN == 128) return launch_tcgen05<128, 6, false>(ta, tb, ta, tb, em, a, stream, dev);

@@ -224,25 +224,29 @@ def test_batch_reduce(K, rng):
     assert rel_err(host(out), want) < TF32_TOL
 
 
-@pytest.mark.parametrize("variant", [1, 2])
+@pytest.mark.parametrize("variant", [1, 2, 3])
 @pytest.mark.parametrize("at,bt", [(0, 0), (0, 1), (1, 0), (1, 1)])
 @pytest.mark.parametrize("M,N,Kd", [(256, 256, 64), (300, 520, 72), (1024, 768, 256)])
 def test_cta_pair_and_single_variants(K, rng, M, N, Kd, at, bt, variant):
     """variant 1: one CTA per 128-row tile; variant 2: a CTA pair per
-    256-row tile (tcgen05.mma.cta_group::2, half of B in each CTA)."""
+    256 x 256 tile (tcgen05.mma.cta_group::2, half of B in each CTA);
+    variant 3: a CTA pair per 256 x 512 tile (two MMAs per K step, the
+    accumulator in all 512 TMEM columns; N = 256 leaves half the tile empty,
+    N = 520 and 768 a ragged second tile)."""
     A, B = operands(rng, M, N, Kd, at, bt)
     out = torch.empty((M, N), device="cuda")
     K.gemm(dev(A), dev(B), out, a_trans=bool(at), b_trans=bool(bt), variant=variant)
     assert rel_err(host(out), exact(A, B, at, bt)) < TF32_TOL
 
 
-def test_cta_pair_features(K, rng):
+@pytest.mark.parametrize("variant", [2, 3])
+def test_cta_pair_features(K, rng, variant):
     """Batched operands, fused epilogue, split-K accumulation and
-    batch-reduce on the CTA-pair kernel."""
+    batch-reduce on the CTA-pair kernel (256- and 512-wide tiles)."""
     batch, M, N, Kd = 3, 256, 384, 128
     A, B = operands(rng, M, N, Kd, 0, 0, batch=batch)
     out = torch.empty((batch, M, N), device="cuda")
-    K.gemm(dev(A), dev(B), out, variant=2)
+    K.gemm(dev(A), dev(B), out, variant=variant)
     got = host(out)
     for b in range(batch):
         assert rel_err(got[b], exact(A[b], B[b], 0, 0)) < TF32_TOL
@@ -251,7 +255,7 @@ def test_cta_pair_features(K, rng):
     R = rng.standard_normal((512, 256)).astype(np.float32)
     y = torch.empty((512, 256), device="cuda")
     pre = torch.empty((512, 256), device="cuda")
-    K.gemm(dev(X), dev(W), y, bias=dev(bias), residual=dev(R), pre_out=pre, act=1, variant=2)
+    K.gemm(dev(X), dev(W), y, bias=dev(bias), residual=dev(R), pre_out=pre, act=1, variant=variant)
     z = exact(X, W, 0, 0) + bias + R
     assert rel_err(host(pre), z) < TF32_TOL
     assert rel_err(host(y), O.act_forward(O.GELU, z.astype(np.float32))) < TF32_TOL
@@ -259,19 +263,19 @@ def test_cta_pair_features(K, rng):
     G = rng.standard_normal((2048, 512)).astype(np.float32)
     G0 = rng.standard_normal((256, 512)).astype(np.float32)
     acc = dev(G0)
-    K.gemm(dev(Xt), dev(G), acc, a_trans=True, accumulate=True, split_k=4, variant=2)
+    K.gemm(dev(Xt), dev(G), acc, a_trans=True, accumulate=True, split_k=4, variant=variant)
     assert rel_err(host(acc), G0 + exact(Xt, G, 1, 0)) < TF32_TOL
     Ab = rng.uniform(-1, 1, (3, 256, 128)).astype(np.float32)
     Bb = rng.uniform(-1, 1, (3, 256, 128)).astype(np.float32)
     Rb = rng.standard_normal((256, 256)).astype(np.float32)
     red = torch.empty((256, 256), device="cuda")
-    K.gemm(dev(Ab), dev(Bb), red, b_trans=True, residual=dev(Rb), reduce_batch=True, variant=2)
+    K.gemm(dev(Ab), dev(Bb), red, b_trans=True, residual=dev(Rb), reduce_batch=True, variant=variant)
     want = Rb + sum(exact(Ab[b], Bb[b], 0, 1) for b in range(3))
     assert rel_err(host(red), want) < TF32_TOL
 
 
-@pytest.mark.parametrize("variant", [1, 2])
-@pytest.mark.parametrize("M,N,Kd", [(300, 200, 72), (512, 384, 128)])
+@pytest.mark.parametrize("variant", [1, 2, 3])
+@pytest.mark.parametrize("M,N,Kd", [(300, 200, 72), (512, 384, 128), (520, 1100, 96)])
 def test_epilogue_tiles_batched_and_shared(K, rng, M, N, Kd, variant):
     """The TMA-staged epilogue on batched outputs: a residual shared by the
     batch (stride 0, a 2-D tensor map), per-item aux and pre-activation
@@ -335,3 +339,23 @@ def test_matrix_multiply_fp32_is_f32_exact(K, rng, M, N, Kd):
     got = host(out)
     assert rel_err(got, exact(A, B, 0, 0)) < 1e-5
     assert rel_err(got, O.gemm(A, B)) < 1e-5
+
+
+@pytest.mark.parametrize("at,bt", [(0, 0), (1, 0), (0, 1)])
+def test_wide_tiles_many_per_pair(K, at, bt):
+    """Long K and enough 256 x 512 tiles that every CTA pair runs several:
+    the automatic choice takes the wide tile here, and each pair reuses its
+    single TMEM accumulator from tile to tile. Also the same product with
+    the 256 x 256 tile forced, which must agree to rounding. The check is a
+    float64 product on the GPU."""
+    g = torch.Generator(device="cuda").manual_seed(11)
+    M, N, Kd = 4096, 4096 + 64, 2048
+    A = torch.randn((Kd, M) if at else (M, Kd), device="cuda", generator=g)
+    B = torch.randn((N, Kd) if bt else (Kd, N), device="cuda", generator=g)
+    want = (A.double().T if at else A.double()) @ (B.double().T if bt else B.double())
+    scale = want.abs().max().item()
+    for variant in (0, 2, 3):
+        out = torch.empty((M, N), device="cuda")
+        K.gemm(A, B, out, a_trans=bool(at), b_trans=bool(bt), variant=variant)
+        err = (out.double() - want).abs().max().item() / scale
+        assert err < TF32_TOL, (variant, err)
