@@ -1643,15 +1643,20 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
     const long long kbl = static_cast<long long>((d->K + BK - 1) / BK) *
                           (d->reduce_batch ? d->batch : 1);
     const long long mt = (d->M + 2 * BM - 1) / (2 * BM), nb = d->reduce_batch ? 1 : d->batch;
-    const long long tiles_w = mt * ((d->N + 511) / 512) * nb;
-    const long long tiles_n = mt * ((d->N + 255) / 256) * nb;
+    long long units_w = mt * ((d->N + 511) / 512) * nb;
+    long long units_n = mt * ((d->N + 255) / 256) * nb;
+    if (d->accumulate && split <= 1 && !d->bias && !d->residual) {
+      // split K as the launch below will, so that the fill compares units
+      units_w *= choose_splits(units_w, static_cast<int>(kbl), sms);
+      units_n *= choose_splits(units_n, static_cast<int>(kbl), sms);
+    }
     const long long pairs = sms / 2;
     auto fill = [pairs](long long t) {
       return static_cast<double>(t) / static_cast<double>(((t + pairs - 1) / pairs) * pairs);
     };
     bool wide = d->variant == 3 ||
-                (d->variant == 0 && d->N >= 512 && kbl >= kWideMinKBlocks && tiles_w >= pairs &&
-                 fill(tiles_w) >= fill(tiles_n) - 0.02);
+                (d->variant == 0 && d->N >= 512 && kbl >= kWideMinKBlocks && units_w >= pairs &&
+                 fill(units_w) >= fill(units_n) - 0.02);
     const char* env = std::getenv("OXF_GEMM_TILE");
     if (env && d->variant == 0) {
       if (std::strcmp(env, "256") == 0) wide = false;
