@@ -1183,6 +1183,77 @@ __global__ void gemm_simt_kernel(const GemmArgs a, const float* __restrict__ A, 
   }
 }
 
+// ---------------------------------------------------------------- tiny products
+// For products of a few million multiply-adds (config 1: 256x64x128) the
+// persistent tcgen05 kernel is all fixed latency: TMEM allocation, a TMA
+// load, the MMAs, a TMEM read and a TMA store in sequence. This kernel needs
+// one memory round trip: a 256-thread CTA owns a 16x16 output tile, loads its
+// whole A panel (16 x K) and B panel (K x 16, K <= 256) into shared memory at
+// once, rounding each operand to TF32 (round to nearest, ties away, as the
+// reference's kernel does), then each thread forms one output with f32 FMAs
+// in K order and applies the fused epilogue of the SIMT kernel.
+constexpr int SMALL_TILE = 16;
+constexpr int SMALL_KMAX = 256;
+constexpr double SMALL_MAX_MACS = 4194304.0;  // 2^22 multiply-adds over the batch
+
+__device__ __forceinline__ float round_tf32_rna(float x) {
+  uint32_t h;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
+  return __uint_as_float(h);
+}
+
+__global__ void __launch_bounds__(256)
+    gemm_small_kernel(const GemmArgs a, const float* __restrict__ A, long long lda, long long sa,
+                      const float* __restrict__ B, long long ldb, long long sb) {
+  __shared__ float As[SMALL_TILE][SMALL_KMAX + 1];
+  __shared__ float Bs[SMALL_KMAX][SMALL_TILE + 1];
+  const int b = blockIdx.z, t = threadIdx.x;
+  const int m0 = blockIdx.y * SMALL_TILE, n0 = blockIdx.x * SMALL_TILE;
+  const int K = a.K;
+  constexpr int PER = SMALL_KMAX / 16;  // k steps of 16 per thread and operand
+  // Thread t owns index pair (t / 16, t % 16): the 16 threads of a
+  // half-warp read 16 consecutive addresses of whichever layout is given
+  // (K-major: along k; MN-major: along m or n), stepping k by 16. Every
+  // load is issued before any is used (one round trip).
+  const int hi = t >> 4, lo = t & 15;
+  const int ar = a.a_mn ? lo : hi, ak = a.a_mn ? hi : lo;  // A: row in tile, first k
+  const int bc = a.b_mn ? lo : hi, bk = a.b_mn ? hi : lo;  // B: column in tile, first k
+  const bool arow_ok = m0 + ar < a.M, bcol_ok = n0 + bc < a.N;
+  const float* ap = A + b * sa + (a.a_mn ? static_cast<long long>(ak) * lda + m0 + ar
+                                         : static_cast<long long>(m0 + ar) * lda + ak);
+  const float* bp = B + b * sb + (a.b_mn ? static_cast<long long>(bk) * ldb + n0 + bc
+                                         : static_cast<long long>(n0 + bc) * ldb + bk);
+  const long long astep = a.a_mn ? 16 * lda : 16, bstep = a.b_mn ? 16 * ldb : 16;
+  float va[PER], vb[PER];
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    va[j] = (arow_ok && ak + 16 * j < K) ? __ldg(ap + j * astep) : 0.f;
+    vb[j] = (bcol_ok && bk + 16 * j < K) ? __ldg(bp + j * bstep) : 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    if (ak + 16 * j < K) As[ar][ak + 16 * j] = round_tf32_rna(va[j]);
+    if (bk + 16 * j < K) Bs[bk + 16 * j][bc] = round_tf32_rna(vb[j]);
+  }
+  __syncthreads();
+  const int r = t / SMALL_TILE, c = t % SMALL_TILE;
+  const int m = m0 + r, nn = n0 + c;
+  float acc = 0.f;
+#pragma unroll 8
+  for (int k = 0; k < K; ++k) acc = fmaf(As[r][k], Bs[k][c], acc);
+  if (m >= a.M || nn >= a.N) return;
+  float* crow = a.C + b * a.sc + static_cast<long long>(m) * a.ldc;
+  float v = acc * a.alpha;
+  if (a.beta != 0.0f) v += a.beta * crow[nn];
+  if (a.bias) v += a.bias[nn];
+  if (a.R) v += a.R[b * a.sr + static_cast<long long>(m) * a.ldr + nn];
+  if (a.P) a.P[b * a.sp + static_cast<long long>(m) * a.ldp + nn] = v;
+  if (a.X) v *= act_derivative(a.grad_act, a.X[b * a.sx + static_cast<long long>(m) * a.ldx + nn]);
+  v = act_forward(a.act, v);
+  if (a.accumulate) atomicAdd(crow + nn, v);
+  else crow[nn] = v;
+}
+
 // ---------------------------------------------------------------- reference algorithm
 // Measurement-only restatement of the reference GEMM (gemm.rs:131-373):
 // 32x32 output tile per 128-thread CTA, four warps of 16x16 (two
@@ -1568,6 +1639,18 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
                                                         d->ldb, d->stride_b,
                                                         d->precision != OXF_PREC_TF32);
     return check_launch("gemm_simt_kernel");
+  }
+
+  // Tiny TF32 products: one memory round trip on the CUDA cores beats the
+  // fixed latency of the tensor-core pipeline (variant 0 only).
+  if (d->variant == 0 && d->precision == OXF_PREC_TF32 && !a.reduce_batch && d->K > 0 &&
+      d->K <= SMALL_KMAX &&
+      static_cast<double>(d->M) * d->N * d->K * d->batch <= SMALL_MAX_MACS) {
+    dim3 grid((d->N + SMALL_TILE - 1) / SMALL_TILE, (d->M + SMALL_TILE - 1) / SMALL_TILE,
+              d->batch);
+    gemm_small_kernel<<<grid, 256, 0, stream>>>(a, d->A, d->lda, d->stride_a, d->B, d->ldb,
+                                                 d->stride_b);
+    return check_launch("gemm_small_kernel");
   }
 
   const bool split3 = d->precision == OXF_PREC_TF32X3;

@@ -359,3 +359,54 @@ def test_wide_tiles_many_per_pair(K, at, bt):
         K.gemm(A, B, out, a_trans=bool(at), b_trans=bool(bt), variant=variant)
         err = (out.double() - want).abs().max().item() / scale
         assert err < TF32_TOL, (variant, err)
+
+
+@pytest.mark.parametrize("at,bt", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("M,N,Kd,batch", [(256, 64, 128, 1), (36, 52, 200, 1), (20, 28, 4, 1),
+                                          (68, 36, 256, 3)])
+def test_small_products_latency_kernel(K, rng, M, N, Kd, batch, at, bt):
+    """Products of at most 2^22 multiply-adds with K <= 256 run on the
+    one-round-trip CUDA-core kernel: TF32-rounded (RNA) operands, f32
+    accumulation, any operand layout, ragged tiles (sizes not multiples of
+    16, leading dimensions multiples of 4), batches."""
+    A, B = operands(rng, M, N, Kd, at, bt, batch=batch if batch > 1 else None)
+    out = torch.empty((batch, M, N) if batch > 1 else (M, N), device="cuda")
+    K.gemm(dev(A), dev(B), out, a_trans=bool(at), b_trans=bool(bt))
+    got = host(out)
+    if batch > 1:
+        for b in range(batch):
+            assert rel_err(got[b], exact(A[b], B[b], at, bt)) < TF32_TOL
+    else:
+        assert rel_err(got, exact(A, B, at, bt)) < TF32_TOL
+
+
+def test_small_products_match_reference_rounding_and_epilogue(K, rng):
+    """Config 1 (256x128 · 128x64) against the oracle with the reference's
+    TF32 RNA operand rounding: equal up to f32 summation order. Then the
+    fused epilogue (alpha, beta·C, bias, residual, pre-activation, GELU),
+    the activation gradient, and accumulation on the same kernel."""
+    x = rng.uniform(-1, 1, (256, 128)).astype(np.float32)
+    w = rng.uniform(-0.09, 0.09, (128, 64)).astype(np.float32)
+    y = torch.empty((256, 64), device="cuda")
+    K.matrix_multiply(dev(x), dev(w), y)
+    want = O.gemm(x, w, rounding=O.GEMM_TF32_RNA)
+    assert np.abs(host(y) - want).max() <= 1e-5 * np.abs(want).max()
+    M, N, Kd = 96, 80, 64
+    A, B = operands(rng, M, N, Kd, 0, 0)
+    bias = (0.1 * rng.standard_normal(N)).astype(np.float32)
+    R = rng.standard_normal((M, N)).astype(np.float32)
+    C0 = rng.standard_normal((M, N)).astype(np.float32)
+    out, pre = dev(C0), torch.empty((M, N), device="cuda")
+    K.gemm(dev(A), dev(B), out, alpha=0.5, beta=0.25, bias=dev(bias), residual=dev(R),
+           pre_out=pre, act=1)
+    z = 0.5 * exact(A, B, 0, 0) + 0.25 * C0 + bias + R
+    assert rel_err(host(pre), z) < TF32_TOL
+    assert rel_err(host(out), O.act_forward(O.GELU, z.astype(np.float32))) < TF32_TOL
+    X = rng.standard_normal((M, N)).astype(np.float32)
+    g = torch.empty((M, N), device="cuda")
+    K.gemm(dev(A), dev(B), g, aux=dev(X), grad_act=1)
+    want = exact(A, B, 0, 0) * O.act_derivative(O.GELU, X).astype(np.float64)
+    assert rel_err(host(g), want) < TF32_TOL
+    acc = dev(C0)
+    K.gemm(dev(A), dev(B), acc, accumulate=True)
+    assert rel_err(host(acc), C0 + exact(A, B, 0, 0)) < TF32_TOL
