@@ -1713,8 +1713,13 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
   {
     const long long tiles2 = static_cast<long long>((d->M + 2 * BM - 1) / (2 * BM)) *
                              ((d->N + 255) / 256) * (d->reduce_batch ? 1 : d->batch);
+    // An accumulating product with long K reaches every pair through K
+    // splits even when it has fewer tiles than pairs (weight gradients).
+    const bool splittable = d->accumulate && split <= 1 && !d->bias && !d->residual &&
+                            static_cast<long long>((d->K + BK - 1) / BK) *
+                                    (d->reduce_batch ? d->batch : 1) >= 2 * kWideMinKBlocks;
     pair = d->variant == 2 || d->variant == 3 ||
-           (d->variant == 0 && d->M >= 2 * BM && tiles2 >= sms / 2);
+           (d->variant == 0 && d->M >= 2 * BM && (tiles2 >= sms / 2 || splittable));
     if (pair) BN = 256;
   }
   // Wide pair tiles (256 x 512): a quarter fewer operand bytes per flop
