@@ -602,12 +602,15 @@ __global__ void row_looped_kernel(int op, float* __restrict__ out, const float* 
 }
 
 // ------------------------------------------------------------------ elementwise
+// Activations use the hardware-exponential forms of the GEMM epilogue
+// (relative error ~3e-7): with IEEE expf and division, GELU's arithmetic
+// alone took half of a memory-bound pass.
 __device__ __forceinline__ float unary_apply(int op, float x, float p) {
   switch (op) {
     case OXF_UNARY_SCALE: return x * p;
     case OXF_UNARY_ADD_SCALAR: return x + p;
-    case OXF_UNARY_ACT_FORWARD: return act_forward(static_cast<int>(p), x);
-    case OXF_UNARY_ACT_DERIV: return act_derivative(static_cast<int>(p), x);
+    case OXF_UNARY_ACT_FORWARD: return act_forward_fast(static_cast<int>(p), x);
+    case OXF_UNARY_ACT_DERIV: return act_derivative_fast(static_cast<int>(p), x);
     default: return 0.5f * x * x;
   }
 }
@@ -640,8 +643,8 @@ __global__ void elementwise_kernel(int kind, int op, float* __restrict__ out,
       float4 r;
       switch (kind) {
         case EW_MUL_ACT_DERIV:
-          r = make_float4(x.x * act_derivative(op, y.x), x.y * act_derivative(op, y.y),
-                          x.z * act_derivative(op, y.z), x.w * act_derivative(op, y.w));
+          r = make_float4(x.x * act_derivative_fast(op, y.x), x.y * act_derivative_fast(op, y.y),
+                          x.z * act_derivative_fast(op, y.z), x.w * act_derivative_fast(op, y.w));
           break;
         case EW_UNARY:
           r = make_float4(unary_apply(op, x.x, p), unary_apply(op, x.y, p),
@@ -670,7 +673,7 @@ __global__ void elementwise_kernel(int kind, int op, float* __restrict__ out,
       if (kind == EW_BY_ROWS || kind == EW_BINARY_BCAST) y = b[i % cols];
       float r;
       switch (kind) {
-        case EW_MUL_ACT_DERIV: r = x * act_derivative(op, y); break;
+        case EW_MUL_ACT_DERIV: r = x * act_derivative_fast(op, y); break;
         case EW_UNARY: r = unary_apply(op, x, p); break;
         case EW_SGD: r = x - y * p; break;
         case EW_MSE_GRAD: r = (x - y) * p; break;
