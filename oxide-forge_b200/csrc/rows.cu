@@ -155,18 +155,23 @@ __global__ void softmax_fwd_kernel(float* __restrict__ m, long long rows, int co
     mx = fmaxf(mx, hmax(a));
   }
   mx = GroupReduce<G>::max(mx, red);
+  // The hardware exponential (arguments <= 0 after the max; a few ulp) and
+  // one reciprocal per row: per-element IEEE expf and division cost more
+  // issue slots than the memory-bound pass can hide.
   float s = 0.f;
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
     float4& a = x.v[j];
-    a.x = expf(a.x - mx); a.y = expf(a.y - mx); a.z = expf(a.z - mx); a.w = expf(a.w - mx);
+    a.x = __expf(a.x - mx); a.y = __expf(a.y - mx); a.z = __expf(a.z - mx);
+    a.w = __expf(a.w - mx);
     s += hsum(a);
   }
   s = GroupReduce<G>::sum(s, red + G / 32);
+  const float inv = 1.0f / s;
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
     float4& a = x.v[j];
-    a.x = a.x / s; a.y = a.y / s; a.z = a.z / s; a.w = a.w / s;
+    a.x *= inv; a.y *= inv; a.z *= inv; a.w *= inv;
   }
   x.store(row, t, cols4);
 }
