@@ -78,6 +78,7 @@ struct EpiMaps {
 };
 
 constexpr int EPI_TILE_BYTES = 32 * 32 * 4;  // one staging tile per warp and buffer
+constexpr int EPI_NB_MAX = 2;                // staging tiles per epilogue warp, at most
 
 template <int BN, int STAGES, bool SPLIT3>
 struct GemmCfg {
@@ -105,7 +106,7 @@ struct GemmCtrl {
   uint64_t empty[STAGES];
   uint64_t tfull[2];
   uint64_t tempty[2];
-  uint64_t epi[EPI_WARPS];  // one per epilogue warp: its staged operand loads
+  uint64_t epi[EPI_WARPS * EPI_NB_MAX];  // per epilogue warp and staging tile: its TMA loads
   uint64_t qfull[TQ];       // tile queue: entry published (one arrive, the leader's producer)
   uint64_t qempty[TQ];      // tile queue (leader CTA): entry read by every consumer
   long long qunit[TQ];      // the published unit, -1 = no more work
@@ -386,50 +387,119 @@ __device__ __forceinline__ const CUtensorMap* epi_first_input(const GemmArgs& a,
   return nullptr;
 }
 
-// Issues the first input of a later chunk into buffer 0 once the stores in
-// flight have read it. Returns whether a load was issued.
-__device__ __forceinline__ bool epi_prefetch(const GemmArgs& a, const EpiMaps& em, uint8_t* bufs,
-                                             uint64_t* bar, int b, int m0, int n0, int lane) {
+// The staging tiles of one epilogue warp, used round-robin: NB tiles of
+// 32 x 32 f32 in the TMA 128B-swizzle layout, each with an mbarrier for the
+// TMA loads into it. Every load into a tile and every store out of one takes
+// the next tile of the ring, and a tile is written again only after the
+// stores issued from it have finished reading it. With one tile, each chunk
+// waits for the previous chunk's store to read the tile; with two, staging a
+// chunk overlaps that read.
+template <int NB>
+struct EpiRing {
+  uint8_t* tiles;
+  uint64_t* bars;
+  uint32_t phases;  // bit k: parity of the next wait on bars[k]
+  int next;         // the tile the next acquire returns
+  int stores;       // bulk store groups committed so far
+  // group number of the last store out of tile 0 / 1, -1 if none pending
+  // (two named fields, not an array, so they stay in registers)
+  int last0, last1;
+  __device__ __forceinline__ uint8_t* tile(int k) const { return tiles + k * EPI_TILE_BYTES; }
+  __device__ __forceinline__ int last(int k) const { return k == 0 ? last0 : last1; }
+  __device__ __forceinline__ void set_last(int k, int g) {
+    if (k == 0) last0 = g;
+    else last1 = g;
+  }
+};
+
+template <int NB>
+__device__ __forceinline__ void ring_init(EpiRing<NB>& r, uint8_t* tiles, uint64_t* bars) {
+  r.tiles = tiles;
+  r.bars = bars;
+  r.phases = 0;
+  r.next = 0;
+  r.stores = 0;
+  r.last0 = -1;
+  r.last1 = -1;
+}
+
+// The next tile of the ring, once the store last issued from it (if any)
+// has read it. Stores commit one group each, in order, and a tile is reused
+// after at most NB - 1 other uses, so at most NB - 1 later groups may stay
+// in flight.
+template <int NB>
+__device__ __forceinline__ int ring_acquire(EpiRing<NB>& r, int lane) {
+  static_assert(NB >= 1 && NB <= EPI_NB_MAX, "staging ring size");
+  const int k = r.next;
+  r.next = k + 1 == NB ? 0 : k + 1;
+  if (r.last(k) >= 0) {
+    const int later = r.stores - 1 - r.last(k);
+    if (lane == 0) {
+      if (NB > 1 && later >= 1) bulk_wait_group_read1();
+      else bulk_wait_group_read0();
+    }
+    __syncwarp();
+    r.set_last(k, -1);
+  }
+  return k;
+}
+
+template <int NB>
+__device__ __forceinline__ void ring_store(EpiRing<NB>& r, int k, const CUtensorMap* map, int is3d,
+                                           int n0, int m0, int b, int lane, bool reduce) {
+  epi_store(r.tile(k), map, is3d, n0, m0, b, lane, reduce);
+  r.set_last(k, r.stores++);
+}
+
+// Waits (bounded) for the load issued last into tile k.
+template <int NB>
+__device__ __forceinline__ bool ring_wait(EpiRing<NB>& r, int k) {
+  const bool ok = mbar_wait(&r.bars[k], (r.phases >> k) & 1u, DEVERR_GEMM_EPI_LOAD);
+  r.phases ^= 1u << k;
+  return ok;
+}
+
+// Issues the first input (epi_first_input) of a later chunk into the next
+// tile of the ring. Returns that tile, or -1 if nothing was loaded.
+template <int NB>
+__device__ __forceinline__ int epi_prefetch(const GemmArgs& a, const EpiMaps& em, EpiRing<NB>& rg,
+                                            int b, int m0, int n0, int lane) {
   int is3d = 0;
   const CUtensorMap* map = epi_first_input(a, em, is3d);
-  if (!map || m0 >= a.M || n0 >= a.N) return false;
-  epi_buffers_free(lane);
-  epi_issue(bufs, map, is3d, bar, n0, m0, b, lane);
-  return true;
+  if (!map || m0 >= a.M || n0 >= a.N) return -1;
+  const int k = ring_acquire(rg, lane);
+  epi_issue(rg.tile(k), map, is3d, &rg.bars[k], n0, m0, b, lane);
+  return k;
 }
 
 // The fused epilogue of one warp's 32 x 32 chunk (rows m0.., columns n0..),
-// in the same arithmetic order as epilogue_chunk, through the warp's one
-// staging tile. `prefetched`: the first input (epi_first_input) is already
-// on its way into the tile. Stores issued earlier may still be reading the
-// tile; the warp waits for them only right before it next writes the tile,
-// so the arithmetic in between overlaps those reads. Returns false if a
-// staged load timed out.
+// in the same arithmetic order as epilogue_chunk, through the warp's staging
+// ring. `pf`: the tile into which the first input (epi_first_input) is
+// already being loaded, or -1. Returns false if a staged load timed out.
+template <int NB>
 __device__ __forceinline__ bool epilogue_chunk_tma(const GemmArgs& a, const EpiMaps& em, int b,
-                                                   int m0, int n0, float (&v)[32], uint8_t* buf,
-                                                   uint64_t* bar, uint32_t& phase, int lane,
-                                                   bool prefetched) {
+                                                   int m0, int n0, float (&v)[32],
+                                                   EpiRing<NB>& rg, int lane, int pf) {
   if (m0 >= a.M) return true;  // rows past the matrix (last tile): nothing to move
-  bool in_use = !prefetched;   // a store may still be reading the tile
-  auto claim = [&] {
-    if (in_use) {
-      epi_buffers_free(lane);
-      in_use = false;
-    }
-  };
   if (a.alpha != 1.0f) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] *= a.alpha;
   }
   float t[32];
-  if (a.beta != 0.0f) {
-    if (!prefetched) {
-      claim();
-      epi_issue(buf, &em.c, a.c3d, bar, n0, m0, b, lane);
+  // Reads one input tile into t: the prefetched one, else a fresh load.
+  auto input = [&](const CUtensorMap* map, int is3d) -> bool {
+    int k = pf;
+    if (k < 0) {
+      k = ring_acquire(rg, lane);
+      epi_issue(rg.tile(k), map, is3d, &rg.bars[k], n0, m0, b, lane);
     }
-    prefetched = false;
-    if (!epi_wait(bar, phase)) return false;
-    stage_read_row(buf, lane, t);
+    pf = -1;
+    if (!ring_wait(rg, k)) return false;
+    stage_read_row(rg.tile(k), lane, t);
+    return true;
+  };
+  if (a.beta != 0.0f) {
+    if (!input(&em.c, a.c3d)) return false;
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] += a.beta * t[j];
   }
@@ -449,35 +519,23 @@ __device__ __forceinline__ bool epilogue_chunk_tma(const GemmArgs& a, const EpiM
     for (int j = 0; j < 32; ++j) v[j] += t[j];
   }
   if (a.R) {
-    if (!prefetched) {
-      claim();
-      epi_issue(buf, &em.r, a.r3d, bar, n0, m0, b, lane);
-    }
-    prefetched = false;
-    if (!epi_wait(bar, phase)) return false;
-    stage_read_row(buf, lane, t);
+    if (!input(&em.r, a.r3d)) return false;
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] += t[j];
   }
   if (a.P) {
-    claim();
-    stage_write_row(buf, lane, v);
-    epi_store(buf, &em.p, a.p3d, n0, m0, b, lane, false);
-    in_use = true;
+    const int k = ring_acquire(rg, lane);
+    stage_write_row(rg.tile(k), lane, v);
+    ring_store(rg, k, &em.p, a.p3d, n0, m0, b, lane, false);
   }
-  if (a.X) {
-    if (!prefetched) {  // aux is prefetched only when there is no pre-activation store
-      claim();
-      epi_issue(buf, &em.x, a.x3d, bar, n0, m0, b, lane);
-    }
-    if (!epi_wait(bar, phase)) return false;
-    stage_read_row(buf, lane, t);
+  if (a.X) {  // aux is prefetched only when there is no pre-activation store
+    if (!input(&em.x, a.x3d)) return false;
     act_grad_chunk(a.grad_act, v, t);
   }
   act_forward_chunk(a.act, v);
-  claim();
-  stage_write_row(buf, lane, v);
-  epi_store(buf, &em.c, a.c3d, n0, m0, b, lane, a.accumulate != 0);
+  const int k = ring_acquire(rg, lane);
+  stage_write_row(rg.tile(k), lane, v);
+  ring_store(rg, k, &em.c, a.c3d, n0, m0, b, lane, a.accumulate != 0);
   return true;
 }
 
@@ -532,7 +590,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       mbar_init(&ctrl->tempty[i], 32 * EPI_WARPS);
     }
 #pragma unroll
-    for (int w = 0; w < EPI_WARPS; ++w) mbar_init(&ctrl->epi[w], 1);
+    for (int w = 0; w < EPI_WARPS * EPI_NB_MAX; ++w) mbar_init(&ctrl->epi[w], 1);
 #pragma unroll
     for (int q = 0; q < TQ; ++q) {
       mbar_init(&ctrl->qfull[q], 1);                // the producer's publish
@@ -691,9 +749,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int group = (warp - 2) / 4;  // which alternate 32-column chunks it takes
     const int row_local = quarter * 32 + lane;
     uint8_t* bufs = ring + STAGES * Cfg::STAGE_BYTES + (warp - 2) * EPI_TILE_BYTES;
-    uint64_t* ebar = &ctrl->epi[warp - 2];
-    uint32_t ephase = 0;
-    bool ok = true, pf = false;  // pf: the next chunk's first input is being loaded
+    EpiRing<1> rg;
+    ring_init(rg, bufs, &ctrl->epi[(warp - 2) * EPI_NB_MAX]);
+    bool ok = true;
+    int pf = -1;  // the tile the next chunk's first input is being loaded into
     for (int local = 0; ok; ++local) {
       long long u;
       if (dyn) {
@@ -727,12 +786,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), v);
         if (args.epi_tma) {
           const int m0 = tm * BM + quarter * 32;
-          if (!epilogue_chunk_tma(args, em, b, m0, n0, v, bufs, ebar, ephase, lane,
-                                        pf)) {
+          if (!epilogue_chunk_tma(args, em, b, m0, n0, v, rg, lane, pf)) {
             ctrl->abort_flag = 1;
-            ok = pf = false;
+            ok = false;
+            pf = -1;
             break;
           }
+          pf = -1;
           int nb, nm0, nn0;
           long long u2 = -2;  // the next unit, for its first chunk's input
           if (dyn) {
@@ -741,8 +801,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           } else {
             u2 = static_unit(args, blockIdx.x, gridDim.x, local + 1);
           }
-          pf = epi_next_chunk<BN>(args, u2, c, group, quarter * 32, b, tn, m0, nb, nm0, nn0) &&
-               epi_prefetch(args, em, bufs, ebar, nb, nm0, nn0, lane);
+          if (epi_next_chunk<BN>(args, u2, c, group, quarter * 32, b, tn, m0, nb, nm0, nn0))
+            pf = epi_prefetch(args, em, rg, nb, nm0, nn0, lane);
         } else if (m < args.M) {
           epilogue_chunk(args, b, m, n0, v);
         }
@@ -750,7 +810,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tc_fence_before();
       mbar_arrive(&ctrl->tempty[acc_slot]);
     }
-    if (pf) epi_wait(ebar, ephase);  // an abandoned prefetch must land before exit
+    if (pf >= 0) ring_wait(rg, pf);  // an abandoned prefetch must land before exit
     if (lane == 0) bulk_wait_group0();  // no store may outlive the CTA's shared memory
     __syncwarp();
   }
@@ -772,7 +832,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 // CTA's full barrier, the leader alone issues the MMAs and multicast-commits
 // to both CTAs' barriers, and each CTA's epilogue drains its own 128 TMEM
 // lanes and releases the accumulator to the leader with a remote arrive.
-template <int BN, int STAGES, bool SPLIT3>
+template <int BN, int STAGES, bool SPLIT3, int NB>
 struct GemmPairCfg {
   static constexpr int A_BYTES = BM * BK * 4;
   static constexpr int B_BYTES = (BN / 2) * BK * 4;
@@ -789,10 +849,12 @@ struct GemmPairCfg {
   static constexpr int ACC_BUFS = 2 * BN <= 512 ? 2 : 1;
   static constexpr int TMEM_COLS = ACC_BUFS * BN;
   static constexpr int CTRL_BYTES = 1024;
-  static constexpr int EPI_BYTES = EPI_WARPS * EPI_TILE_BYTES;  // one staging tile per epilogue warp
+  // NB staging tiles per epilogue warp
+  static constexpr int EPI_BYTES = EPI_WARPS * EPI_TILE_BYTES * NB;
   static constexpr int SMEM_BYTES = 1024 + CTRL_BYTES + STAGES * STAGE_BYTES + EPI_BYTES;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
   static_assert(BN % MMA_N == 0 && TMEM_COLS <= 512, "tile shape");
+  static_assert(NB >= 1 && NB <= EPI_NB_MAX, "staging tiles per warp");
 };
 
 // TMEM column of a pair tile's 32-column output chunk c. CTA r of the pair
@@ -825,14 +887,14 @@ __device__ __forceinline__ void load_operand_pair(uint8_t* dst, const CUtensorMa
   }
 }
 
-template <int BN, int STAGES, bool SPLIT3>
+template <int BN, int STAGES, bool SPLIT3, int NB>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     gemm_tf32_tcgen05_pair(const __grid_constant__ CUtensorMap tmA,
                            const __grid_constant__ CUtensorMap tmB,
                            const __grid_constant__ CUtensorMap tmA_lo,
                            const __grid_constant__ CUtensorMap tmB_lo,
                            const __grid_constant__ EpiMaps em, const GemmArgs args) {
-  using Cfg = GemmPairCfg<BN, STAGES, SPLIT3>;
+  using Cfg = GemmPairCfg<BN, STAGES, SPLIT3, NB>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -856,7 +918,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
       mbar_init(&ctrl->tempty[i], 2 * EPI_WARPS);  // leader: one arrive per epilogue warp of the pair
     }
 #pragma unroll
-    for (int w = 0; w < EPI_WARPS; ++w) mbar_init(&ctrl->epi[w], 1);
+    for (int w = 0; w < EPI_WARPS * EPI_NB_MAX; ++w) mbar_init(&ctrl->epi[w], 1);
 #pragma unroll
     for (int q = 0; q < TQ; ++q) {
       mbar_init(&ctrl->qfull[q], 1);  // the leader producer's publish (local or remote)
@@ -1026,10 +1088,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     const int quarter = warp & 3;
     const int group = (warp - 2) / 4;
     const int row_local = quarter * 32 + lane;
-    uint8_t* bufs = ring + STAGES * Cfg::STAGE_BYTES + (warp - 2) * EPI_TILE_BYTES;
-    uint64_t* ebar = &ctrl->epi[warp - 2];
-    uint32_t ephase = 0;
-    bool ok = true, pf = false;  // pf: the next chunk's first input is being loaded
+    uint8_t* bufs = ring + STAGES * Cfg::STAGE_BYTES + (warp - 2) * EPI_TILE_BYTES * NB;
+    EpiRing<NB> rg;
+    ring_init(rg, bufs, &ctrl->epi[(warp - 2) * EPI_NB_MAX]);
+    bool ok = true;
+    int pf = -1;  // the tile the next chunk's first input is being loaded into
     for (int local = 0; ok; ++local) {
       long long u;
       if (dyn) {
@@ -1064,11 +1127,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
         tmem_ld_32x32b_x32(taddr + pair_chunk_tmem_col<BN>(c), v);
         if (args.epi_tma) {
           const int m0 = m_base + quarter * 32;
-          if (!epilogue_chunk_tma(args, em, b, m0, n0, v, bufs, ebar, ephase, lane, pf)) {
+          if (!epilogue_chunk_tma(args, em, b, m0, n0, v, rg, lane, pf)) {
             ctrl->abort_flag = 1;
-            ok = pf = false;
+            ok = false;
+            pf = -1;
             break;
           }
+          pf = -1;
           int nb, nm0, nn0;
           long long u2 = -2;  // the next unit, for its first chunk's input
           if (dyn) {
@@ -1077,9 +1142,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
           } else {
             u2 = static_unit(args, cluster_id, nclusters, local + 1);
           }
-          pf = epi_next_chunk<BN>(args, u2, c, group, static_cast<int>(rank) * BM + quarter * 32,
-                                  b, tn, m0, nb, nm0, nn0) &&
-               epi_prefetch(args, em, bufs, ebar, nb, nm0, nn0, lane);
+          if (epi_next_chunk<BN>(args, u2, c, group, static_cast<int>(rank) * BM + quarter * 32,
+                                 b, tn, m0, nb, nm0, nn0))
+            pf = epi_prefetch(args, em, rg, nb, nm0, nn0, lane);
         } else if (m < args.M) {
           epilogue_chunk(args, b, m, n0, v);
         }
@@ -1088,7 +1153,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(tempty0 + 8u * static_cast<uint32_t>(acc_slot));
     }
-    if (pf) epi_wait(ebar, ephase);  // an abandoned prefetch must land before exit
+    if (pf >= 0) ring_wait(rg, pf);  // an abandoned prefetch must land before exit
     if (lane == 0) bulk_wait_group0();  // no store may outlive the CTA's shared memory
     __syncwarp();
   }
@@ -1487,14 +1552,14 @@ oxf_status launch_tcgen05(const CUtensorMap& ta, const CUtensorMap& tb, const CU
   return check_launch("gemm_tf32_tcgen05");
 }
 
-template <int BN, int STAGES, bool SPLIT3>
+template <int BN, int STAGES, bool SPLIT3, int NB>
 oxf_status launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta_lo,
                        const CUtensorMap& tb_lo, const EpiMaps& em, GemmArgs& args,
                        cudaStream_t stream, int dev) {
-  using Cfg = GemmPairCfg<BN, STAGES, SPLIT3>;
+  using Cfg = GemmPairCfg<BN, STAGES, SPLIT3, NB>;
   static bool configured[kMaxDevices] = {false};
   if (dev >= 0 && dev < kMaxDevices && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tf32_tcgen05_pair<BN, STAGES, SPLIT3>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_tf32_tcgen05_pair<BN, STAGES, SPLIT3, NB>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg::SMEM_BYTES);
     if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(gemm pair)");
@@ -1505,7 +1570,7 @@ oxf_status launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
   args.sched_next = nullptr;
   args.sched_done = nullptr;
   if (args.units > clusters) schedule_slot(stream, dev, &args.sched_next, &args.sched_done);
-  gemm_tf32_tcgen05_pair<BN, STAGES, SPLIT3>
+  gemm_tf32_tcgen05_pair<BN, STAGES, SPLIT3, NB>
       <<<static_cast<unsigned>(2 * clusters), GEMM_THREADS, Cfg::SMEM_BYTES, stream>>>(
           ta, tb, ta_lo, tb_lo, em, args);
   return check_launch("gemm_tf32_tcgen05_pair");
@@ -1822,10 +1887,13 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
     a.epi_tma = eok ? 1 : 0;
   }
 
-  if (split3 && pair) return launch_pair<256, 3, true>(ta, tb, ta_lo, tb_lo, em, a, stream, dev);
+  if (split3 && pair)
+    return launch_pair<256, 3, true, 1>(ta, tb, ta_lo, tb_lo, em, a, stream, dev);
   if (split3) return launch_tcgen05<128, 3, true>(ta, tb, ta_lo, tb_lo, em, a, stream, dev);
-  if (pair && BN == 512) return launch_pair<512, 4, false>(ta, tb, ta, tb, em, a, stream, dev);
-  if (pair) return launch_pair<256, 6, false>(ta, tb, ta, tb, em, a, stream, dev);
+  // One staging tile per epilogue warp: two (with a stage fewer) measured
+  // the same on the training step.
+  if (pair && BN == 512) return launch_pair<512, 4, false, 1>(ta, tb, ta, tb, em, a, stream, dev);
+  if (pair) return launch_pair<256, 6, false, 1>(ta, tb, ta, tb, em, a, stream, dev);
   if (BN == 256) return launch_tcgen05<256, 4, false>(ta, tb, ta, tb, em, a, stream, dev);
   if (BN == 128) return launch_tcgen05<128, 6, false>(ta, tb, ta, tb, em, a, stream, dev);
   return launch_tcgen05<64, 8, false>(ta, tb, ta, tb, em, a, stream, dev);
