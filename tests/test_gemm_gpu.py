@@ -410,3 +410,45 @@ def test_small_products_match_reference_rounding_and_epilogue(K, rng):
     acc = dev(C0)
     K.gemm(dev(A), dev(B), acc, accumulate=True)
     assert rel_err(host(acc), C0 + exact(A, B, 0, 0)) < TF32_TOL
+
+
+@pytest.mark.parametrize("M,N,Kd", [(4096, 2048, 512), (2048, 4096, 4096)])
+def test_schedules_agree_and_capture(K, monkeypatch, M, N, Kd):
+    """Multi-wave products (more tiles than CTA pairs) on the dynamic tile
+    schedule (units claimed from a per-stream counter, handed through the
+    shared-memory tile queue) and on the static one (OXF_GEMM_SCHEDULE=static)
+    give bit-identical outputs: each tile's arithmetic is the same whichever
+    CTA computes it. The second shape takes the 256 x 512 tile. A CUDA-graph
+    capture of the same product (static schedule under capture) replays to
+    the same bits, and the same product launched on two streams at once
+    (one counter slot each) is right on both."""
+    g = torch.Generator(device="cuda").manual_seed(5)
+    A = torch.randn(M, Kd, device="cuda", generator=g)
+    B = torch.randn(Kd, N, device="cuda", generator=g)
+    dyn = torch.empty(M, N, device="cuda")
+    K.gemm(A, B, dyn)
+    monkeypatch.setenv("OXF_GEMM_SCHEDULE", "static")
+    sta = torch.empty(M, N, device="cuda")
+    K.gemm(A, B, sta)
+    monkeypatch.delenv("OXF_GEMM_SCHEDULE")
+    torch.cuda.synchronize()
+    assert torch.equal(dyn, sta)
+    cap = torch.zeros(M, N, device="cuda")
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side), torch.cuda.graph(graph, stream=side):
+        K.gemm(A, B, cap, stream=side)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(cap, dyn)
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    o1, o2 = torch.empty(M, N, device="cuda"), torch.empty(M, N, device="cuda")
+    s1.wait_stream(torch.cuda.current_stream())
+    s2.wait_stream(torch.cuda.current_stream())
+    for _ in range(3):
+        K.gemm(A, B, o1, stream=s1)
+        K.gemm(A, B, o2, stream=s2)
+    torch.cuda.synchronize()
+    assert torch.equal(o1, dyn) and torch.equal(o2, dyn)
+    assert K.device_error() == 0
