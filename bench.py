@@ -274,6 +274,29 @@ def _time(torch, fn, steps, warmup):
     return e0.elapsed_time(e1) / steps
 
 
+def _graph_time(torch, fn, steps, warmup, reps=50):
+    """Mean device ms per call: `reps` calls captured once in a CUDA graph on
+    a side stream and replayed `steps` times (after `warmup` eager calls)."""
+    for _ in range(max(1, warmup)):
+        fn()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side), torch.cuda.graph(g, stream=side):
+        for _ in range(reps):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = _events(torch)
+    e0.record()
+    for _ in range(max(1, steps)):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / (reps * max(1, steps))
+
+
 def run_gemm(a, torch):
     """Config 3's square sweep (or one shape): TF32 GEMM TFLOP/s against
     cuBLAS TF32 on the same GPU; inputs U(-1,1), 3 x 256 MiB operands at
@@ -302,12 +325,15 @@ def run_gemm(a, torch):
         if prec == _lib.PREC_TF32X3:
             kw["workspace"] = torch.empty(
                 K.gemm_workspace_bytes(M, N, Kd, at, bt) // 4 + 64, device="cuda")
-        ms = _time(torch, lambda: K.gemm(A, B, Cm, a_trans=at, b_trans=bt, precision=prec, **kw),
+        fl = 2.0 * M * N * Kd
+        # Below ~50 GFLOP a call is shorter than its host-side submission, so
+        # both arms are timed as CUDA-graph replays (device time per call).
+        timer = _time if fl >= 5e10 else _graph_time
+        ms = timer(torch, lambda: K.gemm(A, B, Cm, a_trans=at, b_trans=bt, precision=prec, **kw),
                    a.steps, a.warmup)
         torch.backends.cuda.matmul.allow_tf32 = True
-        ref = _time(torch, lambda: torch.matmul(A.T if at else A, B.T if bt else B, out=Cm),
+        ref = timer(torch, lambda: torch.matmul(A.T if at else A, B.T if bt else B, out=Cm),
                     a.steps, a.warmup)
-        fl = 2.0 * M * N * Kd
         res.append({"shape": [M, N, Kd], "mode": a.mode, "epilogue": a.epi,
                     "precision": a.precision, "ms": ms,
                     "tflops": fl / ms / 1e9,

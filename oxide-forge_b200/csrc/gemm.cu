@@ -1774,7 +1774,7 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
   // CTA pairs (256 x 256 tiles, half the L2->SM bytes per flop of a one-CTA
   // tile) whenever there are enough of them to occupy every SM pair;
   // variant 1 forces one CTA, 2 forces pairs.
-  bool pair = false;
+  bool pair = false, autosplit = false;
   {
     const long long tiles2 = static_cast<long long>((d->M + 2 * BM - 1) / (2 * BM)) *
                              ((d->N + 255) / 256) * (d->reduce_batch ? 1 : d->batch);
@@ -1783,8 +1783,19 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
     const bool splittable = d->accumulate && split <= 1 && !d->bias && !d->residual &&
                             static_cast<long long>((d->K + BK - 1) / BK) *
                                     (d->reduce_batch ? d->batch : 1) >= 2 * kWideMinKBlocks;
+    // A plain product (nothing in the epilogue but alpha) with too few tiles
+    // to fill the GPU splits K: C is zeroed and the splits add into it.
+    autosplit = d->variant == 0 && !split3 && !d->accumulate && split <= 1 && d->beta == 0.0f &&
+                !d->bias && !d->residual && !d->pre_out && !d->aux &&
+                d->act == OXF_ACT_IDENTITY && !a.reduce_batch && d->batch == 1 &&
+                d->M >= 2 * BM && tiles2 < (3 * sms / 2) / 4 &&
+                (d->K + BK - 1) / BK >= 16;
+    // One partly filled wave of pairs (at least 3/4 of them busy) beats
+    // 1.5-2 waves of one-CTA tiles with twice the operand bytes per flop.
+    const long long pair_min = (3 * (sms / 2)) / 4;
     pair = d->variant == 2 || d->variant == 3 ||
-           (d->variant == 0 && d->M >= 2 * BM && (tiles2 >= sms / 2 || splittable));
+           (d->variant == 0 && d->M >= 2 * BM &&
+            (tiles2 >= pair_min || splittable || autosplit));
     if (pair) BN = 256;
   }
   // Wide pair tiles (256 x 512): a quarter fewer operand bytes per flop
@@ -1837,6 +1848,16 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
     const bool additive = d->bias != nullptr || d->residual != nullptr;
     a.splits = split > 1 ? std::min(split, a.kblocks)
                          : (additive ? 1 : choose_splits(tiles, a.kblocks, sms));
+  } else if (autosplit) {
+    a.splits = choose_splits(tiles, a.kblocks, pair ? sms / 2 : sms);
+    if (a.splits > 1) {
+      oxf_status zs = check_cuda(cudaMemset2DAsync(d->C, static_cast<size_t>(d->ldc) * 4, 0,
+                                                   static_cast<size_t>(d->N) * 4,
+                                                   static_cast<size_t>(d->M), stream),
+                                 "oxf_gemm: zeroing C for split K");
+      if (zs != OXF_OK) return zs;
+      a.accumulate = 1;
+    }
   } else {
     a.splits = 1;
   }
