@@ -194,6 +194,18 @@ __device__ __forceinline__ long long queue_peek(GemmCtrl<STAGES>* ctrl, int i) {
   return ctrl->qunit[slot];
 }
 
+// Programmatic dependent launch (the persistent kernels are launched with
+// programmatic stream serialisation): the prologue (barriers, TMEM,
+// tensor-map prefetch, cluster sync) runs while the previous kernel of the
+// stream finishes; every thread then waits here for that kernel's completion
+// and memory before any global access, the schedule counter included.
+// Letting dependents launch at this point only pre-stages them: they wait
+// for this grid the same way.
+__device__ __forceinline__ void pdl_after_prologue() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // Dynamic schedule only: the last CTA of the grid to finish resets the
 // counter for the next launch on this slot (every CTA reaches this point,
 // aborted ones included, after its producer stopped claiming).
@@ -614,6 +626,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_after_prologue();
   const uint32_t tmem_base = ctrl->tmem_base;
   const bool dyn = args.sched_next != nullptr;
   const uint32_t qempty0 = map_to_rank(&ctrl->qempty[0], 0);
@@ -943,6 +956,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
   tc_fence_before();
   cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
   tc_fence_after();
+  pdl_after_prologue();
   const uint32_t tmem_base = ctrl->tmem_base;
   const uint32_t full0 = map_to_rank(&ctrl->full[0], 0);
   const uint32_t tempty0 = map_to_rank(&ctrl->tempty[0], 0);
@@ -1528,6 +1542,29 @@ bool encode_map(CUtensorMap* map, const float* ptr, long long inner, long long o
   return r == CUDA_SUCCESS;
 }
 
+// Launches a persistent GEMM kernel with programmatic stream serialisation
+// (see pdl_after_prologue) and counts it.
+using GemmKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap,
+                            const CUtensorMap, const EpiMaps, const GemmArgs);
+oxf_status launch_gemm_pdl(const char* name, GemmKernel kernel, unsigned grid, int smem,
+                           cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb,
+                           const CUtensorMap& ta_lo, const CUtensorMap& tb_lo, const EpiMaps& em,
+                           const GemmArgs& args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(GEMM_THREADS);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, ta_lo, tb_lo, em, args);
+  count_launch();
+  return check_cuda(e != cudaSuccess ? e : cudaGetLastError(), name);
+}
+
 template <int BN, int STAGES, bool SPLIT3>
 oxf_status launch_tcgen05(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta_lo,
                           const CUtensorMap& tb_lo, const EpiMaps& em, GemmArgs& args,
@@ -1546,10 +1583,9 @@ oxf_status launch_tcgen05(const CUtensorMap& ta, const CUtensorMap& tb, const CU
   args.sched_next = nullptr;
   args.sched_done = nullptr;
   if (args.units > grid) schedule_slot(stream, dev, &args.sched_next, &args.sched_done);
-  gemm_tf32_tcgen05<BN, STAGES, SPLIT3>
-      <<<static_cast<unsigned>(grid), GEMM_THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, ta_lo,
-                                                                              tb_lo, em, args);
-  return check_launch("gemm_tf32_tcgen05");
+  return launch_gemm_pdl("gemm_tf32_tcgen05", gemm_tf32_tcgen05<BN, STAGES, SPLIT3>,
+                         static_cast<unsigned>(grid), Cfg::SMEM_BYTES, stream, ta, tb, ta_lo,
+                         tb_lo, em, args);
 }
 
 template <int BN, int STAGES, bool SPLIT3, int NB>
@@ -1570,10 +1606,9 @@ oxf_status launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
   args.sched_next = nullptr;
   args.sched_done = nullptr;
   if (args.units > clusters) schedule_slot(stream, dev, &args.sched_next, &args.sched_done);
-  gemm_tf32_tcgen05_pair<BN, STAGES, SPLIT3, NB>
-      <<<static_cast<unsigned>(2 * clusters), GEMM_THREADS, Cfg::SMEM_BYTES, stream>>>(
-          ta, tb, ta_lo, tb_lo, em, args);
-  return check_launch("gemm_tf32_tcgen05_pair");
+  return launch_gemm_pdl("gemm_tf32_tcgen05_pair", gemm_tf32_tcgen05_pair<BN, STAGES, SPLIT3, NB>,
+                         static_cast<unsigned>(2 * clusters), Cfg::SMEM_BYTES, stream, ta, tb,
+                         ta_lo, tb_lo, em, args);
 }
 
 // Chooses how many K splits an accumulating GEMM uses: minimises
