@@ -452,3 +452,25 @@ def test_schedules_agree_and_capture(K, monkeypatch, M, N, Kd):
     torch.cuda.synchronize()
     assert torch.equal(o1, dyn) and torch.equal(o2, dyn)
     assert K.device_error() == 0
+
+
+@pytest.mark.parametrize("at,bt", [(0, 0), (1, 0), (0, 1)])
+@pytest.mark.parametrize("M,N,Kd", [(1024, 1024, 1024), (512, 768, 2048), (300, 520, 4096)])
+def test_small_plain_products_split_k(K, M, N, Kd, at, bt):
+    """Plain products (alpha only) whose 256 x 256 tiles fill under 3/4 of the
+    CTA pairs split K: the output is zeroed first and the splits add into it.
+    The output starts as garbage here, which must not leak; alpha scales
+    every split. A beta != 0 product of the same shape takes the unsplit
+    path and must also be right."""
+    g = torch.Generator(device="cuda").manual_seed(9)
+    A = torch.randn((Kd, M) if at else (M, Kd), device="cuda", generator=g)
+    B = torch.randn((N, Kd) if bt else (Kd, N), device="cuda", generator=g)
+    want = (A.double().T if at else A.double()) @ (B.double().T if bt else B.double())
+    scale = want.abs().max().item()
+    out = torch.full((M, N), float("nan"), device="cuda")
+    K.gemm(A, B, out, a_trans=bool(at), b_trans=bool(bt), alpha=0.5)
+    assert ((out.double() - 0.5 * want).abs().max().item() / (0.5 * scale)) < TF32_TOL
+    C0 = torch.randn(M, N, device="cuda", generator=g)
+    out2 = C0.clone()
+    K.gemm(A, B, out2, a_trans=bool(at), b_trans=bool(bt), beta=1.0)
+    assert ((out2.double() - want - C0.double()).abs().max().item() / scale) < TF32_TOL
