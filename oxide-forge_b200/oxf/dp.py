@@ -156,6 +156,53 @@ class DataParallelTrainer:
         compute.wait_stream(xs)
         return loss / (self.global_batch * self.seq)
 
+    def save_checkpoint(self, path, cfg) -> None:
+        """Checkpoint v1 (the reference's TOML + little-endian f32 files,
+        src/net/checkpoint/model.rs:138-148) of the model's parameters,
+        described by `cfg` (models.TransformerConfig). Every rank holds the
+        same parameters after a step, so rank 0 alone writes. Collective:
+        every rank returns once the files are complete."""
+        from .checkpoint import dump_transformer_params
+        err = None
+        if self.rank == 0:
+            try:
+                dump_transformer_params(path, cfg, self.model.params.detach().cpu().numpy())
+            except Exception as ex:  # reported on every rank below
+                err = ex
+        self._agree(err is None, err, "rank 0 could not write the checkpoint")
+
+    def load_checkpoint(self, path, cfg) -> None:
+        """Rank 0 reads checkpoint v1 files (model.rs:150-172, with every
+        validation of the format), refuses them unless they describe `cfg`,
+        and every rank receives the parameters by broadcast (no shared file
+        system needed). Collective; raises on every rank if rank 0 failed."""
+        from .checkpoint import load_transformer_params
+        params = self.model.params
+        err = None
+        if self.rank == 0:
+            try:
+                got, flat = load_transformer_params(path)
+                if got != cfg:
+                    raise ValueError(f"checkpoint describes {got}, not {cfg}")
+                if flat.size != params.numel():
+                    raise ValueError(f"checkpoint holds {flat.size} parameters, the model "
+                                     f"{params.numel()}")
+                params.copy_(torch.from_numpy(flat).to(params.device))
+            except Exception as ex:  # reported on every rank below
+                err = ex
+        self._agree(err is None, err, "rank 0 could not load the checkpoint")
+        self.broadcast_params(params)
+
+    def _agree(self, ok: bool, err, message: str) -> None:
+        """Rank 0's outcome, shared with every rank (raises on all of them)."""
+        if self.world > 1:
+            dev = self.model.params.device
+            flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+            dist.broadcast(flag, 0, group=self.group)
+            ok = bool(flag.item())
+        if not ok:
+            raise err if err is not None else RuntimeError(message)
+
     def close(self) -> None:
         """Releases the peer exchange (collective when exchange='peer')."""
         if self._peer is not None:

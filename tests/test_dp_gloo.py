@@ -183,3 +183,64 @@ def test_peer_exchange_needs_cuda_arenas():
         DataParallelTrainer(model, 4, lr=0.1, seq=SEQ, exchange="peer")
     with pytest.raises(ValueError):
         DataParallelTrainer(model, 4, lr=0.1, seq=SEQ, exchange="allgather")
+
+
+def _ckpt_worker(rank, world, port, out_dir):
+    import torch.distributed as dist
+    from datetime import timedelta
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=30))
+    sys.path.insert(0, str(ROOT / "oxide-forge_b200"))
+    from oxf import _lib, models
+    from oxf.dp import DataParallelTrainer
+    cfg = models.transformer_config(SEQ, H, F, norm=_lib.NORM_LAYER)
+    model = OracleModel(_flat0() if rank == 0 else np.zeros_like(_flat0()))
+    tr = DataParallelTrainer(model, 4, lr=0.1, seq=SEQ)
+    tr.broadcast_params(model.params)
+    x, t = _data(4, seed=0)
+    lo, hi = tr.local
+    tr.step(torch.from_numpy(x[lo * SEQ:hi * SEQ]), torch.from_numpy(t[lo * SEQ:hi * SEQ]))
+    saved = model.params.numpy().copy()
+    path = str(Path(out_dir) / "dp_ckpt")
+    tr.save_checkpoint(path, cfg)
+    model.params.zero_()
+    tr.load_checkpoint(path, cfg)
+    result = {"rank": rank, "saved": saved, "loaded": model.params.numpy().copy()}
+    wrong = models.transformer_config(SEQ, H, F + 4, norm=_lib.NORM_LAYER)
+    try:
+        tr.load_checkpoint(path, wrong)
+        result["wrong"] = "accepted"
+    except Exception as ex:
+        result["wrong"] = type(ex).__name__
+    try:
+        tr.load_checkpoint(str(Path(out_dir) / "missing"), cfg)
+        result["missing"] = "accepted"
+    except Exception as ex:
+        result["missing"] = type(ex).__name__
+    np.save(Path(out_dir) / f"ckpt{rank}.npy", result, allow_pickle=True)
+    dist.destroy_process_group()
+
+
+def test_dp_checkpoint_save_by_rank0_load_by_broadcast(tmp_path):
+    """Checkpoint v1 from a data-parallel run: rank 0 writes the (identical)
+    parameters; loading reads them on rank 0, checks them against the model's
+    configuration and broadcasts them; a mismatching configuration or a
+    missing file is an error on every rank."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_ckpt_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+            raise AssertionError("a rank hung")
+        assert p.exitcode == 0
+    r = [np.load(tmp_path / f"ckpt{q}.npy", allow_pickle=True).item() for q in range(2)]
+    np.testing.assert_array_equal(r[0]["saved"], r[1]["saved"])
+    for q in range(2):
+        np.testing.assert_array_equal(r[q]["loaded"], r[0]["saved"])
+        assert r[q]["wrong"] != "accepted" and r[q]["missing"] != "accepted"
+    assert (tmp_path / "dp_ckpt.toml").exists() and (tmp_path / "dp_ckpt.bin").exists()

@@ -325,3 +325,35 @@ def test_full_size_c5_sequence_matches_oracle(M):
     g1 = host(eng.grads)
     check_per_tensor(cfg, lr * (g2 - g1), flat - ref.flat())
     eng.close()
+
+
+def test_trainer_checkpoint_round_trip_on_the_engine(tmp_path):
+    """DataParallelTrainer.save_checkpoint / load_checkpoint on the engine's
+    device arena (one rank): the parameters after a step survive a write,
+    an overwrite of the arena and a read; a checkpoint of another shape is
+    refused and leaves the arena as it was."""
+    import torch
+    from oxf import _lib, models
+    from oxf.dp import DataParallelTrainer
+    cfg = models.transformer_config(64, 128, 256, norm=_lib.NORM_LAYER)
+    m = models.Transformer(cfg, max_batch=2)
+    m.set_params(models.init_transformer_params(cfg, seed=0))
+    tr = DataParallelTrainer(m, 2, 0.05, 64)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    x = torch.randn(2 * 64, 128, device="cuda", generator=g)
+    t = torch.randn(2 * 64, 128, device="cuda", generator=g)
+    tr.step(x, t)
+    torch.cuda.synchronize()
+    saved = m.get_params()
+    path = str(tmp_path / "engine_ckpt")
+    tr.save_checkpoint(path, cfg)
+    m.params.zero_()
+    tr.load_checkpoint(path, cfg)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(m.get_params(), saved)
+    other = models.transformer_config(64, 128, 512, norm=_lib.NORM_LAYER)
+    with pytest.raises(ValueError):
+        tr.load_checkpoint(path, other)
+    np.testing.assert_array_equal(m.get_params(), saved)
+    tr.close()
+    m.close()
