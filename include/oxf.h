@@ -125,6 +125,10 @@ oxf_status oxf_slice_max(oxf_cslice span, float* result, oxf_stream stream);
  * its parameter (as oxf_slice_unary). */
 oxf_status oxf_slice_map_sum(oxf_cslice span, oxf_unary_op op, float param, float* result,
                              oxf_stream stream);
+/* Vector::dot (vector.rs:109-115: an elementwise product into a temporary
+ * vector, then its sum) as one reduction launch with no temporary:
+ * *result = sum_i lhs[i] * rhs[i]. Lengths must match (vector.rs:110). */
+oxf_status oxf_slice_dot(oxf_cslice lhs, oxf_cslice rhs, float* result, oxf_stream stream);
 
 /* ---------------------------------------------------------------- fills */
 /* slice_set (module.rs:15-20): every element = value. */

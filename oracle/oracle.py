@@ -64,6 +64,7 @@ def lib() -> C.CDLL:
             "oxo_fill_random": (None, [fp, sz, C.c_uint32]),
             "oxo_unary": (C.c_float, [C.c_int, C.c_float, C.c_float]),
             "oxo_map_sum": (C.c_float, [fp, sz, C.c_int, C.c_float]),
+            "oxo_dot": (C.c_float, [fp, fp, sz]),
             "oxo_matrix_slice": (None, [fp, fp, sz, sz, sz, sz, sz]),
             "oxo_exchange_sgd": (None, [C.c_void_p, C.c_void_p, C.c_int, sz, sz, C.c_float]),
             "oxo_causal_mask": (None, [fp, sz, sz, sz]),
@@ -206,6 +207,11 @@ def exchange_sgd(params: list, grads: list, offset: int, count: int, lr: float) 
     gp = (C.c_void_p * W)(*[g.ctypes.data for g in gs])
     lib().oxo_exchange_sgd(pp, gp, W, offset, count, lr)
     return ps
+
+
+def dot(x, y):
+    x, y = _c(x), _c(y)
+    return float(lib().oxo_dot(_p(x), _p(y), x.size))
 
 
 def matrix_slice(m, tile_rows, tile_cols, tiles_per_row, n_tiles):

@@ -351,6 +351,17 @@ float oxo_map_sum(const float* x, size_t n, int op, float p) {
     return s;
 }
 
+/* Vector::dot, vector.rs:109-115 (vector_mul, then sum). */
+float oxo_dot(const float* x, const float* y, size_t n) {
+    if (n == 0) return 0.0f;
+    float* t = (float*)malloc(n * sizeof(float));
+    if (!t) return 0.0f;
+    for (size_t i = 0; i < n; ++i) t[i] = x[i] * y[i];
+    const float s = psum(t, n);
+    free(t);
+    return s;
+}
+
 /* Data-parallel update across ranks; contract in oxf_oracle.h. */
 void oxo_exchange_sgd(float* const* params, const float* const* grads, int world, size_t offset,
                       size_t count, float lr) {

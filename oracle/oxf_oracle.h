@@ -82,6 +82,9 @@ void oxo_fill_random(float* out, size_t n, uint32_t seed);
 float oxo_unary(int op, float x, float p);
 /* slice_map_sum, reduction.rs:44-80: sum of f(x_i) (pairwise). */
 float oxo_map_sum(const float* x, size_t n, int op, float p);
+/* Vector::dot, vector.rs:109-115: the elementwise product, then its sum
+ * (pairwise, as oxo_map_sum). */
+float oxo_dot(const float* x, const float* y, size_t n);
 /* matrix_slice, layout.rs:58-86: output element l belongs to tile l / (tr*tc)
  * (tile row = tile / tiles_per_row, tile column = tile % tiles_per_row) at
  * local row (l % (tr*tc)) / tc, local column (l % (tr*tc)) % tc. */

@@ -44,7 +44,7 @@ oxf_status causal_mask(float*, long long, long long, cudaStream_t);
 oxf_status cols_sum(const float*, float*, long long, long long, int, cudaStream_t);
 oxf_status transpose(const float*, float*, long long, long long, cudaStream_t);
 oxf_status slice_reduce(const float*, long long, float*, int, cudaStream_t, int map_op = -1,
-                        float map_p = 0.f);
+                        float map_p = 0.f, const float* y = nullptr);
 oxf_status fill_slice(float*, long long, int, float, int, uint32_t, cudaStream_t);
 oxf_status matrix_slice(const float*, float*, long long, long long, long long, long long,
                         long long, cudaStream_t);
@@ -241,6 +241,15 @@ oxf_status oxf_slice_map_sum(oxf_cslice span, oxf_unary_op op, float param, floa
   if (span.len && !span.ptr) return set_error(OXF_ERR_INVALID_ARG, "oxf_slice_map_sum: null");
   return slice_reduce(span.ptr, static_cast<long long>(span.len), result, 0, S(stream),
                       static_cast<int>(op), param);
+}
+
+oxf_status oxf_slice_dot(oxf_cslice lhs, oxf_cslice rhs, float* result, oxf_stream stream) {
+  OXF_TRY(need(result != nullptr, "oxf_slice_dot: null result"));
+  OXF_TRY(need(lhs.len == rhs.len, "oxf_slice_dot: length mismatch"));  // vector.rs:110
+  if (lhs.len && (!lhs.ptr || !rhs.ptr))
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_slice_dot: null operand");
+  return slice_reduce(lhs.ptr, static_cast<long long>(lhs.len), result, 0, S(stream), -1, 0.f,
+                      rhs.ptr);
 }
 
 oxf_status oxf_slice_set(oxf_slice target, float value, oxf_stream stream) {

@@ -749,14 +749,17 @@ __global__ void fill_kernel(float* p, float v) {
 // One-launch reductions (the reference re-launches slice_sum from the host
 // until one element is left, span.rs:361-385). map_op >= 0 sums
 // unary_apply(map_op, x, map_p) instead of x (slice_map_sum).
+// Sum or max of x (each element first mapped by map_op when >= 0), or the
+// dot product with y when y is given.
 __global__ void slice_reduce_kernel(const float* __restrict__ x, long long n, float* result,
-                                    int is_max, int map_op, float map_p) {
+                                    int is_max, int map_op, float map_p,
+                                    const float* __restrict__ y) {
   pdl_enter();
   __shared__ float red[32];
   float acc = is_max ? -FLT_MAX : 0.f;
   for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const float v = map_op >= 0 ? unary_apply(map_op, x[i], map_p) : x[i];
+    const float v = y ? x[i] * y[i] : map_op >= 0 ? unary_apply(map_op, x[i], map_p) : x[i];
     acc = is_max ? fmaxf(acc, v) : acc + v;
   }
   acc = is_max ? block_max(acc, red) : block_sum(acc, red);
@@ -1106,12 +1109,12 @@ oxf_status transpose(const float* in, float* out, long long rows, long long cols
 }
 
 oxf_status slice_reduce(const float* x, long long n, float* result, int is_max, cudaStream_t s,
-                        int map_op, float map_p) {
+                        int map_op, float map_p, const float* y) {
   const oxf_status st = launch_pdl("fill_kernel", fill_kernel, dim3(1), dim3(1), s, result,
                                    is_max ? -FLT_MAX : 0.f);
   if (st != OXF_OK || n <= 0) return st;
   return launch_pdl("slice_reduce_kernel", slice_reduce_kernel, dim3(ew_blocks((n + 3) / 4)),
-                    dim3(256), s, x, n, result, is_max, map_op, map_p);
+                    dim3(256), s, x, n, result, is_max, map_op, map_p, y);
 }
 
 oxf_status fill_slice(float* out, long long n, int kind, float value, int dir, uint32_t seed,

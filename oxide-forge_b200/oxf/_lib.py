@@ -97,6 +97,7 @@ _SIGS = {
     "oxf_slice_sum": (C.c_int, [CSlice, C.c_void_p, C.c_void_p]),
     "oxf_slice_max": (C.c_int, [CSlice, C.c_void_p, C.c_void_p]),
     "oxf_slice_map_sum": (C.c_int, [CSlice, C.c_int, C.c_float, C.c_void_p, C.c_void_p]),
+    "oxf_slice_dot": (C.c_int, [CSlice, CSlice, C.c_void_p, C.c_void_p]),
     "oxf_slice_set": (C.c_int, [Slice, C.c_float, C.c_void_p]),
     "oxf_wait_timeout_selftest": (C.c_int, [C.c_uint32, C.c_void_p, C.c_void_p]),
     "oxf_slice_set_seq": (C.c_int, [Slice, C.c_int, C.c_void_p]),

@@ -95,6 +95,12 @@ def map_sum(x, op, param, out, stream=None):
     return out
 
 
+def dot(x, y, out, stream=None):
+    """Vector::dot: out[0] = sum_i x[i] * y[i], one reduction launch."""
+    check(lib().oxf_slice_dot(cs(x), cs(y), ptr(out), _stream(stream)))
+    return out
+
+
 def fill(x, value, stream=None):
     check(lib().oxf_slice_set(ms(x), float(value), _stream(stream)))
     return x

@@ -236,6 +236,21 @@ def test_map_sum(K, rng):
         K.map_sum(dev(x), 9, 0.0, out)
 
 
+def test_dot(K, rng):
+    """oxf_slice_dot against the oracle's Vector::dot (vector.rs:109-115),
+    including the empty vector and the length check."""
+    x = rng.standard_normal(123457).astype(np.float32)
+    y = rng.standard_normal(123457).astype(np.float32)
+    out = torch.empty(1, device="cuda")
+    K.dot(dev(x), dev(y), out)
+    want = O.dot(x, y)
+    assert abs(host(out)[0] - want) <= 1e-5 * float(np.sum(np.abs(x * y)))
+    K.dot(dev(x[:0].copy()), dev(y[:0].copy()), out)
+    assert host(out)[0] == 0.0
+    with pytest.raises(Exception, match="length"):
+        K.dot(dev(x), dev(y[:10].copy()), out)
+
+
 def test_matrix_slice(K, rng):
     m = rng.standard_normal((96, 160)).astype(np.float32)
     for tr, tc, tpr, nt in ((32, 40, 4, 12), (96, 160, 1, 1), (1, 1, 160, 160 * 96), (8, 16, 5, 3)):

@@ -250,3 +250,14 @@ def test_exchange_sgd_known_answers():
     lr = np.float32(1.0 - 2.0 ** -24)
     want = np.float32(np.float64(p1[0]) - np.float64(g1[0]) * np.float64(lr))
     assert O.exchange_sgd([p1], [g1], 0, 1, float(lr))[0][0] == want
+
+
+def test_dot_known_answers(rng):
+    """Vector::dot (vector.rs:109-115): 1·1 + 2·2 + ... and a float64 check."""
+    x = np.arange(1, 101, dtype=np.float32)
+    assert O.dot(x, x) == float(np.sum(np.arange(1, 101) ** 2))  # 338350, exact in f32
+    a = rng.standard_normal(100001).astype(np.float32)
+    b = rng.standard_normal(100001).astype(np.float32)
+    want = float(np.dot(a.astype(np.float64), b.astype(np.float64)))
+    assert abs(O.dot(a, b) - want) <= 1e-5 * float(np.sum(np.abs(a * b)))
+    assert O.dot(a[:0], b[:0]) == 0.0
