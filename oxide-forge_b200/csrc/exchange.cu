@@ -75,10 +75,15 @@ __device__ __forceinline__ bool reached(uint32_t v, uint32_t epoch) {
 // fence that orders every store the CTA made before the preceding
 // __syncthreads), then waits, bounded, for rank q's arrival in this rank's
 // pad. Returns false on expiry (after recording `code`).
+// The outcome is combined with __syncthreads_and, so the kernel needs no
+// shared memory: a block then fits beside a GEMM CTA that holds all of its
+// SM's shared memory but one kilobyte, and overlapped exchanges do not keep
+// GEMM CTAs off their SMs.
 template <int W>
-__device__ bool rank_barrier(const XchArgs& a, int phase, uint32_t code, int* ok) {
+__device__ bool rank_barrier(const XchArgs& a, int phase, uint32_t code) {
   __syncthreads();
   const int q = threadIdx.x;
+  int ok = 1;
   if (q < W) {
     __threadfence_system();
     st_release_sys(a.signals[q] + pad_slot(phase, blockIdx.x, a.rank), a.epoch);
@@ -89,14 +94,13 @@ __device__ bool rank_barrier(const XchArgs& a, int phase, uint32_t code, int* ok
         __nanosleep(64);
         if (global_timer_ns() - t0 > a.limit_ns) {
           report_device_error(code);
-          *ok = 0;
+          ok = 0;
           break;
         }
       }
     }
   }
-  __syncthreads();
-  return *ok != 0;
+  return __syncthreads_and(ok) != 0;
 }
 
 __device__ __forceinline__ float4 ld4(const float* p) {
@@ -122,14 +126,14 @@ __device__ __forceinline__ float4 update(float4 p, const float4 (&g)[W], float l
   return make_float4(p.x - s.x * lr, p.y - s.y * lr, p.z - s.z * lr, p.w - s.w * lr);
 }
 
-// U float4 units per thread and iteration, so that every thread has about
-// eight 16-byte peer loads in flight whatever the world size.
+// U float4 units per thread and iteration, so that every thread has up to
+// eight 16-byte loads in flight (fewer at world 4, to stay in 40 registers).
+// At most 40 registers per thread (six 256-thread blocks' worth per SM): a
+// block then also fits in the registers a GEMM CTA leaves free.
 template <int W, int U>
-__global__ void __launch_bounds__(XCH_THREADS)
+__global__ void __launch_bounds__(XCH_THREADS, 6)
     exchange_sgd_kernel(const __grid_constant__ XchArgs a) {
-  __shared__ int ok;
-  if (threadIdx.x == 0) ok = 1;
-  if (!rank_barrier<W>(a, 0, OXF_DEVERR_EXCHANGE_START, &ok)) return;
+  if (!rank_barrier<W>(a, 0, OXF_DEVERR_EXCHANGE_START)) return;
 
   const long long stride = static_cast<long long>(gridDim.x) * XCH_THREADS;
   long long u = a.u0 + static_cast<long long>(blockIdx.x) * XCH_THREADS + threadIdx.x;
@@ -172,12 +176,12 @@ __global__ void __launch_bounds__(XCH_THREADS)
     for (int q = 0; q < W; ++q) __stcg(a.params[q] + e, r);
   }
 
-  rank_barrier<W>(a, 1, OXF_DEVERR_EXCHANGE_END, &ok);
+  rank_barrier<W>(a, 1, OXF_DEVERR_EXCHANGE_END);
 }
 
 template <int W>
 cudaError_t launch_world(const XchArgs& a, int blocks, cudaStream_t s) {
-  constexpr int U = W <= 2 ? 4 : W <= 4 ? 2 : 1;
+  constexpr int U = W <= 2 ? 4 : W <= 3 ? 2 : 1;  // within 40 registers, no spills
   exchange_sgd_kernel<W, U><<<blocks, XCH_THREADS, 0, s>>>(a);
   return cudaGetLastError();
 }
