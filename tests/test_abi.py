@@ -60,3 +60,94 @@ def test_product_never_imports_oracle():
             continue
         text = f.read_text()
         assert "oxf_oracle" not in text and "import oracle" not in text, f
+
+
+# ctypes structure -> (C type name, {ctypes field: C member})
+def _layouts():
+    from oxf import _host_sigs as H, _lib as L
+
+    def same(cls, **rename):
+        return {f: rename.get(f, f) for f, _ in cls._fields_}
+
+    return {
+        L.CSlice: ("oxf_cslice", same(L.CSlice)),
+        L.Slice: ("oxf_slice", same(L.Slice)),
+        L.GemmDesc: ("oxf_gemm_desc", same(L.GemmDesc)),
+        L.IpcHandle: ("oxf_ipc_handle", same(L.IpcHandle)),
+        L.ExchangeDesc: ("oxf_exchange_desc", same(L.ExchangeDesc)),
+        H.LayerSpec: ("oxf_layer_spec", same(H.LayerSpec, in_="in")),
+        H.MlpSpec: ("oxf_mlp_spec", same(H.MlpSpec)),
+        H.TransformerSpec: ("oxf_transformer_spec", same(H.TransformerSpec)),
+    }
+
+
+# Python constant -> C constant of the headers
+_CONSTANTS = {
+    "OK": "OXF_OK", "INVALID_ARG": "OXF_ERR_INVALID_ARG",
+    "UNSUPPORTED_SHAPE": "OXF_ERR_UNSUPPORTED_SHAPE", "CUDA_ERROR": "OXF_ERR_CUDA",
+    "TIMEOUT": "OXF_ERR_TIMEOUT", "DEVICE_CHECK": "OXF_ERR_DEVICE_CHECK", "IO": "OXF_ERR_IO",
+    "STATE": "OXF_ERR_STATE",
+    "ADD": "OXF_ADD", "SUB": "OXF_SUB", "MUL": "OXF_MUL", "DIV": "OXF_DIV",
+    "ACT_IDENTITY": "OXF_ACT_IDENTITY", "ACT_GELU": "OXF_ACT_GELU", "ACT_RELU": "OXF_ACT_RELU",
+    "ACT_SILU": "OXF_ACT_SILU",
+    "UNARY_SCALE": "OXF_UNARY_SCALE", "UNARY_ADD_SCALAR": "OXF_UNARY_ADD_SCALAR",
+    "UNARY_ACT_FORWARD": "OXF_UNARY_ACT_FORWARD", "UNARY_ACT_DERIV": "OXF_UNARY_ACT_DERIV",
+    "UNARY_HALF_SQUARE": "OXF_UNARY_HALF_SQUARE",
+    "PREC_TF32": "OXF_PREC_TF32", "PREC_TF32X3": "OXF_PREC_TF32X3", "PREC_F32": "OXF_PREC_F32",
+    "NORM_RMS": "OXF_NORM_RMS", "NORM_LAYER": "OXF_NORM_LAYER",
+    "EXCHANGE_MAX_RANKS": "OXF_EXCHANGE_MAX_RANKS",
+    "EXCHANGE_MAX_BLOCKS": "OXF_EXCHANGE_MAX_BLOCKS",
+    "EXCHANGE_SIGNAL_BYTES": "OXF_EXCHANGE_SIGNAL_BYTES",
+    "DEVERR_EXCHANGE_START": "OXF_DEVERR_EXCHANGE_START",
+    "DEVERR_EXCHANGE_END": "OXF_DEVERR_EXCHANGE_END",
+}
+
+
+def test_binding_layouts_match_headers(tmp_path):
+    """Every structure the binding passes by value or pointer has the C
+    header's size and member offsets, and every constant its value, as the
+    host C compiler lays them out (a mismatch would hand the library
+    shifted arguments without any error)."""
+    import shutil
+    import subprocess
+
+    from oxf import _host_sigs as H, _lib as L
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    layouts = _layouts()
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "oxf_host.h"',
+             "int main(void) {"]
+    for cls, (cname, fields) in layouts.items():
+        lines.append(f'  printf("{cls.__name__} size %zu\\n", sizeof({cname}));')
+        for py, c in fields.items():
+            lines.append(f'  printf("{cls.__name__} {py} %zu\\n", offsetof({cname}, {c}));')
+    for py, c in _CONSTANTS.items():
+        lines.append(f'  printf("const {py} %lld\\n", (long long)({c}));')
+    lines.append(f'  printf("const MAX_LAYERS %d\\n", OXF_MAX_LAYERS);')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-std=c11", "-Wall", "-Werror", "-I", str(ROOT / "include"), str(src),
+                    "-o", str(exe)], check=True, capture_output=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout
+    got = {}
+    for line in out.splitlines():
+        owner, name, value = line.split()
+        got[(owner, name)] = int(value)
+    bad = []
+    for cls, (_, fields) in layouts.items():
+        if got[(cls.__name__, "size")] != ctypes.sizeof(cls):
+            bad.append((cls.__name__, "size", got[(cls.__name__, "size")], ctypes.sizeof(cls)))
+        for py in fields:
+            off = getattr(cls, py).offset
+            if got[(cls.__name__, py)] != off:
+                bad.append((cls.__name__, py, got[(cls.__name__, py)], off))
+    for py in _CONSTANTS:
+        if got[("const", py)] != getattr(L, py):
+            bad.append(("const", py, got[("const", py)], getattr(L, py)))
+    if got[("const", "MAX_LAYERS")] != H.MAX_LAYERS:
+        bad.append(("const", "MAX_LAYERS", got[("const", "MAX_LAYERS")], H.MAX_LAYERS))
+    assert not bad, bad
