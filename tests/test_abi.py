@@ -151,3 +151,38 @@ def test_binding_layouts_match_headers(tmp_path):
     if got[("const", "MAX_LAYERS")] != H.MAX_LAYERS:
         bad.append(("const", "MAX_LAYERS", got[("const", "MAX_LAYERS")], H.MAX_LAYERS))
     assert not bad, bad
+
+
+def _header_signatures() -> dict[str, int]:
+    """Function name -> parameter count, from the public headers."""
+    sigs = {}
+    for h in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        text = re.sub(r"#.*", "", text)
+        for m in re.finditer(r"\b(oxf_[a-z0-9_]+)\s*\(([^;{)]*)\)\s*;", text):
+            args = m.group(2).strip()
+            sigs[m.group(1)] = 0 if args in ("", "void") else args.count(",") + 1
+    return sigs
+
+
+def _integration_rust_block() -> str:
+    text = (ROOT / "INTEGRATION.md").read_text()
+    start = text.index("// src/cuda/oxf_ffi.rs  (complete)")
+    return text[start:text.index("```", start)]
+
+
+def test_integration_rust_binding_matches_headers():
+    """The complete Rust binding documented for the reference's maintainers
+    declares exactly the headers' functions with the headers' parameter
+    counts, and its structures list the C members in the C order."""
+    block = _integration_rust_block()
+    rust = {}
+    for m in re.finditer(r"pub fn (oxf_[a-z0-9_]+)\(([^)]*)\)", block):
+        args = m.group(2).strip()
+        rust[m.group(1)] = 0 if not args else args.count(":")
+    assert rust == _header_signatures()
+    for cls, (cname, fields) in _layouts().items():
+        m = re.search(r"pub struct " + cname + r"\s*\{([^}]*)\}", block)
+        assert m, cname
+        names = re.findall(r"pub (\w+):", m.group(1))
+        assert names == [c if c != "in" else "in_" for c in fields.values()], cname
