@@ -48,10 +48,9 @@ def _stale(out: Path, deps) -> bool:
 def _compile(src: Path, force: bool) -> Path:
     obj = _obj(src)
     if force or _stale(obj, [src, *HEADERS, Path(__file__)]):
+        # .cpp host files go through nvcc too (same flags), so they may use
+        # the CUDA runtime headers and types.
         cmd = [NVCC, *ARCH, *COMMON, "-c", str(src), "-o", str(obj)]
-        if src.suffix == ".cpp":
-            cmd = [NVCC, *COMMON, "-x", "cu", "-c", str(src), "-o", str(obj)] if False else \
-                [NVCC, *ARCH, *COMMON, "-c", str(src), "-o", str(obj)]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"nvcc failed for {src.name}:\n{r.stdout}\n{r.stderr}")
