@@ -1441,7 +1441,10 @@ EncodeTiledFn get_encode_fn() {
 }
 
 constexpr int kMaxDevices = 64;
-// Wide (256 x 512) pair tiles from this many K blocks of 32 up (K >= 4096).
+// K blocks of 32 (K >= 4096) from which a wide (256 x 512) pair tile's
+// exposed epilogue is short against its MMAs: below it, products with a
+// heavy epilogue keep 256-wide tiles, and wide tiles stage through two
+// tiles per epilogue warp.
 constexpr long long kWideMinKBlocks = 128;
 
 // ---------------------------------------------------------------- schedule slots
@@ -1835,9 +1838,11 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
   }
   // Wide pair tiles (256 x 512): a quarter fewer operand bytes per flop
   // through L2, but a tile fills TMEM, so its epilogue no longer overlaps the
-  // next tile's MMAs. Chosen for long K, where the MMA time per tile dwarfs
-  // the epilogue, and only if the fewer, larger tiles fill the last wave of
-  // CTA pairs about as well. OXF_GEMM_TILE=256 / 512 overrides the choice.
+  // next tile's MMAs. Taken whenever the fewer, larger tiles fill the last
+  // wave of CTA pairs about as well, except for short-K products whose
+  // epilogue reads an input tile or writes a second output: there the
+  // exposed epilogue outweighs the saved bytes, and the 256-wide tile's two
+  // accumulators hide it. OXF_GEMM_TILE=256 / 512 overrides the choice.
   if (pair && !split3) {
     const long long kbl = static_cast<long long>((d->K + BK - 1) / BK) *
                           (d->reduce_batch ? d->batch : 1);
@@ -1853,8 +1858,10 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
     auto fill = [pairs](long long t) {
       return static_cast<double>(t) / static_cast<double>(((t + pairs - 1) / pairs) * pairs);
     };
+    const bool heavy_epilogue = d->pre_out || d->aux || d->residual || d->beta != 0.0f;
     bool wide = d->variant == 3 ||
-                (d->variant == 0 && d->N >= 512 && kbl >= kWideMinKBlocks && units_w >= pairs &&
+                (d->variant == 0 && d->N >= 512 && units_w >= pairs &&
+                 (kbl >= kWideMinKBlocks || !heavy_epilogue) &&
                  fill(units_w) >= fill(units_n) - 0.02);
     const char* env = std::getenv("OXF_GEMM_TILE");
     if (env && d->variant == 0) {
@@ -1946,9 +1953,19 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
   if (split3 && pair)
     return launch_pair<256, 3, true, 1>(ta, tb, ta_lo, tb_lo, em, a, stream, dev);
   if (split3) return launch_tcgen05<128, 3, true>(ta, tb, ta_lo, tb_lo, em, a, stream, dev);
-  // One staging tile per epilogue warp: two (with a stage fewer) measured
-  // the same on the training step.
-  if (pair && BN == 512) return launch_pair<512, 4, false, 1>(ta, tb, ta, tb, em, a, stream, dev);
+  // A wide tile's epilogue is exposed (one accumulator), so its warps stage
+  // through two tiles each, with a ring stage fewer, when the epilogue reads
+  // an input tile, writes a pre-activation, adds into C, or has little K to
+  // hide behind: a chunk's TMA loads and stores then overlap the previous
+  // chunk's. Plain long-K products keep the fourth ring stage (measured 2-4%
+  // faster there). On 256-wide tiles the epilogue hides behind the next
+  // tile's MMAs, and a second staging tile measured no gain.
+  if (pair && BN == 512) {
+    const bool two_staging = a.kblocks < kWideMinKBlocks || a.accumulate || a.R || a.P || a.X ||
+                             a.beta != 0.0f;
+    if (two_staging) return launch_pair<512, 3, false, 2>(ta, tb, ta, tb, em, a, stream, dev);
+    return launch_pair<512, 4, false, 1>(ta, tb, ta, tb, em, a, stream, dev);
+  }
   if (pair) return launch_pair<256, 6, false, 1>(ta, tb, ta, tb, em, a, stream, dev);
   if (BN == 256) return launch_tcgen05<256, 4, false>(ta, tb, ta, tb, em, a, stream, dev);
   if (BN == 128) return launch_tcgen05<128, 6, false>(ta, tb, ta, tb, em, a, stream, dev);

@@ -361,6 +361,54 @@ def test_wide_tiles_many_per_pair(K, at, bt):
         assert err < TF32_TOL, (variant, err)
 
 
+@pytest.mark.parametrize("M,Kd,variant", [(2048, 512, 3), (16384, 4096, 0)])
+@pytest.mark.parametrize("epi", ["residual", "pre_act", "grad_act", "beta", "accumulate"])
+def test_wide_tiles_heavy_epilogues(K, epi, M, Kd, variant):
+    """Every epilogue that reads an input tile, writes a pre-activation or
+    adds into C, on the 256 x 512 pair tile (forced at short K, chosen
+    automatically at long K, where 16384 rows give 128 wide tiles for the
+    74 CTA pairs): its warps stage through two tiles each. Ragged N (1000)
+    leaves the last tile half empty. Checked against a float64 product on
+    the GPU, and against the 256 x 256 tile (variant 2)."""
+    from oxf import _lib
+    g = torch.Generator(device="cuda").manual_seed(13)
+    N = 1000
+    A = torch.randn((M, Kd), device="cuda", generator=g)
+    B = torch.randn((Kd, N), device="cuda", generator=g)
+    R = torch.randn((M, N), device="cuda", generator=g)
+    X = torch.randn((M, N), device="cuda", generator=g)
+    C0 = torch.randn((M, N), device="cuda", generator=g)
+    prod = A.double() @ B.double()
+    scale = prod.abs().max().item()
+    outs = {}
+    for v in (variant, 2):
+        out = C0.clone()
+        pre = torch.empty((M, N), device="cuda")
+        if epi == "residual":
+            K.gemm(A, B, out, residual=R, variant=v)
+            want = prod + R.double()
+        elif epi == "pre_act":
+            K.gemm(A, B, out, pre_out=pre, act=_lib.ACT_GELU, variant=v)
+            want = torch.from_numpy(O.act_forward(O.GELU, prod.float().cpu().numpy())).cuda()
+            err = (pre.double() - prod).abs().max().item() / scale
+            assert err < TF32_TOL, (v, "pre", err)
+        elif epi == "grad_act":
+            K.gemm(A, B, out, aux=X, grad_act=_lib.ACT_GELU, variant=v)
+            d = torch.from_numpy(O.act_derivative(O.GELU, X.cpu().numpy())).cuda()
+            want = prod * d.double()
+        elif epi == "beta":
+            K.gemm(A, B, out, beta=0.5, variant=v)
+            want = prod + 0.5 * C0.double()
+        else:
+            K.gemm(A, B, out, accumulate=True, variant=v)
+            want = prod + C0.double()
+        err = (out.double() - want.double()).abs().max().item() / scale
+        assert err < TF32_TOL, (v, err)
+        outs[v] = out
+    assert (outs[variant] - outs[2]).abs().max().item() <= 2 * TF32_TOL * scale
+    assert K.device_error() == 0
+
+
 @pytest.mark.parametrize("at,bt", [(0, 0), (0, 1), (1, 0), (1, 1)])
 @pytest.mark.parametrize("M,N,Kd,batch", [(256, 64, 128, 1), (36, 52, 200, 1), (20, 28, 4, 1),
                                           (68, 36, 256, 3)])
