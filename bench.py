@@ -40,8 +40,9 @@ sys.path.insert(0, str(ROOT / "oxide-forge_b200"))
 
 SEQ, HIDDEN, FFN, GLOBAL_BATCH, LR = 1024, 2048, 8192, 128, 1e-3
 # DRAM bytes (read + write) of the 18 GEMM launches of one C5 step at N=1,
-# from the ncu launch list in profiles/launches_train_step_c5.md (86.7 GB
-# read + 29.3 GB written); their compulsory traffic is about 74 GB.
+# summed from one ncu capture of this bench's step with the metrics
+# dram__bytes_read.sum and dram__bytes_write.sum (86.7 GB read + 29.3 GB
+# written); their compulsory traffic is about 74 GB.
 GEMM_DRAM_BYTES_PER_STEP = 116.0e9
 METRIC = "Transformer fwd+bwd tokens/s"
 UNIT = "tokens/s"
