@@ -4,13 +4,15 @@ The engine is replaced by a host stand-in built on the oracle (test-only),
 so this checks the driver's own logic: batch sharding, the three bucketed
 all-reduces in cursor order, the global-mean SGD update, equality of the
 N-rank step with the 1-rank step on the same global batch, and that a rank
-which dies leaves the others with an error instead of a hang.
+which dies, raises or stalls leaves the others with an error within the
+process-group timeout instead of a hang.
 """
 from __future__ import annotations
 
 import os
 import socket
 import sys
+import time
 from pathlib import Path
 
 import numpy as np
@@ -19,6 +21,7 @@ import pytest
 ROOT = Path(__file__).resolve().parent.parent
 torch = pytest.importorskip("torch")
 SEQ, H, F = 8, 12, 20
+PG_TIMEOUT_S = 8  # process-group timeout: the bound on a collective that a peer misses
 
 
 def _free_port() -> int:
@@ -71,7 +74,10 @@ class OracleModel:
         return torch.from_numpy(np.concatenate(losses))
 
     def backward_stage(self, s):
-        pass  # gradients were produced in set_target
+        # gradients were produced in set_target; a test may make stage 1 fail
+        # after stage 0's bucket all-reduce has been issued
+        if s == 1 and getattr(self, "fail_in_backward", False):
+            raise RuntimeError("injected failure in backward stage 1")
 
     def bucket(self, s):
         o = self.offsets
@@ -97,21 +103,29 @@ def _flat0():
     return np.concatenate([p.ravel() for p in parts]).astype(np.float32)
 
 
-def _worker(rank, world, port, global_batch, steps, out_dir, fail_rank):
+def _worker(rank, world, port, global_batch, steps, out_dir, fail_rank, fail_mode="exit"):
     import torch.distributed as dist
     from datetime import timedelta
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=8))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=PG_TIMEOUT_S))
     sys.path.insert(0, str(ROOT / "oxide-forge_b200"))
     from oxf.dp import DataParallelTrainer
     model = OracleModel(_flat0() if rank == 0 else np.zeros_like(_flat0()))
     tr = DataParallelTrainer(model, global_batch, lr=0.1, seq=SEQ)
     tr.broadcast_params(model.params)
     result = {"rank": rank}
+    t0 = time.monotonic()
     try:
         for step in range(steps):
             if rank == fail_rank and step == 1:
-                os._exit(3)  # this rank dies between steps
+                if fail_mode == "exit":
+                    os._exit(3)  # this rank dies between steps
+                if fail_mode == "raise":
+                    model.fail_in_backward = True  # raises inside the step
+                if fail_mode == "stall":
+                    time.sleep(PG_TIMEOUT_S + 4)  # misses the next collective
+            t0 = time.monotonic()
             x, t = _data(global_batch, seed=step)
             lo, hi = tr.local
             sl = slice(lo * SEQ, hi * SEQ)
@@ -120,6 +134,7 @@ def _worker(rank, world, port, global_batch, steps, out_dir, fail_rank):
         result["params"] = model.params.numpy().copy()
     except Exception as ex:  # the surviving rank must see an error, not hang
         result["error"] = type(ex).__name__
+        result["error_after_s"] = time.monotonic() - t0
     np.save(Path(out_dir) / f"rank{rank}.npy", result, allow_pickle=True)
     try:
         dist.destroy_process_group()
@@ -127,12 +142,12 @@ def _worker(rank, world, port, global_batch, steps, out_dir, fail_rank):
         pass
 
 
-def _run(world, global_batch, steps, tmp_path, fail_rank=-1):
+def _run(world, global_batch, steps, tmp_path, fail_rank=-1, fail_mode="exit"):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     port = _free_port()
     procs = [ctx.Process(target=_worker, args=(r, world, port, global_batch, steps, str(tmp_path),
-                                               fail_rank)) for r in range(world)]
+                                               fail_rank, fail_mode)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -173,6 +188,26 @@ def test_dead_rank_is_an_error_not_a_hang(tmp_path):
     out = _run(2, 4, 3, tmp_path, fail_rank=1)
     assert 1 not in out                               # rank 1 exited without a result
     assert out[0].get("error"), out[0].keys()        # rank 0 got an error from its collective
+
+
+def test_raising_rank_is_an_error_not_a_hang(tmp_path):
+    """Rank 1 raises inside step 1, after issuing the first bucket's
+    all-reduce but not the second. Rank 1 reports its own exception; rank 0's
+    next collective ends with an error within the process-group timeout."""
+    out = _run(2, 4, 3, tmp_path, fail_rank=1, fail_mode="raise")
+    assert out[1].get("error") == "RuntimeError", out[1].keys()
+    assert out[0].get("error"), out[0].keys()
+    assert out[0]["error_after_s"] < PG_TIMEOUT_S + 10, out[0]["error_after_s"]
+
+
+def test_stalled_rank_is_an_error_not_a_hang(tmp_path):
+    """Rank 1 stalls between steps for longer than the process-group
+    timeout. Rank 0's next collective ends with an error within that bound
+    instead of waiting for it, and both processes finish."""
+    out = _run(2, 4, 3, tmp_path, fail_rank=1, fail_mode="stall")
+    assert out[0].get("error"), out[0].keys()
+    assert out[0]["error_after_s"] < PG_TIMEOUT_S + 10, out[0]["error_after_s"]
+    assert "params" not in out[0]
 
 
 def test_peer_exchange_needs_cuda_arenas():
