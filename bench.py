@@ -161,28 +161,65 @@ def run_reference(a):
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
+    """Samples the SM clock, its maximum and the clock-event reasons of one
+    GPU while the timed region runs. Through NVML (read-only queries, every
+    20 ms) when its Python binding is present; otherwise, or if NVML fails,
+    by polling nvidia-smi every 200 ms, whose process start-up leaves only a
+    sample or two in a sub-second region. Each row holds nvidia-smi's FIELDS
+    in order."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits of the last four FIELDS
+    REASON_BITS = (0x8, 0x40, 0x20, 0x4)  # hw_slowdown, hw_thermal, sw_thermal, sw_power_cap
 
     def __init__(self, gpu: int):
         self.gpu = gpu
         self.rows = []
+        self.source = None
         self._stop = threading.Event()
         self._t = None
 
+    def _nvml(self):
+        """(sample function) for this GPU through NVML, or None."""
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(torch.cuda._get_nvml_device_index(self.gpu))
+            reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+
+            def sample():
+                sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+                bits = int(reasons(h))
+                return [str(self.gpu), str(sm), str(mx), "", hex(bits)] + \
+                    ["Active" if bits & b else "Not Active" for b in self.REASON_BITS]
+
+            sample()  # fails here, not in the sampling thread, if NVML cannot serve it
+            return sample
+        except Exception:
+            return None
+
+    def _smi(self):
+        out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                              "--format=csv,noheader,nounits"],
+                             capture_output=True, text=True, timeout=5).stdout
+        return [c.strip() for c in out.strip().split(",")]
+
     def start(self):
+        nvml = self._nvml()
+        sample, period = (nvml, 0.02) if nvml else (self._smi, 0.2)
+        self.source = "nvml" if nvml else "nvidia-smi"
+
         def run():
             while not self._stop.is_set():
                 try:
-                    out = subprocess.run(["nvidia-smi", "-i", str(self.gpu),
-                                          f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits"],
-                                         capture_output=True, text=True, timeout=5).stdout
-                    self.rows.append([c.strip() for c in out.strip().split(",")])
+                    self.rows.append(sample())
                 except Exception:
                     pass
-                self._stop.wait(0.2)
+                self._stop.wait(period)
         self._t = threading.Thread(target=run, daemon=True)
         self._t.start()
 
@@ -203,7 +240,7 @@ class ClockSampler:
                 pass
         return {"sm_mhz": statistics.median(mhz) if mhz else None,
                 "sm_max_mhz": maxmhz or None, "reasons": sorted(reasons),
-                "samples": len(mhz)}
+                "samples": len(mhz), "source": self.source}
 
 
 # ------------------------------------------------------------------ GPU side
