@@ -261,3 +261,54 @@ def test_parse_errors_are_reported(tmp_path):
     _rewrite(p, "rows = 4", "rows = 4.0")
     with pytest.raises(_lib.OxfError, match="TOML parse error at line"):
         ck.load_linear(p)
+
+
+# ---------------------------------------------------------------- property tests
+from hypothesis import HealthCheck, given, settings, strategies as st  # noqa: E402
+
+ACTS = [_lib.ACT_IDENTITY, _lib.ACT_GELU, _lib.ACT_RELU, _lib.ACT_SILU]
+PROPERTY = settings(max_examples=40, deadline=None,
+                    suppress_health_check=[HealthCheck.function_scoped_fixture])
+
+
+@st.composite
+def mlp_configs(draw):
+    """Any MLP the format describes: 1-6 connected Linear layers of widths
+    1-9, any activation, bias or not, and optionally a residual range
+    [start, end) whose input and output widths agree."""
+    n = draw(st.integers(1, 6))
+    widths = draw(st.lists(st.integers(1, 9), min_size=n + 1, max_size=n + 1))
+    acts = draw(st.lists(st.sampled_from(ACTS), min_size=n, max_size=n))
+    bias = draw(st.lists(st.booleans(), min_size=n, max_size=n))
+    res = None
+    if draw(st.booleans()):
+        start = draw(st.integers(0, n - 1))
+        end = draw(st.integers(start + 1, n))
+        widths[end] = widths[start]
+        res = (start, end)
+    layers = [models.Layer(widths[i], widths[i + 1], acts[i], bias[i]) for i in range(n)]
+    return models.MlpConfig(layers, res)
+
+
+@PROPERTY
+@given(cfg=mlp_configs(), seed=st.integers(0, 2**31 - 1))
+def test_mlp_round_trip_any_spec(tmp_path, cfg, seed):
+    flat = _flat(sum(l.count() for l in cfg.layers), seed)
+    ck.dump_mlp(tmp_path / "any.toml", cfg, flat)
+    assert (tmp_path / "any.bin").stat().st_size == 4 * flat.size
+    got_cfg, got = ck.load_mlp(tmp_path / "any.toml")
+    assert got_cfg == cfg
+    np.testing.assert_array_equal(got, flat)
+
+
+@PROPERTY
+@given(seq=st.integers(1, 6), hidden=st.integers(1, 8), ffn=st.integers(1, 10),
+       out=st.integers(1, 7), norm=st.sampled_from([_lib.NORM_RMS, _lib.NORM_LAYER]),
+       bias=st.booleans(), seed=st.integers(0, 2**31 - 1))
+def test_transformer_round_trip_any_dims(tmp_path, seq, hidden, ffn, out, norm, bias, seed):
+    cfg = models.transformer_config(seq, hidden, ffn, out=out, norm=norm, bias=bias)
+    flat = _flat(cfg.param_count(), seed)
+    ck.dump_transformer_params(tmp_path / "anyt", cfg, flat)
+    got_cfg, got = ck.load_transformer_params(tmp_path / "anyt")
+    assert got_cfg == cfg
+    np.testing.assert_array_equal(got, flat)
