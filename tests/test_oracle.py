@@ -1,6 +1,8 @@
 """CPU tests of the oracle itself: hand-derived known answers, the numpy
-golden fixtures (independent restatement), and finite-difference checks of
-every backward formula. These pin the checker before any GPU test trusts it.
+golden fixtures (independent restatement), finite-difference checks of
+every backward formula, and invariants over random shapes (softmax rows are
+distributions, normalised rows have the stated moments, the GEMM is
+bilinear). These pin the checker before any GPU test trusts it.
 """
 from __future__ import annotations
 
@@ -261,3 +263,82 @@ def test_dot_known_answers(rng):
     want = float(np.dot(a.astype(np.float64), b.astype(np.float64)))
     assert abs(O.dot(a, b) - want) <= 1e-5 * float(np.sum(np.abs(a * b)))
     assert O.dot(a[:0], b[:0]) == 0.0
+
+
+# ---------------------------------------------------------------- invariants (property tests)
+from hypothesis import given, settings, strategies as st  # noqa: E402
+
+INVARIANT = settings(max_examples=30, deadline=None)
+shapes = st.tuples(st.integers(1, 9), st.integers(1, 300))
+
+
+def _rows(shape, seed, scale=3.0):
+    return (scale * np.random.default_rng(seed).standard_normal(shape)).astype(np.float32)
+
+
+@INVARIANT
+@given(shape=shapes, seed=st.integers(0, 2**31 - 1), scale=st.floats(0.1, 4.0))
+def test_softmax_rows_are_distributions(shape, seed, scale):
+    """Every row of softmax(scale·x) is a probability distribution whose
+    order follows x's (max-subtracted exp, row.rs:55-113)."""
+    x = _rows(shape, seed)
+    p = O.softmax_rows(x, scale=scale).astype(np.float64)
+    assert (p >= 0).all() and (p <= 1).all()
+    np.testing.assert_allclose(p.sum(axis=1), 1.0, rtol=0, atol=1e-5)
+    i = np.argmax(x, axis=1)
+    assert (p[np.arange(x.shape[0]), i] >= p.max(axis=1) * (1 - 1e-6)).all()
+
+
+@INVARIANT
+@given(shape=shapes, seed=st.integers(0, 2**31 - 1), period=st.integers(1, 12))
+def test_causal_softmax_rows_see_only_the_past(shape, seed, period):
+    """With causal period s, row r attends to columns 0..r mod s only."""
+    x = _rows(shape, seed)
+    p = O.softmax_rows(x, causal_period=period).astype(np.float64)
+    for r in range(x.shape[0]):
+        last = r % period
+        assert not p[r, last + 1:].any()
+        assert abs(p[r, :last + 1].sum() - 1.0) < 1e-5
+
+
+@INVARIANT
+@given(rows=st.integers(1, 6), cols=st.integers(2, 300), seed=st.integers(0, 2**31 - 1),
+       shift=st.floats(-50, 50), scale=st.floats(0.5, 8.0))
+def test_layer_norm_rows_are_standardised_and_shift_invariant(rows, cols, seed, shift, scale):
+    """LayerNorm output has zero mean and variance var/(var+eps) per row
+    (biased variance, row.rs:115-177), and adding a constant to a row does
+    not change it."""
+    x = _rows((rows, cols), seed, scale)
+    y = O.layer_norm_rows(x).astype(np.float64)
+    var = x.astype(np.float64).var(axis=1)
+    np.testing.assert_allclose(y.mean(axis=1), 0.0, atol=2e-5)
+    np.testing.assert_allclose(y.var(axis=1), var / (var + 1e-5), rtol=2e-4)
+    y2 = O.layer_norm_rows((x + np.float32(shift)).astype(np.float32)).astype(np.float64)
+    np.testing.assert_allclose(y2, y, atol=2e-3 * (1 + abs(shift) / scale))
+
+
+@INVARIANT
+@given(rows=st.integers(1, 6), cols=st.integers(1, 300), seed=st.integers(0, 2**31 - 1))
+def test_rms_norm_rows_have_unit_mean_square(rows, cols, seed):
+    """RMSNorm output has mean square ms/(ms+eps) per row (row.rs:349-396)."""
+    x = _rows((rows, cols), seed)
+    y = O.rms_norm_rows(x).astype(np.float64)
+    ms = (x.astype(np.float64) ** 2).mean(axis=1)
+    np.testing.assert_allclose((y ** 2).mean(axis=1), ms / (ms + 1e-5), rtol=1e-4)
+
+
+@INVARIANT
+@given(m=st.integers(1, 24), n=st.integers(1, 24), k=st.integers(1, 40),
+       seed=st.integers(0, 2**31 - 1), a=st.floats(-3, 3), b=st.floats(-3, 3))
+def test_gemm_is_bilinear(m, n, k, seed, a, b):
+    """The f32 oracle GEMM is linear in each operand to f32 rounding, and
+    agrees with the float64 product (gemm.rs:202-373 semantics)."""
+    rng = np.random.default_rng(seed)
+    A1, A2 = (rng.standard_normal((m, k)).astype(np.float32) for _ in range(2))
+    B = rng.standard_normal((k, n)).astype(np.float32)
+    lhs = O.gemm((np.float32(a) * A1 + np.float32(b) * A2).astype(np.float32), B)
+    rhs = a * O.gemm(A1, B).astype(np.float64) + b * O.gemm(A2, B).astype(np.float64)
+    scale = (abs(a) + abs(b) + 1) * (np.abs(A1).max() + np.abs(A2).max()) * np.abs(B).max() * k
+    assert np.abs(lhs - rhs).max() <= 1e-5 * scale
+    exact = A1.astype(np.float64) @ B.astype(np.float64)
+    assert np.abs(O.gemm(A1, B) - exact).max() <= 1e-5 * max(1.0, np.abs(exact).max()) * k ** 0.5
