@@ -186,3 +186,28 @@ def test_integration_rust_binding_matches_headers():
         assert m, cname
         names = re.findall(r"pub (\w+):", m.group(1))
         assert names == [c if c != "in" else "in_" for c in fields.values()], cname
+
+
+def test_plain_c_client(tmp_path):
+    """tests/c_client/abi_client.c, compiled by the host C compiler against
+    the public headers only and linked to liboxf.so, runs its checks (no GPU
+    calls): the library is a drop-in for a C-ABI host as it stands."""
+    import shutil
+    import subprocess
+
+    from oxf import _lib
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    lib_dir = Path(_lib.LIB_PATH).parent
+    exe = tmp_path / "abi_client"
+    subprocess.run([cc, "-std=c11", "-Wall", "-Wextra", "-Werror", "-I", str(ROOT / "include"),
+                    str(ROOT / "tests" / "c_client" / "abi_client.c"), "-o", str(exe),
+                    "-L", str(lib_dir), "-loxf", f"-Wl,-rpath,{lib_dir}"],
+                   check=True, capture_output=True)
+    r = subprocess.run([str(exe), str(tmp_path / "mlp_ckpt")], capture_output=True, text=True,
+                       timeout=60)
+    assert r.returncode == 0, r.stderr
+    assert r.stdout.strip() == "ok"
+    assert (tmp_path / "mlp_ckpt.toml").exists() and (tmp_path / "mlp_ckpt.bin").exists()
