@@ -342,3 +342,36 @@ def test_gemm_is_bilinear(m, n, k, seed, a, b):
     assert np.abs(lhs - rhs).max() <= 1e-5 * scale
     exact = A1.astype(np.float64) @ B.astype(np.float64)
     assert np.abs(O.gemm(A1, B) - exact).max() <= 1e-5 * max(1.0, np.abs(exact).max()) * k ** 0.5
+
+
+@INVARIANT
+@given(world=st.integers(1, 8), n=st.integers(1, 200), data=st.data(),
+       lr=st.floats(1e-4, 2.0), seed=st.integers(0, 2**31 - 1))
+def test_exchange_sgd_any_world_and_range(world, n, data, lr, seed):
+    """For any world size and ragged range, every rank ends with the same
+    parameters: p - lr * (g_0 + ... + g_{W-1}) inside [offset, offset+count)
+    (rank-order f32 sum, then one rounding: within one ulp of the float64
+    evaluation of that expression), unchanged outside; inputs untouched."""
+    offset = data.draw(st.integers(0, n))
+    count = data.draw(st.integers(0, n - offset))
+    rng = np.random.default_rng(seed)
+    p = rng.standard_normal(n).astype(np.float32)
+    gs = [rng.standard_normal(n).astype(np.float32) for _ in range(world)]
+    p_in, g_in = p.copy(), [g.copy() for g in gs]
+    out = O.exchange_sgd([p] * world, gs, offset, count, lr)
+    np.testing.assert_array_equal(p, p_in)
+    for g, g0 in zip(gs, g_in):
+        np.testing.assert_array_equal(g, g0)
+    s = gs[0].copy()
+    for g in gs[1:]:
+        s = (s + g).astype(np.float32)
+    want = p.copy()
+    sl = slice(offset, offset + count)
+    want[sl] = (p[sl].astype(np.float64) - s[sl].astype(np.float64) * np.float64(np.float32(lr))
+                ).astype(np.float32)
+    for q in range(world):
+        np.testing.assert_array_equal(out[q], out[0])
+    one_ulp = np.spacing(np.maximum(np.abs(out[0]), np.abs(want)))  # sign-safe near zero
+    assert (np.abs(out[0] - want) <= one_ulp).all()
+    np.testing.assert_array_equal(out[0][:offset], p[:offset])
+    np.testing.assert_array_equal(out[0][offset + count:], p[offset + count:])
