@@ -67,8 +67,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-peak", action="store_true",
-                    help="skip the cuBLAS denominator (profiling runs: keeps the launch list "
-                         "to the step's own kernels); roofline.peak is then null")
+                    help="skip the cuBLAS denominator and comparison (profiling runs: keeps "
+                         "the launch list to this library's kernels); peaks are then null")
     ap.add_argument("--workload", default="train",
                     choices=["train", "linear", "gemm", "rows", "mlp", "infer", "exchange"],
                     help="train: the contract line (config 5). The others are supplementary "
@@ -79,9 +79,11 @@ def parse():
     ap.add_argument("--shape", default=None, help="gemm: M,N,K (default: the 512..8192 sweep)")
     ap.add_argument("--mode", default="nn", help="gemm: nn, nt, tn or tt")
     ap.add_argument("--epi", default="none",
-                    choices=["none", "bias_gelu_pre", "gelu_grad_aux", "bias_residual"],
+                    choices=["none", "bias_gelu_pre", "gelu_grad_aux", "bias_residual",
+                             "accumulate"],
                     help="gemm: fused epilogue (FFN1 forward, FFN1 input gradient, FFN2 "
-                         "forward); the cuBLAS comparison stays a plain product")
+                         "forward, weight-gradient accumulation into C); the cuBLAS "
+                         "comparison stays a plain product")
     ap.add_argument("--precision", default="tf32", choices=["tf32", "tf32x3", "f32"],
                     help="gemm: tensor-core TF32, 3xTF32 (f32-faithful splits, three MMAs "
                          "per step) or f32 on the CUDA cores")
@@ -341,7 +343,7 @@ def run_gemm(a, torch):
     8192 (larger than L2)."""
     from oxf import _lib
     from oxf import kernels as K
-    peak = cublas_tf32_peak(torch)
+    peak = None if a.no_peak else cublas_tf32_peak(torch)
     shapes = [tuple(int(v) for v in a.shape.split(","))] if a.shape else \
         [(n, n, n) for n in (512, 1024, 2048, 4096, 8192)]
     at, bt = a.mode[0] == "t", a.mode[1] == "t"
@@ -358,6 +360,9 @@ def run_gemm(a, torch):
             kw = dict(aux=torch.randn(M, N, device="cuda"), grad_act=_lib.ACT_GELU)
         elif a.epi == "bias_residual":
             kw = dict(bias=torch.randn(N, device="cuda"), residual=torch.randn(M, N, device="cuda"))
+        elif a.epi == "accumulate":
+            Cm.zero_()
+            kw = dict(accumulate=True)
         prec = {"tf32": _lib.PREC_TF32, "tf32x3": _lib.PREC_TF32X3, "f32": _lib.PREC_F32}[
             a.precision]
         if prec == _lib.PREC_TF32X3:
@@ -369,13 +374,16 @@ def run_gemm(a, torch):
         timer = _time if fl >= 5e10 else _graph_time
         ms = timer(torch, lambda: K.gemm(A, B, Cm, a_trans=at, b_trans=bt, precision=prec, **kw),
                    a.steps, a.warmup)
-        torch.backends.cuda.matmul.allow_tf32 = True
-        ref = timer(torch, lambda: torch.matmul(A.T if at else A, B.T if bt else B, out=Cm),
-                    a.steps, a.warmup)
+        ref = None
+        if not a.no_peak:
+            torch.backends.cuda.matmul.allow_tf32 = True
+            ref = timer(torch, lambda: torch.matmul(A.T if at else A, B.T if bt else B, out=Cm),
+                        a.steps, a.warmup)
         res.append({"shape": [M, N, Kd], "mode": a.mode, "epilogue": a.epi,
                     "precision": a.precision, "ms": ms,
                     "tflops": fl / ms / 1e9,
-                    "cublas_tflops": fl / ref / 1e9, "frac_of_peak": fl / ms / 1e9 / peak})
+                    "cublas_tflops": fl / ref / 1e9 if ref else None,
+                    "frac_of_peak": fl / ms / 1e9 / peak if peak else None})
         del A, B, Cm
     print(json.dumps({"metric": "GEMM TF32 TFLOP/s", "unit": "TFLOP/s", "workload": "gemm",
                       "peak_cublas_tf32_8192": peak, "results": res}), flush=True)
@@ -738,6 +746,46 @@ def run_infer(a, torch):
         dist.destroy_process_group()
 
 
+def rank_agreement(torch, dist, params) -> float:
+    """max over elements of (max over ranks - min over ranks) of a flat
+    device tensor: 0.0 exactly when every rank holds bit-identical values
+    (two all-reduces, outside any timed region)."""
+    hi = params.detach().clone()
+    lo = params.detach().clone()
+    dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+    dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+    return float((hi - lo).max().item())
+
+
+def exchange_selfcheck(torch, dist, rank: int) -> dict:
+    """The fused peer exchange + SGD (oxf_exchange_step) against NCCL
+    all-reduce + SGD on the same data: every rank holds the same parameters
+    p and its own gradients g_r on a ragged 4,206,599-element arena; after
+    one exchange over a sub-range and one over the whole arena every rank
+    must hold bit-identical parameters equal to p - lr * sum_r g_r up to the
+    summation order (the exchange adds in rank order, NCCL in its own)."""
+    from oxf.exchange import PeerExchange
+    n, lr = (1 << 22) + 12295, 0.01
+    p0 = torch.randn(n, generator=torch.Generator().manual_seed(7)).cuda()
+    g = torch.randn(n, generator=torch.Generator().manual_seed(500 + rank)).cuda()
+    params = p0.clone()
+    x = PeerExchange(params, g)
+    x.step(123457, 400001, lr)
+    x.step(0, n, lr)
+    torch.cuda.synchronize()
+    from oxf import kernels
+    code = kernels.device_error()
+    x.close()
+    gsum = g.clone()
+    dist.all_reduce(gsum)
+    ref = p0 - lr * gsum
+    ref[123457:123457 + 400001] -= lr * gsum[123457:123457 + 400001]
+    err = float(((params - ref).abs().max() / (lr * gsum).abs().max()).item())
+    return {"arena": n, "max_err_vs_nccl_rel": err, "device_error": code,
+            "ranks_bit_identical": rank_agreement(torch, dist, params) == 0.0,
+            "pass": code == 0 and err <= 1e-5}
+
+
 def main():
     a = parse()
     if a.impl == "reference":
@@ -844,6 +892,19 @@ def main():
                       "overlapping the previous step) and reads its loss back; wall clock, "
                       "max over ranks"}
 
+    # ---------------- cross-rank evidence (N > 1, after timing)
+    ranks = None
+    if world > 1:
+        delta = rank_agreement(torch, dist, model.params)
+        losses = [None] * world
+        dist.all_gather_object(losses, final_loss)
+        ranks = {"max_param_delta": delta, "ranks_bit_identical": delta == 0.0,
+                 "final_loss_per_rank": losses,
+                 "note": "parameters after the timed and e2e steps, compared elementwise "
+                         "across ranks (all-reduce MAX - MIN)"}
+        if a.exchange == "peer":
+            ranks["exchange_selfcheck"] = exchange_selfcheck(torch, dist, rank)
+
     # ---------------- CPU baseline (rank 0, N = 1)
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu:
@@ -887,6 +948,12 @@ def main():
             "clocks": clk,
             "final_loss": final_loss,
         }
+        if clk and clk.get("sm_mhz"):
+            # step time x median SM clock: comparable across runs whose
+            # power-capped clocks differ
+            line["ms_x_sm_ghz"] = elapsed_ms / a.steps * clk["sm_mhz"] / 1000.0
+        if ranks is not None:
+            line["ranks"] = ranks
         print(json.dumps(line), flush=True)
     trainer.close()
     model.close()

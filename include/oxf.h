@@ -269,12 +269,16 @@ oxf_status oxf_gemm(const oxf_gemm_desc* d, oxf_stream stream);
  * reference (it has no 3xTF32 mode and no scratch memory).
  * The hi/lo operand splits live in a 16 MiB static device array that every
  * GPU loading the library holds until exit; shapes needing more
- * (oxf_gemm_workspace_size > 16 MiB) return OXF_ERR_UNSUPPORTED_SHAPE. The
- * descriptor's precision and workspace fields are ignored. The first call on
- * a device looks up the array's device address, so make it before any
- * stream capture. All calls on a device share that device's array, which
- * keeps the last call's contents: calls that can overlap on the GPU (issued
- * on different streams of one device) race, so serialise them. */
+ * (oxf_gemm_workspace_size > 16 MiB) return OXF_ERR_UNSUPPORTED_SHAPE.
+ * Descriptors oxf_gemm would refuse get oxf_gemm's error; operands the
+ * tensor cores cannot read (misaligned, K = 0) run on the CUDA cores with no
+ * splits and no size limit. The descriptor's precision and workspace fields
+ * are ignored. The first call on a device, and the first after a device
+ * reset, looks up the array's device address; such a call made inside a
+ * stream capture returns OXF_ERR_INVALID_ARG, so make one call before
+ * capturing. All calls on a device share that device's array, which keeps
+ * the last call's contents: calls that can overlap on the GPU (issued on
+ * different streams of one device) race, so serialise them. */
 oxf_status oxf_gemm_tf32x3_noalloc(const oxf_gemm_desc* desc, oxf_stream stream);
 
 /* matrix_multiply (module.rs:179-191) with the reference's argument order:

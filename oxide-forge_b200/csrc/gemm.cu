@@ -1441,6 +1441,38 @@ EncodeTiledFn get_encode_fn() {
 }
 
 constexpr int kMaxDevices = 64;
+
+// The unique ID of the calling thread's current CUDA context (cuCtxGetId),
+// or 0 when no context is current yet or the driver cannot say. Host-side
+// caches of per-device state (symbol addresses, kernel attributes) record
+// it, so that after a cudaDeviceReset, which destroys the context and with
+// it every device address of this library's module, they look the state up
+// again instead of handing out addresses of the destroyed context.
+unsigned long long current_context_id() {
+  using GetCurrentFn = CUresult (*)(CUcontext*);
+  using GetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrentFn get_current = nullptr;
+  static GetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetIdFn>(p);
+  });
+  if (!get_current || !get_id) return 0;
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
 // K blocks of 32 (K >= 4096) from which a wide (256 x 512) pair tile's
 // exposed epilogue is short against its MMAs: below it, products with a
 // heavy epilogue keep 256-wide tiles, and wide tiles stage through two
@@ -1473,16 +1505,23 @@ bool schedule_slot(cudaStream_t stream, int dev, unsigned long long** next, unsi
   static std::vector<cudaStream_t> streams[kMaxDevices];
   static unsigned long long* next_base[kMaxDevices];
   static unsigned int* done_base[kMaxDevices];
+  static unsigned long long ctx_of[kMaxDevices];
   std::lock_guard<std::mutex> lock(mu);
-  if (!next_base[dev]) {
+  const unsigned long long ctx = current_context_id();
+  if (!next_base[dev] || (ctx != 0 && ctx != ctx_of[dev])) {
+    // first use on this device, or a new context (after a device reset):
+    // fresh addresses, and the old context's streams are gone
     void *p = nullptr, *q = nullptr;
     if (cudaGetSymbolAddress(&p, g_sched_next) != cudaSuccess ||
         cudaGetSymbolAddress(&q, g_sched_done) != cudaSuccess) {
       cudaGetLastError();
+      next_base[dev] = nullptr;
       return false;
     }
     next_base[dev] = static_cast<unsigned long long*>(p);
     done_base[dev] = static_cast<unsigned int*>(q);
+    ctx_of[dev] = current_context_id();
+    streams[dev].clear();
   }
   auto& v = streams[dev];
   const size_t k = static_cast<size_t>(std::find(v.begin(), v.end(), stream) - v.begin());
@@ -1573,13 +1612,15 @@ oxf_status launch_tcgen05(const CUtensorMap& ta, const CUtensorMap& tb, const CU
                           const CUtensorMap& tb_lo, const EpiMaps& em, GemmArgs& args,
                           cudaStream_t stream, int dev) {
   using Cfg = GemmCfg<BN, STAGES, SPLIT3>;
-  static bool configured[kMaxDevices] = {false};
-  if (dev >= 0 && dev < kMaxDevices && !configured[dev]) {
+  // once per device and context (a device reset drops the attribute)
+  static unsigned long long configured[kMaxDevices] = {0};
+  const unsigned long long ctx = current_context_id();
+  if (dev >= 0 && dev < kMaxDevices && (ctx == 0 || configured[dev] != ctx)) {
     cudaError_t e = cudaFuncSetAttribute(gemm_tf32_tcgen05<BN, STAGES, SPLIT3>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg::SMEM_BYTES);
     if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(gemm)");
-    configured[dev] = true;
+    configured[dev] = ctx;
   }
   args.idesc = make_idesc_tf32(BM, BN, args.a_mn != 0, args.b_mn != 0);
   const long long grid = std::min<long long>(args.units, sm_count(dev));
@@ -1596,13 +1637,15 @@ oxf_status launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
                        const CUtensorMap& tb_lo, const EpiMaps& em, GemmArgs& args,
                        cudaStream_t stream, int dev) {
   using Cfg = GemmPairCfg<BN, STAGES, SPLIT3, NB>;
-  static bool configured[kMaxDevices] = {false};
-  if (dev >= 0 && dev < kMaxDevices && !configured[dev]) {
+  // once per device and context (a device reset drops the attribute)
+  static unsigned long long configured[kMaxDevices] = {0};
+  const unsigned long long ctx = current_context_id();
+  if (dev >= 0 && dev < kMaxDevices && (ctx == 0 || configured[dev] != ctx)) {
     cudaError_t e = cudaFuncSetAttribute(gemm_tf32_tcgen05_pair<BN, STAGES, SPLIT3, NB>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg::SMEM_BYTES);
     if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(gemm pair)");
-    configured[dev] = true;
+    configured[dev] = ctx;
   }
   args.idesc = make_idesc_tf32(2 * BM, Cfg::MMA_N, args.a_mn != 0, args.b_mn != 0);
   const long long clusters = std::min<long long>(args.units, sm_count(dev) / 2);
@@ -1667,7 +1710,11 @@ size_t gemm_workspace_bytes(const oxf_gemm_desc* d) {
   return static_cast<size_t>(2 * r(ea) + 2 * r(eb));
 }
 
-oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
+namespace {
+
+// The descriptor checks of oxf_gemm, shared by every GEMM entry point. OK
+// also for an empty output (M or N zero), which the caller treats as a no-op.
+oxf_status gemm_validate(const oxf_gemm_desc* d) {
   if (!d) return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: null descriptor");
   if (d->M < 0 || d->N < 0 || d->K < 0 || d->batch < 1)
     return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: negative shape or batch < 1");
@@ -1696,6 +1743,26 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
   if (d->accumulate && (d->bias || d->residual) && split > 1)
     return set_error(OXF_ERR_INVALID_ARG,
                      "oxf_gemm: split_k would add bias / residual once per split");
+  return OXF_OK;
+}
+
+// Whether a valid, non-empty descriptor runs on the tensor cores: TMA needs
+// 16-byte aligned bases, leading dimensions and batch strides, and
+// OXF_PREC_F32 asks for f32 products on the CUDA cores. Otherwise the SIMT
+// kernel runs, which needs no operand splits for any precision.
+bool gemm_tensor_core_path(const oxf_gemm_desc* d) {
+  return d->K > 0 && tma_ok_ptr(d->A) && tma_ok_ptr(d->B) && d->lda % 4 == 0 &&
+         d->ldb % 4 == 0 && d->stride_a % 4 == 0 && d->stride_b % 4 == 0 &&
+         d->precision != OXF_PREC_F32;
+}
+
+}  // namespace
+
+oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
+  const oxf_status valid = gemm_validate(d);
+  if (valid != OXF_OK) return valid;
+  if (d->M == 0 || d->N == 0) return OXF_OK;
+  const int split = d->split_k > 1 ? d->split_k : 1;
 
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1725,9 +1792,7 @@ oxf_status gemm_run(const oxf_gemm_desc* d, cudaStream_t stream) {
 
   // TMA needs 16-byte aligned bases, leading dimensions and batch strides.
   // OXF_PREC_F32 asks for f32 products on the CUDA cores: the SIMT kernel.
-  const bool tma_ok = d->K > 0 && tma_ok_ptr(d->A) && tma_ok_ptr(d->B) && d->lda % 4 == 0 &&
-                      d->ldb % 4 == 0 && d->stride_a % 4 == 0 && d->stride_b % 4 == 0 &&
-                      d->precision != OXF_PREC_F32;
+  const bool tma_ok = gemm_tensor_core_path(d);
   if (!tma_ok) {
     if (a.reduce_batch)
       return set_error(OXF_ERR_UNSUPPORTED_SHAPE,
@@ -1984,9 +2049,17 @@ constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 oxf_status gemm_tf32x3_noalloc(const oxf_gemm_desc* d, cudaStream_t stream) {
-  if (!d) return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm_tf32x3_noalloc: null descriptor");
+  // The same checks and errors as oxf_gemm, before anything is sized.
+  const oxf_status valid = gemm_validate(d);
+  if (valid != OXF_OK) return valid;
+  if (d->M == 0 || d->N == 0) return OXF_OK;
   oxf_gemm_desc desc = *d;
   desc.precision = OXF_PREC_TF32X3;
+  desc.workspace = nullptr;
+  desc.workspace_bytes = 0;
+  // Operands the tensor cores cannot read (misaligned, or K = 0) take the
+  // SIMT kernel, which splits nothing: no scratch, no size limit.
+  if (!gemm_tensor_core_path(&desc)) return gemm_run(&desc, stream);
   const size_t need = gemm_workspace_bytes(&desc);
   if (need > kNoAllocScratchBytes)
     return set_error(OXF_ERR_UNSUPPORTED_SHAPE,
@@ -1999,23 +2072,37 @@ oxf_status gemm_tf32x3_noalloc(const oxf_gemm_desc* d, cudaStream_t stream) {
   if (dev < 0 || dev >= kMaxDevices)
     return set_error(OXF_ERR_UNSUPPORTED_SHAPE, "oxf_gemm_tf32x3_noalloc: device ordinal %d", dev);
   // In host code the array's name only stands in for it; its device address
-  // is looked up once per device, with that device current, on the first
-  // call there.
+  // is looked up with the device current, on the first call there and again
+  // after a device reset (a new context has a new address). The lookup may
+  // load this library's module, which a stream capture would not allow, so
+  // a lookup that falls inside a capture is refused.
   static std::mutex mu;
   static void* scratch[kMaxDevices] = {nullptr};
+  static unsigned long long ctx_of[kMaxDevices] = {0};
+  void* ptr = nullptr;
   {
     std::lock_guard<std::mutex> lock(mu);
-    if (!scratch[dev]) {
+    const unsigned long long ctx = current_context_id();
+    if (!scratch[dev] || (ctx != 0 && ctx != ctx_of[dev])) {
+      cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+      st = check_cuda(cudaStreamIsCapturing(stream, &cs), "cudaStreamIsCapturing");
+      if (st != OXF_OK) return st;
+      if (cs != cudaStreamCaptureStatusNone)
+        return set_error(OXF_ERR_INVALID_ARG,
+                         "oxf_gemm_tf32x3_noalloc: the first call on a device (and the first "
+                         "after a device reset) must come before any stream capture");
       void* p = nullptr;
       st = check_cuda(cudaGetSymbolAddress(&p, g_noalloc_scratch),
                       "cudaGetSymbolAddress(no-alloc scratch)");
       if (st != OXF_OK) return st;
       scratch[dev] = p;
+      ctx_of[dev] = current_context_id();
     }
+    ptr = scratch[dev];
   }
   // Nothing in the scratch needs to start at zero: the split kernels write
   // every element the GEMM then reads (TMA zero-fills reads past the edges).
-  desc.workspace = scratch[dev];
+  desc.workspace = ptr;
   desc.workspace_bytes = kNoAllocScratchBytes;
   return gemm_run(&desc, stream);
 }

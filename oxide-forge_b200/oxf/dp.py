@@ -48,8 +48,8 @@ class DataParallelTrainer:
     """SGD on the mean gradient of a sharded global batch.
 
     model: an engine with train_forward(x), set_target(t) -> row losses,
-    backward_stage(s), bucket(s) -> (offset, count), grads (flat tensor),
-    zero_grads(), sgd(lr).
+    scaled_loss_sum(scale) -> one-element tensor, backward_stage(s),
+    bucket(s) -> (offset, count), grads (flat tensor), zero_grads(), sgd(lr).
     """
 
     STAGES = (0, 1, 2)
@@ -76,7 +76,6 @@ class DataParallelTrainer:
         self.seq = seq
         self.group = group
         self.overlap = overlap
-        self._loss_buf = None
 
     def broadcast_params(self, params: torch.Tensor) -> None:
         """Every rank starts from rank 0's parameters."""
@@ -96,7 +95,7 @@ class DataParallelTrainer:
         m.train_forward(x)
         if _before_target is not None:
             _before_target()
-        row_loss = m.set_target(target)
+        m.set_target(target)
         works = []
         for s in self.STAGES:
             m.backward_stage(s)
@@ -107,14 +106,15 @@ class DataParallelTrainer:
                     works.append(dist.all_reduce(bucket, group=self.group, async_op=True))
                 else:
                     dist.all_reduce(bucket, group=self.group)
-        loss = row_loss.sum().reshape(1)
+        # this rank's share of the global mean row loss, then summed over ranks
+        loss = m.scaled_loss_sum(1.0 / (self.global_batch * self.seq))
         if self.world > 1:
             works.append(dist.all_reduce(loss, group=self.group, async_op=self.overlap))
             for w in works:
                 if w is not None:
                     w.wait()
         m.sgd(self.lr / self.global_batch)
-        return loss / (self.global_batch * self.seq)
+        return loss
 
     def _step_peer(self, x, target, _before_target):
         """step() with the fused exchange: every bucket's kernel runs on one
@@ -133,7 +133,7 @@ class DataParallelTrainer:
         m.train_forward(x)
         if _before_target is not None:
             _before_target()
-        row_loss = m.set_target(target)
+        m.set_target(target)
         last = self.STAGES[-1]
         for s in self.STAGES:
             m.backward_stage(s)
@@ -150,11 +150,11 @@ class DataParallelTrainer:
             # exchange CTA shares the GPU with a backward GEMM.
             xs.wait_stream(compute)
             self._peer.step(0, m.grads.numel(), lr, blocks=0, stream=xs)
-        loss = row_loss.sum().reshape(1)
+        loss = m.scaled_loss_sum(1.0 / (self.global_batch * self.seq))
         if self.world > 1:
             dist.all_reduce(loss, group=self.group)
         compute.wait_stream(xs)
-        return loss / (self.global_batch * self.seq)
+        return loss
 
     def save_checkpoint(self, path, cfg) -> None:
         """Checkpoint v1 (the reference's TOML + little-endian f32 files,

@@ -14,7 +14,7 @@ from dataclasses import dataclass, field
 import numpy as np
 import torch
 
-from . import _lib
+from . import _lib, kernels
 from ._host_sigs import LayerSpec, MlpSpec, TransformerSpec
 from ._lib import check, lib
 
@@ -203,6 +203,14 @@ class Transformer:
     def set_target(self, target: torch.Tensor) -> torch.Tensor:
         check(lib().oxf_transformer_set_target(self._h, target.data_ptr()))
         return self._views(self._batch)[1]
+
+    def scaled_loss_sum(self, scale: float) -> torch.Tensor:
+        """scale * (sum of the row losses of the last set_target), as a fresh
+        one-element device tensor: one library launch (oxf_slice_map_sum),
+        no PyTorch kernel, on the current stream."""
+        out = torch.empty(1, device=self.params.device)
+        kernels.map_sum(self._views(self._batch)[1], _lib.UNARY_SCALE, float(scale), out)
+        return out
 
     def set_output_gradient(self, dy: torch.Tensor) -> None:
         check(lib().oxf_transformer_set_output_gradient(self._h, dy.data_ptr()))

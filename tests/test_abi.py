@@ -165,17 +165,11 @@ def _header_signatures() -> dict[str, int]:
     return sigs
 
 
-def _integration_rust_block() -> str:
-    text = (ROOT / "INTEGRATION.md").read_text()
-    start = text.index("// src/cuda/oxf_ffi.rs  (complete)")
-    return text[start:text.index("```", start)]
-
-
-def test_integration_rust_binding_matches_headers():
-    """The complete Rust binding documented for the reference's maintainers
-    declares exactly the headers' functions with the headers' parameter
-    counts, and its structures list the C members in the C order."""
-    block = _integration_rust_block()
+def test_rust_binding_matches_headers():
+    """include/oxf_ffi.rs, the complete Rust binding for the reference's
+    maintainers, declares exactly the headers' functions with the headers'
+    parameter counts, and its structures list the C members in the C order."""
+    block = (ROOT / "include" / "oxf_ffi.rs").read_text()
     rust = {}
     for m in re.finditer(r"pub fn (oxf_[a-z0-9_]+)\(([^)]*)\)", block):
         args = m.group(2).strip()

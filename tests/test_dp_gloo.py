@@ -71,7 +71,11 @@ class OracleModel:
                                                        grads=g)
             losses.append(loss)
         self.grads += torch.from_numpy(g)
-        return torch.from_numpy(np.concatenate(losses))
+        self._row_loss = torch.from_numpy(np.concatenate(losses))
+        return self._row_loss
+
+    def scaled_loss_sum(self, scale):
+        return (self._row_loss.sum() * scale).reshape(1)
 
     def backward_stage(self, s):
         # gradients were produced in set_target; a test may make stage 1 fail

@@ -49,6 +49,15 @@ def operands(rng, M, N, Kd, at, bt, batch=None, dist="uniform"):
     return gen(a_shape).astype(np.float32), gen(b_shape).astype(np.float32)
 
 
+def config1_operands():
+    """Config 1: X [256,128] U(-1,1) from seed 0, then W [128,64]
+    U(-1/sqrt(128), 1/sqrt(128)) from the same generator."""
+    g = np.random.default_rng(0)
+    x = g.uniform(-1, 1, (256, 128)).astype(np.float32)
+    w = g.uniform(-1 / np.sqrt(128), 1 / np.sqrt(128), (128, 64)).astype(np.float32)
+    return x, w
+
+
 def exact(A, B, at, bt):
     """float64 product of the f32 operands (numpy BLAS; the oracle's
     oxo_gemm_f64 computes the same thing, far slower)."""
@@ -94,9 +103,8 @@ def test_gemm_tf32x3(K, rng, M, N, Kd, variant, at, bt):
 
 def test_matrix_multiply_reference_signature(K, rng):
     """matrix_multiply(lhs, rhs, out, len, rows, cols) of module.rs:179-191
-    on config 1's shapes and distributions."""
-    x = rng.uniform(-1, 1, (256, 128)).astype(np.float32)
-    w = rng.uniform(-1 / np.sqrt(128), 1 / np.sqrt(128), (128, 64)).astype(np.float32)
+    on config 1's shapes and distributions (seed 0, as the config states)."""
+    x, w = config1_operands()
     out = torch.empty((256, 64), device="cuda")
     K.matrix_multiply(dev(x), dev(w), out)
     assert rel_err(host(out), exact(x, w, 0, 0)) < TF32_TOL
@@ -433,8 +441,7 @@ def test_small_products_match_reference_rounding_and_epilogue(K, rng):
     TF32 RNA operand rounding: equal up to f32 summation order. Then the
     fused epilogue (alpha, beta·C, bias, residual, pre-activation, GELU),
     the activation gradient, and accumulation on the same kernel."""
-    x = rng.uniform(-1, 1, (256, 128)).astype(np.float32)
-    w = rng.uniform(-0.09, 0.09, (128, 64)).astype(np.float32)
+    x, w = config1_operands()
     y = torch.empty((256, 64), device="cuda")
     K.matrix_multiply(dev(x), dev(w), y)
     want = O.gemm(x, w, rounding=O.GEMM_TF32_RNA)
