@@ -499,7 +499,8 @@ def run_rows(a, torch):
 def run_linear(a, torch):
     """Config 1: Linear forward exactly as the repository example (X [256,128]
     U(-1,1) from seed 0, W [128,64] U(-1/sqrt(128), 1/sqrt(128)), no bias,
-    Identity) through matrix_multiply's argument order (module.rs:179-191):
+    Identity) through the Linear API (oxf_linear_forward; the raw
+    matrix_multiply of module.rs:179-191 is timed beside it):
     device time per call, against the C oracle (TF32 RNA operands, as the
     reference's kernel rounds) and the reference-algorithm restatement."""
     import numpy as np
@@ -533,8 +534,13 @@ def run_linear(a, torch):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / (reps * max(1, a.steps))
 
-    ms = graph_ms(lambda: K.matrix_multiply(xd, wd, y))
-    host_ms = _time(torch, lambda: K.matrix_multiply(xd, wd, y), a.steps * 20, a.warmup)
+    from oxf import models
+    rt = models.Runtime()
+    lin = models.Linear(rt, w)  # Linear::new(W, None, Identity), linear.rs:89-95
+    ms = graph_ms(lambda: lin.forward(xd, y=y))
+    host_ms = _time(torch, lambda: lin.forward(xd, y=y), a.steps * 20, a.warmup)
+    ms_mm = graph_ms(lambda: K.matrix_multiply(xd, wd, y))
+    lin.forward(xd, y=y)
     got = y.cpu().numpy()
     want = O.gemm(x, w, rounding=O.GEMM_TF32_RNA)
     ms_ref = graph_ms(lambda: K.matrix_multiply_refalgo(xd, wd, y))
@@ -547,10 +553,12 @@ def run_linear(a, torch):
     print(json.dumps({"metric": "Linear [256,128]x[128,64] forward latency", "value": ms * 1e3,
                       "unit": "us", "workload": "linear", "higher_is_better": False,
                       "gflops": fl / ms / 1e6, "refalgo_us": ms_ref * 1e3,
+                      "matrix_multiply_us": ms_mm * 1e3,
                       "fp32_cuda_core_us": ms_f32 * 1e3,
                       "host_call_us": host_ms * 1e3, "cpu_oracle_us": cpu_ms * 1e3,
                       "max_rel_err_vs_oracle": float(np.abs(got - want).max() / np.abs(want).max()),
-                      "config": {"workload": "C1 Linear forward, repository example shape",
+                      "config": {"workload": "C1 Linear forward, repository example shape, "
+                                             "through the Linear API (oxf_linear_forward)",
                                  "timing": "value/refalgo_us: device time per call (200 calls "
                                            "replayed as a CUDA graph); host_call_us: calls "
                                            "issued one by one from Python"}}),

@@ -192,6 +192,31 @@ extern "C" {
                             rows: usize) -> oxf_status;
     pub fn oxf_mlp_zero_grads(m: *mut c_void) -> oxf_status;
     pub fn oxf_mlp_sgd(m: *mut c_void, lr: f32) -> oxf_status;
+    pub fn oxf_runtime_create(device: c_int, stream: oxf_stream, out: *mut *mut c_void)
+                              -> oxf_status;
+    pub fn oxf_runtime_destroy(rt: *mut c_void) -> oxf_status;
+    pub fn oxf_runtime_stream(rt: *mut c_void) -> oxf_stream;
+    pub fn oxf_runtime_sync(rt: *mut c_void) -> oxf_status;
+    pub fn oxf_runtime_reserve_buffers(rt: *mut c_void, len: usize, count: usize) -> oxf_status;
+    pub fn oxf_runtime_pooled_buffers(rt: *mut c_void, count: *mut usize) -> oxf_status;
+    pub fn oxf_linear_create(rt: *mut c_void, spec: *const oxf_layer_spec,
+                             weights_host: *const f32, bias_host: *const f32,
+                             out: *mut *mut c_void) -> oxf_status;
+    pub fn oxf_linear_destroy(l: *mut c_void) -> oxf_status;
+    pub fn oxf_linear_params(l: *mut c_void, weights: *mut *mut f32, bias: *mut *mut f32)
+                             -> oxf_status;
+    pub fn oxf_linear_forward(l: *mut c_void, x: *const f32, rows: usize, residual: *const f32,
+                              y: *mut f32, pre_activation: *mut f32, stream: oxf_stream)
+                              -> oxf_status;
+    pub fn oxf_linear_backward(l: *mut c_void, pre_activation: *const f32,
+                               output_gradient: *const f32, residual_gradient: *const f32,
+                               rows: usize, gradient: *mut f32, bias_gradient: *mut f32,
+                               stream: oxf_stream) -> oxf_status;
+    pub fn oxf_linear_learn(l: *mut c_void, x: *const f32, gradient: *const f32,
+                            bias_gradient: *const f32, rows: usize, learning_rate: f32,
+                            stream: oxf_stream) -> oxf_status;
+    pub fn oxf_linear_input_gradient(l: *mut c_void, gradient: *const f32, rows: usize,
+                                     dx: *mut f32, stream: oxf_stream) -> oxf_status;
     pub fn oxf_checkpoint_write_linear(path: *const c_char, spec: *const oxf_layer_spec,
                                        params_host: *const f32, count: usize) -> oxf_status;
     pub fn oxf_checkpoint_write_mlp(path: *const c_char, spec: *const oxf_mlp_spec,

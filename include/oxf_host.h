@@ -127,6 +127,63 @@ oxf_status oxf_mlp_backward(oxf_mlp m, const float* dy, float* dx, size_t rows);
 oxf_status oxf_mlp_zero_grads(oxf_mlp m);
 oxf_status oxf_mlp_sgd(oxf_mlp m, float lr);
 
+/* ---------------------------------------------------------------- runtime + Linear */
+/* CudaRuntime (src/cuda/runtime.rs:24-212): a device, its primary stream
+ * and an exact-size pool of device buffers (runtime.rs:47-110) from which
+ * the Linear below takes its parameters. stream NULL: the runtime creates
+ * its own non-blocking primary stream (the reference creates one per
+ * runtime, runtime.rs:34-45); otherwise it borrows `stream`. */
+typedef struct oxf_runtime_s* oxf_runtime;
+oxf_status oxf_runtime_create(int device, oxf_stream stream, oxf_runtime* out);
+/* Synchronises, then frees the pool and the streams the runtime created. */
+oxf_status oxf_runtime_destroy(oxf_runtime rt);
+oxf_stream oxf_runtime_stream(oxf_runtime rt);
+/* CudaRuntime::sync (runtime.rs:112-114). */
+oxf_status oxf_runtime_sync(oxf_runtime rt);
+/* CudaRuntime::reserve_buffers (runtime.rs:75-91): at least `count` free
+ * pooled buffers of `len` floats. */
+oxf_status oxf_runtime_reserve_buffers(oxf_runtime rt, size_t len, size_t count);
+/* Free buffers held by the pool, all lengths. */
+oxf_status oxf_runtime_pooled_buffers(oxf_runtime rt, size_t* count);
+
+/* Linear (src/net/linear.rs:72-533): weights [in, out] row-major, a bias
+ * [out] when spec->bias, spec->act. The parameters live in the runtime's
+ * pool buffers, copied from host memory at creation (Linear::new,
+ * linear.rs:89-95, after matrix_from_host). The layer belongs to the
+ * runtime: destroy it before the runtime. Every call takes device pointers
+ * of rows x (in or out) matrices and runs on `stream`: NULL is the
+ * runtime's primary stream; another stream first waits for the primary
+ * stream (the reference's stream.join(runtime.stream())). */
+typedef struct oxf_linear_s* oxf_linear;
+oxf_status oxf_linear_create(oxf_runtime rt, const oxf_layer_spec* spec, const float* weights_host,
+                             const float* bias_host, oxf_linear* out);
+oxf_status oxf_linear_destroy(oxf_linear l);
+/* Device pointers of the weights [in, out] and the bias [out] (NULL without
+ * a bias); updated in place by oxf_linear_learn. */
+oxf_status oxf_linear_params(oxf_linear l, float** weights, float** bias);
+/* Linear::forward (linear.rs:116-132, 185-230): y = act(x·W + b +
+ * residual), in that order, as one GEMM with a fused epilogue. residual
+ * (rows x out) may be NULL; pre_activation (rows x out, may be NULL)
+ * receives x·W + b + residual, which Linear::backward needs. */
+oxf_status oxf_linear_forward(oxf_linear l, const float* x, size_t rows, const float* residual,
+                              float* y, float* pre_activation, oxf_stream stream);
+/* Linear::backward / backward_with_res (linear.rs:232-306, 446-533):
+ * gradient = (output_gradient [+ residual_gradient]) ⊙ act'(pre_activation)
+ * and, for a biased layer, bias_gradient = its column sums (NULL
+ * pre_activation only for Identity; residual_gradient may be NULL). */
+oxf_status oxf_linear_backward(oxf_linear l, const float* pre_activation,
+                               const float* output_gradient, const float* residual_gradient,
+                               size_t rows, float* gradient, float* bias_gradient,
+                               oxf_stream stream);
+/* Linear::learn (linear.rs:350-415): W -= lr·xᵀ·gradient, b -= lr·bias_gradient
+ * (bias_gradient required for a biased layer). */
+oxf_status oxf_linear_learn(oxf_linear l, const float* x, const float* gradient,
+                            const float* bias_gradient, size_t rows, float learning_rate,
+                            oxf_stream stream);
+/* Linear::input_gradient (linear.rs:417-446): dx [rows, in] = gradient·Wᵀ. */
+oxf_status oxf_linear_input_gradient(oxf_linear l, const float* gradient, size_t rows,
+                                     float* dx, oxf_stream stream);
+
 /* ---------------------------------------------------------------- checkpoints (v1) */
 /* The reference's checkpoint format (src/net/checkpoint/model.rs:17-21,
  * io.rs:14-181): <name>.toml holds format_version = 1, model_type

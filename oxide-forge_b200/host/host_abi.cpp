@@ -11,6 +11,7 @@
 #include "checkpoint.hpp"
 #include "engine.hpp"
 #include "errors.hpp"
+#include "linear.hpp"
 #include "oxf_host.h"
 
 struct oxf_transformer_s {
@@ -21,6 +22,15 @@ struct oxf_transformer_s {
   float* x_dev = nullptr;  // staging for the host-memory training step
   float* t_dev = nullptr;
   float* loss_dev = nullptr;
+};
+
+struct oxf_runtime_s {
+  oxf::CudaRuntime* rt = nullptr;
+};
+
+struct oxf_linear_s {
+  oxf::CudaRuntime* rt = nullptr;
+  oxf::Linear* layer = nullptr;
 };
 
 struct oxf_mlp_s {
@@ -376,6 +386,163 @@ oxf_status oxf_mlp_sgd(oxf_mlp m, float lr) {
 }
 
 // ---------------------------------------------------------------- checkpoints (v1)
+// ================================================================ runtime + Linear
+oxf_status oxf_runtime_create(int device, oxf_stream stream, oxf_runtime* out) {
+  if (!out) return oxf::set_error(OXF_ERR_INVALID_ARG, "oxf_runtime_create: null out");
+  *out = nullptr;
+  return guard([&] {
+    auto* r = new oxf_runtime_s;
+    try {
+      r->rt = new oxf::CudaRuntime(device, reinterpret_cast<cudaStream_t>(stream));
+    } catch (...) {
+      delete r;
+      throw;
+    }
+    *out = r;
+  });
+}
+
+oxf_status oxf_runtime_destroy(oxf_runtime r) {
+  if (!r) return OXF_OK;
+  delete r->rt;
+  delete r;
+  return OXF_OK;
+}
+
+oxf_stream oxf_runtime_stream(oxf_runtime r) {
+  return r ? reinterpret_cast<oxf_stream>(r->rt->stream()) : nullptr;
+}
+
+oxf_status oxf_runtime_sync(oxf_runtime r) {
+  if (!r) return oxf::set_error(OXF_ERR_INVALID_ARG, "oxf_runtime_sync: null runtime");
+  return guard([&] { r->rt->sync(); });
+}
+
+oxf_status oxf_runtime_reserve_buffers(oxf_runtime r, size_t len, size_t count) {
+  if (!r) return oxf::set_error(OXF_ERR_INVALID_ARG, "oxf_runtime_reserve_buffers: null runtime");
+  return guard([&] { r->rt->reserve_buffers(len, count); });
+}
+
+oxf_status oxf_runtime_pooled_buffers(oxf_runtime r, size_t* count) {
+  if (!r || !count)
+    return oxf::set_error(OXF_ERR_INVALID_ARG, "oxf_runtime_pooled_buffers: null argument");
+  *count = r->rt->pooled_buffers();
+  return OXF_OK;
+}
+
+oxf_status oxf_linear_create(oxf_runtime r, const oxf_layer_spec* spec, const float* weights_host,
+                             const float* bias_host, oxf_linear* out) {
+  if (!r || !spec || !weights_host || !out)
+    return oxf::set_error(OXF_ERR_INVALID_ARG, "oxf_linear_create: null argument");
+  *out = nullptr;
+  return guard([&] {
+    const oxf::LayerSpec s = layer(*spec);
+    oxf::require(!s.bias || bias_host != nullptr, "oxf_linear_create: a biased layer needs bias_host");
+    oxf::CudaRuntime& rt = *r->rt;
+    oxf::Matrix w = rt.matrix_from_host(weights_host, static_cast<size_t>(s.in),
+                                        static_cast<size_t>(s.out));
+    std::optional<oxf::Vector> b;
+    if (s.bias) b.emplace(rt.vector_from_host(bias_host, static_cast<size_t>(s.out)));
+    auto* l = new oxf_linear_s;
+    l->rt = r->rt;
+    try {
+      l->layer = new oxf::Linear(std::move(w), std::move(b), static_cast<oxf::Activation>(s.act));
+    } catch (...) {
+      delete l;
+      throw;
+    }
+    rt.sync();  // the host arrays may be released on return
+    *out = l;
+  });
+}
+
+oxf_status oxf_linear_destroy(oxf_linear l) {
+  if (!l) return OXF_OK;
+  delete l->layer;  // its buffers go back to the runtime's pool
+  delete l;
+  return OXF_OK;
+}
+
+oxf_status oxf_linear_params(oxf_linear l, float** weights, float** bias) {
+  if (!l) return oxf::set_error(OXF_ERR_INVALID_ARG, "oxf_linear_params: null layer");
+  if (weights) *weights = l->layer->weights().data();
+  if (bias) *bias = l->layer->bias() ? l->layer->bias()->data() : nullptr;
+  return OXF_OK;
+}
+
+namespace {
+
+// A borrowed rows x cols view of caller-owned device memory. Views of null
+// optional arguments are built but never passed on.
+oxf::Matrix view(const float* p, size_t rows, size_t cols) {
+  return oxf::Matrix::view(const_cast<float*>(p), rows, cols);
+}
+
+}  // namespace
+
+oxf_status oxf_linear_forward(oxf_linear l, const float* x, size_t rows, const float* residual,
+                              float* y, float* pre_activation, oxf_stream stream) {
+  if (!l) return oxf::set_error(OXF_ERR_INVALID_ARG, "oxf_linear_forward: null layer");
+  return guard([&] {
+    const oxf::Linear& L = *l->layer;
+    oxf::require(rows == 0 || (x && y), "oxf_linear_forward: null x or y");
+    const oxf::Matrix xm = view(x, rows, L.input_neurons());
+    oxf::Matrix ym = view(y, rows, L.output_neurons());
+    const oxf::Matrix rm = view(residual, rows, L.output_neurons());
+    oxf::Matrix pm = view(pre_activation, rows, L.output_neurons());
+    L.forward_into(xm, residual ? &rm : nullptr, ym, pre_activation ? &pm : nullptr, *l->rt,
+                   reinterpret_cast<cudaStream_t>(stream));
+  });
+}
+
+oxf_status oxf_linear_backward(oxf_linear l, const float* pre_activation,
+                               const float* output_gradient, const float* residual_gradient,
+                               size_t rows, float* gradient, float* bias_gradient,
+                               oxf_stream stream) {
+  if (!l) return oxf::set_error(OXF_ERR_INVALID_ARG, "oxf_linear_backward: null layer");
+  return guard([&] {
+    const oxf::Linear& L = *l->layer;
+    const size_t o = L.output_neurons();
+    oxf::require(rows == 0 || (output_gradient && gradient),
+                 "oxf_linear_backward: null output_gradient or gradient");
+    const oxf::Matrix zm = view(pre_activation, rows, o);
+    const oxf::Matrix dym = view(output_gradient, rows, o);
+    const oxf::Matrix drm = view(residual_gradient, rows, o);
+    oxf::Matrix gm = view(gradient, rows, o);
+    oxf::Vector bg = oxf::Vector::view(bias_gradient, bias_gradient ? o : 0);
+    L.backward_into(pre_activation ? &zm : nullptr, dym, residual_gradient ? &drm : nullptr, gm,
+                    bias_gradient ? &bg : nullptr, *l->rt, reinterpret_cast<cudaStream_t>(stream));
+  });
+}
+
+oxf_status oxf_linear_learn(oxf_linear l, const float* x, const float* gradient,
+                            const float* bias_gradient, size_t rows, float learning_rate,
+                            oxf_stream stream) {
+  if (!l) return oxf::set_error(OXF_ERR_INVALID_ARG, "oxf_linear_learn: null layer");
+  return guard([&] {
+    oxf::Linear& L = *l->layer;
+    oxf::require(rows == 0 || (x && gradient), "oxf_linear_learn: null x or gradient");
+    const oxf::Matrix xm = view(x, rows, L.input_neurons());
+    const oxf::Matrix gm = view(gradient, rows, L.output_neurons());
+    const oxf::Vector bg =
+        oxf::Vector::view(const_cast<float*>(bias_gradient), bias_gradient ? L.output_neurons() : 0);
+    L.learn(xm, gm, bias_gradient ? &bg : nullptr, learning_rate, *l->rt,
+            reinterpret_cast<cudaStream_t>(stream));
+  });
+}
+
+oxf_status oxf_linear_input_gradient(oxf_linear l, const float* gradient, size_t rows, float* dx,
+                                     oxf_stream stream) {
+  if (!l) return oxf::set_error(OXF_ERR_INVALID_ARG, "oxf_linear_input_gradient: null layer");
+  return guard([&] {
+    const oxf::Linear& L = *l->layer;
+    oxf::require(rows == 0 || (gradient && dx), "oxf_linear_input_gradient: null gradient or dx");
+    const oxf::Matrix gm = view(gradient, rows, L.output_neurons());
+    oxf::Matrix dxm = view(dx, rows, L.input_neurons());
+    L.input_gradient_into(gm, dxm, *l->rt, reinterpret_cast<cudaStream_t>(stream));
+  });
+}
+
 oxf_status oxf_checkpoint_write_linear(const char* path, const oxf_layer_spec* spec,
                                        const float* params_host, size_t count) {
   return write_ckpt<oxf_layer_spec>(

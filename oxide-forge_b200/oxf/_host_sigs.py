@@ -57,6 +57,19 @@ SIGS: dict = {
     "oxf_mlp_backward": (C.c_int, [_h, _fp, _fp, _sz]),
     "oxf_mlp_zero_grads": (C.c_int, [_h]),
     "oxf_mlp_sgd": (C.c_int, [_h, C.c_float]),
+    "oxf_runtime_create": (C.c_int, [C.c_int, C.c_void_p, C.POINTER(C.c_void_p)]),
+    "oxf_runtime_destroy": (C.c_int, [_h]),
+    "oxf_runtime_stream": (C.c_void_p, [_h]),
+    "oxf_runtime_sync": (C.c_int, [_h]),
+    "oxf_runtime_reserve_buffers": (C.c_int, [_h, _sz, _sz]),
+    "oxf_runtime_pooled_buffers": (C.c_int, [_h, C.POINTER(_sz)]),
+    "oxf_linear_create": (C.c_int, [_h, C.POINTER(LayerSpec), _fp, _fp, C.POINTER(C.c_void_p)]),
+    "oxf_linear_destroy": (C.c_int, [_h]),
+    "oxf_linear_params": (C.c_int, [_h, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)]),
+    "oxf_linear_forward": (C.c_int, [_h, _fp, _sz, _fp, _fp, _fp, C.c_void_p]),
+    "oxf_linear_backward": (C.c_int, [_h, _fp, _fp, _fp, _sz, _fp, _fp, C.c_void_p]),
+    "oxf_linear_learn": (C.c_int, [_h, _fp, _fp, _fp, _sz, C.c_float, C.c_void_p]),
+    "oxf_linear_input_gradient": (C.c_int, [_h, _fp, _sz, _fp, C.c_void_p]),
     "oxf_checkpoint_write_linear": (C.c_int, [C.c_char_p, C.POINTER(LayerSpec), _fp, _sz]),
     "oxf_checkpoint_write_mlp": (C.c_int, [C.c_char_p, C.POINTER(MlpSpec), _fp, _sz]),
     "oxf_checkpoint_write_transformer": (C.c_int, [C.c_char_p, C.POINTER(TransformerSpec), _fp,

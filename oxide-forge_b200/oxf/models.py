@@ -302,3 +302,121 @@ class Mlp:
             self.close()
         except Exception:
             pass
+
+
+class Runtime:
+    """CudaRuntime (src/cuda/runtime.rs:24-212) through include/oxf_host.h:
+    a device, its primary stream and an exact-size buffer pool. By default it
+    borrows torch's current stream as its primary stream, so tensors made by
+    torch and the runtime's work are ordered on one stream."""
+
+    def __init__(self, device: int | None = None, stream=None):
+        if device is None:
+            device = torch.cuda.current_device()
+        if stream is None:
+            stream = torch.cuda.current_stream()
+        h = C.c_void_p()
+        check(lib().oxf_runtime_create(int(device), C.c_void_p(stream.cuda_stream), C.byref(h)))
+        self._h = h
+
+    @property
+    def handle(self):
+        return self._h
+
+    def sync(self) -> None:
+        check(lib().oxf_runtime_sync(self._h))
+
+    def reserve_buffers(self, length: int, count: int) -> None:
+        check(lib().oxf_runtime_reserve_buffers(self._h, int(length), int(count)))
+
+    def pooled_buffers(self) -> int:
+        n = C.c_size_t()
+        check(lib().oxf_runtime_pooled_buffers(self._h, C.byref(n)))
+        return n.value
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().oxf_runtime_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _sp(stream):
+    return None if stream is None else C.c_void_p(stream.cuda_stream)
+
+
+def _dp(t):
+    return None if t is None else t.data_ptr()
+
+
+class Linear:
+    """Linear (src/net/linear.rs:72-533) through include/oxf_host.h: weights
+    [in, out] and an optional bias held in the runtime's pool, copied from
+    host arrays. Methods take float32 CUDA tensors of rows x in / rows x out
+    and run on the runtime's primary stream unless `stream` is given."""
+
+    def __init__(self, rt: Runtime, weights, bias=None, act: int = _lib.ACT_IDENTITY):
+        w = np.ascontiguousarray(weights, np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+        self.in_, self.out = w.shape
+        self.act = act
+        spec = LayerSpec(self.in_, self.out, int(act), int(b is not None))
+        h = C.c_void_p()
+        check(lib().oxf_linear_create(rt.handle, C.byref(spec), w.ctypes.data,
+                                      None if b is None else b.ctypes.data, C.byref(h)))
+        self._h = h
+        self._rt = rt
+        wp, bp = C.c_void_p(), C.c_void_p()
+        check(lib().oxf_linear_params(h, C.byref(wp), C.byref(bp)))
+        self.weights = device_view(wp.value, (self.in_, self.out), self)
+        self.bias = device_view(bp.value, (self.out,), self) if bp.value else None
+
+    def forward(self, x, residual=None, y=None, pre_activation=None, stream=None):
+        """Linear::forward: y = act(x·W + b + residual); pre_activation, if
+        given, receives x·W + b + residual."""
+        rows = x.shape[0]
+        if y is None:
+            y = torch.empty((rows, self.out), device=x.device)
+        check(lib().oxf_linear_forward(self._h, _dp(x), rows, _dp(residual), _dp(y),
+                                       _dp(pre_activation), _sp(stream)))
+        return y
+
+    def backward(self, pre_activation, output_gradient, residual_gradient=None, stream=None):
+        """Linear::backward / backward_with_res: (G, bias gradient or None)."""
+        rows = output_gradient.shape[0]
+        g = torch.empty_like(output_gradient)
+        bg = torch.empty(self.out, device=g.device) if self.bias is not None else None
+        check(lib().oxf_linear_backward(self._h, _dp(pre_activation), _dp(output_gradient),
+                                        _dp(residual_gradient), rows, _dp(g), _dp(bg),
+                                        _sp(stream)))
+        return g, bg
+
+    def learn(self, x, gradient, bias_gradient, lr: float, stream=None) -> None:
+        """Linear::learn: W -= lr·xᵀ·G, b -= lr·bias_gradient."""
+        check(lib().oxf_linear_learn(self._h, _dp(x), _dp(gradient), _dp(bias_gradient),
+                                     x.shape[0], float(lr), _sp(stream)))
+
+    def input_gradient(self, gradient, dx=None, stream=None):
+        """Linear::input_gradient: G·Wᵀ."""
+        rows = gradient.shape[0]
+        if dx is None:
+            dx = torch.empty((rows, self.in_), device=gradient.device)
+        check(lib().oxf_linear_input_gradient(self._h, _dp(gradient), rows, _dp(dx),
+                                              _sp(stream)))
+        return dx
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().oxf_linear_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
