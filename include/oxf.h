@@ -281,6 +281,33 @@ oxf_status oxf_gemm(const oxf_gemm_desc* d, oxf_stream stream);
  * different streams of one device) race, so serialise them. */
 oxf_status oxf_gemm_tf32x3_noalloc(const oxf_gemm_desc* desc, oxf_stream stream);
 
+/* Scaled dot-product attention of Attention::forward
+ * (src/net/transformer/attention.rs:243-253, 359-401) for `batch` independent
+ * sequences, with the row softmax fused into its two products:
+ *   out = residual + softmax(scale * Q·Kᵀ) · V
+ * with the decoder's causal mask (key j of row i kept for j <= i) when causal
+ * is 1. q, k: [batch][seq][d_qk]; v, residual (may be NULL), out:
+ * [batch][seq][d_v]; all row-major device arrays. scores: caller workspace of
+ * batch*seq*seq floats; stats: caller workspace of
+ * oxf_attention_stats_floats(batch, seq) floats (8-byte aligned). No
+ * allocation. Two forms compute the same result:
+ *  - three launches (the default): scores = scale·Q·Kᵀ, the row softmax in
+ *    place, then P·V + residual; scores then holds the probabilities.
+ *  - fused (environment OXF_ATTENTION=fused, read at every call; rows must
+ *    be 16-byte aligned, else the three launches run): the score product's
+ *    epilogue stores, for each 32-column chunk of a row, exp(logit - chunk
+ *    maximum) into scores (0 where masked) and (chunk maximum, chunk sum)
+ *    into stats; the P·V product reads those values as its A operand and
+ *    scales each tile in shared memory by exp(chunk maximum - row maximum)
+ *    / row sum before the tensor cores read it, so the probabilities are
+ *    never written and no softmax pass runs. On B200 at config 4's widths it
+ *    measured slower than the three launches. */
+size_t oxf_attention_stats_floats(int batch, int seq);
+oxf_status oxf_attention_forward(const float* q, const float* k, const float* v,
+                                 const float* residual, float* out, float* scores, float* stats,
+                                 int batch, int seq, int d_qk, int d_v, float scale, int causal,
+                                 oxf_stream stream);
+
 /* matrix_multiply (module.rs:179-191) with the reference's argument order:
  * result[rows,cols] = lhs[rows,len] · rhs[len,cols], TF32 operands, f32
  * accumulation. The reference asserts rows, cols, len % 16 == 0

@@ -140,6 +140,12 @@ extern "C" {
     pub fn oxf_gemm_workspace_size(d: *const oxf_gemm_desc) -> usize;
     pub fn oxf_gemm(d: *const oxf_gemm_desc, stream: oxf_stream) -> oxf_status;
     pub fn oxf_gemm_tf32x3_noalloc(desc: *const oxf_gemm_desc, stream: oxf_stream) -> oxf_status;
+    pub fn oxf_attention_stats_floats(batch: c_int, seq: c_int) -> usize;
+    pub fn oxf_attention_forward(q: *const f32, k: *const f32, v: *const f32,
+                                 residual: *const f32, out: *mut f32, scores: *mut f32,
+                                 stats: *mut f32, batch: c_int, seq: c_int, d_qk: c_int,
+                                 d_v: c_int, scale: f32, causal: c_int, stream: oxf_stream)
+                                 -> oxf_status;
     pub fn oxf_matrix_multiply(lhs: oxf_cslice, rhs: oxf_cslice, result: oxf_slice, len: usize,
                                rows: usize, cols: usize, stream: oxf_stream) -> oxf_status;
     pub fn oxf_matrix_multiply_fp32(lhs: oxf_cslice, rhs: oxf_cslice, result: oxf_slice,

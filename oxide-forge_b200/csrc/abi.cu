@@ -56,6 +56,9 @@ oxf_status gemm_refalgo(const float*, const float*, float*, size_t, size_t, size
 oxf_status gemm_read_device_error(uint32_t*);
 oxf_status wait_selftest(unsigned long long, int*, cudaStream_t);
 oxf_status gemm_tf32x3_noalloc(const oxf_gemm_desc*, cudaStream_t);
+long long attention_stats_parts(long long);
+oxf_status attention_forward(const float*, const float*, const float*, const float*, float*,
+                             float*, float*, int, int, int, int, float, int, cudaStream_t);
 // exchange.cu
 oxf_status exchange_sgd(const oxf_exchange_desc*, size_t, size_t, float, cudaStream_t);
 oxf_status exchange_read_device_error(uint32_t*);
@@ -462,6 +465,20 @@ oxf_status oxf_gemm_tf32x3_noalloc(const oxf_gemm_desc* d, oxf_stream stream) {
   if (d && (!valid_act(d->act) || !valid_act(d->grad_act)))
     return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm_tf32x3_noalloc: bad activation");
   return gemm_tf32x3_noalloc(d, S(stream));
+}
+
+size_t oxf_attention_stats_floats(int batch, int seq) {
+  if (batch <= 0 || seq <= 0) return 0;
+  return static_cast<size_t>(batch) * static_cast<size_t>(seq) *
+         static_cast<size_t>(attention_stats_parts(seq)) * 2;
+}
+
+oxf_status oxf_attention_forward(const float* q, const float* k, const float* v,
+                                 const float* residual, float* out, float* scores, float* stats,
+                                 int batch, int seq, int d_qk, int d_v, float scale, int causal,
+                                 oxf_stream stream) {
+  return attention_forward(q, k, v, residual, out, scores, stats, batch, seq, d_qk, d_v, scale,
+                           causal, S(stream));
 }
 
 oxf_status oxf_matrix_multiply(oxf_cslice lhs, oxf_cslice rhs, oxf_slice result, size_t len,

@@ -311,6 +311,7 @@ TransformerEngine::TransformerEngine(const TransformerSpec& spec, int max_batch,
   qkv_ = alloc(T * qkvw);
   if (spec_.q.act || spec_.k.act || spec_.v.act) qkv_pre_ = alloc(T * qkvw);
   p_ = alloc(static_cast<size_t>(max_batch) * S * S);
+  stats_ = alloc(oxf_attention_stats_floats(max_batch, S));
   pre_norm_ = alloc(T * H);
   h1_ = alloc(T * H);
   pre2_ = alloc(T * H);
@@ -365,7 +366,6 @@ void TransformerEngine::qkv_project(int batch) {
 }
 
 void TransformerEngine::attention_forward(const float* x, int batch, bool causal, bool training) {
-  (void)training;
   const int S = spec_.seq, H = spec_.hidden, D = spec_.q.out;
   const size_t T = static_cast<size_t>(batch) * S;
   // positioned = input + position (inference.rs:78, encoder.rs:117)
@@ -375,6 +375,21 @@ void TransformerEngine::attention_forward(const float* x, int batch, bool causal
   const float* q = qkv_;
   const float* k = qkv_ + T * D;
   const float* v = qkv_ + 2 * T * D;
+  if (!training) {
+    // pre_norm = positioned + softmax(Q·Kᵀ / sqrt(query.cols)) · V
+    // (attention.rs:243-253, 347-401) through oxf_attention_forward: three
+    // launches by default, the fused form under OXF_ATTENTION=fused (then
+    // p_ holds per-chunk exponentials, not probabilities; inference keeps
+    // nothing for backward).
+    const oxf_status st =
+        oxf_attention_forward(q, k, v, pos_, pre_norm_, p_, stats_, batch, S, D, H,
+                              1.0f / std::sqrt(static_cast<float>(D)), causal ? 1 : 0,
+                              ST(stream_));
+    check(st);
+    check(oxf_norm_rows(cs(pre_norm_, T * H), ms(h1_, T * H), H, spec_.norm, 1e-5f, nullptr,
+                        nullptr, ST(stream_)));
+    return;
+  }
   // scores = Q·Kᵀ / sqrt(query.cols) (attention.rs:359-374), per sequence
   Gemm(S, S, D, false, true, q, k, p_)
       .batch(batch, static_cast<long long>(S) * D, static_cast<long long>(S) * D,
@@ -396,12 +411,16 @@ void TransformerEngine::attention_forward(const float* x, int batch, bool causal
 }
 
 void TransformerEngine::forward(const float* x, int batch, bool causal) {
+  forward_impl(x, batch, causal, false);
+}
+
+void TransformerEngine::forward_impl(const float* x, int batch, bool causal, bool training) {
   TimingScope timing_scope(this);
   require(batch >= 1 && batch <= max_batch_, "transformer: batch outside [1, max_batch]");
   batch_ = batch;
   const int H = spec_.hidden;
   const size_t T = static_cast<size_t>(batch) * spec_.seq;
-  attention_forward(x, batch, causal, false);
+  attention_forward(x, batch, causal, training);
   // ffn + residual (inference.rs:90-101)
   ffn_->forward(h1_, pre2_, T, h1_, stream_);
   check(oxf_norm_rows(cs(pre2_, T * H), ms(enc_, T * H), H, spec_.norm, 1e-5f, nullptr, nullptr,
@@ -414,7 +433,9 @@ void TransformerEngine::forward(const float* x, int batch, bool causal) {
   g.run(stream_);
 }
 
-void TransformerEngine::train_forward(const float* x, int batch) { forward(x, batch, false); }
+void TransformerEngine::train_forward(const float* x, int batch) {
+  forward_impl(x, batch, false, true);
+}
 
 void TransformerEngine::set_target(const float* target) {
   const size_t T = static_cast<size_t>(batch_) * spec_.seq, O = spec_.o.out;

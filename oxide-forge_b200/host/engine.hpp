@@ -181,6 +181,9 @@ class TransformerEngine {
   };
 
  private:
+  void forward_impl(const float* x, int batch, bool causal, bool training);
+  // training: P is kept for backward (three launches); inference: the
+  // softmax is fused into the two products (oxf_attention_forward)
   void attention_forward(const float* x, int batch, bool causal, bool training);
   void qkv_project(int batch);
 
@@ -195,6 +198,7 @@ class TransformerEngine {
   int batch_ = 0;
   // activations
   float *x_ = nullptr, *pos_ = nullptr, *qkv_ = nullptr, *qkv_pre_ = nullptr, *p_ = nullptr;
+  float* stats_ = nullptr;  // softmax row statistics of the fused inference attention
   float *pre_norm_ = nullptr, *h1_ = nullptr, *pre2_ = nullptr, *enc_ = nullptr;
   float *zo_ = nullptr, *y_ = nullptr, *loss_ = nullptr;
   // gradients

@@ -131,6 +131,10 @@ _SIGS = {
     "oxf_gemm_workspace_size": (C.c_size_t, [C.POINTER(GemmDesc)]),
     "oxf_gemm": (C.c_int, [C.POINTER(GemmDesc), C.c_void_p]),
     "oxf_gemm_tf32x3_noalloc": (C.c_int, [C.POINTER(GemmDesc), C.c_void_p]),
+    "oxf_attention_stats_floats": (C.c_size_t, [C.c_int, C.c_int]),
+    "oxf_attention_forward": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                        C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                        C.c_int, C.c_int, C.c_float, C.c_int, C.c_void_p]),
     "oxf_matrix_multiply": (C.c_int, [CSlice, CSlice, Slice, C.c_size_t, C.c_size_t, C.c_size_t,
                                       C.c_void_p]),
     "oxf_matrix_multiply_fp32": (C.c_int, [CSlice, CSlice, Slice, C.c_size_t, C.c_size_t,

@@ -304,6 +304,31 @@ def gemm_workspace_bytes(M, N, K, a_trans=False, b_trans=False, batch=1, batched
     return int(lib().oxf_gemm_workspace_size(C.byref(d)))
 
 
+def attention_stats_floats(batch: int, seq: int) -> int:
+    return int(lib().oxf_attention_stats_floats(int(batch), int(seq)))
+
+
+def attention_forward(q, k, v, out, scores, stats, scale, residual=None, causal=False,
+                      stream=None):
+    """out = residual + softmax(scale * Q·Kᵀ [causal]) · V per sequence
+    (oxf_attention_forward). q, k: [batch, seq, d_qk]; v, out, residual:
+    [batch, seq, d_v]; scores: [batch, seq, seq] workspace; stats:
+    attention_stats_floats(batch, seq) floats of workspace."""
+    batch, seq, dqk = q.shape
+    dv = v.shape[-1]
+    for name, tns in (("q", q), ("k", k), ("v", v), ("out", out), ("scores", scores),
+                      ("stats", stats), ("residual", residual)):
+        if tns is not None:
+            _f32(tns, name)
+    if stats.numel() < attention_stats_floats(batch, seq):
+        raise ValueError("stats workspace too small")
+    check(lib().oxf_attention_forward(q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                      residual.data_ptr() if residual is not None else None,
+                                      out.data_ptr(), scores.data_ptr(), stats.data_ptr(), batch,
+                                      seq, dqk, dv, float(scale), int(causal), _stream(stream)))
+    return out
+
+
 def device_error() -> int:
     code = C.c_uint32(0)
     check(lib().oxf_device_error(C.byref(code)))
