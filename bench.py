@@ -39,11 +39,14 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "oxide-forge_b200"))
 
 SEQ, HIDDEN, FFN, GLOBAL_BATCH, LR = 1024, 2048, 8192, 128, 1e-3
-# DRAM bytes (read + write) of the 18 GEMM launches of one C5 step at N=1,
-# summed from one ncu capture of this bench's step with the metrics
-# dram__bytes_read.sum and dram__bytes_write.sum (86.7 GB read + 29.3 GB
-# written); their compulsory traffic is about 74 GB.
-GEMM_DRAM_BYTES_PER_STEP = 116.0e9
+# DRAM bytes (read + write) of the 18 GEMM launches of one training step on
+# 16 sequences (16384 tokens), each product on the kernel it takes at 128
+# sequences, from single-kernel ncu captures of three launches each on that
+# small step (profiles/launches_train_step_c5.md; 10.67 GB compulsory). The
+# traffic grows with the tokens a rank processes: T tokens move about
+# T / 16384 times this.
+GEMM_DRAM_BYTES_16SEQ = 15.99e9
+GEMM_LAUNCHES_PER_STEP = 18
 METRIC = "Transformer fwd+bwd tokens/s"
 UNIT = "tokens/s"
 
@@ -726,12 +729,15 @@ def run_infer(a, torch):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
     e0, e1 = _events(torch)
     e0.record(stream)
     for _ in range(a.steps):
         model.forward(x)
     e1.record(stream)
     torch.cuda.synchronize()
+    clk = clocks.stop()
     ms = e0.elapsed_time(e1) / a.steps
     if world > 1:
         tt = torch.tensor([ms], device="cuda")
@@ -743,7 +749,7 @@ def run_infer(a, torch):
         print(json.dumps({"metric": "Transformer inference tokens/s",
                           "value": tokens / ms * 1e3, "unit": "tokens/s", "workload": "infer",
                           "n_gpus": world, "ms_per_batch": ms, "scaling": "strong",
-                          "model_tflops": tokens / ms * 1e3 * fpt / 1e12,
+                          "model_tflops": tokens / ms * 1e3 * fpt / 1e12, "clocks": clk,
                           "config": {"workload": "C4 single-head Post-Norm transformer "
                                                  "inference, NormType::Rms",
                                      "seq_len": seq, "hidden": hidden, "ffn": ffn,
@@ -940,10 +946,14 @@ def main():
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
                          "unit": "TFLOP/s",
                          "frac": (achieved / peak) if achieved and peak else None,
-                         "traffic": GEMM_DRAM_BYTES_PER_STEP / 18 if world == 1 else None,
-                         "traffic_note": "DRAM bytes per GEMM launch, mean over the 18 GEMMs "
-                                         "of a step (ncu launch list, profiles/); compulsory "
-                                         "≈74 GB per step = 4.1 GB per launch",
+                         "traffic": (GEMM_DRAM_BYTES_16SEQ * (local_batch * a.seq / 16384)
+                                     / GEMM_LAUNCHES_PER_STEP)
+                                    if (a.seq, a.hidden, a.ffn) == (SEQ, HIDDEN, FFN) else None,
+                         "traffic_note": "DRAM bytes per GEMM launch on this rank, mean over "
+                                         "the 18 GEMMs of a step: single-kernel ncu captures "
+                                         "of a 16-sequence step scaled by the rank's tokens "
+                                         "(profiles/launches_train_step_c5.md); compulsory is "
+                                         "0.67 of it",
                          "kernel": "gemm_tf32_tcgen05 (all GEMMs of a step)",
                          "gemm_launches_per_step": gemm_launches // max(1, a.steps),
                          "gemm_share_of_step": gemm_ms / elapsed_ms if elapsed_ms else None,

@@ -2133,6 +2133,10 @@ oxf_status gemm_run_fused(const oxf_gemm_desc* d, const GemmFuse* fuse, cudaStre
   // tile rows. Both measured the lowest DRAM traffic on the transformer's
   // GEMMs (e.g. 2.0 GB vs 3.5 GB for a 32768 x 8192 x 2048 product).
   a.group_m = a.tiles_n <= 16 ? 1 : 16;
+  if (const char* g = std::getenv("OXF_GEMM_GROUP_M")) {  // measurement override
+    const int v = std::atoi(g);
+    if (v >= 1) a.group_m = std::min(v, a.tiles_m);
+  }
   a.kblocks_item = (d->K + BK - 1) / BK;
   a.kblocks = a.kblocks_item * (a.reduce_batch ? d->batch : 1);
   const long long tiles =
