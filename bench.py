@@ -41,10 +41,10 @@ sys.path.insert(0, str(ROOT / "oxide-forge_b200"))
 SEQ, HIDDEN, FFN, GLOBAL_BATCH, LR = 1024, 2048, 8192, 128, 1e-3
 # DRAM bytes (read + write) of the 18 GEMM launches of one training step on
 # 16 sequences (16384 tokens), each product on the kernel it takes at 128
-# sequences, from single-kernel ncu captures of three launches each on that
-# small step (profiles/launches_train_step_c5.md; 10.67 GB compulsory). The
-# traffic grows with the tokens a rank processes: T tokens move about
-# T / 16384 times this.
+# sequences: ncu captures of dram__bytes_read.sum and dram__bytes_write.sum,
+# one kernel and three launches per capture, on that small step (10.67 GB
+# compulsory). The traffic grows with the tokens a rank processes: T tokens
+# move about T / 16384 times this.
 GEMM_DRAM_BYTES_16SEQ = 15.99e9
 GEMM_LAUNCHES_PER_STEP = 18
 METRIC = "Transformer fwd+bwd tokens/s"
@@ -951,9 +951,8 @@ def main():
                                     if (a.seq, a.hidden, a.ffn) == (SEQ, HIDDEN, FFN) else None,
                          "traffic_note": "DRAM bytes per GEMM launch on this rank, mean over "
                                          "the 18 GEMMs of a step: single-kernel ncu captures "
-                                         "of a 16-sequence step scaled by the rank's tokens "
-                                         "(profiles/launches_train_step_c5.md); compulsory is "
-                                         "0.67 of it",
+                                         "of a 16-sequence step scaled by the rank's tokens; "
+                                         "compulsory is 0.67 of it",
                          "kernel": "gemm_tf32_tcgen05 (all GEMMs of a step)",
                          "gemm_launches_per_step": gemm_launches // max(1, a.steps),
                          "gemm_share_of_step": gemm_ms / elapsed_ms if elapsed_ms else None,

@@ -300,8 +300,8 @@ oxf_status oxf_gemm_tf32x3_noalloc(const oxf_gemm_desc* desc, oxf_stream stream)
  *    into stats; the P·V product reads those values as its A operand and
  *    scales each tile in shared memory by exp(chunk maximum - row maximum)
  *    / row sum before the tensor cores read it, so the probabilities are
- *    never written and no softmax pass runs. On B200 at config 4's widths it
- *    measured slower than the three launches. */
+ *    never written and no softmax pass runs. On B200 at 64 sequences of
+ *    [2048, 1024] it took 3.5 ms against 2.2 ms for the three launches. */
 size_t oxf_attention_stats_floats(int batch, int seq);
 oxf_status oxf_attention_forward(const float* q, const float* k, const float* v,
                                  const float* residual, float* out, float* scores, float* stats,

@@ -111,6 +111,52 @@ __device__ __forceinline__ void pdl_enter() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
+__device__ __forceinline__ void pdl_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Inputs of at most this many bytes per launch are prefetched into L2 before
+// griddepcontrol.wait, so that this kernel's first DRAM reads overlap the
+// previous kernel's last writes. L2 is the GPU's point of coherence, so a
+// line prefetched before the previous kernel writes it is updated there and
+// the loads after the wait read the final data; the cost of such a line is
+// one wasted DRAM read. Larger inputs would only evict each other (and the
+// previous kernel's working set), so they are not prefetched.
+constexpr long long kPrefetchMaxBytes = 64ll << 20;
+
+// Bulk L2 prefetch of one row (16-byte aligned start, bytes % 16 == 0).
+__device__ __forceinline__ void prefetch_l2(const void* p, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// PDL entry of a row kernel with inputs a (and b), [rows, cols] each: the
+// first thread of each row's group prefetches the row of every input when
+// they are small enough, then the kernel waits for its predecessor.
+template <int G>
+__device__ __forceinline__ void row_enter(long long rows, int cols, const float* a,
+                                          const float* b = nullptr) {
+  pdl_launch();
+  const long long bytes = rows * cols * 4ll * (b ? 2 : 1);
+  if (bytes <= kPrefetchMaxBytes) {
+    long long r;
+    int t;
+    if constexpr (G == 32) {
+      r = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+      t = threadIdx.x & 31;
+    } else {
+      r = blockIdx.x;
+      t = threadIdx.x;
+    }
+    if (t == 0 && r < rows) {
+      prefetch_l2(a + r * cols, static_cast<unsigned>(cols) * 4u);
+      if (b) prefetch_l2(b + r * cols, static_cast<unsigned>(cols) * 4u);
+    }
+  }
+  pdl_wait();
+}
+
 __device__ __forceinline__ float hsum(float4 a) { return (a.x + a.y) + (a.z + a.w); }
 __device__ __forceinline__ float hmax(float4 a) { return fmaxf(fmaxf(a.x, a.y), fmaxf(a.z, a.w)); }
 
@@ -132,7 +178,7 @@ __device__ __forceinline__ bool row_index(long long rows, long long& r, int& t) 
 template <int G, int NV>
 __global__ void softmax_fwd_kernel(float* __restrict__ m, long long rows, int cols, float scale,
                                    long long period) {
-  pdl_enter();
+  row_enter<G>(rows, cols, m);
   __shared__ float red[2 * (G / 32)];
   long long r;
   int t;
@@ -181,7 +227,7 @@ __global__ void softmax_fwd_kernel(float* __restrict__ m, long long rows, int co
 template <int G, int NV>
 __global__ void softmax_bwd_kernel(const float* __restrict__ p, const float* __restrict__ dy,
                                    float* __restrict__ dx, long long rows, int cols, float scale) {
-  pdl_enter();
+  row_enter<G>(rows, cols, p, dy);
   __shared__ float red[G / 32];
   long long r;
   int t;
@@ -212,7 +258,7 @@ template <int G, int NV>
 __global__ void layernorm_fwd_kernel(const float* in, float* out, long long rows, int cols,
                                      float eps, const float* __restrict__ gamma,
                                      const float* __restrict__ beta) {
-  pdl_enter();
+  row_enter<G>(rows, cols, in);
   __shared__ float red[2 * (G / 32)];
   // Warp-per-row blocks hold several rows: gamma and beta are staged in
   // shared memory once per block, while the rows' loads are in flight, so
@@ -270,7 +316,7 @@ __global__ void layernorm_fwd_kernel(const float* in, float* out, long long rows
 template <int G, int NV>
 __global__ void layernorm_bwd_kernel(const float* __restrict__ xin, const float* __restrict__ dy,
                                      float* __restrict__ dx, long long rows, int cols, float eps) {
-  pdl_enter();
+  row_enter<G>(rows, cols, xin, dy);
   __shared__ float red[4 * (G / 32)];
   long long r;
   int t;
@@ -322,7 +368,7 @@ __global__ void layernorm_bwd_kernel(const float* __restrict__ xin, const float*
 template <int G, int NV>
 __global__ void rmsnorm_fwd_kernel(const float* in, float* out, long long rows, int cols,
                                    float eps, const float* __restrict__ gamma) {
-  pdl_enter();
+  row_enter<G>(rows, cols, in);
   __shared__ float red[G / 32];
   long long r;
   int t;
@@ -355,7 +401,7 @@ __global__ void rmsnorm_fwd_kernel(const float* in, float* out, long long rows, 
 template <int G, int NV>
 __global__ void rmsnorm_bwd_kernel(const float* __restrict__ xin, const float* __restrict__ dy,
                                    float* __restrict__ dx, long long rows, int cols, float eps) {
-  pdl_enter();
+  row_enter<G>(rows, cols, xin, dy);
   __shared__ float red[2 * (G / 32)];
   long long r;
   int t;
@@ -391,7 +437,7 @@ __global__ void rmsnorm_bwd_kernel(const float* __restrict__ xin, const float* _
 template <int G, int NV>
 __global__ void sum_rows_kernel(const float* __restrict__ m, float* __restrict__ out,
                                 long long rows, int cols) {
-  pdl_enter();
+  row_enter<G>(rows, cols, m);
   __shared__ float red[G / 32];
   long long r;
   int t;
@@ -435,7 +481,7 @@ template <int G, int NV>
 __global__ void loss_grad_rows_kernel(const float* __restrict__ y, const float* __restrict__ tg,
                                       float* __restrict__ out, float* __restrict__ dy,
                                       long long rows, int cols) {
-  pdl_enter();
+  row_enter<G>(rows, cols, y, tg);
   __shared__ float red[G / 32];
   long long r;
   int t;
@@ -628,9 +674,28 @@ template <bool VEC>
 __global__ void elementwise_kernel(int kind, int op, float* __restrict__ out,
                                    const float* __restrict__ a, const float* __restrict__ b,
                                    long long n, float p, long long cols) {
-  pdl_enter();
+  pdl_launch();
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
   long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if constexpr (VEC) {
+    // L2 prefetch of this block's 4 KB pieces of the full-length inputs (see
+    // kPrefetchMaxBytes); a row-vector operand (by-rows kinds) stays in L2
+    // anyway.
+    const float* x_src = (kind == EW_BINARY || kind == EW_BINARY_BCAST || kind == EW_MSE_GRAD)
+                             ? a : out;
+    const float* y_src = (kind == EW_BINARY || kind == EW_BINARY_ASSIGN || kind == EW_SGD ||
+                          kind == EW_MSE_GRAD || kind == EW_MUL_ACT_DERIV) ? b : nullptr;
+    if (threadIdx.x == 0 && n * 4ll * (y_src ? 2 : 1) <= kPrefetchMaxBytes) {
+      const long long n4 = n >> 2;
+      for (long long c = static_cast<long long>(blockIdx.x) * blockDim.x; c < n4; c += stride) {
+        const unsigned bytes =
+            static_cast<unsigned>(min(n4 - c, static_cast<long long>(blockDim.x))) * 16u;
+        prefetch_l2(reinterpret_cast<const float4*>(x_src) + c, bytes);
+        if (y_src) prefetch_l2(reinterpret_cast<const float4*>(y_src) + c, bytes);
+      }
+    }
+  }
+  pdl_wait();
   if constexpr (VEC) {
     const long long n4 = n >> 2;
     for (; i < n4; i += stride) {
