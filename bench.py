@@ -777,7 +777,8 @@ def exchange_selfcheck(torch, dist, rank: int) -> dict:
     p and its own gradients g_r on a ragged 4,206,599-element arena; after
     one exchange over a sub-range and one over the whole arena every rank
     must hold bit-identical parameters equal to p - lr * sum_r g_r up to the
-    summation order (the exchange adds in rank order, NCCL in its own)."""
+    summation order (the exchange adds in rank order, NCCL in its own):
+    max|difference| / max|expected| within 1e-6, about one f32 rounding."""
     from oxf.exchange import PeerExchange
     n, lr = (1 << 22) + 12295, 0.01
     p0 = torch.randn(n, generator=torch.Generator().manual_seed(7)).cuda()
@@ -794,10 +795,10 @@ def exchange_selfcheck(torch, dist, rank: int) -> dict:
     dist.all_reduce(gsum)
     ref = p0 - lr * gsum
     ref[123457:123457 + 400001] -= lr * gsum[123457:123457 + 400001]
-    err = float(((params - ref).abs().max() / (lr * gsum).abs().max()).item())
+    err = float(((params - ref).abs().max() / ref.abs().max()).item())
     return {"arena": n, "max_err_vs_nccl_rel": err, "device_error": code,
             "ranks_bit_identical": rank_agreement(torch, dist, params) == 0.0,
-            "pass": code == 0 and err <= 1e-5}
+            "pass": code == 0 and err <= 1e-6}
 
 
 def main():
