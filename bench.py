@@ -420,6 +420,7 @@ def run_rows(a, torch):
                                  2 * mat),
         "layernorm_bwd": (nothing, lambda: K.layer_norm_backward(x, dy, out), 3 * mat),
         "rmsnorm_fwd": (nothing, lambda: K.norm_rows(x, out, 0), 2 * mat),
+        "rmsnorm_fwd_gamma": (nothing, lambda: K.norm_rows(x, out, 0, 1e-5, gamma), 2 * mat),
         "rmsnorm_bwd": (nothing, lambda: K.rms_norm_backward(x, dy, out), 3 * mat),
         "gelu_fwd": (reset(x), lambda: K.unary(work, 2, 1), 2 * mat),
         "gelu_bwd": (reset(dy), lambda: K.mul_act_derivative(work, x, 1), 3 * mat),
@@ -456,6 +457,7 @@ def run_rows(a, torch):
                                  2 * mat),
         "layernorm_bwd": (lambda i: K.layer_norm_backward(xs[i], dys[i], outs[i]), 3 * mat),
         "rmsnorm_fwd": (lambda i: K.norm_rows(xs[i], outs[i], 0), 2 * mat),
+        "rmsnorm_fwd_gamma": (lambda i: K.norm_rows(xs[i], outs[i], 0, 1e-5, gamma), 2 * mat),
         "rmsnorm_bwd": (lambda i: K.rms_norm_backward(xs[i], dys[i], outs[i]), 3 * mat),
         "gelu_fwd": (lambda i: K.unary(outs[i], 2, 1), 2 * mat),
         "gelu_bwd": (lambda i: K.mul_act_derivative(outs[i], xs[i], 1), 3 * mat),

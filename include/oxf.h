@@ -76,8 +76,12 @@ typedef enum { OXF_NORM_RMS = 0, OXF_NORM_LAYER = 1 } oxf_norm_type;
 /* ---------------------------------------------------------------- status */
 const char* oxf_last_error_string(void);
 /* Reads and clears the device error word that bounded in-kernel waits set
- * (0 = none). Synchronises the current device. */
+ * (0 = none). Synchronises the current device. Codes: 0x101-0x107 GEMM
+ * pipeline waits, 0x1FF the self-test below, OXF_DEVERR_EXCHANGE_START / _END
+ * the exchange barriers, OXF_DEVERR_ROW_PARAMS a norm kernel's gamma / beta
+ * copy into shared memory. */
 oxf_status oxf_device_error(uint32_t* code);
+#define OXF_DEVERR_ROW_PARAMS 0x301u
 /* Failure-detection self-test: a one-thread kernel waits on an mbarrier
  * that nothing completes, bounded by limit_us (1..1e6), exactly as every
  * pipeline wait in this library is bounded. On expiry it writes 1 to the

@@ -18,6 +18,7 @@
 
 #include "common.cuh"
 #include "status.cuh"
+#include "ptx.cuh"
 
 namespace oxf {
 
@@ -157,6 +158,40 @@ __device__ __forceinline__ void row_enter(long long rows, int cols, const float*
   pdl_wait();
 }
 
+// Norm parameters (gamma, beta) of a warp-per-row block, which holds eight
+// rows: staged once per block in shared memory by bulk copies that one
+// thread issues after the PDL wait and that complete on an mbarrier. Each
+// warp waits on that mbarrier only when it applies the parameters, after its
+// row's reductions, so no block barrier sits between a row's loads and its
+// stores; the one barrier, after the mbarrier's initialisation, comes before
+// the PDL wait. The wait is bounded: on expiry it records DEVERR_ROW_PARAMS.
+__device__ __forceinline__ void params_init(uint64_t* bar) {
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+}
+
+// Bulk copy global -> shared (both 16-byte aligned, bytes % 16 == 0).
+__device__ __forceinline__ void bulk_load_smem(void* dst, const void* src, unsigned bytes,
+                                               uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Thread 0 copies cols floats of g (and of b) into sg (sb); null skips one.
+__device__ __forceinline__ void params_issue(uint64_t* bar, float4* sg, const float* g, float4* sb,
+                                             const float* b, int cols) {
+  if (threadIdx.x != 0) return;
+  const unsigned bytes = static_cast<unsigned>(cols) * 4u;
+  mbar_arrive_expect_tx(bar, bytes * ((g ? 1u : 0u) + (b ? 1u : 0u)));
+  if (g) bulk_load_smem(sg, g, bytes, bar);
+  if (b) bulk_load_smem(sb, b, bytes, bar);
+}
+
 __device__ __forceinline__ float hsum(float4 a) { return (a.x + a.y) + (a.z + a.w); }
 __device__ __forceinline__ float hmax(float4 a) { return fmaxf(fmaxf(a.x, a.y), fmaxf(a.z, a.w)); }
 
@@ -254,33 +289,27 @@ __global__ void softmax_bwd_kernel(const float* __restrict__ p, const float* __r
 
 // ------------------------------------------------------------------ LayerNorm
 // row.rs:115-177: mean, biased variance of (x - mean), 1/sqrt(var + eps).
-template <int G, int NV>
-__global__ void layernorm_fwd_kernel(const float* in, float* out, long long rows, int cols,
-                                     float eps, const float* __restrict__ gamma,
-                                     const float* __restrict__ beta) {
-  row_enter<G>(rows, cols, in);
+// STAGED (launched when gamma or beta is given): a warp-per-row block stages
+// them in shared memory (params_issue); the plain kernel carries no staging.
+template <int G, int NV, bool STAGED>
+__device__ __forceinline__ void layernorm_fwd_body(const float* in, float* out, long long rows,
+                                                   int cols, float eps,
+                                                   const float* __restrict__ gamma,
+                                                   const float* __restrict__ beta) {
   __shared__ float red[2 * (G / 32)];
-  // Warp-per-row blocks hold several rows: gamma and beta are staged in
-  // shared memory once per block, while the rows' loads are in flight, so
-  // they are not an L2 round trip on each row's critical path.
-  constexpr int STAGE = G == 32 ? 32 * NV : 1;
-  __shared__ float4 sg[STAGE], sb[STAGE];
+  constexpr bool staged = STAGED && G == 32;
+  constexpr int STAGE = staged ? 32 * NV : 1;
+  __shared__ alignas(16) float4 sg[STAGE], sb[STAGE];
+  __shared__ alignas(8) uint64_t bar;
+  if constexpr (staged) params_init(&bar);
+  row_enter<G>(rows, cols, in);
+  if constexpr (staged) params_issue(&bar, sg, gamma, sb, beta, cols);
   long long r;
   int t;
-  const bool live = row_index<G>(rows, r, t);
+  if (!row_index<G>(rows, r, t)) return;
   const int cols4 = cols >> 2;
   Row<G, NV> x;
-  if (live) x.load(in + r * cols, t, cols4, 0.f);
-  if constexpr (G == 32) {
-    if (gamma || beta) {
-      for (int i = threadIdx.x; i < cols4; i += blockDim.x) {
-        if (gamma) sg[i] = reinterpret_cast<const float4*>(gamma)[i];
-        if (beta) sb[i] = reinterpret_cast<const float4*>(beta)[i];
-      }
-      __syncthreads();
-    }
-  }
-  if (!live) return;
+  x.load(in + r * cols, t, cols4, 0.f);
   float s = 0.f;
 #pragma unroll
   for (int j = 0; j < NV; ++j) s += hsum(x.v[j]);
@@ -295,21 +324,36 @@ __global__ void layernorm_fwd_kernel(const float* in, float* out, long long rows
   }
   v = GroupReduce<G>::sum(v, red + G / 32);
   const float inv_std = 1.0f / sqrtf(v / static_cast<float>(cols) + eps);
+  if constexpr (staged) mbar_wait(&bar, 0, DEVERR_ROW_PARAMS);
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
     if (!Row<G, NV>::active(j, t, cols4)) continue;
     float4& a = x.v[j];
     a.x *= inv_std; a.y *= inv_std; a.z *= inv_std; a.w *= inv_std;
     if (gamma) {
-      const float4 g = G == 32 ? sg[t + j * G] : reinterpret_cast<const float4*>(gamma)[t + j * G];
+      const float4 g = staged ? sg[t + j * G] : reinterpret_cast<const float4*>(gamma)[t + j * G];
       a.x *= g.x; a.y *= g.y; a.z *= g.z; a.w *= g.w;
     }
     if (beta) {
-      const float4 b = G == 32 ? sb[t + j * G] : reinterpret_cast<const float4*>(beta)[t + j * G];
+      const float4 b = staged ? sb[t + j * G] : reinterpret_cast<const float4*>(beta)[t + j * G];
       a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
     }
   }
   x.store(out + r * cols, t, cols4);
+}
+
+template <int G, int NV>
+__global__ void layernorm_fwd_kernel(const float* in, float* out, long long rows, int cols,
+                                     float eps, const float* __restrict__ gamma,
+                                     const float* __restrict__ beta) {
+  layernorm_fwd_body<G, NV, false>(in, out, rows, cols, eps, gamma, beta);
+}
+
+template <int G, int NV>
+__global__ void layernorm_fwd_staged_kernel(const float* in, float* out, long long rows, int cols,
+                                            float eps, const float* __restrict__ gamma,
+                                            const float* __restrict__ beta) {
+  layernorm_fwd_body<G, NV, true>(in, out, rows, cols, eps, gamma, beta);
 }
 
 // row.rs:239-347: dx = inv_std/N * (N*dy - sum(dy) - xhat*sum(dy*xhat)).
@@ -365,11 +409,19 @@ __global__ void layernorm_bwd_kernel(const float* __restrict__ xin, const float*
 
 // ------------------------------------------------------------------ RMSNorm
 // row.rs:349-396: y = x / sqrt(mean(x^2) + eps).
-template <int G, int NV>
-__global__ void rmsnorm_fwd_kernel(const float* in, float* out, long long rows, int cols,
-                                   float eps, const float* __restrict__ gamma) {
-  row_enter<G>(rows, cols, in);
+// STAGED as for LayerNorm (launched when gamma is given).
+template <int G, int NV, bool STAGED>
+__device__ __forceinline__ void rmsnorm_fwd_body(const float* in, float* out, long long rows,
+                                                 int cols, float eps,
+                                                 const float* __restrict__ gamma) {
   __shared__ float red[G / 32];
+  constexpr bool staged = STAGED && G == 32;
+  constexpr int STAGE = staged ? 32 * NV : 1;
+  __shared__ alignas(16) float4 sg[STAGE];
+  __shared__ alignas(8) uint64_t bar;
+  if constexpr (staged) params_init(&bar);
+  row_enter<G>(rows, cols, in);
+  if constexpr (staged) params_issue(&bar, sg, gamma, nullptr, nullptr, cols);
   long long r;
   int t;
   if (!row_index<G>(rows, r, t)) return;
@@ -384,17 +436,30 @@ __global__ void rmsnorm_fwd_kernel(const float* in, float* out, long long rows, 
   }
   s = GroupReduce<G>::sum(s, red);
   const float rms = sqrtf(s / static_cast<float>(cols) + eps);
+  if constexpr (staged) mbar_wait(&bar, 0, DEVERR_ROW_PARAMS);
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
     if (!Row<G, NV>::active(j, t, cols4)) continue;
     float4& a = x.v[j];
     a.x = a.x / rms; a.y = a.y / rms; a.z = a.z / rms; a.w = a.w / rms;
     if (gamma) {
-      const float4 g = reinterpret_cast<const float4*>(gamma)[t + j * G];
+      const float4 g = staged ? sg[t + j * G] : reinterpret_cast<const float4*>(gamma)[t + j * G];
       a.x *= g.x; a.y *= g.y; a.z *= g.z; a.w *= g.w;
     }
   }
   x.store(out + r * cols, t, cols4);
+}
+
+template <int G, int NV>
+__global__ void rmsnorm_fwd_kernel(const float* in, float* out, long long rows, int cols,
+                                   float eps, const float* __restrict__ gamma) {
+  rmsnorm_fwd_body<G, NV, false>(in, out, rows, cols, eps, gamma);
+}
+
+template <int G, int NV>
+__global__ void rmsnorm_fwd_staged_kernel(const float* in, float* out, long long rows, int cols,
+                                          float eps, const float* __restrict__ gamma) {
+  rmsnorm_fwd_body<G, NV, true>(in, out, rows, cols, eps, gamma);
 }
 
 // row.rs:398-468: dx = dy/r - x*(sum(x*dy)/N)/r^3.
@@ -669,6 +734,26 @@ __device__ __forceinline__ float unary_apply(int op, float x, float p) {
 enum EwOp { EW_BINARY, EW_BINARY_ASSIGN, EW_UNARY, EW_SGD, EW_MSE_GRAD, EW_BY_ROWS,
              EW_BINARY_BCAST, EW_MUL_ACT_DERIV };
 
+// In-place activation over float4s, software-pipelined: each thread loads
+// its next float4 before it computes and stores the current one, so the
+// exponential and reciprocal of one piece overlap the load of the next.
+template <int ACT>
+__device__ __forceinline__ void act_forward_pipelined(float4* __restrict__ o, long long i,
+                                                      long long stride, long long n4) {
+  if (i >= n4) return;
+  float4 x = o[i];
+  while (true) {
+    const long long nx = i + stride;
+    float4 xn = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (nx < n4) xn = o[nx];
+    o[i] = make_float4(act_forward_fast(ACT, x.x), act_forward_fast(ACT, x.y),
+                       act_forward_fast(ACT, x.z), act_forward_fast(ACT, x.w));
+    if (nx >= n4) break;
+    x = xn;
+    i = nx;
+  }
+}
+
 // Grid-stride elementwise kernel; VEC processes float4s.
 template <bool VEC>
 __global__ void elementwise_kernel(int kind, int op, float* __restrict__ out,
@@ -698,6 +783,15 @@ __global__ void elementwise_kernel(int kind, int op, float* __restrict__ out,
   pdl_wait();
   if constexpr (VEC) {
     const long long n4 = n >> 2;
+    if (kind == EW_UNARY && op == OXF_UNARY_ACT_FORWARD) {
+      float4* o = reinterpret_cast<float4*>(out);
+      switch (static_cast<int>(p)) {
+        case OXF_ACT_GELU: act_forward_pipelined<OXF_ACT_GELU>(o, i, stride, n4); return;
+        case OXF_ACT_SILU: act_forward_pipelined<OXF_ACT_SILU>(o, i, stride, n4); return;
+        case OXF_ACT_RELU: act_forward_pipelined<OXF_ACT_RELU>(o, i, stride, n4); return;
+        default: break;  // identity: the generic loop below
+      }
+    }
     for (; i < n4; i += stride) {
       float4 x = (kind == EW_BINARY || kind == EW_BINARY_BCAST)
                      ? reinterpret_cast<const float4*>(a)[i]
@@ -964,10 +1058,17 @@ OXF_ROW_LAUNCHER(LnFwdL, layernorm_fwd_kernel,
                  P_(const float* in, float* out, int cols, float eps, const float* g,
                     const float* b),
                  P_(in, out, rows, cols, eps, g, b))
+OXF_ROW_LAUNCHER(LnFwdStagedL, layernorm_fwd_staged_kernel,
+                 P_(const float* in, float* out, int cols, float eps, const float* g,
+                    const float* b),
+                 P_(in, out, rows, cols, eps, g, b))
 OXF_ROW_LAUNCHER(LnBwdL, layernorm_bwd_kernel,
                  P_(const float* x, const float* dy, float* dx, int cols, float eps),
                  P_(x, dy, dx, rows, cols, eps))
 OXF_ROW_LAUNCHER(RmsFwdL, rmsnorm_fwd_kernel,
+                 P_(const float* in, float* out, int cols, float eps, const float* g),
+                 P_(in, out, rows, cols, eps, g))
+OXF_ROW_LAUNCHER(RmsFwdStagedL, rmsnorm_fwd_staged_kernel,
                  P_(const float* in, float* out, int cols, float eps, const float* g),
                  P_(in, out, rows, cols, eps, g))
 OXF_ROW_LAUNCHER(RmsBwdL, rmsnorm_bwd_kernel,
@@ -1040,7 +1141,10 @@ oxf_status rows_layernorm(const float* in, float* out, long long rows, long long
   if (rows == 0 || cols == 0) return OXF_OK;
   oxf_status st = OXF_OK;
   if (al(in) && al(out) && al(g) && al(b) &&
-      dispatch_row<LnFwdL>(rows, cols, s, &st, in, out, static_cast<int>(cols), eps, g, b))
+      ((g || b) ? dispatch_row<LnFwdStagedL>(rows, cols, s, &st, in, out, static_cast<int>(cols),
+                                             eps, g, b)
+                : dispatch_row<LnFwdL>(rows, cols, s, &st, in, out, static_cast<int>(cols), eps,
+                                       g, b)))
     return st;
   return looped(LOOP_LN, out, in, nullptr, rows, cols, eps, 0.f, 0, g, b, s);
 }
@@ -1060,7 +1164,8 @@ oxf_status rows_rmsnorm(const float* in, float* out, long long rows, long long c
   if (rows == 0 || cols == 0) return OXF_OK;
   oxf_status st = OXF_OK;
   if (al(in) && al(out) && al(g) &&
-      dispatch_row<RmsFwdL>(rows, cols, s, &st, in, out, static_cast<int>(cols), eps, g))
+      (g ? dispatch_row<RmsFwdStagedL>(rows, cols, s, &st, in, out, static_cast<int>(cols), eps, g)
+         : dispatch_row<RmsFwdL>(rows, cols, s, &st, in, out, static_cast<int>(cols), eps, g)))
     return st;
   return looped(LOOP_RMS, out, in, nullptr, rows, cols, eps, 0.f, 0, g, nullptr, s);
 }
@@ -1195,6 +1300,17 @@ oxf_status matrix_slice(const float* in, float* out, long long n, long long inpu
   if (n <= 0) return OXF_OK;
   return launch_pdl("matrix_slice_kernel", matrix_slice_kernel, dim3(ew_blocks(n)), dim3(256), s,
                     in, out, n, input_cols, tile_rows, tile_cols, tiles_per_row);
+}
+
+oxf_status rows_read_device_error(uint32_t* code) {
+  uint32_t v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_oxf_device_error, sizeof(v));
+  if (e != cudaSuccess) return check_cuda(e, "read device error word");
+  const uint32_t zero = 0;
+  e = cudaMemcpyToSymbol(g_oxf_device_error, &zero, sizeof(zero));
+  if (e != cudaSuccess) return check_cuda(e, "clear device error word");
+  *code = v;
+  return OXF_OK;
 }
 
 }  // namespace oxf

@@ -38,13 +38,14 @@ enum DeviceErrorCode : uint32_t {
   DEVERR_GEMM_EPI_LOAD = 0x106,
   DEVERR_GEMM_QUEUE = 0x107,  // tile queue (dynamic schedule): entry never published / freed
   DEVERR_WAIT_SELFTEST = 0x1FF,  // oxf_wait_timeout_selftest: the expected expiry
+  DEVERR_ROW_PARAMS = 0x301,  // a norm kernel's gamma/beta copy into shared memory never landed
 };
 
 }  // namespace oxf
 
-// One error word per translation unit that includes this header. Only the
-// GEMM translation unit has waits; it exposes the word through
-// oxf_device_error().
+// One error word per translation unit that includes this header. The GEMM,
+// row-kernel and exchange translation units have bounded waits; each exposes
+// its word to oxf_device_error().
 static __device__ unsigned int g_oxf_device_error = 0;
 
 namespace oxf {

@@ -63,6 +63,7 @@ EXCHANGE_MAX_RANKS = 8
 EXCHANGE_MAX_BLOCKS = 1024
 EXCHANGE_SIGNAL_BYTES = 2 * EXCHANGE_MAX_BLOCKS * EXCHANGE_MAX_RANKS * 4
 DEVERR_EXCHANGE_START, DEVERR_EXCHANGE_END = 0x201, 0x202
+DEVERR_ROW_PARAMS = 0x301
 
 
 class IpcHandle(C.Structure):

@@ -88,6 +88,44 @@ def test_rms_norm_rows(K, rng):
     assert rel_err(host(K.rms_norm_rows(dev(x), 1e-5, dev(g))), O.rms_norm_rows(x, 1e-5, g)) < TOL
 
 
+
+@pytest.mark.parametrize("c", [64, 200, 512, 1000, 2048])
+def test_norm_params_staged_per_block(K, rng, c):
+    """Warp-per-row widths (up to 2048), where a block of eight rows stages
+    gamma and beta in shared memory once: 37 rows leave the last block with
+    five live rows. gamma only, beta only and both, LayerNorm and RMSNorm,
+    out of place and in place; the device error word stays clear."""
+    from oxf import _lib
+    r = 37
+    x = (rng.standard_normal((r, c)) * 2 + 0.5).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(c)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(c)).astype(np.float32)
+    for gg, bb in [(g, b), (g, None), (None, b)]:
+        want = O.layer_norm_rows(x, 1e-5, gg, bb)
+        out = torch.empty((r, c), device="cuda")
+        K.norm_rows(dev(x), out, _lib.NORM_LAYER, 1e-5, None if gg is None else dev(gg),
+                    None if bb is None else dev(bb))
+        assert rel_err(host(out), want) < TOL, (c, gg is None, bb is None)
+        got = host(K.layer_norm_rows(dev(x), 1e-5, None if gg is None else dev(gg),
+                                     None if bb is None else dev(bb)))
+        assert rel_err(got, want) < TOL
+    out = torch.empty((r, c), device="cuda")
+    K.norm_rows(dev(x), out, _lib.NORM_RMS, 1e-5, dev(g))
+    assert rel_err(host(out), O.rms_norm_rows(x, 1e-5, g)) < TOL
+    assert rel_err(host(K.rms_norm_rows(dev(x), 1e-5, dev(g))), O.rms_norm_rows(x, 1e-5, g)) < TOL
+    assert K.device_error() == 0
+
+
+def test_activation_forward_several_pieces_per_thread(K, rng):
+    """In-place activation forward over 700001 float4s, more than the grid
+    covers in one pass, so threads load their next piece before storing the
+    current one and the last pass is ragged; identity takes the generic loop."""
+    n = 4 * 700001
+    a = (3 * rng.standard_normal(n)).astype(np.float32)
+    for act in (O.GELU, O.RELU, O.SILU):
+        assert rel_err(host(K.unary(dev(a), 2, act)), O.act_forward(act, a)) < TOL, act
+    np.testing.assert_array_equal(host(K.unary(dev(a), 2, 0)), a)
+
 def close(got, want, scale, tol=TOL):
     """max|got - want| <= tol * scale, where scale is the magnitude of the
     largest term the formula combines (not of its possibly cancelling
