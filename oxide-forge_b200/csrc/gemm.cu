@@ -827,6 +827,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     ring_init(rg, bufs, &ctrl->epi[(warp - 2) * EPI_NB_MAX]);
     bool ok = true;
     int pf = -1;  // the tile the next chunk's first input is being loaded into
+    // only an epilogue that reads an input tile first looks ahead to prefetch it
+    int la3d = 0;
+    const bool lookahead = args.epi_tma && epi_first_input(args, em, la3d) != nullptr;
     for (int local = 0; ok; ++local) {
       long long u;
       if (dyn) {
@@ -867,16 +870,20 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             break;
           }
           pf = -1;
-          int nb, nm0, nn0;
-          long long u2 = -2;  // the next unit, for its first chunk's input
-          if (dyn) {
-            if (lane == 0) u2 = queue_peek(ctrl, local + 1);
-            u2 = __shfl_sync(0xffffffffu, u2, 0);
-          } else {
-            u2 = static_unit(args, blockIdx.x, gridDim.x, local + 1);
+          if (lookahead) {
+            int nb, nm0, nn0;
+            long long u2 = -2;  // the next unit, needed after the tile's last chunk only
+            if (c + EPI_GROUPS >= BN / 32 || tn * BN + (c + EPI_GROUPS) * 32 >= args.N) {
+              if (dyn) {
+                if (lane == 0) u2 = queue_peek(ctrl, local + 1);
+                u2 = __shfl_sync(0xffffffffu, u2, 0);
+              } else {
+                u2 = static_unit(args, blockIdx.x, gridDim.x, local + 1);
+              }
+            }
+            if (epi_next_chunk<BN>(args, u2, c, group, quarter * 32, b, tn, m0, nb, nm0, nn0))
+              pf = epi_prefetch(args, em, rg, nb, nm0, nn0, lane);
           }
-          if (epi_next_chunk<BN>(args, u2, c, group, quarter * 32, b, tn, m0, nb, nm0, nn0))
-            pf = epi_prefetch(args, em, rg, nb, nm0, nn0, lane);
         } else if (m < args.M) {
           epilogue_chunk(args, b, m, n0, v);
         }
@@ -1267,6 +1274,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     ring_init(rg, bufs, &ctrl->epi[(warp - 2) * EPI_NB_MAX]);
     bool ok = true;
     int pf = -1;  // the tile the next chunk's first input is being loaded into
+    // only an epilogue that reads an input tile first looks ahead to prefetch it
+    int la3d = 0;
+    const bool lookahead = args.epi_tma && epi_first_input(args, em, la3d) != nullptr;
     for (int local = 0; ok; ++local) {
       long long u;
       if (dyn) {
@@ -1308,17 +1318,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
             break;
           }
           pf = -1;
-          int nb, nm0, nn0;
-          long long u2 = -2;  // the next unit, for its first chunk's input
-          if (dyn) {
-            if (lane == 0) u2 = queue_peek(ctrl, local + 1);
-            u2 = __shfl_sync(0xffffffffu, u2, 0);
-          } else {
-            u2 = static_unit(args, cluster_id, nclusters, local + 1);
+          if (lookahead) {
+            int nb, nm0, nn0;
+            long long u2 = -2;  // the next unit, needed after the tile's last chunk only
+            if (c + cstep >= BN / 32 || tn * BN + (c + cstep) * 32 >= args.N) {
+              if (dyn) {
+                if (lane == 0) u2 = queue_peek(ctrl, local + 1);
+                u2 = __shfl_sync(0xffffffffu, u2, 0);
+              } else {
+                u2 = static_unit(args, cluster_id, nclusters, local + 1);
+              }
+            }
+            if (epi_next_chunk<BN>(args, u2, c, group, static_cast<int>(rank) * BM + quarter * 32,
+                                   b, tn, m0, nb, nm0, nn0, cstep))
+              pf = epi_prefetch(args, em, rg, nb, nm0, nn0, lane);
           }
-          if (epi_next_chunk<BN>(args, u2, c, group, static_cast<int>(rank) * BM + quarter * 32,
-                                 b, tn, m0, nb, nm0, nn0, cstep))
-            pf = epi_prefetch(args, em, rg, nb, nm0, nn0, lane);
         } else if (m < args.M) {
           epilogue_chunk(args, b, m, n0, v);
         }
