@@ -2071,6 +2071,18 @@ oxf_status gemm_run_fused(const oxf_gemm_desc* d, const GemmFuse* fuse, cudaStre
                            d->batch;
     if (t256 < sms && !d->accumulate) BN = 128;  // more, smaller tiles when the grid is thin
   }
+  // A plain product: nothing in the epilogue but alpha, so K may be split.
+  const bool plain = !fuse && d->variant == 0 && !split3 && !d->accumulate && split <= 1 &&
+                     d->beta == 0.0f && !d->bias && !d->residual && !d->pre_out && !d->aux &&
+                     d->act == OXF_ACT_IDENTITY && !a.reduce_batch && d->batch == 1;
+  // A small plain product (at most half a wave of 128 x 64 tiles, K <= 1024;
+  // 512^3 has 32) runs on one-CTA 128 x 64 tiles, K split as below: a pair
+  // tile's longer set-up and per-tile drain outweigh its operand savings
+  // there (512^3: 9 against 13 us per call).
+  const bool small_tiles =
+      plain && (d->K + BK - 1) / BK <= 32 &&
+      static_cast<long long>((d->M + BM - 1) / BM) * ((d->N + 63) / 64) * 2 <= sms;
+  if (small_tiles) BN = 64;
   // CTA pairs (256 x 256 tiles, half the L2->SM bytes per flop of a one-CTA
   // tile) whenever there are enough of them to occupy every SM pair;
   // variant 1 forces one CTA, 2 forces pairs.
@@ -2085,17 +2097,13 @@ oxf_status gemm_run_fused(const oxf_gemm_desc* d, const GemmFuse* fuse, cudaStre
                                     (d->reduce_batch ? d->batch : 1) >= 2 * kWideMinKBlocks;
     // A plain product (nothing in the epilogue but alpha) with too few tiles
     // to fill the GPU splits K: C is zeroed and the splits add into it.
-    autosplit = !fuse && d->variant == 0 && !split3 && !d->accumulate && split <= 1 &&
-                d->beta == 0.0f &&
-                !d->bias && !d->residual && !d->pre_out && !d->aux &&
-                d->act == OXF_ACT_IDENTITY && !a.reduce_batch && d->batch == 1 &&
-                d->M >= 2 * BM && tiles2 < (3 * sms / 2) / 4 &&
+    autosplit = plain && d->M >= 2 * BM && tiles2 < (3 * sms / 2) / 4 &&
                 (d->K + BK - 1) / BK >= 16;
     // One partly filled wave of pairs (at least 3/4 of them busy) beats
     // 1.5-2 waves of one-CTA tiles with twice the operand bytes per flop.
     const long long pair_min = (3 * (sms / 2)) / 4;
     pair = fuse != nullptr || d->variant == 2 || d->variant == 3 ||
-           (d->variant == 0 && d->M >= 2 * BM &&
+           (d->variant == 0 && !small_tiles && d->M >= 2 * BM &&
             (tiles2 >= pair_min || splittable || autosplit));
     if (pair) BN = 256;
   }
