@@ -67,6 +67,9 @@ def parse():
     ap.add_argument("--no-overlap", action="store_true",
                     help="train at N>1: exchange gradients after the whole backward pass "
                          "instead of per bucket during it")
+    ap.add_argument("--heads", type=int, default=1,
+                    help="train / infer: attention heads (1: the reference's single-head "
+                         "attention; h > 1 splits Q, K, V into h column slices)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-peak", action="store_true",
@@ -94,8 +97,11 @@ def parse():
 
 
 def config_dict(a, world, l2_note=True):
-    return {"workload": "C5 single-head Post-Norm transformer training step (fwd+bwd+SGD)",
+    heads = getattr(a, "heads", 1)
+    attn = "single-head" if heads == 1 else f"{heads}-head"
+    return {"workload": f"C5 {attn} Post-Norm transformer training step (fwd+bwd+SGD)",
             "model": "oxide-forge transformer block", "seq_len": a.seq, "hidden": a.hidden,
+            **({"heads": heads} if heads != 1 else {}),
             "ffn": a.ffn, "out": a.hidden, "norm": "layer", "global_batch": a.global_batch,
             "tokens_per_step": a.global_batch * a.seq, "parallelism": f"dp{world}",
             "lr": LR, "l2": "inputs larger than L2 (1 GiB activations); no flush needed",
@@ -132,7 +138,7 @@ def cpu_train_sequence(a, threads: int = 0):
     x = rng.standard_normal((a.seq, a.hidden)).astype(np.float32)
     tg = rng.standard_normal((a.seq, a.hidden)).astype(np.float32)
     t0 = time.perf_counter()
-    O.transformer_train_step(t, x, tg, LR, rounding=O.GEMM_TF32_RNA)
+    O.transformer_train_step(t, x, tg, LR, rounding=O.GEMM_TF32_RNA, heads=getattr(a, "heads", 1))
     return time.perf_counter() - t0, n
 
 
@@ -722,7 +728,7 @@ def run_infer(a, torch):
     local = nseq // world
     cfg = models.transformer_config(seq, hidden, ffn, norm=_lib.NORM_RMS)
     stream = torch.cuda.current_stream()
-    model = models.Transformer(cfg, max_batch=local, stream=stream)
+    model = models.Transformer(cfg, max_batch=local, stream=stream, heads=a.heads)
     model.set_params(models.init_transformer_params(cfg, seed=4000))
     g = torch.Generator(device="cuda").manual_seed(4001 + rank)
     x = torch.randn(local * seq, hidden, device="cuda", generator=g)
@@ -752,8 +758,10 @@ def run_infer(a, torch):
                           "value": tokens / ms * 1e3, "unit": "tokens/s", "workload": "infer",
                           "n_gpus": world, "ms_per_batch": ms, "scaling": "strong",
                           "model_tflops": tokens / ms * 1e3 * fpt / 1e12, "clocks": clk,
-                          "config": {"workload": "C4 single-head Post-Norm transformer "
-                                                 "inference, NormType::Rms",
+                          "config": {"workload": ("C4 single-head" if a.heads == 1 else
+                                                  f"C4 {a.heads}-head") +
+                                                 " Post-Norm transformer inference, NormType::Rms",
+                                     **({"heads": a.heads} if a.heads != 1 else {}),
                                      "seq_len": seq, "hidden": hidden, "ffn": ffn,
                                      "sequences": nseq, "parallelism": f"batch-shard {world}"}}),
               flush=True)
@@ -834,7 +842,7 @@ def main():
     cfg = models.transformer_config(a.seq, a.hidden, a.ffn, norm=_lib.NORM_LAYER)
     local_batch = a.global_batch // world
     stream = torch.cuda.current_stream()
-    model = models.Transformer(cfg, max_batch=local_batch, stream=stream)
+    model = models.Transformer(cfg, max_batch=local_batch, stream=stream, heads=a.heads)
     model.set_params(models.init_transformer_params(cfg, seed=0))
     # One GPU has nothing to exchange: the step ends with the plain SGD kernel.
     trainer = DataParallelTrainer(model, a.global_batch, LR, a.seq,
@@ -951,7 +959,8 @@ def main():
                          "frac": (achieved / peak) if achieved and peak else None,
                          "traffic": (GEMM_DRAM_BYTES_16SEQ * (local_batch * a.seq / 16384)
                                      / GEMM_LAUNCHES_PER_STEP)
-                                    if (a.seq, a.hidden, a.ffn) == (SEQ, HIDDEN, FFN) else None,
+                                    if (a.seq, a.hidden, a.ffn, a.heads) == (SEQ, HIDDEN, FFN, 1)
+                                    else None,
                          "traffic_note": "DRAM bytes per GEMM launch on this rank, mean over "
                                          "the 18 GEMMs of a step: single-kernel ncu captures "
                                          "of a 16-sequence step scaled by the rank's tokens; "

@@ -77,7 +77,7 @@ typedef enum { OXF_NORM_RMS = 0, OXF_NORM_LAYER = 1 } oxf_norm_type;
 const char* oxf_last_error_string(void);
 /* Reads and clears the device error word that bounded in-kernel waits set
  * (0 = none). Synchronises the current device. Codes: 0x101-0x107 GEMM
- * pipeline waits, 0x1FF the self-test below, OXF_DEVERR_EXCHANGE_START / _END
+ * pipeline waits, 0x108 the fused multi-head attention's waits, 0x1FF the self-test below, OXF_DEVERR_EXCHANGE_START / _END
  * the exchange barriers, OXF_DEVERR_ROW_PARAMS a norm kernel's gamma / beta
  * copy into shared memory. */
 oxf_status oxf_device_error(uint32_t* code);
@@ -311,6 +311,22 @@ oxf_status oxf_attention_forward(const float* q, const float* k, const float* v,
                                  const float* residual, float* out, float* scores, float* stats,
                                  int batch, int seq, int d_qk, int d_v, float scale, int causal,
                                  oxf_stream stream);
+/* Multi-head attention in one fused kernel: for every head j and sequence,
+ *   out[:, j*w .. (j+1)*w) = residual + softmax(Q_j·K_jᵀ / sqrt(w)) · V_j
+ * where Q_j, K_j, V_j are columns [j*w, (j+1)*w) of q, k, v and
+ * w = d_qk/heads (the head split docs/api.md:440-442 anticipates;
+ * heads = 1 is Attention::forward with query width w). q, k:
+ * [batch][seq][d_qk]; v, residual (may be NULL), out: [batch][seq][d_v].
+ * Each CTA keeps a 128-row query tile's scores in TMEM and runs the softmax
+ * online, so the seq x seq scores are never written: no workspace, no
+ * allocation. heads must divide d_qk and d_v (else INVALID_ARG). Needs
+ * d_qk = d_v, w = 32 or 64, seq a multiple of 128 and 16-byte aligned
+ * matrices; otherwise OXF_ERR_UNSUPPORTED_SHAPE and nothing runs. A stalled
+ * pipeline wait records 0x108 in the device error word. */
+oxf_status oxf_attention_heads_forward(const float* q, const float* k, const float* v,
+                                       const float* residual, float* out, int batch, int seq,
+                                       int d_qk, int d_v, int heads, int causal,
+                                       oxf_stream stream);
 
 /* matrix_multiply (module.rs:179-191) with the reference's argument order:
  * result[rows,cols] = lhs[rows,len] · rhs[len,cols], TF32 operands, f32

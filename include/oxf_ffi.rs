@@ -146,6 +146,10 @@ extern "C" {
                                  stats: *mut f32, batch: c_int, seq: c_int, d_qk: c_int,
                                  d_v: c_int, scale: f32, causal: c_int, stream: oxf_stream)
                                  -> oxf_status;
+    pub fn oxf_attention_heads_forward(q: *const f32, k: *const f32, v: *const f32,
+                                       residual: *const f32, out: *mut f32, batch: c_int,
+                                       seq: c_int, d_qk: c_int, d_v: c_int, heads: c_int,
+                                       causal: c_int, stream: oxf_stream) -> oxf_status;
     pub fn oxf_matrix_multiply(lhs: oxf_cslice, rhs: oxf_cslice, result: oxf_slice, len: usize,
                                rows: usize, cols: usize, stream: oxf_stream) -> oxf_status;
     pub fn oxf_matrix_multiply_fp32(lhs: oxf_cslice, rhs: oxf_cslice, result: oxf_slice,
@@ -179,6 +183,8 @@ extern "C" {
                                   count: *mut usize) -> oxf_status;
     pub fn oxf_transformer_zero_grads(t: *mut c_void) -> oxf_status;
     pub fn oxf_transformer_sgd(t: *mut c_void, lr: f32) -> oxf_status;
+    pub fn oxf_transformer_set_heads(t: *mut c_void, heads: c_int) -> oxf_status;
+    pub fn oxf_transformer_heads(t: *mut c_void) -> c_int;
     pub fn oxf_transformer_output(t: *mut c_void, y: *mut *const f32, row_loss: *mut *const f32,
                                   input_gradient: *mut *const f32) -> oxf_status;
     pub fn oxf_transformer_set_timing(t: *mut c_void, on: c_int) -> oxf_status;

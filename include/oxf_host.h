@@ -93,6 +93,16 @@ oxf_status oxf_transformer_zero_grads(oxf_transformer t);
 /* params -= lr * grads (the reference's per-Linear SGD, linear.rs:373-391,
  * and position update, encoder.rs:180-184, applied once). */
 oxf_status oxf_transformer_sgd(oxf_transformer t, float lr);
+/* Attention heads (default 1: the reference's single-head attention,
+ * attention.rs:359-401). Head j attends over columns [j*D/h, (j+1)*D/h) of Q
+ * and K and [j*H/h, (j+1)*H/h) of V with scale 1/sqrt(D/h) and writes those
+ * columns of the attention output; the projections and all other layers
+ * are unchanged (the multi-head path docs/api.md:440-442 anticipates). h
+ * must divide the query width D and hidden H (INVALID_ARG otherwise); the
+ * score buffers grow to h per sequence. Takes effect from the next forward.
+ * The checkpoint format has no head count: a loaded engine has one head. */
+oxf_status oxf_transformer_set_heads(oxf_transformer t, int heads);
+int oxf_transformer_heads(oxf_transformer t);
 /* Device views of the last output [batch*seq, out], per-row loss
  * [batch*seq] and input gradient [batch*seq, hidden]. */
 oxf_status oxf_transformer_output(oxf_transformer t, const float** y, const float** row_loss,

@@ -312,6 +312,14 @@ def _define_structs(h):
         "oxo_transformer_train_step": (None, [C.POINTER(Transformer), fp, fp, fp, fp, fp,
                                               C.c_float, fp, C.c_int]),
         "oxo_transformer_param_count": (C.c_size_t, [C.POINTER(Transformer)]),
+        "oxo_transformer_forward_heads": (None, [C.POINTER(Transformer), fp, fp, C.c_int,
+                                                 C.c_int, C.c_int]),
+        "oxo_transformer_train_step_heads": (None, [C.POINTER(Transformer), fp, fp, fp, fp, fp,
+                                                    C.c_float, fp, C.c_int, C.c_int]),
+        "oxo_attention_forward_heads": (None, [fp, fp, fp, fp, fp, C.c_size_t, C.c_size_t,
+                                               C.c_size_t, C.c_size_t, C.c_int, C.c_int]),
+        "oxo_attention_backward_heads": (None, [fp, fp, fp, fp, fp, fp, fp, fp, C.c_size_t,
+                                                C.c_size_t, C.c_size_t, C.c_size_t, C.c_int]),
     }
     for name, (res, args) in sigs.items():
         f = getattr(h, name)
@@ -414,23 +422,58 @@ class TransformerParams:
         return copy.deepcopy(self)
 
 
-def transformer_forward(t: TransformerParams, x, causal=False, rounding=GEMM_F32):
+def transformer_forward(t: TransformerParams, x, causal=False, rounding=GEMM_F32, heads=1):
+    """Inference forward of one sequence; heads > 1 splits the attention
+    into that many heads (oxo_attention_forward_heads)."""
     x = _c(x)
     y = np.empty((t.seq, t.o.w.shape[1]), F32)
     s, keep = t.struct()
-    lib().oxo_transformer_forward(C.byref(s), _p(x), _p(y), int(causal), rounding)
+    if heads == 1:
+        lib().oxo_transformer_forward(C.byref(s), _p(x), _p(y), int(causal), rounding)
+    else:
+        lib().oxo_transformer_forward_heads(C.byref(s), _p(x), _p(y), int(causal), rounding,
+                                            int(heads))
     return y
 
 
-def transformer_train_step(t: TransformerParams, x, target, lr, grads=None, rounding=GEMM_F32):
+def transformer_train_step(t: TransformerParams, x, target, lr, grads=None, rounding=GEMM_F32,
+                           heads=1):
     """One reference training step on one sequence. Returns (y, row_loss, dx).
     If `grads` (flat, cursor order) is given, parameter gradients are added
-    to it."""
+    to it. heads > 1: multi-head attention."""
     x, target = _c(x), _c(target)
     y = np.empty((t.seq, t.o.w.shape[1]), F32)
     loss = np.empty(t.seq, F32)
     dx = np.empty_like(x)
     s, keep = t.struct()
-    lib().oxo_transformer_train_step(C.byref(s), _p(x), _p(target), _p(y), _p(loss), _p(dx), lr,
-                                     _p(grads) if grads is not None else None, rounding)
+    g = _p(grads) if grads is not None else None
+    if heads == 1:
+        lib().oxo_transformer_train_step(C.byref(s), _p(x), _p(target), _p(y), _p(loss), _p(dx),
+                                         lr, g, rounding)
+    else:
+        lib().oxo_transformer_train_step_heads(C.byref(s), _p(x), _p(target), _p(y), _p(loss),
+                                               _p(dx), lr, g, rounding, int(heads))
     return y, loss, dx
+
+
+def attention_heads(q, k, v, heads, causal=False, rounding=GEMM_F32):
+    """The attention core alone: (att [S, Hv], P [heads, S, S])."""
+    q, k, v = _c(q), _c(k), _c(v)
+    S, D = q.shape
+    Hv = v.shape[1]
+    att = np.empty((S, Hv), F32)
+    p = np.empty((heads, S, S), F32)
+    lib().oxo_attention_forward_heads(_p(q), _p(k), _p(v), _p(p), _p(att), S, D, Hv, heads,
+                                      int(causal), rounding)
+    return att, p
+
+
+def attention_heads_backward(q, k, v, p, dr, heads, rounding=GEMM_F32):
+    """Gradients (dq, dk, dv) of the attention core given dL/d(att) = dr."""
+    q, k, v, p, dr = _c(q), _c(k), _c(v), _c(p), _c(dr)
+    S, D = q.shape
+    Hv = v.shape[1]
+    dq, dk, dv = np.empty_like(q), np.empty_like(k), np.empty_like(v)
+    lib().oxo_attention_backward_heads(_p(q), _p(k), _p(v), _p(p), _p(dr), _p(dq), _p(dk),
+                                       _p(dv), S, D, Hv, heads, rounding)
+    return dq, dk, dv

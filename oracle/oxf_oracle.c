@@ -678,10 +678,88 @@ static void norm_backward(int norm, const float* x, const float* dy, float* dx, 
         oxo_rms_norm_backward(x, dy, dx, rows, cols, 1e-5f);
 }
 
+/* Columns [c0, c0 + w) of a row-major [rows, ld] matrix, as a contiguous
+ * [rows, w] copy, and the reverse. */
+static float* gather_cols(const float* m, size_t rows, size_t ld, size_t c0, size_t w) {
+    float* out = falloc(rows * w);
+    for (size_t r = 0; r < rows; ++r) memcpy(out + r * w, m + r * ld + c0, w * sizeof(float));
+    return out;
+}
+
+static void scatter_cols(const float* src, float* m, size_t rows, size_t ld, size_t c0, size_t w) {
+    for (size_t r = 0; r < rows; ++r) memcpy(m + r * ld + c0, src + r * w, w * sizeof(float));
+}
+
+/* Attention core with `heads` heads. The reference is single-head
+ * (attention.rs:359-401: scores = Q·Kᵀ scaled by 1/sqrt(query.cols),
+ * softmax rows, P·V) and anticipates a multi-head path that keeps the
+ * projections and changes only "the projected-matrix head layout and
+ * per-head score calculation" (docs/api.md:440-442). Head j takes columns
+ * [j·D/h, (j+1)·D/h) of Q and K and [j·Hv/h, (j+1)·Hv/h) of V, scales its
+ * scores by 1/sqrt(D/h), and writes its output into the same columns of
+ * `att` [S, Hv]; heads = 1 is the reference's attention. p_keep (may be
+ * NULL): [heads, S, S] probabilities, kept for backward. */
+void oxo_attention_forward_heads(const float* q, const float* k, const float* v, float* p_keep,
+                                 float* att, size_t S, size_t D, size_t Hv, size_t heads,
+                                 int causal, int rounding) {
+    const size_t dq = D / heads, dv = Hv / heads;
+    const float scale = 1.0f / sqrtf((float)dq);
+    for (size_t j = 0; j < heads; ++j) {
+        float* qj = gather_cols(q, S, D, j * dq, dq);
+        float* kj = gather_cols(k, S, D, j * dq, dq);
+        float* vj = gather_cols(v, S, Hv, j * dv, dv);
+        float* sc = p_keep ? p_keep + j * S * S : falloc(S * S);
+        /* scores, then the scale (attention.rs:366-372, 398) */
+        oxo_gemm_mt(qj, kj, sc, S, S, dq, 0, 1, rounding, 1.0f, 0.0f);
+        for (size_t i = 0; i < S * S; ++i) sc[i] *= scale;
+        if (causal) oxo_causal_mask(sc, S, S, S);
+        oxo_softmax_rows(sc, S, S, 1.0f, 0);
+        float* aj = falloc(S * dv);
+        oxo_gemm_mt(sc, vj, aj, S, dv, S, 0, 0, rounding, 1.0f, 0.0f);
+        scatter_cols(aj, att, S, Hv, j * dv, dv);
+        free(qj); free(kj); free(vj); free(aj);
+        if (!p_keep) free(sc);
+    }
+}
+
+/* Backward of the core (Attention::backward_self, attention.rs:297-308),
+ * head by head: dP = dR·Vᵀ, dV = Pᵀ·dR, dS = softmax'(P, dP)·scale,
+ * dQ = dS·K, dK = dSᵀ·Q, each in its head's columns. dr: [S, Hv]. */
+void oxo_attention_backward_heads(const float* q, const float* k, const float* v,
+                                  const float* p, const float* dr, float* dq, float* dk,
+                                  float* dv, size_t S, size_t D, size_t Hv, size_t heads,
+                                  int rounding) {
+    const size_t hq = D / heads, hv = Hv / heads;
+    const float scale = 1.0f / sqrtf((float)hq);
+    for (size_t j = 0; j < heads; ++j) {
+        float* qj = gather_cols(q, S, D, j * hq, hq);
+        float* kj = gather_cols(k, S, D, j * hq, hq);
+        float* vj = gather_cols(v, S, Hv, j * hv, hv);
+        float* drj = gather_cols(dr, S, Hv, j * hv, hv);
+        const float* pj = p + j * S * S;
+        float* dp = falloc(S * S);
+        oxo_gemm_mt(drj, vj, dp, S, S, hv, 0, 1, rounding, 1.0f, 0.0f);  /* dR·Vᵀ */
+        float* dvj = falloc(S * hv);
+        oxo_gemm_mt(pj, drj, dvj, S, hv, S, 1, 0, rounding, 1.0f, 0.0f); /* Pᵀ·dR */
+        float* ds = falloc(S * S);
+        oxo_softmax_backward(pj, dp, ds, S, S, 1.0f);
+        for (size_t i = 0; i < S * S; ++i) ds[i] *= scale; /* attention.rs:304 */
+        float* dqj = falloc(S * hq);
+        oxo_gemm_mt(ds, kj, dqj, S, hq, S, 0, 0, rounding, 1.0f, 0.0f);  /* dS·K */
+        float* dkj = falloc(S * hq);
+        oxo_gemm_mt(ds, qj, dkj, S, hq, S, 1, 0, rounding, 1.0f, 0.0f);  /* dSᵀ·Q */
+        scatter_cols(dqj, dq, S, D, j * hq, hq);
+        scatter_cols(dkj, dk, S, D, j * hq, hq);
+        scatter_cols(dvj, dv, S, Hv, j * hv, hv);
+        free(qj); free(kj); free(vj); free(drj); free(dp); free(dvj); free(ds); free(dqj);
+        free(dkj);
+    }
+}
+
 /* InferenceBlock::forward / forward_mask (inference.rs:76-109) with
  * Attention::forward (attention.rs:221-253, 336-387). */
-void oxo_transformer_forward(const oxo_transformer* t, const float* x, float* y, int causal,
-                             int rounding) {
+void oxo_transformer_forward_heads(const oxo_transformer* t, const float* x, float* y,
+                                   int causal, int rounding, int heads) {
     const size_t S = t->seq, H = t->hidden;
     float* pos = falloc(S * H);
     oxo_binary(x, t->position, pos, S * H, OXO_ADD);
@@ -692,14 +770,10 @@ void oxo_transformer_forward(const oxo_transformer* t, const float* x, float* y,
     oxo_linear_forward(&t->k, pos, NULL, k, NULL, S, rounding);
     oxo_linear_forward(&t->v, pos, NULL, v, NULL, S, rounding);
     const size_t D = t->q.out;
-    float* sc = falloc(S * S);
-    /* scores = Q·Kᵀ, then scale 1/sqrt(query.cols) (attention.rs:366-372) */
-    oxo_gemm_mt(q, k, sc, S, S, D, 0, 1, rounding, 1.0f, 0.0f);
-    for (size_t i = 0; i < S * S; ++i) sc[i] *= 1.0f / sqrtf((float)D);
-    if (causal) oxo_causal_mask(sc, S, S, S);
-    oxo_softmax_rows(sc, S, S, 1.0f, 0);
+    /* softmax(Q·Kᵀ / sqrt(query.cols))·V per head (attention.rs:359-401) */
     float* att = falloc(S * t->v.out);
-    oxo_gemm_mt(sc, v, att, S, t->v.out, S, 0, 0, rounding, 1.0f, 0.0f);
+    oxo_attention_forward_heads(q, k, v, NULL, att, S, D, t->v.out, (size_t)heads, causal,
+                                rounding);
     float* h1 = falloc(S * H);
     oxo_binary(pos, att, h1, S * H, OXO_ADD); /* attention.rs:249 */
     norm_forward(t->norm, h1, S, H);
@@ -710,7 +784,12 @@ void oxo_transformer_forward(const oxo_transformer* t, const float* x, float* y,
     oxo_binary(h1, ffn, h2, S * H, OXO_ADD); /* inference.rs:99 */
     norm_forward(t->norm, h2, S, H);
     oxo_linear_forward(&t->o, h2, NULL, y, NULL, S, rounding);
-    free(pos); free(q); free(k); free(v); free(sc); free(att); free(h1); free(ffn); free(h2);
+    free(pos); free(q); free(k); free(v); free(att); free(h1); free(ffn); free(h2);
+}
+
+void oxo_transformer_forward(const oxo_transformer* t, const float* x, float* y, int causal,
+                             int rounding) {
+    oxo_transformer_forward_heads(t, x, y, causal, rounding, 1);
 }
 
 size_t oxo_transformer_param_count(const oxo_transformer* t) {
@@ -728,11 +807,11 @@ size_t oxo_transformer_param_count(const oxo_transformer* t) {
 /* TrainingTransformer::forward + backward, encoder.rs:114-186, with
  * Attention::forward_self_training / backward_self (attention.rs:258-321)
  * and QkvProjection::backward_self (attention.rs:104-144). */
-void oxo_transformer_train_step(oxo_transformer* t, const float* x, const float* target,
-                                float* y, float* row_loss, float* dx, float lr, float* grads,
-                                int rounding) {
+void oxo_transformer_train_step_heads(oxo_transformer* t, const float* x, const float* target,
+                                      float* y, float* row_loss, float* dx, float lr,
+                                      float* grads, int rounding, int heads) {
     const size_t S = t->seq, H = t->hidden, D = t->q.out, O = t->o.out;
-    const float scale = 1.0f / sqrtf((float)D);
+    const size_t nh = (size_t)heads;
     /* gradient slots in cursor order */
     float *g_q = NULL, *g_qb = NULL, *g_k = NULL, *g_kb = NULL, *g_v = NULL, *g_vb = NULL;
     float *g_pos = NULL, *g_o = NULL, *g_ob = NULL;
@@ -763,12 +842,9 @@ void oxo_transformer_train_step(oxo_transformer* t, const float* x, const float*
     oxo_linear_forward(&t->q, pos, NULL, q, q_pre, S, rounding);
     oxo_linear_forward(&t->k, pos, NULL, k, k_pre, S, rounding);
     oxo_linear_forward(&t->v, pos, NULL, v, v_pre, S, rounding);
-    float* p = falloc(S * S);
-    oxo_gemm_mt(q, k, p, S, S, D, 0, 1, rounding, 1.0f, 0.0f);
-    for (size_t i = 0; i < S * S; ++i) p[i] *= scale; /* attention.rs:398 */
-    oxo_softmax_rows(p, S, S, 1.0f, 0);
+    float* p = falloc(nh * S * S); /* kept for backward (attention.rs:183-190) */
     float* att = falloc(S * t->v.out);
-    oxo_gemm_mt(p, v, att, S, t->v.out, S, 0, 0, rounding, 1.0f, 0.0f);
+    oxo_attention_forward_heads(q, k, v, p, att, S, D, t->v.out, nh, 0, rounding);
     float* pre_norm = falloc(S * H);
     oxo_binary(pos, att, pre_norm, S * H, OXO_ADD);
     float* h1 = fdup(pre_norm, S * H);
@@ -804,17 +880,10 @@ void oxo_transformer_train_step(oxo_transformer* t, const float* x, const float*
     /* Attention::backward_self */
     float* dr = falloc(S * H);
     norm_backward(t->norm, pre_norm, d1, dr, S, H);
-    float* dp = falloc(S * S);
-    oxo_gemm_mt(dr, v, dp, S, S, t->v.out, 0, 1, rounding, 1.0f, 0.0f);     /* dR·Vᵀ */
-    float* dv = falloc(S * t->v.out);
-    oxo_gemm_mt(p, dr, dv, S, t->v.out, S, 1, 0, rounding, 1.0f, 0.0f);     /* Pᵀ·dR */
-    float* ds = falloc(S * S);
-    oxo_softmax_backward(p, dp, ds, S, S, 1.0f);
-    for (size_t i = 0; i < S * S; ++i) ds[i] *= scale; /* attention.rs:304 */
     float* dq = falloc(S * D);
-    oxo_gemm_mt(ds, k, dq, S, D, S, 0, 0, rounding, 1.0f, 0.0f);            /* dS·K */
     float* dk = falloc(S * t->k.out);
-    oxo_gemm_mt(ds, q, dk, S, t->k.out, S, 1, 0, rounding, 1.0f, 0.0f);     /* dSᵀ·Q */
+    float* dv = falloc(S * t->v.out);
+    oxo_attention_backward_heads(q, k, v, p, dr, dq, dk, dv, S, D, t->v.out, nh, rounding);
     float* dpos = fdup(dr, S * H);
     {
         oxo_linear* ls[3] = {&t->q, &t->k, &t->v};
@@ -841,6 +910,12 @@ void oxo_transformer_train_step(oxo_transformer* t, const float* x, const float*
     free(tape); free(g_fw); free(g_fb);
     free(pos); free(q); free(k); free(v); free(q_pre); free(k_pre); free(v_pre); free(p);
     free(att); free(pre_norm); free(h1); free(ffn); free(pre2); free(enc); free(o_pre); free(dy);
-    free(g_out); free(d_enc); free(d2); free(d_ffn_in); free(d1); free(dr); free(dp); free(dv);
-    free(ds); free(dq); free(dk); free(dpos);
+    free(g_out); free(d_enc); free(d2); free(d_ffn_in); free(d1); free(dr); free(dv);
+    free(dq); free(dk); free(dpos);
+}
+
+void oxo_transformer_train_step(oxo_transformer* t, const float* x, const float* target,
+                                float* y, float* row_loss, float* dx, float lr, float* grads,
+                                int rounding) {
+    oxo_transformer_train_step_heads(t, x, target, y, row_loss, dx, lr, grads, rounding, 1);
 }

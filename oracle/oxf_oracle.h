@@ -199,6 +199,23 @@ void oxo_transformer_train_step(oxo_transformer* t, const float* x, const float*
 /* Number of f32 parameters in cursor order (inference.rs:52-66). */
 size_t oxo_transformer_param_count(const oxo_transformer* t);
 
+/* Attention core with `heads` heads (heads = 1: the reference's
+ * attention.rs:359-401; see oxf_oracle.c). q, k: [S, D]; v, att, dr, dv:
+ * [S, Hv]; p: [heads, S, S]; D and Hv divisible by heads. */
+void oxo_attention_forward_heads(const float* q, const float* k, const float* v, float* p_keep,
+                                 float* att, size_t S, size_t D, size_t Hv, size_t heads,
+                                 int causal, int rounding);
+void oxo_attention_backward_heads(const float* q, const float* k, const float* v,
+                                  const float* p, const float* dr, float* dq, float* dk,
+                                  float* dv, size_t S, size_t D, size_t Hv, size_t heads,
+                                  int rounding);
+/* oxo_transformer_forward / _train_step with multi-head attention. */
+void oxo_transformer_forward_heads(const oxo_transformer* t, const float* x, float* y,
+                                   int causal, int rounding, int heads);
+void oxo_transformer_train_step_heads(oxo_transformer* t, const float* x, const float* target,
+                                      float* y, float* row_loss, float* dx, float lr,
+                                      float* grads, int rounding, int heads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -60,6 +60,8 @@ oxf_status gemm_tf32x3_noalloc(const oxf_gemm_desc*, cudaStream_t);
 long long attention_stats_parts(long long);
 oxf_status attention_forward(const float*, const float*, const float*, const float*, float*,
                              float*, float*, int, int, int, int, float, int, cudaStream_t);
+oxf_status attention_heads_forward(const float*, const float*, const float*, const float*, float*,
+                                   int, int, int, int, int, int, cudaStream_t);
 // exchange.cu
 oxf_status exchange_sgd(const oxf_exchange_desc*, size_t, size_t, float, cudaStream_t);
 oxf_status exchange_read_device_error(uint32_t*);
@@ -481,6 +483,14 @@ oxf_status oxf_attention_forward(const float* q, const float* k, const float* v,
                                  oxf_stream stream) {
   return attention_forward(q, k, v, residual, out, scores, stats, batch, seq, d_qk, d_v, scale,
                            causal, S(stream));
+}
+
+oxf_status oxf_attention_heads_forward(const float* q, const float* k, const float* v,
+                                       const float* residual, float* out, int batch, int seq,
+                                       int d_qk, int d_v, int heads, int causal,
+                                       oxf_stream stream) {
+  return attention_heads_forward(q, k, v, residual, out, batch, seq, d_qk, d_v, heads, causal,
+                                 S(stream));
 }
 
 oxf_status oxf_matrix_multiply(oxf_cslice lhs, oxf_cslice rhs, oxf_slice result, size_t len,

@@ -2456,6 +2456,363 @@ oxf_status gemm_tf32x3_noalloc(const oxf_gemm_desc* d, cudaStream_t stream) {
   return gemm_run(&desc, stream);
 }
 
+// ---------------------------------------------------------------- fused multi-head attention
+// Multi-head attention forward in one kernel, FlashAttention-style: for a
+// 128-row query tile of one head of one sequence, the scores of each
+// 128-row key/value tile go to TMEM, the softmax runs online in registers
+// (running row maximum and sum, the accumulated output rescaled when the
+// maximum grows), the probabilities are written to shared memory as the A
+// operand of the P·V product, and the output accumulates in TMEM. The S x S
+// score matrix never reaches HBM. Head j reads columns [j*HD, (j+1)*HD) of
+// Q, K and V; out = residual + softmax(Q_j K_jᵀ / sqrt(HD)) V_j in the same
+// columns (attention.rs:359-401 per head; docs/api.md:440-442 anticipates the
+// head split). Warp 0 issues the TMA loads, warp 1 the MMAs, warps 2-5 run
+// the softmax, one query row per thread. Every wait is bounded.
+constexpr int FA_ROWS = 128;
+constexpr int FA_THREADS = 192;
+
+struct FaArgs {
+  float* out;             // [batch * seq, ldo]
+  const float* residual;  // the same layout, or null
+  long long ldo;
+  int seq, tiles;         // tiles = seq / 128
+  int causal;
+  float scale;            // 1 / sqrt(HD)
+};
+
+template <int HD>
+struct FaCfg {
+  static constexpr int KB = HD / 32;                    // 32-column blocks of a Q / K row
+  static constexpr int Q_BYTES = KB * 16384;            // [128 x HD], K-major, 128B swizzle
+  static constexpr int K_BYTES = KB * 16384;            // [128 keys x HD], K-major
+  static constexpr int V_KBLOCK = (HD / 32) * 4096;     // 32 keys x HD, MN-major
+  static constexpr int V_BYTES = 4 * V_KBLOCK;          // 128 keys
+  static constexpr int P_BYTES = 4 * 16384;             // [128 x 128 keys], K-major
+  static constexpr int CTRL_BYTES = 1024;
+  static constexpr int SMEM_BYTES =
+      1024 + CTRL_BYTES + Q_BYTES + 2 * (K_BYTES + V_BYTES) + P_BYTES;
+  static constexpr uint32_t TMEM_COLS = 512;            // S x 2 (256 columns) + O (HD)
+  static constexpr uint32_t O_COL = 256;
+  static_assert(HD == 32 || HD == 64, "head widths 32 and 64");
+  static_assert(SMEM_BYTES <= 232448, "shared memory");
+};
+
+struct FaCtrl {
+  uint64_t q_full;
+  uint64_t kv_full[2], kv_empty[2];  // K and V tile ring
+  uint64_t s_full[2], s_free[2];     // score buffers in TMEM
+  uint64_t p_ready, pv_done;         // P in shared memory, O rescaled / P·V finished
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(FA_THREADS, 1)
+    attention_heads_flash_kernel(const __grid_constant__ CUtensorMap tmQ,
+                                 const __grid_constant__ CUtensorMap tmK,
+                                 const __grid_constant__ CUtensorMap tmV, const FaArgs args) {
+  using Cfg = FaCfg<HD>;
+  extern __shared__ __align__(1024) uint8_t fa_smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fa_smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  auto* ctrl = reinterpret_cast<FaCtrl*>(base);
+  uint8_t* qs = base + Cfg::CTRL_BYTES;
+  uint8_t* ks = qs + Cfg::Q_BYTES;      // two stages
+  uint8_t* vs = ks + 2 * Cfg::K_BYTES;  // two stages
+  uint8_t* ps = vs + 2 * Cfg::V_BYTES;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x, head = blockIdx.y, seq_i = blockIdx.z;
+  const int n_tiles = args.causal ? qt + 1 : args.tiles;
+  const int q_row0 = seq_i * args.seq + qt * FA_ROWS;  // first query row of the tile
+  const int kv_row0 = seq_i * args.seq;
+  const int col0 = head * HD;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&ctrl->q_full, 1);
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&ctrl->kv_full[s], 1);
+      mbar_init(&ctrl->kv_empty[s], 1);
+      mbar_init(&ctrl->s_full[s], 1);
+      mbar_init(&ctrl->s_free[s], 4);  // one arrive per softmax warp
+    }
+    mbar_init(&ctrl->p_ready, 4);
+    mbar_init(&ctrl->pv_done, 1);
+    ctrl->abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(&ctrl->tmem_base, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctrl->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol = make_l2_policy(L2_NORMAL);
+      mbar_arrive_expect_tx(&ctrl->q_full, Cfg::Q_BYTES);
+#pragma unroll
+      for (int kb = 0; kb < Cfg::KB; ++kb)
+        tma_load_2d(qs + kb * 16384, &tmQ, &ctrl->q_full, col0 + kb * 32, q_row0, pol);
+      int fills = 0;
+      for (int t = 0; t < n_tiles && !ctrl->abort_flag; ++t) {
+        const int st = t & 1;
+        if (t >= 2 && !mbar_wait(&ctrl->kv_empty[st], ((t - 2) >> 1) & 1, DEVERR_ATTN_WAIT)) {
+          ctrl->abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&ctrl->kv_full[st], Cfg::K_BYTES + Cfg::V_BYTES);
+        const int kv0 = kv_row0 + t * FA_ROWS;
+#pragma unroll
+        for (int kb = 0; kb < Cfg::KB; ++kb)
+          tma_load_2d(ks + st * Cfg::K_BYTES + kb * 16384, &tmK, &ctrl->kv_full[st],
+                      col0 + kb * 32, kv0, pol);
+#pragma unroll
+        for (int kb = 0; kb < 4; ++kb)
+          load_operand<HD>(vs + st * Cfg::V_BYTES + kb * Cfg::V_KBLOCK, &tmV, &ctrl->kv_full[st],
+                           1, 0, HD > 32 ? 1 : 0, col0, kv0 + kb * 32, 0, pol);
+        ++fills;
+      }
+      // no copy may still be landing when the CTA exits
+      mbar_wait(&ctrl->q_full, 0, DEVERR_ATTN_WAIT);
+      for (int t = fills > 2 ? fills - 2 : 0; t < fills; ++t)
+        mbar_wait(&ctrl->kv_full[t & 1], (t >> 1) & 1, DEVERR_ATTN_WAIT);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_s = make_idesc_tf32(128, 128, false, false);
+      constexpr uint32_t id_o = make_idesc_tf32(128, HD, false, true);
+      const uint32_t q_addr = smem_u32(qs), k_addr = smem_u32(ks), v_addr = smem_u32(vs),
+                     p_addr = smem_u32(ps);
+      // O += P·V for tile t, once its probabilities are in shared memory
+      auto issue_pv = [&](int t) -> bool {
+        if (!mbar_wait(&ctrl->p_ready, t & 1, DEVERR_ATTN_WAIT)) return false;
+        tc_fence_after();
+        const int st = t & 1;
+#pragma unroll
+        for (int kb = 0; kb < 4; ++kb)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_tf32(tmem + Cfg::O_COL,
+                      desc_advance(operand_desc(p_addr + kb * 16384, 0, 0), kk * 32),
+                      desc_advance(operand_desc(v_addr + st * Cfg::V_BYTES + kb * Cfg::V_KBLOCK,
+                                                1, 0),
+                                   kk * 1024),
+                      id_o, (t > 0 || kb > 0 || kk > 0) ? 1u : 0u);
+        // the stage's release first: once pv_done completes, no arrive is pending
+        umma_commit(&ctrl->kv_empty[st]);
+        umma_commit(&ctrl->pv_done);
+        return true;
+      };
+      bool ok = mbar_wait(&ctrl->q_full, 0, DEVERR_ATTN_WAIT);
+      for (int t = 0; ok && t < n_tiles; ++t) {
+        const int st = t & 1;
+        ok = mbar_wait(&ctrl->kv_full[st], (t >> 1) & 1, DEVERR_ATTN_WAIT) &&
+             (t < 2 || mbar_wait(&ctrl->s_free[st], ((t - 2) >> 1) & 1, DEVERR_ATTN_WAIT));
+        if (!ok) break;
+        tc_fence_after();
+        // S[st] = Q·K_tᵀ (the scale is applied in the softmax)
+#pragma unroll
+        for (int kb = 0; kb < Cfg::KB; ++kb)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_tf32(tmem + st * 128,
+                      desc_advance(operand_desc(q_addr + kb * 16384, 0, 0), kk * 32),
+                      desc_advance(operand_desc(k_addr + st * Cfg::K_BYTES + kb * 16384, 0, 0),
+                                   kk * 32),
+                      id_s, (kb > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&ctrl->s_full[st]);
+        // the previous tile's P·V runs while the softmax works on this one
+        if (t > 0) ok = issue_pv(t - 1);
+      }
+      if (ok) ok = issue_pv(n_tiles - 1);
+      if (!ok) ctrl->abort_flag = 1;
+    }
+  } else {
+    // softmax warps: thread r of the tile owns query row r = TMEM lane r
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t row_tmem = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    float m = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int t = 0; t < n_tiles; ++t) {
+      const int st = t & 1;
+      if (!mbar_wait(&ctrl->s_full[st], (t >> 1) & 1, DEVERR_ATTN_WAIT)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float v[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(row_tmem + st * 128 + c * 32, v[c]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctrl->s_free[st]);
+      // scaled scores; on the diagonal tile of a causal pass, key j > row r is masked
+      const bool diag = args.causal && t == qt;
+      float mt = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float x = v[c][j] * args.scale;
+          if (diag && c * 32 + j > r) x = -INFINITY;
+          v[c][j] = x;
+          mt = fmaxf(mt, x);
+        }
+      const float m_new = fmaxf(m, mt);
+      const float alpha = __expf(m - m_new);  // 0 on the first tile
+      float sum = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float p = __expf(v[c][j] - m_new);
+          v[c][j] = p;
+          sum += p;
+        }
+      l = l * alpha + sum;
+      m = m_new;
+      if (t > 0) {
+        // the previous P·V has finished: P is free and O holds tiles 0..t-1
+        if (!mbar_wait(&ctrl->pv_done, (t - 1) & 1, DEVERR_ATTN_WAIT)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+          for (int c = 0; c < HD / 32; ++c) {
+            float o[32];
+            tmem_ld_32x32b_x32(row_tmem + Cfg::O_COL + c * 32, o);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) o[j] *= alpha;
+            tmem_st_32x32b_x32(row_tmem + Cfg::O_COL + c * 32, o);
+          }
+          tmem_st_wait();
+        }
+      }
+      // P row into shared memory: K-major, 128B swizzle, 32 keys per block
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          *stage_unit(ps + c * 16384, r, j) =
+              make_float4(v[c][4 * j], v[c][4 * j + 1], v[c][4 * j + 2], v[c][4 * j + 3]);
+      fence_proxy_async_smem();  // generic writes, read next by the tensor cores
+      tc_fence_before();         // the O rescale's TMEM stores
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctrl->p_ready);
+    }
+    if (ok) ok = mbar_wait(&ctrl->pv_done, (n_tiles - 1) & 1, DEVERR_ATTN_WAIT);
+    if (ok) {
+      tc_fence_after();
+      const float inv = 1.0f / l;
+      const long long row = q_row0 + r;
+      float* orow = args.out + row * args.ldo + col0;
+      const float* rrow = args.residual ? args.residual + row * args.ldo + col0 : nullptr;
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        float o[32];
+        tmem_ld_32x32b_x32(row_tmem + Cfg::O_COL + c * 32, o);
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          float4 y = make_float4(o[j] * inv, o[j + 1] * inv, o[j + 2] * inv, o[j + 3] * inv);
+          if (rrow) {
+            const float4 x = *reinterpret_cast<const float4*>(rrow + c * 32 + j);
+            y.x += x.x; y.y += x.y; y.z += x.z; y.w += x.w;
+          }
+          *reinterpret_cast<float4*>(orow + c * 32 + j) = y;
+        }
+      }
+    } else {
+      ctrl->abort_flag = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
+}
+
+template <int HD>
+oxf_status launch_attention_heads(const CUtensorMap& tq, const CUtensorMap& tk,
+                                  const CUtensorMap& tv, const FaArgs& args, int batch, int heads,
+                                  cudaStream_t stream, int dev) {
+  using Cfg = FaCfg<HD>;
+  static unsigned long long configured[kMaxDevices] = {0};
+  const unsigned long long ctx = current_context_id();
+  if (dev >= 0 && dev < kMaxDevices && (ctx == 0 || configured[dev] != ctx)) {
+    cudaError_t e = cudaFuncSetAttribute(attention_heads_flash_kernel<HD>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(attention)");
+    configured[dev] = ctx;
+  }
+  dim3 grid(static_cast<unsigned>(args.tiles), static_cast<unsigned>(heads),
+            static_cast<unsigned>(batch));
+  attention_heads_flash_kernel<HD><<<grid, FA_THREADS, Cfg::SMEM_BYTES, stream>>>(tq, tk, tv,
+                                                                                  args);
+  return check_launch("attention_heads_flash_kernel");
+}
+
+// out[:, j*HD..] = residual + softmax(Q_j K_jᵀ / sqrt(HD)) V_j for every
+// head j of every sequence, in one launch. q, k: [batch*seq, dqk]; v, out,
+// residual: [batch*seq, dv]; HD = dqk/heads = dv/heads. UNSUPPORTED_SHAPE
+// (nothing launched) unless HD is 32 or 64, seq is a multiple of 128 and
+// every matrix is 16-byte aligned.
+oxf_status attention_heads_forward(const float* q, const float* k, const float* v,
+                                   const float* residual, float* out, int batch, int seq,
+                                   int dqk, int dv, int heads, int causal, cudaStream_t stream) {
+  if (batch < 0 || seq < 0 || dqk < 0 || dv < 0 || heads < 1)
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_attention_heads_forward: bad shape");
+  if (batch == 0 || seq == 0 || dv == 0) return OXF_OK;
+  if (!q || !k || !v || !out)
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_attention_heads_forward: null pointer");
+  if (dqk % heads || dv % heads)
+    return set_error(OXF_ERR_INVALID_ARG,
+                     "oxf_attention_heads_forward: heads must divide d_qk and d_v");
+  const int hd = dqk / heads;
+  if (dv / heads != hd || (hd != 32 && hd != 64) || seq % FA_ROWS != 0 || batch > 65535 ||
+      heads > 65535 ||
+      !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) ||
+      (residual && !aligned16(residual)))
+    return set_error(OXF_ERR_UNSUPPORTED_SHAPE,
+                     "oxf_attention_heads_forward: needs equal query and value head widths of "
+                     "32 or 64, seq a multiple of 128 and 16-byte aligned matrices");
+  const long long rows = static_cast<long long>(batch) * seq;
+  CUtensorMap tq, tk, tv;
+  int is3d = 0;
+  bool ok = encode_map(&tq, q, dqk, rows, dqk, 1, 0, 32, FA_ROWS, false, &is3d) &&
+            encode_map(&tk, k, dqk, rows, dqk, 1, 0, 32, FA_ROWS, false, &is3d) &&
+            encode_map(&tv, v, dv, rows, dv, 1, 0, 32, hd, true, &is3d);
+  if (!ok) return set_error(OXF_ERR_CUDA, "oxf_attention_heads_forward: tensor map encode failed");
+  FaArgs a;
+  a.out = out;
+  a.residual = residual;
+  a.ldo = dv;
+  a.seq = seq;
+  a.tiles = seq / FA_ROWS;
+  a.causal = causal ? 1 : 0;
+  a.scale = 1.0f / std::sqrt(static_cast<float>(hd));
+  int dev = 0;
+  oxf_status st = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  if (st != OXF_OK) return st;
+  return hd == 32 ? launch_attention_heads<32>(tq, tk, tv, a, batch, heads, stream, dev)
+                  : launch_attention_heads<64>(tq, tk, tv, a, batch, heads, stream, dev);
+}
+
 oxf_status gemm_refalgo(const float* A, const float* B, float* C, size_t len, size_t rows,
                         size_t cols, cudaStream_t stream) {
   if (rows % 16 || cols % 16 || len % 16)

@@ -37,6 +37,7 @@ enum DeviceErrorCode : uint32_t {
   DEVERR_GEMM_DRAIN = 0x105,
   DEVERR_GEMM_EPI_LOAD = 0x106,
   DEVERR_GEMM_QUEUE = 0x107,  // tile queue (dynamic schedule): entry never published / freed
+  DEVERR_ATTN_WAIT = 0x108,  // fused multi-head attention: a pipeline wait expired
   DEVERR_WAIT_SELFTEST = 0x1FF,  // oxf_wait_timeout_selftest: the expected expiry
   DEVERR_ROW_PARAMS = 0x301,  // a norm kernel's gamma/beta copy into shared memory never landed
 };

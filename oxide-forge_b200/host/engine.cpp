@@ -276,6 +276,35 @@ void MlpEngine::backward(const float* dy, float* dx, size_t rows, const float* e
 // ================================================================ TransformerEngine
 float* TransformerEngine::alloc(size_t n) { return dev_alloc(n, allocs_); }
 
+void TransformerEngine::release(float* p) {
+  if (!p) return;
+  for (size_t i = 0; i < allocs_.size(); ++i)
+    if (allocs_[i] == p) {
+      cudaFree(p);
+      allocs_.erase(allocs_.begin() + static_cast<long>(i));
+      return;
+    }
+}
+
+void TransformerEngine::set_heads(int h) {
+  const int S = spec_.seq, H = spec_.hidden, D = spec_.q.out;
+  require(h >= 1 && D % h == 0 && H % h == 0,
+          "transformer: heads must divide the query width and hidden");
+  if (h > score_heads_) {
+    // per-head probabilities of every sequence, [heads, batch, S, S]
+    check_cuda_call(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+    const size_t n = static_cast<size_t>(h) * max_batch_ * S * S;
+    float* p = alloc(n);
+    float* dp = alloc(n);
+    release(p_);
+    release(dp_);
+    p_ = p;
+    dp_ = dp;
+    score_heads_ = h;
+  }
+  heads_ = h;
+}
+
 TransformerEngine::TransformerEngine(const TransformerSpec& spec, int max_batch,
                                      cudaStream_t stream)
     : spec_(spec), max_batch_(max_batch), stream_(stream) {
@@ -375,6 +404,12 @@ void TransformerEngine::attention_forward(const float* x, int batch, bool causal
   const float* q = qkv_;
   const float* k = qkv_ + T * D;
   const float* v = qkv_ + 2 * T * D;
+  if (heads_ > 1) {
+    attention_heads_forward(batch, causal, training);
+    check(oxf_norm_rows(cs(pre_norm_, T * H), ms(h1_, T * H), H, spec_.norm, 1e-5f, nullptr,
+                        nullptr, ST(stream_)));
+    return;
+  }
   if (!training) {
     // pre_norm = positioned + softmax(Q·Kᵀ / sqrt(query.cols)) · V
     // (attention.rs:243-253, 347-401) through oxf_attention_forward: three
@@ -408,6 +443,86 @@ void TransformerEngine::attention_forward(const float* x, int batch, bool causal
   // Post-Norm (Normalization::forward, attention.rs:157-162)
   check(oxf_norm_rows(cs(pre_norm_, T * H), ms(h1_, T * H), H, spec_.norm, 1e-5f, nullptr,
                       nullptr, ST(stream_)));
+}
+
+// Multi-head core: for each head j, a batched product over the sequences
+// on column slices of Q, K, V (leading dimensions D and H, offsets j*hq and
+// j*hv); the probabilities of head j occupy p_[j*batch*S*S, ...), so one
+// softmax launch covers every head's rows. P·V adds the positioned input of
+// the head's columns as the residual (attention.rs:249).
+void TransformerEngine::attention_heads_forward(int batch, bool causal, bool training) {
+  const int S = spec_.seq, H = spec_.hidden, D = spec_.q.out, h = heads_;
+  const int hq = D / h, hv = H / h;
+  const size_t T = static_cast<size_t>(batch) * S;
+  const float* q = qkv_;
+  const float* k = qkv_ + T * D;
+  const float* v = qkv_ + 2 * T * D;
+  if (!training) {
+    // one fused launch: the scores stay on chip (head widths 32 / 64)
+    const oxf_status st = oxf_attention_heads_forward(q, k, v, pos_, pre_norm_, batch, S, D, H,
+                                                      h, causal ? 1 : 0, ST(stream_));
+    if (st != OXF_ERR_UNSUPPORTED_SHAPE) {
+      check(st);
+      return;
+    }
+  }
+  const long long sSS = static_cast<long long>(S) * S, sSD = static_cast<long long>(S) * D,
+                  sSH = static_cast<long long>(S) * H, head = static_cast<long long>(batch) * sSS;
+  for (int j = 0; j < h; ++j)
+    Gemm(S, S, hq, false, true, q + j * hq, k + j * hq, p_ + j * head)
+        .ld(D, D, S)
+        .batch(batch, sSD, sSD, sSS)
+        .alpha(1.0f / std::sqrt(static_cast<float>(hq)))
+        .run(stream_);
+  check(oxf_matrix_softmax_rows(ms(p_, static_cast<size_t>(h) * head), S, 1.0f,
+                                causal ? S : 0, ST(stream_)));
+  for (int j = 0; j < h; ++j)
+    Gemm(S, hv, S, false, false, p_ + j * head, v + j * hv, pre_norm_ + j * hv)
+        .ld(S, H, H)
+        .batch(batch, sSS, sSH, sSH)
+        .residual(pos_ + j * hv, H, sSH)
+        .run(stream_);
+}
+
+// Backward of the multi-head core into dqkv_ (Attention::backward_self,
+// attention.rs:297-308, per head): dP = dR·Vᵀ, dV = Pᵀ·dR, dS =
+// softmax'(P, dP)/sqrt(hq) for every head in one launch, dQ = dS·K,
+// dK = dSᵀ·Q, each written into the head's columns.
+void TransformerEngine::attention_heads_backward(int batch) {
+  const int S = spec_.seq, H = spec_.hidden, D = spec_.q.out, h = heads_;
+  const int hq = D / h, hv = H / h;
+  const size_t T = static_cast<size_t>(batch) * S;
+  const float* q = qkv_;
+  const float* k = qkv_ + T * D;
+  const float* v = qkv_ + 2 * T * D;
+  float* dq = dqkv_;
+  float* dk = dqkv_ + T * D;
+  float* dv = dqkv_ + 2 * T * D;
+  const long long sSS = static_cast<long long>(S) * S, sSD = static_cast<long long>(S) * D,
+                  sSH = static_cast<long long>(S) * H, head = static_cast<long long>(batch) * sSS;
+  for (int j = 0; j < h; ++j) {
+    Gemm(S, S, hv, false, true, dr_ + j * hv, v + j * hv, dp_ + j * head)
+        .ld(H, H, S)
+        .batch(batch, sSH, sSH, sSS)
+        .run(stream_);
+    Gemm(S, hv, S, true, false, p_ + j * head, dr_ + j * hv, dv + j * hv)
+        .ld(S, H, H)
+        .batch(batch, sSS, sSH, sSH)
+        .run(stream_);
+  }
+  const size_t rows = static_cast<size_t>(h) * T;
+  check(oxf_softmax_rows_backward(cs(p_, rows * S), cs(dp_, rows * S), ms(dp_, rows * S), S,
+                                  1.0f / std::sqrt(static_cast<float>(hq)), ST(stream_)));
+  for (int j = 0; j < h; ++j) {
+    Gemm(S, hq, S, false, false, dp_ + j * head, k + j * hq, dq + j * hq)
+        .ld(S, D, D)
+        .batch(batch, sSS, sSD, sSD)
+        .run(stream_);
+    Gemm(S, hq, S, true, false, dp_ + j * head, q + j * hq, dk + j * hq)
+        .ld(S, D, D)
+        .batch(batch, sSS, sSD, sSD)
+        .run(stream_);
+  }
 }
 
 void TransformerEngine::forward(const float* x, int batch, bool causal) {
@@ -500,15 +615,19 @@ void TransformerEngine::backward_stage(int stage) {
                     sSD = static_cast<long long>(S) * D;
     check(oxf_norm_rows_backward(cs(pre_norm_, T * H), cs(d1_, T * H), ms(dr_, T * H), H,
                                  spec_.norm, 1e-5f, ST(stream_)));
-    // dP = dR·Vᵀ, dV = Pᵀ·dR (attention.rs:297-300)
-    Gemm(S, S, H, false, true, dr_, v, dp_).batch(batch, sSH, sSH, sSS).run(stream_);
-    Gemm(S, H, S, true, false, p_, dr_, dv).batch(batch, sSS, sSH, sSH).run(stream_);
-    // dS = softmax'(P, dP) / sqrt(d) (attention.rs:302-304), in place
-    check(oxf_softmax_rows_backward(cs(p_, T * S), cs(dp_, T * S), ms(dp_, T * S), S,
-                                    1.0f / std::sqrt(static_cast<float>(D)), ST(stream_)));
-    // dQ = dS·K, dK = dSᵀ·Q (attention.rs:306-308)
-    Gemm(S, D, S, false, false, dp_, k, dq).batch(batch, sSS, sSD, sSD).run(stream_);
-    Gemm(S, D, S, true, false, dp_, q, dk).batch(batch, sSS, sSD, sSD).run(stream_);
+    if (heads_ > 1) {
+      attention_heads_backward(batch);
+    } else {
+      // dP = dR·Vᵀ, dV = Pᵀ·dR (attention.rs:297-300)
+      Gemm(S, S, H, false, true, dr_, v, dp_).batch(batch, sSH, sSH, sSS).run(stream_);
+      Gemm(S, H, S, true, false, p_, dr_, dv).batch(batch, sSS, sSH, sSH).run(stream_);
+      // dS = softmax'(P, dP) / sqrt(d) (attention.rs:302-304), in place
+      check(oxf_softmax_rows_backward(cs(p_, T * S), cs(dp_, T * S), ms(dp_, T * S), S,
+                                      1.0f / std::sqrt(static_cast<float>(D)), ST(stream_)));
+      // dQ = dS·K, dK = dSᵀ·Q (attention.rs:306-308)
+      Gemm(S, D, S, false, false, dp_, k, dq).batch(batch, sSS, sSD, sSD).run(stream_);
+      Gemm(S, D, S, true, false, dp_, q, dk).batch(batch, sSS, sSD, sSD).run(stream_);
+    }
     // QkvProjection::backward_self (attention.rs:104-144)
     const LayerSpec* ls[3] = {&spec_.q, &spec_.k, &spec_.v};
     const size_t offs[3] = {off_q_, off_k_, off_v_};

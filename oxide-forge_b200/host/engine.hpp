@@ -169,6 +169,14 @@ class TransformerEngine {
   void zero_grads();
   // params -= lr * grads (Linear::learn, linear.rs:373-391, applied once).
   void sgd(float lr);
+  // Attention heads (1, the reference's single-head attention, by default).
+  // Head j attends over columns [j*D/h, (j+1)*D/h) of Q and K and
+  // [j*H/h, (j+1)*H/h) of V with scale 1/sqrt(D/h), writing those columns
+  // of the attention output; the projections and every other layer are
+  // unchanged. h must divide the query width D and hidden H. Takes effect
+  // from the next forward; the score buffers grow to h per sequence.
+  void set_heads(int h);
+  int heads() const { return heads_; }
   // GEMM event timing (off by default).
   void set_timing(bool on) { timing_ = on; }
   void read_timing(double* ms, double* flops, int* launches) { timer_.read(ms, flops, launches); }
@@ -185,6 +193,11 @@ class TransformerEngine {
   // training: P is kept for backward (three launches); inference: the
   // softmax is fused into the two products (oxf_attention_forward)
   void attention_forward(const float* x, int batch, bool causal, bool training);
+  // the core with heads_ > 1: in inference the fused kernel
+  // (oxf_attention_heads_forward) where it applies, else per-head batched
+  // products over column slices (training keeps P for backward)
+  void attention_heads_forward(int batch, bool causal, bool training);
+  void attention_heads_backward(int batch);
   void qkv_project(int batch);
 
   TransformerSpec spec_;
@@ -204,8 +217,11 @@ class TransformerEngine {
   // gradients
   float *dy_ = nullptr, *denc_ = nullptr, *d2_ = nullptr, *d1_ = nullptr, *dr_ = nullptr;
   float *dp_ = nullptr, *dqkv_ = nullptr, *dpos_ = nullptr;
+  int heads_ = 1;
+  int score_heads_ = 1;  // heads the p_ / dp_ buffers are sized for
   std::vector<void*> allocs_;
   float* alloc(size_t n);
+  void release(float* p);  // frees one of allocs_
   bool timing_ = false;
   GemmTimer timer_;
 };

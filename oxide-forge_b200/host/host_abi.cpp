@@ -249,6 +249,13 @@ oxf_status oxf_transformer_sgd(oxf_transformer t, float lr) {
   return guard([&] { t->engine->sgd(lr); });
 }
 
+oxf_status oxf_transformer_set_heads(oxf_transformer t, int heads) {
+  if (!t) return oxf::set_error(OXF_ERR_INVALID_ARG, "null argument");
+  return guard([&] { t->engine->set_heads(heads); });
+}
+
+int oxf_transformer_heads(oxf_transformer t) { return t ? t->engine->heads() : 0; }
+
 oxf_status oxf_transformer_output(oxf_transformer t, const float** y, const float** row_loss,
                                   const float** input_gradient) {
   if (!t) return oxf::set_error(OXF_ERR_INVALID_ARG, "null argument");

@@ -41,6 +41,8 @@ SIGS: dict = {
     "oxf_transformer_bucket": (C.c_int, [_h, C.c_int, C.POINTER(_sz), C.POINTER(_sz)]),
     "oxf_transformer_zero_grads": (C.c_int, [_h]),
     "oxf_transformer_sgd": (C.c_int, [_h, C.c_float]),
+    "oxf_transformer_set_heads": (C.c_int, [_h, C.c_int]),
+    "oxf_transformer_heads": (C.c_int, [_h]),
     "oxf_transformer_output": (C.c_int, [_h, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
                                          C.POINTER(C.c_void_p)]),
     "oxf_transformer_train_step_host": (C.c_int, [_h, _fp, _fp, C.c_int, C.c_float,

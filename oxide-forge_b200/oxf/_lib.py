@@ -136,6 +136,9 @@ _SIGS = {
     "oxf_attention_forward": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                         C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
                                         C.c_int, C.c_int, C.c_float, C.c_int, C.c_void_p]),
+    "oxf_attention_heads_forward": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                              C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                              C.c_int, C.c_int, C.c_void_p]),
     "oxf_matrix_multiply": (C.c_int, [CSlice, CSlice, Slice, C.c_size_t, C.c_size_t, C.c_size_t,
                                       C.c_void_p]),
     "oxf_matrix_multiply_fp32": (C.c_int, [CSlice, CSlice, Slice, C.c_size_t, C.c_size_t,

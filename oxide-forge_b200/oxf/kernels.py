@@ -329,6 +329,22 @@ def attention_forward(q, k, v, out, scores, stats, scale, residual=None, causal=
     return out
 
 
+def attention_heads_forward(q, k, v, out, heads, residual=None, causal=False, stream=None):
+    """Multi-head attention in one fused kernel (oxf_attention_heads_forward):
+    out[..., j*w:(j+1)*w] = residual + softmax(Q_j·K_jᵀ/sqrt(w))·V_j, w =
+    d/heads. q, k: [batch, seq, d_qk]; v, out, residual: [batch, seq, d_v]."""
+    batch, seq, dqk = q.shape
+    dv = v.shape[-1]
+    for name, tns in (("q", q), ("k", k), ("v", v), ("out", out), ("residual", residual)):
+        if tns is not None:
+            _f32(tns, name)
+    check(lib().oxf_attention_heads_forward(q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                            residual.data_ptr() if residual is not None else None,
+                                            out.data_ptr(), batch, seq, dqk, dv, int(heads),
+                                            int(causal), _stream(stream)))
+    return out
+
+
 def device_error() -> int:
     code = C.c_uint32(0)
     check(lib().oxf_device_error(C.byref(code)))

@@ -147,7 +147,8 @@ def split_params(cfg, flat: np.ndarray) -> list:
 class Transformer:
     """Batched single-block Post-Norm transformer (inference + training)."""
 
-    def __init__(self, cfg: TransformerConfig, max_batch: int = 1, stream=None, _handle=None):
+    def __init__(self, cfg: TransformerConfig, max_batch: int = 1, stream=None, _handle=None,
+                 heads: int = 1):
         self.cfg = cfg
         self.max_batch = max_batch
         if stream is None:
@@ -162,6 +163,8 @@ class Transformer:
         self._h = h
         self.n = int(lib().oxf_transformer_param_count(h))
         assert self.n == cfg.param_count(), (self.n, cfg.param_count())
+        if heads != 1:
+            self.set_heads(heads)
         self.params = device_view(lib().oxf_transformer_params(h), (self.n,), self)
         self.grads = device_view(lib().oxf_transformer_grads(h), (self.n,), self)
 
@@ -228,6 +231,15 @@ class Transformer:
 
     def sgd(self, lr: float) -> None:
         check(lib().oxf_transformer_sgd(self._h, float(lr)))
+
+    def set_heads(self, heads: int) -> None:
+        """Multi-head attention (oxf_transformer_set_heads); 1 is the
+        reference's single-head attention."""
+        check(lib().oxf_transformer_set_heads(self._h, int(heads)))
+
+    @property
+    def heads(self) -> int:
+        return int(lib().oxf_transformer_heads(self._h))
 
     def train_step_host(self, x: np.ndarray, target: np.ndarray, lr: float) -> float:
         """The e2e API: host arrays in, one SGD step, mean row loss out."""

@@ -165,6 +165,87 @@ def test_inference_forward(M, causal):
     eng.close()
 
 
+MH_CASES = [
+    # seq, hidden, ffn, norm, bias, heads
+    (32, 64, 128, 1, False, 2),
+    (64, 128, 256, 0, True, 4),
+    (32, 128, 256, 1, False, 16),   # 8-wide heads
+    (16, 48, 96, 1, True, 8),       # 6-wide heads: column slices TMA cannot describe
+]
+
+
+@pytest.mark.parametrize("seq,hidden,ffn,norm,bias,heads", MH_CASES)
+def test_multi_head_training_step(M, seq, hidden, ffn, norm, bias, heads):
+    """Multi-head attention (oxf_transformer_set_heads): B = 2 sequences
+    through one training step against the oracle's per-head restatement
+    (oxo_transformer_train_step_heads), gradients summed over sequences."""
+    cfg = M.transformer_config(seq, hidden, ffn, norm=norm, bias=bias)
+    flat = M.init_transformer_params(cfg, seed=17)
+    rng = np.random.default_rng(6)
+    B = 2
+    x = rng.standard_normal((B, seq, hidden)).astype(np.float32)
+    t = rng.standard_normal((B, seq, hidden)).astype(np.float32)
+    g_ref = np.zeros(flat.size, np.float32)
+    ys, dxs = [], []
+    for b in range(B):
+        ref = oracle_model(M, cfg, flat)
+        y, _, dx = O.transformer_train_step(ref, x[b], t[b], 0.0, grads=g_ref, rounding=RZ,
+                                            heads=heads)
+        ys.append(y)
+        dxs.append(dx)
+    eng = M.Transformer(cfg, max_batch=B, heads=heads)
+    assert eng.heads == heads
+    eng.set_params(flat)
+    eng.zero_grads()
+    y = host(eng.train_forward(dev(x.reshape(B * seq, hidden))))
+    eng.set_target(dev(t.reshape(B * seq, hidden)))
+    dx = host(eng.backward())
+    g = host(eng.grads)
+    assert rel_err(y, np.concatenate(ys)) < FWD_TOL
+    assert rel_err(dx, np.concatenate(dxs)) < GRAD_TOL
+    check_per_tensor(cfg, g, g_ref)
+    eng.close()
+
+
+@pytest.mark.parametrize("seq,heads", [(64, 4), (256, 4), (256, 2)])
+@pytest.mark.parametrize("causal", [False, True])
+def test_multi_head_inference_forward(M, causal, seq, heads):
+    """Multi-head inference forward (encoder and the decoder's causal mask)
+    on two sequences against the oracle: per-head products at seq 64, the
+    fused kernel (oxf_attention_heads_forward, 32- and 64-wide heads) at
+    seq 256."""
+    hidden, ffn, B = 128, 256, 2
+    cfg = M.transformer_config(seq, hidden, ffn, norm=0)
+    flat = M.init_transformer_params(cfg, seed=23)
+    x = np.random.default_rng(3).standard_normal((B, seq, hidden)).astype(np.float32)
+    eng = M.Transformer(cfg, max_batch=B)
+    eng.set_params(flat)
+    y1 = host(eng.forward(dev(x.reshape(B * seq, hidden)), causal=causal))
+    eng.set_heads(heads)
+    y = host(eng.forward(dev(x.reshape(B * seq, hidden)), causal=causal))
+    ref = oracle_model(M, cfg, flat)
+    for b in range(B):
+        want = O.transformer_forward(ref, x[b], causal=causal, rounding=RZ, heads=heads)
+        assert rel_err(y[b * seq:(b + 1) * seq], want) < FWD_TOL
+    # back to one head: the single-head result again, bit for bit
+    eng.set_heads(1)
+    y1b = host(eng.forward(dev(x.reshape(B * seq, hidden)), causal=causal))
+    np.testing.assert_array_equal(y1b, y1)
+    eng.close()
+
+
+def test_set_heads_rejects_non_divisors(M):
+    from oxf import _lib
+    cfg = M.transformer_config(16, 64, 128)
+    eng = M.Transformer(cfg, max_batch=1)
+    for bad in (0, -2, 3, 128):
+        with pytest.raises(RuntimeError):
+            eng.set_heads(bad)
+    assert eng.heads == 1
+    assert _lib.lib().oxf_transformer_set_heads(None, 2) == _lib.INVALID_ARG
+    eng.close()
+
+
 def test_train_step_host_api(M):
     """The host-memory step (H2D, forward, loss, backward, SGD on the mean
     gradient, loss D2H) equals the device-level calls."""

@@ -375,3 +375,93 @@ def test_exchange_sgd_any_world_and_range(world, n, data, lr, seed):
     assert (np.abs(out[0] - want) <= one_ulp).all()
     np.testing.assert_array_equal(out[0][:offset], p[:offset])
     np.testing.assert_array_equal(out[0][offset + count:], p[offset + count:])
+
+
+# ---------------------------------------------------------------- multi-head attention
+def _mha_f64(q, k, v, h, causal):
+    """Multi-head attention in float64: head j takes columns j·D/h.. of Q, K
+    and j·Hv/h.. of V, scores scaled by 1/sqrt(D/h); outputs concatenated."""
+    q, k, v = (np.asarray(a, np.float64) for a in (q, k, v))
+    S, D = q.shape
+    Hv = v.shape[1]
+    dq, dv = D // h, Hv // h
+    att, P = np.zeros((S, Hv)), np.zeros((h, S, S))
+    for j in range(h):
+        s = q[:, j * dq:(j + 1) * dq] @ k[:, j * dq:(j + 1) * dq].T / np.sqrt(dq)
+        if causal:
+            s[np.triu_indices(S, 1)] = -np.inf
+        e = np.exp(s - s.max(1, keepdims=True))
+        P[j] = e / e.sum(1, keepdims=True)
+        att[:, j * dv:(j + 1) * dv] = P[j] @ v[:, j * dv:(j + 1) * dv]
+    return att, P
+
+
+def _mha_backward_f64(q, k, v, P, dr, h):
+    q, k, v, dr = (np.asarray(a, np.float64) for a in (q, k, v, dr))
+    S, D = q.shape
+    Hv = v.shape[1]
+    hq, hv = D // h, Hv // h
+    dq, dk, dv = np.zeros_like(q), np.zeros_like(k), np.zeros_like(v)
+    for j in range(h):
+        cq, cv = slice(j * hq, (j + 1) * hq), slice(j * hv, (j + 1) * hv)
+        p = P[j]
+        dp = dr[:, cv] @ v[:, cv].T
+        dv[:, cv] = p.T @ dr[:, cv]
+        ds = p * (dp - (p * dp).sum(1, keepdims=True)) / np.sqrt(hq)
+        dq[:, cq] = ds @ k[:, cq]
+        dk[:, cq] = ds.T @ q[:, cq]
+    return dq, dk, dv
+
+
+@pytest.mark.parametrize("heads", [1, 2, 4])
+@pytest.mark.parametrize("causal", [False, True])
+def test_attention_heads_against_float64(heads, causal):
+    """The oracle's multi-head attention core (forward and backward) against
+    an independent float64 restatement; heads = 1 is the reference's
+    single-head attention (attention.rs:359-401, 297-308)."""
+    rng = np.random.default_rng(40 + heads)
+    S, D, Hv = 24, 32, 48
+    q = rng.standard_normal((S, D)).astype(np.float32)
+    k = rng.standard_normal((S, D)).astype(np.float32)
+    v = rng.standard_normal((S, Hv)).astype(np.float32)
+    dr = rng.standard_normal((S, Hv)).astype(np.float32)
+    att, p = O.attention_heads(q, k, v, heads, causal)
+    att_ref, p_ref = _mha_f64(q, k, v, heads, causal)
+    assert rel_err(att, att_ref) < 1e-5
+    assert rel_err(p, p_ref) < 1e-5
+    got = O.attention_heads_backward(q, k, v, p, dr, heads)
+    want = _mha_backward_f64(q, k, v, p_ref, dr, heads)
+    for g, w in zip(got, want):
+        assert rel_err(g, w) < 1e-5
+
+
+def test_transformer_heads_one_is_the_single_head_block():
+    """The multi-head entry points with one head reproduce the single-head
+    block bit for bit (forward and one training step), and more heads
+    change the result."""
+    seq, hidden, ffn = 16, 32, 64
+    rng = np.random.default_rng(8)
+    def lin(i, o, act=O.IDENTITY):
+        return O.LinearParams((rng.standard_normal((i, o)) * 0.2).astype(np.float32), None, act)
+    t = O.TransformerParams(lin(hidden, hidden), lin(hidden, hidden), lin(hidden, hidden),
+                            (0.1 * rng.standard_normal((seq, hidden))).astype(np.float32),
+                            O.MlpParams([lin(hidden, ffn, O.GELU), lin(ffn, hidden)]),
+                            lin(hidden, hidden), O.NORM_LAYER, seq)
+    x = rng.standard_normal((seq, hidden)).astype(np.float32)
+    tg = rng.standard_normal((seq, hidden)).astype(np.float32)
+    s, keep = t.struct()
+    y1 = np.empty((seq, hidden), np.float32)
+    O.lib().oxo_transformer_forward_heads(O.C.byref(s), O._p(x), O._p(y1), 0, O.GEMM_F32, 1)
+    np.testing.assert_array_equal(y1, O.transformer_forward(t, x))
+    g1 = np.zeros(t.flat().size, np.float32)
+    g2 = np.zeros_like(g1)
+    r1 = O.transformer_train_step(t.copy(), x, tg, 0.0, grads=g1)
+    s2, keep2 = t.struct()
+    y2, l2, dx2 = (np.empty((seq, hidden), np.float32), np.empty(seq, np.float32),
+                   np.empty_like(x))
+    O.lib().oxo_transformer_train_step_heads(O.C.byref(s2), O._p(x), O._p(tg), O._p(y2),
+                                             O._p(l2), O._p(dx2), 0.0, O._p(g2), O.GEMM_F32, 1)
+    np.testing.assert_array_equal(r1[2], dx2)
+    np.testing.assert_array_equal(g1, g2)
+    y4 = O.transformer_forward(t, x, heads=4)
+    assert rel_err(y4, y1) > 1e-4
