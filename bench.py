@@ -76,12 +76,15 @@ def parse():
                     help="skip the cuBLAS denominator and comparison (profiling runs: keeps "
                          "the launch list to this library's kernels); peaks are then null")
     ap.add_argument("--workload", default="train",
-                    choices=["train", "linear", "gemm", "rows", "mlp", "infer", "exchange"],
+                    choices=["train", "linear", "gemm", "rows", "mlp", "infer", "exchange",
+                             "attention"],
                     help="train: the contract line (config 5). The others are supplementary "
                          "single-GPU measurements of configs 1-4: linear (config 1), gemm "
                          "(square sweep / one shape), rows (config 2 row suite), mlp "
                          "(config 3), infer (config 4); exchange: gradient exchange + SGD over the "
                          "config-5 arena at N GPUs, fused peer kernel vs NCCL + SGD")
+    ap.add_argument("--sequences", type=int, default=64,
+                    help="attention: sequences of config 4's shape ([2048, 1024]) per call")
     ap.add_argument("--shape", default=None, help="gemm: M,N,K (default: the 512..8192 sweep)")
     ap.add_argument("--mode", default="nn", help="gemm: nn, nt, tn or tt")
     ap.add_argument("--epi", default="none",
@@ -623,6 +626,35 @@ def run_mlp(a, torch):
     eng.close()
 
 
+def run_attention(a, torch):
+    """The fused multi-head attention kernel alone (oxf_attention_heads_forward)
+    at config 4's widths: --sequences sequences of [2048, 1024] split into
+    --heads heads (16 by default when --heads is 1: 64-wide heads), with the
+    residual. Device time per call with CUDA events; TFLOP/s counts the two
+    products, 4 * seq^2 * d per sequence (no causal mask). The inputs
+    (4 x 0.5 GB at 64 sequences) exceed L2."""
+    from oxf import kernels as K
+    seq, d = 2048, 1024
+    heads = a.heads if a.heads > 1 else 16
+    n = a.sequences
+    g = torch.Generator(device="cuda").manual_seed(4100)
+    q, k, v, r = (torch.randn(n, seq, d, device="cuda", generator=g) for _ in range(4))
+    out = torch.empty(n, seq, d, device="cuda")
+    fn = lambda: K.attention_heads_forward(q, k, v, out, heads, residual=r)
+    sampler = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
+    sampler.start()
+    ms = _time(torch, fn, a.steps, max(3, a.warmup))
+    clocks = sampler.stop()
+    flops = 4.0 * seq * seq * d * n
+    print(json.dumps({"metric": "fused multi-head attention TFLOP/s", "unit": "TFLOP/s",
+                      "value": flops / ms / 1e9, "ms": ms, "workload": "attention",
+                      "kernel": "attention_heads_flash_kernel", "clocks": clocks,
+                      "config": {"sequences": n, "seq_len": seq, "d": d, "heads": heads,
+                                 "head_width": d // heads, "causal": False,
+                                 "l2": "inputs larger than L2"}}), flush=True)
+    assert K.device_error() == 0
+
+
 def run_exchange(a, torch):
     """Gradient exchange + SGD over a parameter arena the size of config 5's
     (seq, hidden, ffn as given; 52.4 M f32 at the defaults) on N GPUs: the
@@ -820,7 +852,8 @@ def main():
         import torch
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
         {"gemm": run_gemm, "rows": run_rows, "mlp": run_mlp, "infer": run_infer,
-         "linear": run_linear, "exchange": run_exchange}[a.workload](
+         "linear": run_linear, "exchange": run_exchange,
+         "attention": run_attention}[a.workload](
             a, torch)
         return
     import numpy as np

@@ -2466,10 +2466,11 @@ oxf_status gemm_tf32x3_noalloc(const oxf_gemm_desc* d, cudaStream_t stream) {
 // score matrix never reaches HBM. Head j reads columns [j*HD, (j+1)*HD) of
 // Q, K and V; out = residual + softmax(Q_j K_jᵀ / sqrt(HD)) V_j in the same
 // columns (attention.rs:359-401 per head; docs/api.md:440-442 anticipates the
-// head split). Warp 0 issues the TMA loads, warp 1 the MMAs, warps 2-5 run
-// the softmax, one query row per thread. Every wait is bounded.
+// head split). Warp 0 issues the TMA loads, warp 1 the MMAs, warps 2-9 run
+// the softmax, two threads per query row. Every wait is bounded.
 constexpr int FA_ROWS = 128;
-constexpr int FA_THREADS = 192;
+constexpr int FA_SOFTMAX_WARPS = 8;
+constexpr int FA_THREADS = 64 + 32 * FA_SOFTMAX_WARPS;
 
 struct FaArgs {
   float* out;             // [batch * seq, ldo]
@@ -2487,21 +2488,26 @@ struct FaCfg {
   static constexpr int K_BYTES = KB * 16384;            // [128 keys x HD], K-major
   static constexpr int V_KBLOCK = (HD / 32) * 4096;     // 32 keys x HD, MN-major
   static constexpr int V_BYTES = 4 * V_KBLOCK;          // 128 keys
-  static constexpr int P_BYTES = 4 * 16384;             // [128 x 128 keys], K-major
-  static constexpr int CTRL_BYTES = 1024;
-  static constexpr int SMEM_BYTES =
-      1024 + CTRL_BYTES + Q_BYTES + 2 * (K_BYTES + V_BYTES) + P_BYTES;
-  static constexpr uint32_t TMEM_COLS = 512;            // S x 2 (256 columns) + O (HD)
+  static constexpr int STAGES = HD == 32 ? 6 : 3;       // K / V ring depth
+  static constexpr int CTRL_BYTES = 2048;               // barriers; row-sum exchange at 1024
+  static constexpr int SMEM_BYTES = 1024 + CTRL_BYTES + Q_BYTES + STAGES * (K_BYTES + V_BYTES);
+  static constexpr uint32_t TMEM_COLS = 512;            // S / P x 2 (256 columns) + O (HD)
   static constexpr uint32_t O_COL = 256;
   static_assert(HD == 32 || HD == 64, "head widths 32 and 64");
   static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
 
+constexpr int FA_MAX_STAGES = 6;
+
 struct FaCtrl {
   uint64_t q_full;
-  uint64_t kv_full[2], kv_empty[2];  // K and V tile ring
-  uint64_t s_full[2], s_free[2];     // score buffers in TMEM
-  uint64_t p_ready, pv_done;         // P in shared memory, O rescaled / P·V finished
+  uint64_t k_full[FA_MAX_STAGES], k_empty[FA_MAX_STAGES];  // K ring: S products release
+  uint64_t v_full[FA_MAX_STAGES], v_empty[FA_MAX_STAGES];  // V ring: P·V products release
+  uint64_t s_full[2];   // S landed in TMEM buffer b
+  uint64_t s_read[2];   // every softmax warp has read buffer b (P may overwrite it)
+  uint64_t s_free[2];   // the P·V that read buffer b has finished
+  uint64_t p_ready;     // P of the tile in TMEM, O rescaled
+  uint64_t pv_done;     // the tile's P·V has finished
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -2512,14 +2518,15 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                                  const __grid_constant__ CUtensorMap tmK,
                                  const __grid_constant__ CUtensorMap tmV, const FaArgs args) {
   using Cfg = FaCfg<HD>;
+  constexpr int NS = Cfg::STAGES;
   extern __shared__ __align__(1024) uint8_t fa_smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fa_smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   auto* ctrl = reinterpret_cast<FaCtrl*>(base);
+  float* lsum = reinterpret_cast<float*>(base + 1024);  // [2][128] row-sum halves
   uint8_t* qs = base + Cfg::CTRL_BYTES;
-  uint8_t* ks = qs + Cfg::Q_BYTES;      // two stages
-  uint8_t* vs = ks + 2 * Cfg::K_BYTES;  // two stages
-  uint8_t* ps = vs + 2 * Cfg::V_BYTES;
+  uint8_t* ks = qs + Cfg::Q_BYTES;       // NS stages
+  uint8_t* vs = ks + NS * Cfg::K_BYTES;  // NS stages
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x, head = blockIdx.y, seq_i = blockIdx.z;
@@ -2531,13 +2538,19 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   if (threadIdx.x == 0) {
     mbar_init(&ctrl->q_full, 1);
 #pragma unroll
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&ctrl->kv_full[s], 1);
-      mbar_init(&ctrl->kv_empty[s], 1);
-      mbar_init(&ctrl->s_full[s], 1);
-      mbar_init(&ctrl->s_free[s], 4);  // one arrive per softmax warp
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&ctrl->k_full[s], 1);
+      mbar_init(&ctrl->k_empty[s], 1);
+      mbar_init(&ctrl->v_full[s], 1);
+      mbar_init(&ctrl->v_empty[s], 1);
     }
-    mbar_init(&ctrl->p_ready, 4);
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&ctrl->s_full[s], 1);
+      mbar_init(&ctrl->s_read[s], FA_SOFTMAX_WARPS);
+      mbar_init(&ctrl->s_free[s], 1);
+    }
+    mbar_init(&ctrl->p_ready, FA_SOFTMAX_WARPS);
     mbar_init(&ctrl->pv_done, 1);
     ctrl->abort_flag = 0;
     fence_barrier_init();
@@ -2563,74 +2576,87 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 #pragma unroll
       for (int kb = 0; kb < Cfg::KB; ++kb)
         tma_load_2d(qs + kb * 16384, &tmQ, &ctrl->q_full, col0 + kb * 32, q_row0, pol);
-      int fills = 0;
+      int kfills = 0, vfills = 0;  // tiles whose K / V loads were issued
       for (int t = 0; t < n_tiles && !ctrl->abort_flag; ++t) {
-        const int st = t & 1;
-        if (t >= 2 && !mbar_wait(&ctrl->kv_empty[st], ((t - 2) >> 1) & 1, DEVERR_ATTN_WAIT)) {
+        const int st = t % NS;
+        const uint32_t prev = static_cast<uint32_t>((t / NS - 1) & 1);
+        const int kv0 = kv_row0 + t * FA_ROWS;
+        if (t >= NS && !mbar_wait(&ctrl->k_empty[st], prev, DEVERR_ATTN_WAIT)) {
           ctrl->abort_flag = 1;
           break;
         }
-        mbar_arrive_expect_tx(&ctrl->kv_full[st], Cfg::K_BYTES + Cfg::V_BYTES);
-        const int kv0 = kv_row0 + t * FA_ROWS;
+        mbar_arrive_expect_tx(&ctrl->k_full[st], Cfg::K_BYTES);
 #pragma unroll
         for (int kb = 0; kb < Cfg::KB; ++kb)
-          tma_load_2d(ks + st * Cfg::K_BYTES + kb * 16384, &tmK, &ctrl->kv_full[st],
+          tma_load_2d(ks + st * Cfg::K_BYTES + kb * 16384, &tmK, &ctrl->k_full[st],
                       col0 + kb * 32, kv0, pol);
+        kfills = t + 1;
+        if (t >= NS && !mbar_wait(&ctrl->v_empty[st], prev, DEVERR_ATTN_WAIT)) {
+          ctrl->abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&ctrl->v_full[st], Cfg::V_BYTES);
 #pragma unroll
         for (int kb = 0; kb < 4; ++kb)
-          load_operand<HD>(vs + st * Cfg::V_BYTES + kb * Cfg::V_KBLOCK, &tmV, &ctrl->kv_full[st],
+          load_operand<HD>(vs + st * Cfg::V_BYTES + kb * Cfg::V_KBLOCK, &tmV, &ctrl->v_full[st],
                            1, 0, HD > 32 ? 1 : 0, col0, kv0 + kb * 32, 0, pol);
-        ++fills;
+        vfills = t + 1;
       }
       // no copy may still be landing when the CTA exits
       mbar_wait(&ctrl->q_full, 0, DEVERR_ATTN_WAIT);
-      for (int t = fills > 2 ? fills - 2 : 0; t < fills; ++t)
-        mbar_wait(&ctrl->kv_full[t & 1], (t >> 1) & 1, DEVERR_ATTN_WAIT);
+      for (int t = kfills > NS ? kfills - NS : 0; t < kfills; ++t)
+        mbar_wait(&ctrl->k_full[t % NS], (t / NS) & 1, DEVERR_ATTN_WAIT);
+      for (int t = vfills > NS ? vfills - NS : 0; t < vfills; ++t)
+        mbar_wait(&ctrl->v_full[t % NS], (t / NS) & 1, DEVERR_ATTN_WAIT);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t id_s = make_idesc_tf32(128, 128, false, false);
       constexpr uint32_t id_o = make_idesc_tf32(128, HD, false, true);
-      const uint32_t q_addr = smem_u32(qs), k_addr = smem_u32(ks), v_addr = smem_u32(vs),
-                     p_addr = smem_u32(ps);
-      // O += P·V for tile t, once its probabilities are in shared memory
+      const uint32_t q_addr = smem_u32(qs), k_addr = smem_u32(ks), v_addr = smem_u32(vs);
+      // O += P·V for tile t: P is read from TMEM (it overwrote the tile's S)
       auto issue_pv = [&](int t) -> bool {
-        if (!mbar_wait(&ctrl->p_ready, t & 1, DEVERR_ATTN_WAIT)) return false;
+        const int st = t % NS;
+        if (!mbar_wait(&ctrl->p_ready, t & 1, DEVERR_ATTN_WAIT) ||
+            !mbar_wait(&ctrl->v_full[st], (t / NS) & 1, DEVERR_ATTN_WAIT))
+          return false;
         tc_fence_after();
-        const int st = t & 1;
+        const uint32_t p_col = tmem + static_cast<uint32_t>((t & 1) * 128);
 #pragma unroll
         for (int kb = 0; kb < 4; ++kb)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_tf32(tmem + Cfg::O_COL,
-                      desc_advance(operand_desc(p_addr + kb * 16384, 0, 0), kk * 32),
-                      desc_advance(operand_desc(v_addr + st * Cfg::V_BYTES + kb * Cfg::V_KBLOCK,
-                                                1, 0),
-                                   kk * 1024),
-                      id_o, (t > 0 || kb > 0 || kk > 0) ? 1u : 0u);
-        // the stage's release first: once pv_done completes, no arrive is pending
-        umma_commit(&ctrl->kv_empty[st]);
+            umma_tf32_tmem_a(tmem + Cfg::O_COL, p_col + kb * 32 + kk * 8,
+                             desc_advance(operand_desc(v_addr + st * Cfg::V_BYTES +
+                                                           kb * Cfg::V_KBLOCK,
+                                                       1, 0),
+                                          kk * 1024),
+                             id_o, (t > 0 || kb > 0 || kk > 0) ? 1u : 0u);
+        // releases first: once pv_done completes, no arrive is pending
+        umma_commit(&ctrl->v_empty[st]);
+        umma_commit(&ctrl->s_free[t & 1]);
         umma_commit(&ctrl->pv_done);
         return true;
       };
       bool ok = mbar_wait(&ctrl->q_full, 0, DEVERR_ATTN_WAIT);
       for (int t = 0; ok && t < n_tiles; ++t) {
-        const int st = t & 1;
-        ok = mbar_wait(&ctrl->kv_full[st], (t >> 1) & 1, DEVERR_ATTN_WAIT) &&
-             (t < 2 || mbar_wait(&ctrl->s_free[st], ((t - 2) >> 1) & 1, DEVERR_ATTN_WAIT));
+        const int st = t % NS, sb = t & 1;
+        ok = mbar_wait(&ctrl->k_full[st], (t / NS) & 1, DEVERR_ATTN_WAIT) &&
+             (t < 2 || mbar_wait(&ctrl->s_free[sb], ((t - 2) >> 1) & 1, DEVERR_ATTN_WAIT));
         if (!ok) break;
         tc_fence_after();
-        // S[st] = Q·K_tᵀ (the scale is applied in the softmax)
+        // S[sb] = Q·K_tᵀ (the scale is applied in the softmax)
 #pragma unroll
         for (int kb = 0; kb < Cfg::KB; ++kb)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_tf32(tmem + st * 128,
+            umma_tf32(tmem + sb * 128,
                       desc_advance(operand_desc(q_addr + kb * 16384, 0, 0), kk * 32),
                       desc_advance(operand_desc(k_addr + st * Cfg::K_BYTES + kb * 16384, 0, 0),
                                    kk * 32),
                       id_s, (kb > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&ctrl->s_full[st]);
+        umma_commit(&ctrl->k_empty[st]);
+        umma_commit(&ctrl->s_full[sb]);
         // the previous tile's P·V runs while the softmax works on this one
         if (t > 0) ok = issue_pv(t - 1);
       }
@@ -2638,104 +2664,122 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       if (!ok) ctrl->abort_flag = 1;
     }
   } else {
-    // softmax warps: thread r of the tile owns query row r = TMEM lane r
+    // Softmax: two threads per query row r (= TMEM lane r). Warps 2-5 own
+    // keys 0-63 of every tile, warps 6-9 keys 64-127; each thread reads the
+    // whole row for the row maximum, then exponentiates its own 64 keys,
+    // writes their probabilities over the scores in TMEM (the A operand of
+    // P·V), rescales its 32-column chunk of the output, and finally
+    // normalises and stores that chunk.
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
     const uint32_t row_tmem = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const float scale2 = args.scale * 1.4426950408889634f;  // exp(s * scale) = 2^(s * scale2)
+    const bool own_o = half < HD / 32;  // HD = 32: one chunk, owned by half 0
     float m = -INFINITY, l = 0.0f;
     bool ok = true;
     for (int t = 0; t < n_tiles; ++t) {
-      const int st = t & 1;
-      if (!mbar_wait(&ctrl->s_full[st], (t >> 1) & 1, DEVERR_ATTN_WAIT)) {
+      const int sb = t & 1;
+      if (!mbar_wait(&ctrl->s_full[sb], (t >> 1) & 1, DEVERR_ATTN_WAIT)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float v[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(row_tmem + st * 128 + c * 32, v[c]);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&ctrl->s_free[st]);
-      // scaled scores; on the diagonal tile of a causal pass, key j > row r is masked
+      const uint32_t s_row = row_tmem + sb * 128;
+      // on the diagonal tile of a causal pass, key j > row r is masked
       const bool diag = args.causal && t == qt;
       float mt = -INFINITY;
+      {
+        float o2[32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < 2; ++c) {
+          const int kc = (1 - half) * 2 + c;  // the other half's chunks: maximum only
+          tmem_ld_32x32b_x32(s_row + kc * 32, o2);
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            mt = fmaxf(mt, (diag && kc * 32 + j > r) ? -INFINITY : o2[j]);
+        }
+      }
+      float v[2][32];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int kc = half * 2 + c;
+        tmem_ld_32x32b_x32(s_row + kc * 32, v[c]);
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          float x = v[c][j] * args.scale;
-          if (diag && c * 32 + j > r) x = -INFINITY;
-          v[c][j] = x;
-          mt = fmaxf(mt, x);
+          if (diag && kc * 32 + j > r) v[c][j] = -INFINITY;
+          mt = fmaxf(mt, v[c][j]);
         }
-      const float m_new = fmaxf(m, mt);
-      const float alpha = __expf(m - m_new);  // 0 on the first tile
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctrl->s_read[sb]);
+      const float m_new = fmaxf(m, mt * scale2);  // scale2 > 0
+      const float alpha = exp2f(m - m_new);       // 0 on the first tile
       float sum = 0.0f;
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int c = 0; c < 2; ++c)
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const float p = __expf(v[c][j] - m_new);
+          const float p = exp2f(fmaf(v[c][j], scale2, -m_new));
           v[c][j] = p;
           sum += p;
         }
       l = l * alpha + sum;
       m = m_new;
       if (t > 0) {
-        // the previous P·V has finished: P is free and O holds tiles 0..t-1
+        // the previous P·V has finished: O holds tiles 0..t-1
         if (!mbar_wait(&ctrl->pv_done, (t - 1) & 1, DEVERR_ATTN_WAIT)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+        if (own_o && __any_sync(0xffffffffu, alpha != 1.0f)) {
+          float o[32];
+          tmem_ld_32x32b_x32(row_tmem + Cfg::O_COL + half * 32, o);
 #pragma unroll
-          for (int c = 0; c < HD / 32; ++c) {
-            float o[32];
-            tmem_ld_32x32b_x32(row_tmem + Cfg::O_COL + c * 32, o);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) o[j] *= alpha;
-            tmem_st_32x32b_x32(row_tmem + Cfg::O_COL + c * 32, o);
-          }
-          tmem_st_wait();
+          for (int j = 0; j < 32; ++j) o[j] *= alpha;
+          tmem_st_32x32b_x32(row_tmem + Cfg::O_COL + half * 32, o);
         }
       }
-      // P row into shared memory: K-major, 128B swizzle, 32 keys per block
+      // the partner thread has read this half's scores: overwrite them with P
+      if (!mbar_wait(&ctrl->s_read[sb], (t >> 1) & 1, DEVERR_ATTN_WAIT)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          *stage_unit(ps + c * 16384, r, j) =
-              make_float4(v[c][4 * j], v[c][4 * j + 1], v[c][4 * j + 2], v[c][4 * j + 3]);
-      fence_proxy_async_smem();  // generic writes, read next by the tensor cores
-      tc_fence_before();         // the O rescale's TMEM stores
+      for (int c = 0; c < 2; ++c) tmem_st_32x32b_x32(s_row + (half * 2 + c) * 32, v[c]);
+      tmem_st_wait();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctrl->p_ready);
     }
     if (ok) ok = mbar_wait(&ctrl->pv_done, (n_tiles - 1) & 1, DEVERR_ATTN_WAIT);
-    if (ok) {
+    if (!ok) ctrl->abort_flag = 1;
+    // the row sum is split over the two halves; the named barrier is reached
+    // by all eight softmax warps on every path
+    lsum[half * FA_ROWS + r] = l;
+    asm volatile("bar.sync 1, %0;" ::"r"(32 * FA_SOFTMAX_WARPS) : "memory");
+    l += lsum[(1 - half) * FA_ROWS + r];
+    if (ok && own_o) {
       tc_fence_after();
       const float inv = 1.0f / l;
       const long long row = q_row0 + r;
-      float* orow = args.out + row * args.ldo + col0;
-      const float* rrow = args.residual ? args.residual + row * args.ldo + col0 : nullptr;
+      float* orow = args.out + row * args.ldo + col0 + half * 32;
+      const float* rrow =
+          args.residual ? args.residual + row * args.ldo + col0 + half * 32 : nullptr;
+      float o[32];
+      tmem_ld_32x32b_x32(row_tmem + Cfg::O_COL + half * 32, o);
 #pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
-        float o[32];
-        tmem_ld_32x32b_x32(row_tmem + Cfg::O_COL + c * 32, o);
-#pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          float4 y = make_float4(o[j] * inv, o[j + 1] * inv, o[j + 2] * inv, o[j + 3] * inv);
-          if (rrow) {
-            const float4 x = *reinterpret_cast<const float4*>(rrow + c * 32 + j);
-            y.x += x.x; y.y += x.y; y.z += x.z; y.w += x.w;
-          }
-          *reinterpret_cast<float4*>(orow + c * 32 + j) = y;
+      for (int j = 0; j < 32; j += 4) {
+        float4 y = make_float4(o[j] * inv, o[j + 1] * inv, o[j + 2] * inv, o[j + 3] * inv);
+        if (rrow) {
+          const float4 x = *reinterpret_cast<const float4*>(rrow + j);
+          y.x += x.x; y.y += x.y; y.z += x.z; y.w += x.w;
         }
+        *reinterpret_cast<float4*>(orow + j) = y;
       }
-    } else {
-      ctrl->abort_flag = 1;
     }
   }
   tc_fence_before();

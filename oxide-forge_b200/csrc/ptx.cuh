@@ -231,6 +231,20 @@ __device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] · B[smem desc], kind::tf32, one CTA: A is read from
+// tensor memory (M = 128: lane i holds row i, one 32-bit column per K
+// element, starting at a_tmem's column).
+__device__ __forceinline__ void umma_tf32_tmem_a(uint32_t d_tmem, uint32_t a_tmem,
+                                                 uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive on an mbarrier once all previously issued tcgen05.mma of this
 // thread have completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
