@@ -2493,6 +2493,7 @@ struct FaCfg {
   static constexpr int SMEM_BYTES = 1024 + CTRL_BYTES + Q_BYTES + STAGES * (K_BYTES + V_BYTES);
   static constexpr uint32_t TMEM_COLS = 512;            // S / P x 2 (256 columns) + O (HD)
   static constexpr uint32_t O_COL = 256;
+  static constexpr uint32_t X_COL = 448;                // row-maximum exchange, 4 columns
   static_assert(HD == 32 || HD == 64, "head widths 32 and 64");
   static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
@@ -2504,7 +2505,7 @@ struct FaCtrl {
   uint64_t k_full[FA_MAX_STAGES], k_empty[FA_MAX_STAGES];  // K ring: S products release
   uint64_t v_full[FA_MAX_STAGES], v_empty[FA_MAX_STAGES];  // V ring: P·V products release
   uint64_t s_full[2];   // S landed in TMEM buffer b
-  uint64_t s_read[2];   // every softmax warp has read buffer b (P may overwrite it)
+  uint64_t s_read[2];   // every softmax warp has posted its half-row maxima of buffer b
   uint64_t s_free[2];   // the P·V that read buffer b has finished
   uint64_t p_ready;     // P of the tile in TMEM, O rescaled
   uint64_t pv_done;     // the tile's P·V has finished
@@ -2665,11 +2666,11 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     }
   } else {
     // Softmax: two threads per query row r (= TMEM lane r). Warps 2-5 own
-    // keys 0-63 of every tile, warps 6-9 keys 64-127; each thread reads the
-    // whole row for the row maximum, then exponentiates its own 64 keys,
-    // writes their probabilities over the scores in TMEM (the A operand of
-    // P·V), rescales its 32-column chunk of the output, and finally
-    // normalises and stores that chunk.
+    // keys 0-63 of every tile, warps 6-9 keys 64-127; the two threads of a
+    // row exchange their half-row maxima, then each exponentiates its own 64
+    // keys, writes their probabilities over its scores in TMEM (the A
+    // operand of P·V), rescales its 32-column chunk of the output, and
+    // finally normalises and stores that chunk.
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
@@ -2688,19 +2689,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       const uint32_t s_row = row_tmem + sb * 128;
       // on the diagonal tile of a causal pass, key j > row r is masked
       const bool diag = args.causal && t == qt;
-      float mt = -INFINITY;
-      {
-        float o2[32];
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const int kc = (1 - half) * 2 + c;  // the other half's chunks: maximum only
-          tmem_ld_32x32b_x32(s_row + kc * 32, o2);
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            mt = fmaxf(mt, (diag && kc * 32 + j > r) ? -INFINITY : o2[j]);
-        }
-      }
       float v[2][32];
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const int kc = half * 2 + c;
@@ -2708,24 +2698,35 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           if (diag && kc * 32 + j > r) v[c][j] = -INFINITY;
-          mt = fmaxf(mt, v[c][j]);
+          mx[j & 3] = fmaxf(mx[j & 3], v[c][j]);
         }
       }
+      // the row maximum: this half's, exchanged with the partner thread
+      // through a spare TMEM column per (buffer, half)
+      const float mine = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      tmem_st_32x32b_x1(row_tmem + Cfg::X_COL + sb * 2 + half, mine);
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctrl->s_read[sb]);
+      if (!mbar_wait(&ctrl->s_read[sb], (t >> 1) & 1, DEVERR_ATTN_WAIT)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float mt = fmaxf(mine, tmem_ld_32x32b_x1(row_tmem + Cfg::X_COL + sb * 2 + (1 - half)));
       const float m_new = fmaxf(m, mt * scale2);  // scale2 > 0
-      const float alpha = exp2f(m - m_new);       // 0 on the first tile
-      float sum = 0.0f;
+      const float alpha = ex2_approx(m - m_new);  // 0 on the first tile
+      float sm[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int c = 0; c < 2; ++c)
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const float p = exp2f(fmaf(v[c][j], scale2, -m_new));
+          const float p = ex2_approx(fmaf(v[c][j], scale2, -m_new));
           v[c][j] = p;
-          sum += p;
+          sm[j & 3] += p;
         }
-      l = l * alpha + sum;
+      l = l * alpha + ((sm[0] + sm[1]) + (sm[2] + sm[3]));
       m = m_new;
       if (t > 0) {
         // the previous P·V has finished: O holds tiles 0..t-1
@@ -2742,12 +2743,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           tmem_st_32x32b_x32(row_tmem + Cfg::O_COL + half * 32, o);
         }
       }
-      // the partner thread has read this half's scores: overwrite them with P
-      if (!mbar_wait(&ctrl->s_read[sb], (t >> 1) & 1, DEVERR_ATTN_WAIT)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
+      // this half's probabilities over its own scores
 #pragma unroll
       for (int c = 0; c < 2; ++c) tmem_st_32x32b_x32(s_row + (half * 2 + c) * 32, v[c]);
       tmem_st_wait();

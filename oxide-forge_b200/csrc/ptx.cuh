@@ -291,6 +291,28 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const float (
       : "memory");
 }
 
+// One 32-bit column: thread t of the warp reads / writes lane (base_lane + t).
+__device__ __forceinline__ float tmem_ld_32x32b_x1(uint32_t taddr) {
+  uint32_t r;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+  return __uint_as_float(r);
+}
+
+__device__ __forceinline__ void tmem_st_32x32b_x1(uint32_t taddr, float v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr),
+               "r"(__float_as_uint(v))
+               : "memory");
+}
+
+// 2^x by the hardware's approximate base-2 exponential (PTX ex2.approx.ftz:
+// maximum relative error 2^-22 per the PTX ISA; subnormal results flush to 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
