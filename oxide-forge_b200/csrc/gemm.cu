@@ -2786,6 +2786,342 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   }
 }
 
+// Two query tiles per CTA (rows 256*i .. 256*i+255 of one head of one
+// sequence), so that the tensor cores work on one tile's products while the
+// other tile's softmax runs: the MMA thread issues, per key/value tile t,
+// P·V of tile A, S of tile A for t+1, P·V of tile B, S of tile B for t+1.
+// Each query tile has its own score buffer (128 TMEM columns, overwritten
+// by its P), output accumulator and group of four softmax warps (one thread
+// per row). K and V are loaded once for both tiles.
+constexpr int FA2_THREADS = 64 + 32 * 8;
+
+template <int HD>
+struct Fa2Cfg {
+  static constexpr int KB = HD / 32;
+  static constexpr int Q_BYTES = KB * 16384;            // one query tile, K-major
+  static constexpr int K_BYTES = KB * 16384;
+  static constexpr int V_KBLOCK = (HD / 32) * 4096;
+  static constexpr int V_BYTES = 4 * V_KBLOCK;
+  static constexpr int STAGES = HD == 32 ? 6 : 2;
+  static constexpr int CTRL_BYTES = 2048;
+  static constexpr int SMEM_BYTES =
+      1024 + CTRL_BYTES + 2 * Q_BYTES + STAGES * (K_BYTES + V_BYTES);
+  static constexpr uint32_t TMEM_COLS = 512;  // S_A 0, S_B 128, O_A 256, O_B 320
+  static_assert(HD == 32 || HD == 64, "head widths 32 and 64");
+  static_assert(SMEM_BYTES <= 232448, "shared memory");
+};
+
+struct Fa2Ctrl {
+  uint64_t q_full;
+  uint64_t k_full[FA_MAX_STAGES], k_empty[FA_MAX_STAGES];
+  uint64_t v_full[FA_MAX_STAGES], v_empty[FA_MAX_STAGES];
+  uint64_t s_full[2];   // per query tile: S landed
+  uint64_t s_free[2];   // per query tile: its P·V finished (S may be overwritten)
+  uint64_t p_ready[2];  // per query tile: P in TMEM, O rescaled
+  uint64_t pv_done[2];  // per query tile: P·V finished
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(FA2_THREADS, 1)
+    attention_heads_flash2_kernel(const __grid_constant__ CUtensorMap tmQ,
+                                  const __grid_constant__ CUtensorMap tmK,
+                                  const __grid_constant__ CUtensorMap tmV, const FaArgs args) {
+  using Cfg = Fa2Cfg<HD>;
+  constexpr int NS = Cfg::STAGES;
+  extern __shared__ __align__(1024) uint8_t fa2_smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fa2_smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  auto* ctrl = reinterpret_cast<Fa2Ctrl*>(base);
+  uint8_t* qs = base + Cfg::CTRL_BYTES;  // tile A, then tile B
+  uint8_t* ks = qs + 2 * Cfg::Q_BYTES;
+  uint8_t* vs = ks + NS * Cfg::K_BYTES;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pair = blockIdx.x, head = blockIdx.y, seq_i = blockIdx.z;
+  const int qa = 2 * pair;  // query tile index of A (B is qa + 1)
+  // key/value tiles each query tile visits; causal: up to its diagonal
+  const int n_a = args.causal ? qa + 1 : args.tiles;
+  const int n_b = args.causal ? qa + 2 : args.tiles;
+  const int q_row0 = seq_i * args.seq + qa * FA_ROWS;
+  const int kv_row0 = seq_i * args.seq;
+  const int col0 = head * HD;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&ctrl->q_full, 1);
+#pragma unroll
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&ctrl->k_full[s], 1);
+      mbar_init(&ctrl->k_empty[s], 1);
+      mbar_init(&ctrl->v_full[s], 1);
+      mbar_init(&ctrl->v_empty[s], 1);
+    }
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(&ctrl->s_full[g], 1);
+      mbar_init(&ctrl->s_free[g], 1);
+      mbar_init(&ctrl->p_ready[g], 4);
+      mbar_init(&ctrl->pv_done[g], 1);
+    }
+    ctrl->abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(&ctrl->tmem_base, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctrl->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol = make_l2_policy(L2_NORMAL);
+      mbar_arrive_expect_tx(&ctrl->q_full, 2 * Cfg::Q_BYTES);
+#pragma unroll
+      for (int g = 0; g < 2; ++g)
+#pragma unroll
+        for (int kb = 0; kb < Cfg::KB; ++kb)
+          tma_load_2d(qs + g * Cfg::Q_BYTES + kb * 16384, &tmQ, &ctrl->q_full, col0 + kb * 32,
+                      q_row0 + g * FA_ROWS, pol);
+      int kfills = 0, vfills = 0;
+      for (int t = 0; t < n_b && !ctrl->abort_flag; ++t) {
+        const int st = t % NS;
+        const uint32_t prev = static_cast<uint32_t>((t / NS - 1) & 1);
+        const int kv0 = kv_row0 + t * FA_ROWS;
+        if (t >= NS && !mbar_wait(&ctrl->k_empty[st], prev, DEVERR_ATTN_WAIT)) {
+          ctrl->abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&ctrl->k_full[st], Cfg::K_BYTES);
+#pragma unroll
+        for (int kb = 0; kb < Cfg::KB; ++kb)
+          tma_load_2d(ks + st * Cfg::K_BYTES + kb * 16384, &tmK, &ctrl->k_full[st],
+                      col0 + kb * 32, kv0, pol);
+        kfills = t + 1;
+        if (t >= NS && !mbar_wait(&ctrl->v_empty[st], prev, DEVERR_ATTN_WAIT)) {
+          ctrl->abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&ctrl->v_full[st], Cfg::V_BYTES);
+#pragma unroll
+        for (int kb = 0; kb < 4; ++kb)
+          load_operand<HD>(vs + st * Cfg::V_BYTES + kb * Cfg::V_KBLOCK, &tmV, &ctrl->v_full[st],
+                           1, 0, HD > 32 ? 1 : 0, col0, kv0 + kb * 32, 0, pol);
+        vfills = t + 1;
+      }
+      // no copy may still be landing when the CTA exits
+      mbar_wait(&ctrl->q_full, 0, DEVERR_ATTN_WAIT);
+      for (int t = kfills > NS ? kfills - NS : 0; t < kfills; ++t)
+        mbar_wait(&ctrl->k_full[t % NS], (t / NS) & 1, DEVERR_ATTN_WAIT);
+      for (int t = vfills > NS ? vfills - NS : 0; t < vfills; ++t)
+        mbar_wait(&ctrl->v_full[t % NS], (t / NS) & 1, DEVERR_ATTN_WAIT);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_s = make_idesc_tf32(128, 128, false, false);
+      constexpr uint32_t id_o = make_idesc_tf32(128, HD, false, true);
+      const uint32_t q_addr = smem_u32(qs), k_addr = smem_u32(ks), v_addr = smem_u32(vs);
+      // S_g = Q_g · K_tᵀ into tile g's buffer, once its previous P·V is done
+      auto issue_s = [&](int g, int t) -> bool {
+        if (t > 0 && !mbar_wait(&ctrl->s_free[g], (t - 1) & 1, DEVERR_ATTN_WAIT)) return false;
+        tc_fence_after();
+        const int st = t % NS;
+#pragma unroll
+        for (int kb = 0; kb < Cfg::KB; ++kb)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_tf32(tmem + g * 128,
+                      desc_advance(operand_desc(q_addr + g * Cfg::Q_BYTES + kb * 16384, 0, 0),
+                                   kk * 32),
+                      desc_advance(operand_desc(k_addr + st * Cfg::K_BYTES + kb * 16384, 0, 0),
+                                   kk * 32),
+                      id_s, (kb > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&ctrl->s_full[g]);
+        return true;
+      };
+      // O_g += P_g · V_t, P read from tile g's score buffer in TMEM
+      auto issue_pv = [&](int g, int t) -> bool {
+        const int st = t % NS;
+        if (!mbar_wait(&ctrl->p_ready[g], t & 1, DEVERR_ATTN_WAIT) ||
+            !mbar_wait(&ctrl->v_full[st], (t / NS) & 1, DEVERR_ATTN_WAIT))
+          return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kb = 0; kb < 4; ++kb)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_tf32_tmem_a(tmem + 256 + g * 64, tmem + g * 128 + kb * 32 + kk * 8,
+                             desc_advance(operand_desc(v_addr + st * Cfg::V_BYTES +
+                                                           kb * Cfg::V_KBLOCK,
+                                                       1, 0),
+                                          kk * 1024),
+                             id_o, (t > 0 || kb > 0 || kk > 0) ? 1u : 0u);
+        return true;
+      };
+      bool ok = mbar_wait(&ctrl->q_full, 0, DEVERR_ATTN_WAIT) &&
+                mbar_wait(&ctrl->k_full[0], 0, DEVERR_ATTN_WAIT);
+      if (ok) ok = issue_s(0, 0) && issue_s(1, 0);
+      if (ok) umma_commit(&ctrl->k_empty[0]);
+      for (int t = 0; ok && t < n_b; ++t) {
+        const int st = t % NS;
+        const bool next = t + 1 < n_b;
+        const int st1 = (t + 1) % NS;
+        if (t < n_a) {
+          ok = issue_pv(0, t);
+          if (!ok) break;
+          umma_commit(&ctrl->s_free[0]);
+          umma_commit(&ctrl->pv_done[0]);
+        }
+        if (next && !(ok = mbar_wait(&ctrl->k_full[st1], ((t + 1) / NS) & 1, DEVERR_ATTN_WAIT)))
+          break;
+        if (t + 1 < n_a && !(ok = issue_s(0, t + 1))) break;
+        ok = issue_pv(1, t);
+        if (!ok) break;
+        // tile B is the last reader of V_t
+        umma_commit(&ctrl->v_empty[st]);
+        umma_commit(&ctrl->s_free[1]);
+        umma_commit(&ctrl->pv_done[1]);
+        if (next) {
+          if (!(ok = issue_s(1, t + 1))) break;
+          umma_commit(&ctrl->k_empty[st1]);  // tile B is the last reader of K_{t+1}
+        }
+      }
+      if (!ok) ctrl->abort_flag = 1;
+    }
+  } else {
+    // softmax of query tile g (warps 2-5: A, warps 6-9: B); thread r of the
+    // group owns row r of the tile (= TMEM lane r)
+    const int g = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int n = g == 0 ? n_a : n_b;
+    const int diag_t = qa + g;  // the tile's diagonal key/value tile (causal)
+    const uint32_t row_tmem = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t s_row = row_tmem + g * 128;
+    const uint32_t o_row = row_tmem + 256 + g * 64;
+    const float scale2 = args.scale * 1.4426950408889634f;  // exp(s * scale) = 2^(s * scale2)
+    float m = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int t = 0; t < n; ++t) {
+      if (!mbar_wait(&ctrl->s_full[g], t & 1, DEVERR_ATTN_WAIT)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool diag = args.causal && t == diag_t;
+      float v[4][32];
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        tmem_ld_32x32b_x32(s_row + c * 32, v[c]);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (diag && c * 32 + j > r) v[c][j] = -INFINITY;
+          mx[j & 3] = fmaxf(mx[j & 3], v[c][j]);
+        }
+      }
+      const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      const float m_new = fmaxf(m, mt * scale2);  // scale2 > 0
+      const float alpha = ex2_approx(m - m_new);  // 0 on the first tile
+      float sm[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float p = ex2_approx(fmaf(v[c][j], scale2, -m_new));
+          v[c][j] = p;
+          sm[j & 3] += p;
+        }
+      l = l * alpha + ((sm[0] + sm[1]) + (sm[2] + sm[3]));
+      m = m_new;
+      if (t > 0) {
+        // the tile's previous P·V has finished: O holds key tiles 0..t-1
+        if (!mbar_wait(&ctrl->pv_done[g], (t - 1) & 1, DEVERR_ATTN_WAIT)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+          for (int c = 0; c < HD / 32; ++c) {
+            float o[32];
+            tmem_ld_32x32b_x32(o_row + c * 32, o);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) o[j] *= alpha;
+            tmem_st_32x32b_x32(o_row + c * 32, o);
+          }
+        }
+      }
+      // P over the scores: the A operand of this tile's P·V
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_st_32x32b_x32(s_row + c * 32, v[c]);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctrl->p_ready[g]);
+    }
+    if (ok) ok = mbar_wait(&ctrl->pv_done[g], (n - 1) & 1, DEVERR_ATTN_WAIT);
+    if (ok) {
+      tc_fence_after();
+      const float inv = 1.0f / l;
+      const long long row = q_row0 + g * FA_ROWS + r;
+      float* orow = args.out + row * args.ldo + col0;
+      const float* rrow = args.residual ? args.residual + row * args.ldo + col0 : nullptr;
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        float o[32];
+        tmem_ld_32x32b_x32(o_row + c * 32, o);
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          float4 y = make_float4(o[j] * inv, o[j + 1] * inv, o[j + 2] * inv, o[j + 3] * inv);
+          if (rrow) {
+            const float4 x = *reinterpret_cast<const float4*>(rrow + c * 32 + j);
+            y.x += x.x; y.y += x.y; y.z += x.z; y.w += x.w;
+          }
+          *reinterpret_cast<float4*>(orow + c * 32 + j) = y;
+        }
+      }
+    } else {
+      ctrl->abort_flag = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
+}
+
+template <int HD>
+oxf_status launch_attention_heads2(const CUtensorMap& tq, const CUtensorMap& tk,
+                                   const CUtensorMap& tv, const FaArgs& args, int batch,
+                                   int heads, cudaStream_t stream, int dev) {
+  using Cfg = Fa2Cfg<HD>;
+  static unsigned long long configured[kMaxDevices] = {0};
+  const unsigned long long ctx = current_context_id();
+  if (dev >= 0 && dev < kMaxDevices && (ctx == 0 || configured[dev] != ctx)) {
+    cudaError_t e = cudaFuncSetAttribute(attention_heads_flash2_kernel<HD>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(attention)");
+    configured[dev] = ctx;
+  }
+  dim3 grid(static_cast<unsigned>(args.tiles / 2), static_cast<unsigned>(heads),
+            static_cast<unsigned>(batch));
+  attention_heads_flash2_kernel<HD><<<grid, FA2_THREADS, Cfg::SMEM_BYTES, stream>>>(tq, tk, tv,
+                                                                                    args);
+  return check_launch("attention_heads_flash2_kernel");
+}
+
 template <int HD>
 oxf_status launch_attention_heads(const CUtensorMap& tq, const CUtensorMap& tk,
                                   const CUtensorMap& tv, const FaArgs& args, int batch, int heads,
@@ -2849,6 +3185,12 @@ oxf_status attention_heads_forward(const float* q, const float* k, const float* 
   int dev = 0;
   oxf_status st = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
   if (st != OXF_OK) return st;
+  // two query tiles per CTA where the sequence has an even number of them
+  const char* env = std::getenv("OXF_ATTENTION_TILES");  // measurement: "1" forces one
+  const bool two = a.tiles % 2 == 0 && !(env && std::strcmp(env, "1") == 0);
+  if (two)
+    return hd == 32 ? launch_attention_heads2<32>(tq, tk, tv, a, batch, heads, stream, dev)
+                    : launch_attention_heads2<64>(tq, tk, tv, a, batch, heads, stream, dev);
   return hd == 32 ? launch_attention_heads<32>(tq, tk, tv, a, batch, heads, stream, dev)
                   : launch_attention_heads<64>(tq, tk, tv, a, batch, heads, stream, dev);
 }
