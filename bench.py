@@ -648,7 +648,8 @@ def run_attention(a, torch):
     flops = 4.0 * seq * seq * d * n
     print(json.dumps({"metric": "fused multi-head attention TFLOP/s", "unit": "TFLOP/s",
                       "value": flops / ms / 1e9, "ms": ms, "workload": "attention",
-                      "kernel": "attention_heads_flash_kernel", "clocks": clocks,
+                      "kernel": "attention_heads_flash2_kernel (two query tiles per CTA)",
+                      "clocks": clocks,
                       "config": {"sequences": n, "seq_len": seq, "d": d, "heads": heads,
                                  "head_width": d // heads, "causal": False,
                                  "l2": "inputs larger than L2"}}), flush=True)

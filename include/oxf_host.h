@@ -98,8 +98,11 @@ oxf_status oxf_transformer_sgd(oxf_transformer t, float lr);
  * and K and [j*H/h, (j+1)*H/h) of V with scale 1/sqrt(D/h) and writes those
  * columns of the attention output; the projections and all other layers
  * are unchanged (the multi-head path docs/api.md:440-442 anticipates). h
- * must divide the query width D and hidden H (INVALID_ARG otherwise); the
- * score buffers grow to h per sequence. Takes effect from the next forward.
+ * must divide the query width D and hidden H (INVALID_ARG otherwise). Takes
+ * effect from the next forward. Inference runs the fused kernel
+ * (oxf_attention_heads_forward) where it applies and keeps no scores; the
+ * first training step, or inference the kernel cannot take, allocates score
+ * buffers of h per sequence (after synchronising the engine's stream).
  * The checkpoint format has no head count: a loaded engine has one head. */
 oxf_status oxf_transformer_set_heads(oxf_transformer t, int heads);
 int oxf_transformer_heads(oxf_transformer t);

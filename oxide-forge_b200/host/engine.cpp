@@ -287,22 +287,27 @@ void TransformerEngine::release(float* p) {
 }
 
 void TransformerEngine::set_heads(int h) {
-  const int S = spec_.seq, H = spec_.hidden, D = spec_.q.out;
+  const int H = spec_.hidden, D = spec_.q.out;
   require(h >= 1 && D % h == 0 && H % h == 0,
           "transformer: heads must divide the query width and hidden");
-  if (h > score_heads_) {
-    // per-head probabilities of every sequence, [heads, batch, S, S]
-    check_cuda_call(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
-    const size_t n = static_cast<size_t>(h) * max_batch_ * S * S;
-    float* p = alloc(n);
-    float* dp = alloc(n);
-    release(p_);
-    release(dp_);
-    p_ = p;
-    dp_ = dp;
-    score_heads_ = h;
-  }
   heads_ = h;
+}
+
+// The per-head probabilities of every sequence, [heads, batch, S, S], for
+// the paths that materialise them (training, and inference the fused kernel
+// cannot take); allocated on first use, after the stream drains.
+void TransformerEngine::ensure_score_buffers() {
+  if (heads_ <= score_heads_) return;
+  const int S = spec_.seq;
+  check_cuda_call(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+  const size_t n = static_cast<size_t>(heads_) * max_batch_ * S * S;
+  float* p = alloc(n);
+  float* dp = alloc(n);
+  release(p_);
+  release(dp_);
+  p_ = p;
+  dp_ = dp;
+  score_heads_ = heads_;
 }
 
 TransformerEngine::TransformerEngine(const TransformerSpec& spec, int max_batch,
@@ -466,6 +471,7 @@ void TransformerEngine::attention_heads_forward(int batch, bool causal, bool tra
       return;
     }
   }
+  ensure_score_buffers();
   const long long sSS = static_cast<long long>(S) * S, sSD = static_cast<long long>(S) * D,
                   sSH = static_cast<long long>(S) * H, head = static_cast<long long>(batch) * sSS;
   for (int j = 0; j < h; ++j)

@@ -174,7 +174,9 @@ class TransformerEngine {
   // [j*H/h, (j+1)*H/h) of V with scale 1/sqrt(D/h), writing those columns
   // of the attention output; the projections and every other layer are
   // unchanged. h must divide the query width D and hidden H. Takes effect
-  // from the next forward; the score buffers grow to h per sequence.
+  // from the next forward; the paths that keep per-head scores (training,
+  // and inference the fused kernel cannot take) grow the score buffers to h
+  // per sequence on first use.
   void set_heads(int h);
   int heads() const { return heads_; }
   // GEMM event timing (off by default).
@@ -198,6 +200,7 @@ class TransformerEngine {
   // products over column slices (training keeps P for backward)
   void attention_heads_forward(int batch, bool causal, bool training);
   void attention_heads_backward(int batch);
+  void ensure_score_buffers();
   void qkv_project(int batch);
 
   TransformerSpec spec_;
