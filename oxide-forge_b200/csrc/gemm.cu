@@ -2469,6 +2469,7 @@ oxf_status gemm_tf32x3_noalloc(const oxf_gemm_desc* d, cudaStream_t stream) {
 // head split). Warp 0 issues the TMA loads, warp 1 the MMAs, warps 2-9 run
 // the softmax, two threads per query row. Every wait is bounded.
 constexpr int FA_ROWS = 128;
+constexpr float FA_RESCALE = 8.0f;  // see the softmax: lazy output rescaling
 constexpr int FA_SOFTMAX_WARPS = 8;
 constexpr int FA_THREADS = 64 + 32 * FA_SOFTMAX_WARPS;
 
@@ -2715,8 +2716,13 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       }
       tc_fence_after();
       const float mt = fmaxf(mine, tmem_ld_32x32b_x1(row_tmem + Cfg::X_COL + sb * 2 + (1 - half)));
-      const float m_new = fmaxf(m, mt * scale2);  // scale2 > 0
-      const float alpha = ex2_approx(m - m_new);  // 0 on the first tile
+      // The exponent reference m moves only when the tile's maximum exceeds it
+      // by more than FA_RESCALE (log2 units): probabilities then stay <= 2^8,
+      // and the output rescale below is skipped on most tiles. O / l does not
+      // depend on the reference.
+      const float mts = mt * scale2;  // scale2 > 0
+      const float m_new = mts > m + FA_RESCALE ? mts : m;
+      const float alpha = ex2_approx(m - m_new);  // 1 if kept; 0 on the first tile
       float sm[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int c = 0; c < 2; ++c)
@@ -3029,8 +3035,13 @@ __global__ void __launch_bounds__(FA2_THREADS, 1)
         }
       }
       const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-      const float m_new = fmaxf(m, mt * scale2);  // scale2 > 0
-      const float alpha = ex2_approx(m - m_new);  // 0 on the first tile
+      // The exponent reference m moves only when the tile's maximum exceeds it
+      // by more than FA_RESCALE (log2 units): probabilities then stay <= 2^8,
+      // and the output rescale below is skipped on most tiles. O / l does not
+      // depend on the reference.
+      const float mts = mt * scale2;  // scale2 > 0
+      const float m_new = mts > m + FA_RESCALE ? mts : m;
+      const float alpha = ex2_approx(m - m_new);  // 1 if kept; 0 on the first tile
       float sm[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int c = 0; c < 4; ++c)

@@ -272,6 +272,72 @@ class Transformer:
             pass
 
 
+class TransformerStack:
+    """A stack of L Post-Norm transformer blocks, block i's output feeding
+    block i+1 (every block but the last maps hidden to hidden). The reference
+    executor takes exactly one block (model.rs:448-449, although its
+    checkpoint metadata carries a block count); this is the multi-block
+    executor built from single-block engines. Forward chains the blocks;
+    backward sets the last block's loss gradient, then hands each block's
+    input gradient to the block below as its output gradient
+    (oxf_transformer_set_output_gradient). Gradients accumulate per block,
+    and sgd applies each block's step. Every kernel is the library's; only
+    the loop over blocks is here."""
+
+    def __init__(self, cfgs, max_batch: int = 1, stream=None, heads: int = 1):
+        cfgs = list(cfgs)
+        if not cfgs:
+            raise ValueError("a stack needs at least one block")
+        for lo, hi in zip(cfgs, cfgs[1:]):
+            if lo.out != hi.hidden or lo.seq != hi.seq:
+                raise ValueError("block output width must equal the next block's hidden")
+        self.blocks = [Transformer(c, max_batch, stream, heads=heads) for c in cfgs]
+
+    def __len__(self) -> int:
+        return len(self.blocks)
+
+    def set_params(self, flats) -> None:
+        for b, f in zip(self.blocks, flats):
+            b.set_params(f)
+
+    def get_params(self):
+        return [b.get_params() for b in self.blocks]
+
+    def forward(self, x: torch.Tensor, causal: bool = False) -> torch.Tensor:
+        for b in self.blocks:
+            x = b.forward(x, causal)
+        return x
+
+    def train_forward(self, x: torch.Tensor) -> torch.Tensor:
+        for b in self.blocks:
+            x = b.train_forward(x)
+        return x
+
+    def set_target(self, target: torch.Tensor) -> torch.Tensor:
+        """Row losses of the last block's output against target."""
+        return self.blocks[-1].set_target(target)
+
+    def backward(self) -> torch.Tensor:
+        """dL/dx of the stack's input; parameter gradients accumulate."""
+        dx = self.blocks[-1].backward()
+        for b in reversed(self.blocks[:-1]):
+            b.set_output_gradient(dx)
+            dx = b.backward()
+        return dx
+
+    def zero_grads(self) -> None:
+        for b in self.blocks:
+            b.zero_grads()
+
+    def sgd(self, lr: float) -> None:
+        for b in self.blocks:
+            b.sgd(lr)
+
+    def close(self) -> None:
+        for b in self.blocks:
+            b.close()
+
+
 class Mlp:
     """Batched MlpExecutor (forward, backward with deferred SGD)."""
 

@@ -246,6 +246,49 @@ def test_set_heads_rejects_non_divisors(M):
     eng.close()
 
 
+def test_two_block_stack_matches_oracle_composition(M):
+    """TransformerStack: two blocks, block 1's output feeding block 2, one
+    training step on two sequences. The oracle runs block 2's reference step
+    on block 1's output; block 1's step then gets block 2's input gradient
+    as its output gradient (a target of y1 - dL/dy1 * width gives exactly
+    that MSE gradient). Outputs, input gradients and every tensor's summed
+    gradient against the oracle."""
+    seq, hidden, ffn, B = 32, 64, 128, 2
+    cfgs = [M.transformer_config(seq, hidden, ffn, norm=1),
+            M.transformer_config(seq, hidden, ffn, norm=0, bias=True)]
+    flats = [M.init_transformer_params(c, seed=40 + i) for i, c in enumerate(cfgs)]
+    rng = np.random.default_rng(12)
+    x = rng.standard_normal((B, seq, hidden)).astype(np.float32)
+    t = rng.standard_normal((B, seq, hidden)).astype(np.float32)
+    g_ref = [np.zeros(f.size, np.float32) for f in flats]
+    ys, dxs = [], []
+    for b in range(B):
+        r1, r2 = (oracle_model(M, c, f) for c, f in zip(cfgs, flats))
+        y1 = O.transformer_forward(r1, x[b], rounding=RZ)
+        y2, _, dy1 = O.transformer_train_step(r2, y1, t[b], 0.0, grads=g_ref[1], rounding=RZ)
+        _, _, dx = O.transformer_train_step(oracle_model(M, cfgs[0], flats[0]), x[b],
+                                            y1 - dy1 * np.float32(hidden), 0.0, grads=g_ref[0],
+                                            rounding=RZ)
+        ys.append(y2)
+        dxs.append(dx)
+    st = M.TransformerStack(cfgs, max_batch=B)
+    st.set_params(flats)
+    st.zero_grads()
+    y = host(st.train_forward(dev(x.reshape(B * seq, hidden))))
+    st.set_target(dev(t.reshape(B * seq, hidden)))
+    dx = host(st.backward())
+    assert rel_err(y, np.concatenate(ys)) < FWD_TOL
+    assert rel_err(dx, np.concatenate(dxs)) < GRAD_TOL
+    for blk, cfg, gr in zip(st.blocks, cfgs, g_ref):
+        check_per_tensor(cfg, host(blk.grads), gr)
+    # inference through the stack equals the training forward's output
+    np.testing.assert_allclose(host(st.forward(dev(x.reshape(B * seq, hidden)))), y,
+                               rtol=0, atol=1e-5 * np.abs(y).max())
+    with pytest.raises(ValueError):
+        M.TransformerStack([M.transformer_config(seq, hidden, ffn, out=32), cfgs[1]])
+    st.close()
+
+
 def test_train_step_host_api(M):
     """The host-memory step (H2D, forward, loss, backward, SGD on the mean
     gradient, loss D2H) equals the device-level calls."""
