@@ -17,6 +17,8 @@ namespace oxf {
 
 // rows.cu
 oxf_status rows_read_device_error(uint32_t*);
+// attention.cu
+oxf_status attention_read_device_error(uint32_t*);
 oxf_status rows_softmax(float*, long long, long long, float, long long, cudaStream_t);
 oxf_status rows_softmax_bwd(const float*, const float*, float*, long long, long long, float,
                             cudaStream_t);
@@ -132,12 +134,13 @@ oxf_status oxf_device_error(uint32_t* code) {
   if (!code) return set_error(OXF_ERR_INVALID_ARG, "oxf_device_error: null code");
   OXF_TRY(check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize"));
   // Each translation unit with bounded waits has its own word; report the
-  // first nonzero one and clear all three.
-  uint32_t g = 0, x = 0, r = 0;
+  // first nonzero one and clear them all.
+  uint32_t g = 0, x = 0, r = 0, a = 0;
   OXF_TRY(gemm_read_device_error(&g));
   OXF_TRY(exchange_read_device_error(&x));
   OXF_TRY(rows_read_device_error(&r));
-  *code = g ? g : (x ? x : r);
+  OXF_TRY(attention_read_device_error(&a));
+  *code = g ? g : (x ? x : (r ? r : a));
   return OXF_OK;
 }
 

@@ -45,8 +45,8 @@ enum DeviceErrorCode : uint32_t {
 }  // namespace oxf
 
 // One error word per translation unit that includes this header. The GEMM,
-// row-kernel and exchange translation units have bounded waits; each exposes
-// its word to oxf_device_error().
+// attention, row-kernel and exchange translation units have bounded waits;
+// each exposes its word to oxf_device_error().
 static __device__ unsigned int g_oxf_device_error = 0;
 
 namespace oxf {
