@@ -205,3 +205,16 @@ def test_plain_c_client(tmp_path):
     assert r.returncode == 0, r.stderr
     assert r.stdout.strip() == "ok"
     assert (tmp_path / "mlp_ckpt.toml").exists() and (tmp_path / "mlp_ckpt.bin").exists()
+
+
+def test_stack_validates_block_widths_without_gpu():
+    """TransformerStack refuses blocks whose widths do not chain (block i's
+    output must be block i+1's hidden width, at the same sequence length)
+    before it creates any engine."""
+    from oxf import models
+    a = models.transformer_config(16, 64, 128, out=32)
+    b = models.transformer_config(16, 64, 128)
+    c = models.transformer_config(8, 64, 128)
+    for cfgs in ([a, b], [b, c], []):
+        with pytest.raises(ValueError):
+            models.TransformerStack(cfgs)
