@@ -1,6 +1,6 @@
 #!/usr/bin/env python
-"""Benchmark: Transformer fwd+bwd tokens/s (BASELINE.json metric) on the
-training config: single-head Post-Norm transformer, seq 1024, hidden 2048,
+"""Benchmark: Transformer fwd+bwd tokens/s (the headline metric) on the
+training config (config 5): single-head Post-Norm transformer, seq 1024, hidden 2048,
 FFN 2048->8192->2048 GELU, NormType::Layer, output width = hidden,
 Xavier-uniform weights, inputs and MSE targets N(0,1); a global batch of
 128 sequences, data-parallel over the GPUs (one process per GPU, NCCL

@@ -107,7 +107,7 @@ class TransformerConfig:
 
 def transformer_config(seq, hidden, ffn, out=None, norm=_lib.NORM_LAYER, bias=False,
                        ffn_act=_lib.ACT_GELU) -> TransformerConfig:
-    """The BASELINE transformer shape: FFN hidden -> ffn (GELU) -> hidden."""
+    """The configurations' transformer shape: FFN hidden -> ffn (GELU) -> hidden."""
     mlp = MlpConfig([Layer(hidden, ffn, ffn_act, bias), Layer(ffn, hidden, _lib.ACT_IDENTITY, bias)])
     return TransformerConfig(seq, hidden, mlp, out or hidden, norm, bias=bias)
 

@@ -1,4 +1,4 @@
-"""Every BASELINE configuration at its own size, on the GPU, against the
+"""Every benchmark configuration (configs 1-5) at its own size, on the GPU, against the
 oracle (oracle/oxf_oracle.c, multithreaded) or float64.
 
 GEMM-bearing outputs are compared with the oracle run in the reference's
@@ -13,8 +13,8 @@ max|want| of the same output unless a scale is named:
   row / elementwise kernels                    1e-5 (backward kernels: of the
                                                scale of the terms they combine)
 
-Config sources: BASELINE.json configs[0..4]; layouts and distributions as
-named there (seeded host RNGs, numpy default_rng).
+Layouts and distributions are the configurations' own (seeded host RNGs,
+numpy default_rng).
 """
 from __future__ import annotations
 
