@@ -85,7 +85,9 @@ oxf_status oxf_transformer_set_target(oxf_transformer t, const float* target);
 oxf_status oxf_transformer_set_output_gradient(oxf_transformer t, const float* dy);
 /* TrainingTransformer::backward (encoder.rs:135-186) in stages 0 (output
  * Linear), 1 (feed-forward), 2 (attention, Q/K/V, position). Parameter
- * gradients ACCUMULATE into the gradient arena; nothing is updated. */
+ * gradients ACCUMULATE into the gradient arena; nothing is updated. Needs
+ * oxf_transformer_train_forward as the last forward: the inference forward
+ * keeps neither probabilities nor pre-activations (OXF_ERR_INVALID_ARG). */
 oxf_status oxf_transformer_backward_stage(oxf_transformer t, int stage);
 /* [offset, offset+count) of the gradient arena that stage writes. */
 oxf_status oxf_transformer_bucket(oxf_transformer t, int stage, size_t* offset, size_t* count);

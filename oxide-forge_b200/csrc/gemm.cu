@@ -1725,13 +1725,14 @@ oxf_status launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
 }
 
 // Chooses how many K splits an accumulating GEMM uses: minimises
-// waves * k-blocks-per-unit plus a per-split epilogue cost.
-int choose_splits(long long tiles, int kblocks, int sms) {
+// waves * k-blocks-per-unit plus a per-split epilogue cost, for `slots`
+// concurrent units (SMs, or CTA pairs for pair tiles).
+int choose_splits(long long tiles, int kblocks, int slots) {
   int best = 1;
   double best_cost = 1e300;
   for (int s = 1; s <= 32 && s <= kblocks; ++s) {
     const long long units = tiles * s;
-    const long long waves = (units + sms - 1) / sms;
+    const long long waves = (units + slots - 1) / slots;
     const double cost = static_cast<double>(waves) * ((kblocks + s - 1) / s) + 2.0 * s;
     if (cost < best_cost - 1e-9) {
       best_cost = cost;
@@ -2082,12 +2083,12 @@ oxf_status gemm_run_fused(const oxf_gemm_desc* d, const GemmFuse* fuse, cudaStre
     const long long mt = (d->M + 2 * BM - 1) / (2 * BM), nb = d->reduce_batch ? 1 : d->batch;
     long long units_w = mt * ((d->N + 511) / 512) * nb;
     long long units_n = mt * ((d->N + 255) / 256) * nb;
+    const long long pairs = sms / 2;
     if (d->accumulate && split <= 1 && !d->bias && !d->residual) {
       // split K as the launch below will, so that the fill compares units
-      units_w *= choose_splits(units_w, static_cast<int>(kbl), sms);
-      units_n *= choose_splits(units_n, static_cast<int>(kbl), sms);
+      units_w *= choose_splits(units_w, static_cast<int>(kbl), static_cast<int>(pairs));
+      units_n *= choose_splits(units_n, static_cast<int>(kbl), static_cast<int>(pairs));
     }
-    const long long pairs = sms / 2;
     auto fill = [pairs](long long t) {
       return static_cast<double>(t) / static_cast<double>(((t + pairs - 1) / pairs) * pairs);
     };
@@ -2129,8 +2130,9 @@ oxf_status gemm_run_fused(const oxf_gemm_desc* d, const GemmFuse* fuse, cudaStre
     // Each K split adds its partial product into C, so terms added once per
     // output (bias, residual) rule splitting out.
     const bool additive = d->bias != nullptr || d->residual != nullptr;
+    // waves are counted in CTA pairs for pair tiles
     a.splits = split > 1 ? std::min(split, a.kblocks)
-                         : (additive ? 1 : choose_splits(tiles, a.kblocks, sms));
+                         : (additive ? 1 : choose_splits(tiles, a.kblocks, pair ? sms / 2 : sms));
   } else if (autosplit) {
     a.splits = choose_splits(tiles, a.kblocks, pair ? sms / 2 : sms);
     if (a.splits > 1) {

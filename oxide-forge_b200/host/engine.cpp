@@ -193,7 +193,7 @@ float* MlpEngine::bias_grad(int i) const {
 // MlpExecutor::forward / TrainingMlp::forward (mlp.rs:53-85, 233-254):
 // Linear::forward per layer (GEMM, bias, residual, activation) as one GEMM.
 void MlpEngine::forward(const float* x, float* y, size_t rows, const float* extra_residual,
-                        cudaStream_t s) {
+                        cudaStream_t s, bool keep_pre) {
   require(rows <= max_rows_, "MlpEngine::forward: more rows than the engine was sized for");
   const int L = static_cast<int>(spec_.layers.size());
   x_ = x;
@@ -211,7 +211,10 @@ void MlpEngine::forward(const float* x, float* y, size_t rows, const float* extr
       g.residual(extra_residual, l.out);
       extra_fused = true;
     }
-    if (l.act != OXF_ACT_IDENTITY) g.pre_out(pres_[i], l.out).act(l.act);
+    if (l.act != OXF_ACT_IDENTITY) {
+      if (keep_pre) g.pre_out(pres_[i], l.out);
+      g.act(l.act);
+    }
     g.run(s);
     if (i == L - 1 && extra_residual && !extra_fused)
       check(oxf_slice_binary_assign(ms(out, rows * l.out), cs(extra_residual, rows * l.out),
@@ -372,7 +375,7 @@ TransformerEngine::~TransformerEngine() {
 // Q, K, V = act(pos·W + b) (QkvProjection::project, attention.rs:65-94): one
 // batched GEMM when the three projections share shape, activation and have
 // no bias; otherwise three GEMMs.
-void TransformerEngine::qkv_project(int batch) {
+void TransformerEngine::qkv_project(int batch, bool keep_pre) {
   const int H = spec_.hidden;
   const int T = batch * spec_.seq;
   const int D = spec_.q.out;
@@ -385,8 +388,10 @@ void TransformerEngine::qkv_project(int batch) {
   if (uniform) {
     Gemm g(T, D, H, false, false, pos_, params_ + off_q_, qkv_);
     g.batch(3, 0, static_cast<long long>(spec_.q.param_count()), static_cast<long long>(T) * D);
-    if (spec_.q.act)
-      g.pre_out(qkv_pre_, D, static_cast<long long>(T) * D).act(spec_.q.act);
+    if (spec_.q.act) {
+      if (keep_pre) g.pre_out(qkv_pre_, D, static_cast<long long>(T) * D);
+      g.act(spec_.q.act);
+    }
     g.run(stream_);
     return;
   }
@@ -394,7 +399,10 @@ void TransformerEngine::qkv_project(int batch) {
     const LayerSpec& l = *ls[j];
     Gemm g(T, l.out, H, false, false, pos_, params_ + offs[j], outs[j]);
     if (l.bias) g.bias(params_ + offs[j] + static_cast<size_t>(l.in) * l.out);
-    if (l.act) g.pre_out(qkv_pre_ + (outs[j] - qkv_), l.out).act(l.act);
+    if (l.act) {
+      if (keep_pre) g.pre_out(qkv_pre_ + (outs[j] - qkv_), l.out);
+      g.act(l.act);
+    }
     g.run(stream_);
   }
 }
@@ -405,7 +413,7 @@ void TransformerEngine::attention_forward(const float* x, int batch, bool causal
   // positioned = input + position (inference.rs:78, encoder.rs:117)
   check(oxf_slice_binary_broadcast(cs(x, T * H), cs(params_ + off_pos_, static_cast<size_t>(S) * H),
                                    ms(pos_, T * H), OXF_ADD, ST(stream_)));
-  qkv_project(batch);
+  qkv_project(batch, training);
   const float* q = qkv_;
   const float* k = qkv_ + T * D;
   const float* v = qkv_ + 2 * T * D;
@@ -539,18 +547,22 @@ void TransformerEngine::forward_impl(const float* x, int batch, bool causal, boo
   TimingScope timing_scope(this);
   require(batch >= 1 && batch <= max_batch_, "transformer: batch outside [1, max_batch]");
   batch_ = batch;
+  trained_ = training;
   const int H = spec_.hidden;
   const size_t T = static_cast<size_t>(batch) * spec_.seq;
   attention_forward(x, batch, causal, training);
-  // ffn + residual (inference.rs:90-101)
-  ffn_->forward(h1_, pre2_, T, h1_, stream_);
+  // ffn + residual (inference.rs:90-101); inference keeps no pre-activations
+  ffn_->forward(h1_, pre2_, T, h1_, stream_, training);
   check(oxf_norm_rows(cs(pre2_, T * H), ms(enc_, T * H), H, spec_.norm, 1e-5f, nullptr, nullptr,
                       ST(stream_)));
   // output Linear (inference.rs:102-107)
   const LayerSpec& o = spec_.o;
   Gemm g(static_cast<int>(T), o.out, H, false, false, enc_, params_ + off_o_, y_);
   if (o.bias) g.bias(params_ + off_o_ + static_cast<size_t>(o.in) * o.out);
-  if (o.act) g.pre_out(zo_, o.out).act(o.act);
+  if (o.act) {
+    if (training) g.pre_out(zo_, o.out);
+    g.act(o.act);
+  }
   g.run(stream_);
 }
 
@@ -587,6 +599,7 @@ void TransformerEngine::backward_stage(int stage) {
   const int S = spec_.seq, H = spec_.hidden, D = spec_.q.out;
   const int batch = batch_;
   require(batch >= 1, "backward before forward");
+  require(trained_, "backward needs the training forward (train_forward), not the inference one");
   const size_t T = static_cast<size_t>(batch) * S;
   const int Ti = static_cast<int>(T);
   const LayerSpec& o = spec_.o;

@@ -112,9 +112,10 @@ class MlpEngine {
   float* bias_grad(int i) const;
 
   // y = MLP(x) (+ extra_residual added after the last activation).
-  // x must stay valid until backward; with keep = false nothing is kept.
+  // x must stay valid until backward. keep_pre = false (inference) skips
+  // storing the pre-activations, which only backward reads.
   void forward(const float* x, float* y, size_t rows, const float* extra_residual,
-               cudaStream_t s);
+               cudaStream_t s, bool keep_pre = true);
   // Given dL/dy, accumulates parameter gradients and writes dL/dx
   // (+ extra_dx added to it). Requires the preceding forward.
   void backward(const float* dy, float* dx, size_t rows, const float* extra_dx, cudaStream_t s);
@@ -201,7 +202,7 @@ class TransformerEngine {
   void attention_heads_forward(int batch, bool causal, bool training);
   void attention_heads_backward(int batch);
   void ensure_score_buffers();
-  void qkv_project(int batch);
+  void qkv_project(int batch, bool keep_pre);
 
   TransformerSpec spec_;
   int max_batch_;
@@ -212,6 +213,7 @@ class TransformerEngine {
   float* grads_ = nullptr;
   MlpEngine* ffn_ = nullptr;
   int batch_ = 0;
+  bool trained_ = false;  // the last forward kept what backward reads
   // activations
   float *x_ = nullptr, *pos_ = nullptr, *qkv_ = nullptr, *qkv_pre_ = nullptr, *p_ = nullptr;
   float* stats_ = nullptr;  // softmax row statistics of the fused inference attention

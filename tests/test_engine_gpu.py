@@ -246,6 +246,25 @@ def test_set_heads_rejects_non_divisors(M):
     eng.close()
 
 
+def test_backward_needs_the_training_forward(M):
+    """The inference forward stores no pre-activations (FFN, output Linear)
+    and no probabilities, so a backward after it is refused; after
+    train_forward it runs, and both forwards give the same output."""
+    rng = np.random.default_rng(31)
+    cfg = M.transformer_config(32, 64, 128)
+    eng = M.Transformer(cfg, max_batch=1)
+    eng.set_params(rng.uniform(-0.1, 0.1, cfg.param_count()).astype(np.float32))
+    x = dev(rng.standard_normal((32, 64)))
+    y_inf = host(eng.forward(x))
+    with pytest.raises(RuntimeError, match="train_forward"):
+        eng.backward_stage(0)
+    y_tr = host(eng.train_forward(x))
+    assert rel_err(y_inf, y_tr) < FWD_TOL
+    eng.set_target(dev(rng.standard_normal((32, 64))))
+    eng.backward()
+    eng.close()
+
+
 def test_two_block_stack_matches_oracle_composition(M):
     """TransformerStack: two blocks, block 1's output feeding block 2, one
     training step on two sequences. The oracle runs block 2's reference step
