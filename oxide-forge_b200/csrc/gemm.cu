@@ -2074,9 +2074,10 @@ oxf_status gemm_run_fused(const oxf_gemm_desc* d, const GemmFuse* fuse, cudaStre
   // through L2, but a tile fills TMEM, so its epilogue no longer overlaps the
   // next tile's MMAs. Taken whenever the fewer, larger tiles fill the last
   // wave of CTA pairs about as well, except for short-K products whose
-  // epilogue reads an input tile or writes a second output: there the
-  // exposed epilogue outweighs the saved bytes, and the 256-wide tile's two
-  // accumulators hide it. OXF_GEMM_TILE=256 / 512 overrides the choice.
+  // epilogue reads an input tile, writes a second output or applies an
+  // activation: there the exposed epilogue outweighs the saved bytes, and
+  // the 256-wide tile's two accumulators hide it. OXF_GEMM_TILE=256 / 512
+  // overrides the choice.
   if (pair && !split3) {
     const long long kbl = static_cast<long long>((d->K + BK - 1) / BK) *
                           (d->reduce_batch ? d->batch : 1);
@@ -2092,7 +2093,9 @@ oxf_status gemm_run_fused(const oxf_gemm_desc* d, const GemmFuse* fuse, cudaStre
     auto fill = [pairs](long long t) {
       return static_cast<double>(t) / static_cast<double>(((t + pairs - 1) / pairs) * pairs);
     };
-    const bool heavy_epilogue = d->pre_out || d->aux || d->residual || d->beta != 0.0f;
+    // an activation makes a drain of the same bytes about half as long again
+    const bool heavy_epilogue = d->pre_out || d->aux || d->residual || d->beta != 0.0f ||
+                                d->act != OXF_ACT_IDENTITY;
     bool wide = d->variant == 3 ||
                 (d->variant == 0 && d->N >= 512 && units_w >= pairs &&
                  (kbl >= kWideMinKBlocks || !heavy_epilogue) &&
