@@ -358,11 +358,16 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 
 // Two query tiles per CTA (rows 256*i .. 256*i+255 of one head of one
 // sequence), so that the tensor cores work on one tile's products while the
-// other tile's softmax runs: the MMA thread issues, per key/value tile t,
-// P·V of tile A, S of tile A for t+1, P·V of tile B, S of tile B for t+1.
-// Each query tile has its own score buffer (128 TMEM columns, overwritten
-// by its P), output accumulator and group of four softmax warps (one thread
-// per row). K and V are loaded once for both tiles.
+// other tile's softmax runs. Each query tile has its own score buffer (128
+// TMEM columns), output accumulator and group of four softmax warps (one
+// thread per row); the probabilities of both tiles pass through one shared
+// 128-column P buffer. A tile's next scores S(t+1) are issued as soon as its
+// softmax has loaded S(t) into registers, so they overlap that softmax's
+// exponentials instead of waiting for its P·V; P·V of one tile reads the P
+// buffer while the other tile's softmax computes, and a softmax writes P
+// once the previous P·V (in issue order: A(t), B(t), A(t+1), ...) has read
+// it. Per key/value tile t the MMA thread issues S_A(t+1), S_B(t+1),
+// P·V_A(t), P·V_B(t). K and V are loaded once for both tiles.
 constexpr int FA2_THREADS = 64 + 32 * 8;
 
 template <int HD>
@@ -376,7 +381,9 @@ struct Fa2Cfg {
   static constexpr int CTRL_BYTES = 2048;
   static constexpr int SMEM_BYTES =
       1024 + CTRL_BYTES + 2 * Q_BYTES + STAGES * (K_BYTES + V_BYTES);
-  static constexpr uint32_t TMEM_COLS = 512;  // S_A 0, S_B 128, O_A 256, O_B 320
+  static constexpr uint32_t TMEM_COLS = 512;  // S_A 0, S_B 128, P 256, O_A 384, O_B 384 + HD
+  static constexpr uint32_t P_COL = 256;
+  static constexpr uint32_t O_COL = 384;
   static_assert(HD == 32 || HD == 64, "head widths 32 and 64");
   static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
@@ -386,9 +393,9 @@ struct Fa2Ctrl {
   uint64_t k_full[FA_MAX_STAGES], k_empty[FA_MAX_STAGES];
   uint64_t v_full[FA_MAX_STAGES], v_empty[FA_MAX_STAGES];
   uint64_t s_full[2];   // per query tile: S landed
-  uint64_t s_free[2];   // per query tile: its P·V finished (S may be overwritten)
-  uint64_t p_ready[2];  // per query tile: P in TMEM, O rescaled
-  uint64_t pv_done[2];  // per query tile: P·V finished
+  uint64_t s_read[2];   // per query tile: its softmax holds S in registers (S may be overwritten)
+  uint64_t p_ready[2];  // per query tile: P in the shared P buffer, O rescaled
+  uint64_t pv_done[2];  // per query tile: P·V finished (O final for t, P buffer read)
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -430,7 +437,7 @@ __global__ void __launch_bounds__(FA2_THREADS, 1)
 #pragma unroll
     for (int g = 0; g < 2; ++g) {
       mbar_init(&ctrl->s_full[g], 1);
-      mbar_init(&ctrl->s_free[g], 1);
+      mbar_init(&ctrl->s_read[g], 4);
       mbar_init(&ctrl->p_ready[g], 4);
       mbar_init(&ctrl->pv_done[g], 1);
     }
@@ -499,9 +506,9 @@ __global__ void __launch_bounds__(FA2_THREADS, 1)
       constexpr uint32_t id_s = make_idesc_tf32(128, 128, false, false);
       constexpr uint32_t id_o = make_idesc_tf32(128, HD, false, true);
       const uint32_t q_addr = smem_u32(qs), k_addr = smem_u32(ks), v_addr = smem_u32(vs);
-      // S_g = Q_g · K_tᵀ into tile g's buffer, once its previous P·V is done
+      // S_g = Q_g · K_tᵀ into tile g's buffer, once its softmax holds S_g(t-1)
       auto issue_s = [&](int g, int t) -> bool {
-        if (t > 0 && !mbar_wait(&ctrl->s_free[g], (t - 1) & 1, DEVERR_ATTN_WAIT)) return false;
+        if (t > 0 && !mbar_wait(&ctrl->s_read[g], (t - 1) & 1, DEVERR_ATTN_WAIT)) return false;
         tc_fence_after();
         const int st = t % NS;
 #pragma unroll
@@ -517,7 +524,7 @@ __global__ void __launch_bounds__(FA2_THREADS, 1)
         umma_commit(&ctrl->s_full[g]);
         return true;
       };
-      // O_g += P_g · V_t, P read from tile g's score buffer in TMEM
+      // O_g += P_g · V_t, P read from the shared P buffer in TMEM
       auto issue_pv = [&](int g, int t) -> bool {
         const int st = t % NS;
         if (!mbar_wait(&ctrl->p_ready[g], t & 1, DEVERR_ATTN_WAIT) ||
@@ -528,12 +535,13 @@ __global__ void __launch_bounds__(FA2_THREADS, 1)
         for (int kb = 0; kb < 4; ++kb)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_tf32_tmem_a(tmem + 256 + g * 64, tmem + g * 128 + kb * 32 + kk * 8,
+            umma_tf32_tmem_a(tmem + Cfg::O_COL + g * HD, tmem + Cfg::P_COL + kb * 32 + kk * 8,
                              desc_advance(operand_desc(v_addr + st * Cfg::V_BYTES +
                                                            kb * Cfg::V_KBLOCK,
                                                        1, 0),
                                           kk * 1024),
                              id_o, (t > 0 || kb > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&ctrl->pv_done[g]);
         return true;
       };
       bool ok = mbar_wait(&ctrl->q_full, 0, DEVERR_ATTN_WAIT) &&
@@ -542,27 +550,16 @@ __global__ void __launch_bounds__(FA2_THREADS, 1)
       if (ok) umma_commit(&ctrl->k_empty[0]);
       for (int t = 0; ok && t < n_b; ++t) {
         const int st = t % NS;
-        const bool next = t + 1 < n_b;
         const int st1 = (t + 1) % NS;
-        if (t < n_a) {
-          ok = issue_pv(0, t);
-          if (!ok) break;
-          umma_commit(&ctrl->s_free[0]);
-          umma_commit(&ctrl->pv_done[0]);
-        }
-        if (next && !(ok = mbar_wait(&ctrl->k_full[st1], ((t + 1) / NS) & 1, DEVERR_ATTN_WAIT)))
-          break;
-        if (t + 1 < n_a && !(ok = issue_s(0, t + 1))) break;
-        ok = issue_pv(1, t);
-        if (!ok) break;
-        // tile B is the last reader of V_t
-        umma_commit(&ctrl->v_empty[st]);
-        umma_commit(&ctrl->s_free[1]);
-        umma_commit(&ctrl->pv_done[1]);
-        if (next) {
+        if (t + 1 < n_b) {
+          if (!(ok = mbar_wait(&ctrl->k_full[st1], ((t + 1) / NS) & 1, DEVERR_ATTN_WAIT))) break;
+          if (t + 1 < n_a && !(ok = issue_s(0, t + 1))) break;
           if (!(ok = issue_s(1, t + 1))) break;
           umma_commit(&ctrl->k_empty[st1]);  // tile B is the last reader of K_{t+1}
         }
+        if (t < n_a && !(ok = issue_pv(0, t))) break;
+        if (!(ok = issue_pv(1, t))) break;
+        umma_commit(&ctrl->v_empty[st]);  // tile B is the last reader of V_t
       }
       if (!ok) ctrl->abort_flag = 1;
     }
@@ -576,7 +573,8 @@ __global__ void __launch_bounds__(FA2_THREADS, 1)
     const int diag_t = qa + g;  // the tile's diagonal key/value tile (causal)
     const uint32_t row_tmem = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const uint32_t s_row = row_tmem + g * 128;
-    const uint32_t o_row = row_tmem + 256 + g * 64;
+    const uint32_t p_row = row_tmem + Cfg::P_COL;
+    const uint32_t o_row = row_tmem + Cfg::O_COL + g * HD;
     const float scale2 = args.scale * 1.4426950408889634f;  // exp(s * scale) = 2^(s * scale2)
     float m = -INFINITY, l = 0.0f;
     bool ok = true;
@@ -598,6 +596,10 @@ __global__ void __launch_bounds__(FA2_THREADS, 1)
           mx[j & 3] = fmaxf(mx[j & 3], v[c][j]);
         }
       }
+      // S(t) is in registers: the MMA thread may overwrite it with S(t+1)
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctrl->s_read[g]);
       const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
       // The exponent reference m moves only when the tile's maximum exceeds it
       // by more than FA_RESCALE (log2 units): probabilities then stay <= 2^8,
@@ -617,13 +619,20 @@ __global__ void __launch_bounds__(FA2_THREADS, 1)
         }
       l = l * alpha + ((sm[0] + sm[1]) + (sm[2] + sm[3]));
       m = m_new;
-      if (t > 0) {
-        // the tile's previous P·V has finished: O holds key tiles 0..t-1
-        if (!mbar_wait(&ctrl->pv_done[g], (t - 1) & 1, DEVERR_ATTN_WAIT)) {
+      // The P buffer's previous reader, in P·V issue order A(0), B(0), A(1),
+      // ...: B(t-1) for tile A; A(t) for tile B, or B(t-1) where A has no
+      // key tile t (causal). Its completion also covers this tile's own
+      // previous P·V, issued before it: O then holds key tiles 0..t-1.
+      if (g == 1 || t > 0) {
+        const int gb = (g == 0 || t < n_a) ? 1 - g : g;
+        const int done = (g == 1 && t < n_a) ? t : t - 1;
+        if (!mbar_wait(&ctrl->pv_done[gb], static_cast<uint32_t>(done & 1), DEVERR_ATTN_WAIT)) {
           ok = false;
           break;
         }
         tc_fence_after();
+      }
+      if (t > 0) {
         if (__any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll
           for (int c = 0; c < HD / 32; ++c) {
@@ -635,9 +644,9 @@ __global__ void __launch_bounds__(FA2_THREADS, 1)
           }
         }
       }
-      // P over the scores: the A operand of this tile's P·V
+      // P into the shared buffer: the A operand of this tile's P·V
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_st_32x32b_x32(s_row + c * 32, v[c]);
+      for (int c = 0; c < 4; ++c) tmem_st_32x32b_x32(p_row + c * 32, v[c]);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
