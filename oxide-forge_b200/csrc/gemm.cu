@@ -2073,7 +2073,9 @@ oxf_status gemm_run_fused(const oxf_gemm_desc* d, const GemmFuse* fuse, cudaStre
   // Wide pair tiles (256 x 512): a quarter fewer operand bytes per flop
   // through L2, but a tile fills TMEM, so its epilogue no longer overlaps the
   // next tile's MMAs. Taken whenever the fewer, larger tiles fill the last
-  // wave of CTA pairs about as well, except for short-K products whose
+  // wave of CTA pairs about as well and keep at least 3/4 of the pairs busy
+  // (config 3's 8192-row products: 64 wide units, against 64 or 128 on the
+  // 256 tile, run 3-18% faster wide), except for short-K products whose
   // epilogue reads an input tile, writes a second output or applies an
   // activation: there the exposed epilogue outweighs the saved bytes, and
   // the 256-wide tile's two accumulators hide it. OXF_GEMM_TILE=256 / 512
@@ -2085,7 +2087,8 @@ oxf_status gemm_run_fused(const oxf_gemm_desc* d, const GemmFuse* fuse, cudaStre
     long long units_w = mt * ((d->N + 511) / 512) * nb;
     long long units_n = mt * ((d->N + 255) / 256) * nb;
     const long long pairs = sms / 2;
-    if (d->accumulate && split <= 1 && !d->bias && !d->residual) {
+    const bool auto_split = d->accumulate && split <= 1 && !d->bias && !d->residual;
+    if (auto_split) {
       // split K as the launch below will, so that the fill compares units
       units_w *= choose_splits(units_w, static_cast<int>(kbl), static_cast<int>(pairs));
       units_n *= choose_splits(units_n, static_cast<int>(kbl), static_cast<int>(pairs));
@@ -2096,10 +2099,16 @@ oxf_status gemm_run_fused(const oxf_gemm_desc* d, const GemmFuse* fuse, cudaStre
     // an activation makes a drain of the same bytes about half as long again
     const bool heavy_epilogue = d->pre_out || d->aux || d->residual || d->beta != 0.0f ||
                                 d->act != OXF_ACT_IDENTITY;
+    // A K-split product whose wide units fit one wave takes them even where
+    // the 256 tile fills the last wave better: the 256 tile gets there only
+    // through several times more K splits, each a unit with its own pipeline
+    // start and drain (config 3's weight gradients: 64 wide units of 2 splits
+    // ran 18-21% faster than 512 narrow units of 8).
+    const bool one_wave_split = auto_split && units_w <= pairs;
     bool wide = d->variant == 3 ||
-                (d->variant == 0 && d->N >= 512 && units_w >= pairs &&
+                (d->variant == 0 && d->N >= 512 && units_w >= (3 * pairs) / 4 &&
                  (kbl >= kWideMinKBlocks || !heavy_epilogue) &&
-                 fill(units_w) >= fill(units_n) - 0.02);
+                 (fill(units_w) >= fill(units_n) - 0.02 || one_wave_split));
     const char* env = std::getenv("OXF_GEMM_TILE");
     if (env && d->variant == 0) {
       if (std::strcmp(env, "256") == 0) wide = false;
