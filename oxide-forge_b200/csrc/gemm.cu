@@ -2087,28 +2087,40 @@ oxf_status gemm_run_fused(const oxf_gemm_desc* d, const GemmFuse* fuse, cudaStre
     long long units_w = mt * ((d->N + 511) / 512) * nb;
     long long units_n = mt * ((d->N + 255) / 256) * nb;
     const long long pairs = sms / 2;
+    auto waves = [pairs](long long u) { return (u + pairs - 1) / pairs; };
+    auto fill = [pairs, waves](long long t) {
+      return static_cast<double>(t) / static_cast<double>(waves(t) * pairs);
+    };
     const bool auto_split = d->accumulate && split <= 1 && !d->bias && !d->residual;
+    // For a K-split product: the estimated time of each tile in 256-tile K
+    // blocks. A wave of units costs its K blocks (a wide one 1.77: twice the
+    // flops at the wide tile's 13% higher rate) plus about 8 for the unit's
+    // pipeline start and drain.
+    double est_w = 0.0, est_n = 0.0;
     if (auto_split) {
       // split K as the launch below will, so that the fill compares units
-      units_w *= choose_splits(units_w, static_cast<int>(kbl), static_cast<int>(pairs));
-      units_n *= choose_splits(units_n, static_cast<int>(kbl), static_cast<int>(pairs));
+      const int sw = choose_splits(units_w, static_cast<int>(kbl), static_cast<int>(pairs));
+      const int sn = choose_splits(units_n, static_cast<int>(kbl), static_cast<int>(pairs));
+      units_w *= sw;
+      units_n *= sn;
+      est_w = static_cast<double>(waves(units_w)) * (1.77 * ((kbl + sw - 1) / sw) + 8.0);
+      est_n = static_cast<double>(waves(units_n)) * (static_cast<double>((kbl + sn - 1) / sn) + 8.0);
     }
-    auto fill = [pairs](long long t) {
-      return static_cast<double>(t) / static_cast<double>(((t + pairs - 1) / pairs) * pairs);
-    };
     // an activation makes a drain of the same bytes about half as long again
     const bool heavy_epilogue = d->pre_out || d->aux || d->residual || d->beta != 0.0f ||
                                 d->act != OXF_ACT_IDENTITY;
-    // A K-split product whose wide units fit one wave takes them even where
-    // the 256 tile fills the last wave better: the 256 tile gets there only
-    // through several times more K splits, each a unit with its own pipeline
-    // start and drain (config 3's weight gradients: 64 wide units of 2 splits
-    // ran 18-21% faster than 512 narrow units of 8).
-    const bool one_wave_split = auto_split && units_w <= pairs;
+    // A K-split product also takes wide tiles where the 256 tile fills the
+    // last wave better but only through several times more K splits, each a
+    // unit with its own pipeline start and drain, so that its estimated time
+    // is longer: config 3's weight gradients ran 18-21% faster on 64 wide
+    // units of 2 splits than on 512 narrow units of 8, and the Q/K/V weight
+    // gradients of a 16-sequence training step 16% faster on 288 wide units
+    // of 3 splits than on 960 narrow units of 5.
+    const bool split_prefers_wide = auto_split && est_w <= est_n;
     bool wide = d->variant == 3 ||
                 (d->variant == 0 && d->N >= 512 && units_w >= (3 * pairs) / 4 &&
                  (kbl >= kWideMinKBlocks || !heavy_epilogue) &&
-                 (fill(units_w) >= fill(units_n) - 0.02 || one_wave_split));
+                 (fill(units_w) >= fill(units_n) - 0.02 || split_prefers_wide));
     const char* env = std::getenv("OXF_GEMM_TILE");
     if (env && d->variant == 0) {
       if (std::strcmp(env, "256") == 0) wide = false;
