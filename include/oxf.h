@@ -266,6 +266,33 @@ void oxf_gemm_desc_init(oxf_gemm_desc* d, int M, int N, int K, int a_trans, int 
 size_t oxf_gemm_workspace_size(const oxf_gemm_desc* d);
 oxf_status oxf_gemm(const oxf_gemm_desc* d, oxf_stream stream);
 
+/* Which kernel oxf_gemm runs a descriptor on, with what tile, K splits and
+ * raster: the library's own choice, reported for integrators tuning their
+ * shapes and for tests of that choice. No counterpart in the reference,
+ * whose GEMM has one 32 x 32 tiling (gemm.rs:202-373). Nothing is launched
+ * and the operand pointers are only checked for alignment. sm_count <= 0
+ * asks the current device (a GPU is then needed); > 0 plans for that many
+ * SMs (148 on B200). Invalid descriptors get oxf_gemm's errors. */
+typedef enum {
+  OXF_GEMM_PATH_NONE = 0,     /* M or N is 0: nothing runs */
+  OXF_GEMM_PATH_SIMT = 1,     /* operands TMA cannot read, K = 0, or OXF_PREC_F32 */
+  OXF_GEMM_PATH_TINY = 2,     /* a tiny TF32 product on the CUDA cores */
+  OXF_GEMM_PATH_ONE_CTA = 3,  /* tcgen05, one CTA per 128-row tile */
+  OXF_GEMM_PATH_CTA_PAIR = 4  /* tcgen05 cta_group::2, a CTA pair per 256-row tile */
+} oxf_gemm_path;
+typedef struct {
+  int path;        /* oxf_gemm_path */
+  int tile_m;      /* output tile rows (per CTA pair on the pair path) */
+  int tile_n;      /* output tile columns */
+  int stages;      /* operand ring stages (tensor-core paths) */
+  int staging;     /* epilogue staging tiles per warp */
+  int splits;      /* K splits (1: none) */
+  int group_m;     /* tile rows per raster group (1: N fastest) */
+  int zero_c;      /* 1: C is zeroed first and the K splits add into it */
+  long long units; /* work units: tiles x splits (tiles for SIMT and tiny) */
+} oxf_gemm_plan_info;
+oxf_status oxf_gemm_plan(const oxf_gemm_desc* d, int sm_count, oxf_gemm_plan_info* out);
+
 /* oxf_gemm in 3xTF32 precision without any allocation, for callers that
  * cannot call cudaMalloc: plugin hosts that own the device memory budget
  * through their own allocator, and latency-critical paths that must not

@@ -49,6 +49,19 @@ pub struct oxf_exchange_desc {
 
 #[repr(C)] #[derive(Clone, Copy)] pub struct oxf_ipc_handle { pub handle: [u8; 64], pub offset: u64 }
 
+pub const OXF_GEMM_PATH_NONE: c_int = 0;
+pub const OXF_GEMM_PATH_SIMT: c_int = 1;
+pub const OXF_GEMM_PATH_TINY: c_int = 2;
+pub const OXF_GEMM_PATH_ONE_CTA: c_int = 3;
+pub const OXF_GEMM_PATH_CTA_PAIR: c_int = 4;
+
+#[repr(C)] #[derive(Clone, Copy)]
+pub struct oxf_gemm_plan_info {
+    pub path: c_int, pub tile_m: c_int, pub tile_n: c_int, pub stages: c_int,
+    pub staging: c_int, pub splits: c_int, pub group_m: c_int, pub zero_c: c_int,
+    pub units: i64,
+}
+
 #[repr(C)] #[derive(Clone, Copy)]
 pub struct oxf_layer_spec { pub in_: c_int, pub out: c_int, pub act: c_int, pub bias: c_int }
 #[repr(C)] #[derive(Clone, Copy)]
@@ -139,6 +152,8 @@ extern "C" {
                               C: *mut f32);
     pub fn oxf_gemm_workspace_size(d: *const oxf_gemm_desc) -> usize;
     pub fn oxf_gemm(d: *const oxf_gemm_desc, stream: oxf_stream) -> oxf_status;
+    pub fn oxf_gemm_plan(d: *const oxf_gemm_desc, sm_count: c_int,
+                         out: *mut oxf_gemm_plan_info) -> oxf_status;
     pub fn oxf_gemm_tf32x3_noalloc(desc: *const oxf_gemm_desc, stream: oxf_stream) -> oxf_status;
     pub fn oxf_attention_stats_floats(batch: c_int, seq: c_int) -> usize;
     pub fn oxf_attention_forward(q: *const f32, k: *const f32, v: *const f32,

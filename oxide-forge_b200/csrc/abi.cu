@@ -59,6 +59,7 @@ oxf_status gemm_refalgo(const float*, const float*, float*, size_t, size_t, size
 oxf_status gemm_read_device_error(uint32_t*);
 oxf_status wait_selftest(unsigned long long, int*, cudaStream_t);
 oxf_status gemm_tf32x3_noalloc(const oxf_gemm_desc*, cudaStream_t);
+oxf_status gemm_plan_report(const oxf_gemm_desc*, int, oxf_gemm_plan_info*);
 long long attention_stats_parts(long long);
 oxf_status attention_forward(const float*, const float*, const float*, const float*, float*,
                              float*, float*, int, int, int, int, float, int, cudaStream_t);
@@ -466,6 +467,12 @@ oxf_status oxf_gemm(const oxf_gemm_desc* d, oxf_stream stream) {
   if (d && (!valid_act(d->act) || !valid_act(d->grad_act)))
     return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm: bad activation");
   return gemm_run(d, S(stream));
+}
+
+oxf_status oxf_gemm_plan(const oxf_gemm_desc* d, int sm_count, oxf_gemm_plan_info* out) {
+  if (d && (!valid_act(d->act) || !valid_act(d->grad_act)))
+    return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm_plan: bad activation");
+  return gemm_plan_report(d, sm_count, out);
 }
 
 oxf_status oxf_gemm_tf32x3_noalloc(const oxf_gemm_desc* d, oxf_stream stream) {

@@ -1894,6 +1894,196 @@ bool gemm_tensor_core_path(const oxf_gemm_desc* d) {
          d->precision != OXF_PREC_F32;
 }
 
+// The kernel a tensor-core product runs on, its tile, K splits and raster:
+// a pure function of the descriptor and the SM count, so that the rule can
+// be reported (oxf_gemm_plan) and tested without a GPU.
+struct GemmPlan {
+  int bn = 256;            // tile width along N (per CTA pair for pair tiles)
+  bool pair = false;       // a CTA pair per 256-row tile, else one CTA per 128 rows
+  bool split3 = false;     // 3xTF32: hi/lo operand splits, three MMAs per K step
+  bool zero_c = false;     // a plain product whose K splits add into a zeroed C
+  int stages = 0;          // operand ring stages
+  int staging = 1;         // epilogue staging tiles per warp
+  int bm = BM, tiles_m = 0, tiles_n = 0, group_m = 1;
+  int kblocks_item = 0, kblocks = 0, splits = 1;
+  long long units = 0;
+};
+
+GemmPlan plan_gemm(const oxf_gemm_desc* d, bool fused, bool fused_transform, int sms) {
+  GemmPlan p;
+  const int split = d->split_k > 1 ? d->split_k : 1;
+  const bool reduce = d->reduce_batch && d->batch > 1;
+  const bool split3 = d->precision == OXF_PREC_TF32X3;
+  p.split3 = split3;
+  // Tile width along N.
+  // The one-CTA 3xTF32 kernel is instantiated for BN = 128 only.
+  int BN = 256;
+  if (split3 || d->N <= 128) BN = 128;
+  if (!split3 && d->N <= 64) BN = 64;
+  if (!split3 && BN == 256) {
+    const long long t256 = static_cast<long long>((d->M + BM - 1) / BM) * ((d->N + 255) / 256) *
+                           d->batch;
+    if (t256 < sms && !d->accumulate) BN = 128;  // more, smaller tiles when the grid is thin
+  }
+  // A plain product: nothing in the epilogue but alpha, so K may be split.
+  const bool plain = !fused && d->variant == 0 && !split3 && !d->accumulate && split <= 1 &&
+                     d->beta == 0.0f && !d->bias && !d->residual && !d->pre_out && !d->aux &&
+                     d->act == OXF_ACT_IDENTITY && !reduce && d->batch == 1;
+  // A small plain product (at most half a wave of 128 x 64 tiles, K <= 1024;
+  // 512^3 has 32) runs on one-CTA 128 x 64 tiles, K split as below: a pair
+  // tile's longer set-up and per-tile drain outweigh its operand savings
+  // there (512^3: 9 against 13 us per call).
+  const bool small_tiles =
+      plain && (d->K + BK - 1) / BK <= 32 &&
+      static_cast<long long>((d->M + BM - 1) / BM) * ((d->N + 63) / 64) * 2 <= sms;
+  if (small_tiles) BN = 64;
+  // CTA pairs (256 x 256 tiles, half the L2->SM bytes per flop of a one-CTA
+  // tile) whenever there are enough of them to occupy every SM pair;
+  // variant 1 forces one CTA, 2 forces pairs.
+  bool pair = false, autosplit = false;
+  {
+    const long long tiles2 = static_cast<long long>((d->M + 2 * BM - 1) / (2 * BM)) *
+                             ((d->N + 255) / 256) * (d->reduce_batch ? 1 : d->batch);
+    // An accumulating product with long K reaches every pair through K
+    // splits even when it has fewer tiles than pairs (weight gradients).
+    const bool splittable = d->accumulate && split <= 1 && !d->bias && !d->residual &&
+                            static_cast<long long>((d->K + BK - 1) / BK) *
+                                    (d->reduce_batch ? d->batch : 1) >= 2 * kWideMinKBlocks;
+    // A plain product (nothing in the epilogue but alpha) with too few tiles
+    // to fill the GPU splits K: C is zeroed and the splits add into it.
+    autosplit = plain && d->M >= 2 * BM && tiles2 < (3 * sms / 2) / 4 &&
+                (d->K + BK - 1) / BK >= 16;
+    // One partly filled wave of pairs (at least 3/4 of them busy) beats
+    // 1.5-2 waves of one-CTA tiles with twice the operand bytes per flop.
+    const long long pair_min = (3 * (sms / 2)) / 4;
+    pair = fused || d->variant == 2 || d->variant == 3 ||
+           (d->variant == 0 && !small_tiles && d->M >= 2 * BM &&
+            (tiles2 >= pair_min || splittable || autosplit));
+    if (pair) BN = 256;
+  }
+  // Wide pair tiles (256 x 512): a quarter fewer operand bytes per flop
+  // through L2, but a tile fills TMEM, so its epilogue no longer overlaps the
+  // next tile's MMAs. Taken whenever the fewer, larger tiles fill the last
+  // wave of CTA pairs about as well and keep at least 3/4 of the pairs busy
+  // (config 3's 8192-row products: 64 wide units, against 64 or 128 on the
+  // 256 tile, run 3-18% faster wide), except for short-K products whose
+  // epilogue reads an input tile, writes a second output or applies an
+  // activation: there the exposed epilogue outweighs the saved bytes, and
+  // the 256-wide tile's two accumulators hide it. OXF_GEMM_TILE=256 / 512
+  // overrides the choice.
+  if (pair && !split3) {
+    const long long kbl = static_cast<long long>((d->K + BK - 1) / BK) *
+                          (d->reduce_batch ? d->batch : 1);
+    const long long mt = (d->M + 2 * BM - 1) / (2 * BM), nb = d->reduce_batch ? 1 : d->batch;
+    long long units_w = mt * ((d->N + 511) / 512) * nb;
+    long long units_n = mt * ((d->N + 255) / 256) * nb;
+    const long long pairs = sms / 2;
+    auto waves = [pairs](long long u) { return (u + pairs - 1) / pairs; };
+    auto fill = [pairs, waves](long long t) {
+      return static_cast<double>(t) / static_cast<double>(waves(t) * pairs);
+    };
+    const bool auto_split = d->accumulate && split <= 1 && !d->bias && !d->residual;
+    // For a K-split product: the estimated time of each tile in 256-tile K
+    // blocks. A wave of units costs its K blocks (a wide one 1.77: twice the
+    // flops at the wide tile's 13% higher rate) plus about 8 for the unit's
+    // pipeline start and drain.
+    double est_w = 0.0, est_n = 0.0;
+    if (auto_split) {
+      // split K as the launch below will, so that the fill compares units
+      const int sw = choose_splits(units_w, static_cast<int>(kbl), static_cast<int>(pairs));
+      const int sn = choose_splits(units_n, static_cast<int>(kbl), static_cast<int>(pairs));
+      units_w *= sw;
+      units_n *= sn;
+      est_w = static_cast<double>(waves(units_w)) * (1.77 * ((kbl + sw - 1) / sw) + 8.0);
+      est_n = static_cast<double>(waves(units_n)) * (static_cast<double>((kbl + sn - 1) / sn) + 8.0);
+    }
+    // an activation makes a drain of the same bytes about half as long again
+    const bool heavy_epilogue = d->pre_out || d->aux || d->residual || d->beta != 0.0f ||
+                                d->act != OXF_ACT_IDENTITY;
+    // A K-split product also takes wide tiles where the 256 tile fills the
+    // last wave better but only through several times more K splits, each a
+    // unit with its own pipeline start and drain, so that its estimated time
+    // is longer: config 3's weight gradients ran 18-21% faster on 64 wide
+    // units of 2 splits than on 512 narrow units of 8, and the Q/K/V weight
+    // gradients of a 16-sequence training step 16% faster on 288 wide units
+    // of 3 splits than on 960 narrow units of 5.
+    const bool split_prefers_wide = auto_split && est_w <= est_n;
+    bool wide = d->variant == 3 ||
+                (d->variant == 0 && d->N >= 512 && units_w >= (3 * pairs) / 4 &&
+                 (kbl >= kWideMinKBlocks || !heavy_epilogue) &&
+                 (fill(units_w) >= fill(units_n) - 0.02 || split_prefers_wide));
+    const char* env = std::getenv("OXF_GEMM_TILE");
+    if (env && d->variant == 0) {
+      if (std::strcmp(env, "256") == 0) wide = false;
+      if (std::strcmp(env, "512") == 0) wide = d->N >= 512;
+    }
+    // fused attention products: 256-wide tiles, whose two accumulators let the
+    // heavier epilogue (scores) or the 4-warp epilogue (P·V) overlap the MMAs;
+    // the transform kernel is instantiated at 256 only
+    if (fused) wide = false;
+    if (wide) BN = 512;
+  }
+  p.bm = pair ? 2 * BM : BM;
+  p.tiles_m = (d->M + p.bm - 1) / p.bm;
+  p.tiles_n = (d->N + BN - 1) / BN;
+  // Raster order for L2 reuse. Concurrent tiles share A panels along a
+  // tile row and B panels along a tile column. With few column tiles (N up
+  // to 16 tiles) walk N fastest, so a handful of row panels and every
+  // column panel stay hot; with many, walk M fastest inside groups of 16
+  // tile rows. Both measured the lowest DRAM traffic on the transformer's
+  // GEMMs (e.g. 2.0 GB vs 3.5 GB for a 32768 x 8192 x 2048 product).
+  p.group_m = p.tiles_n <= 16 ? 1 : 16;
+  if (const char* g = std::getenv("OXF_GEMM_GROUP_M")) {  // measurement override
+    const int v = std::atoi(g);
+    if (v >= 1) p.group_m = std::min(v, p.tiles_m);
+  }
+  p.kblocks_item = (d->K + BK - 1) / BK;
+  p.kblocks = p.kblocks_item * (reduce ? d->batch : 1);
+  const long long tiles =
+      static_cast<long long>(p.tiles_m) * p.tiles_n * (reduce ? 1 : d->batch);
+  if (d->accumulate) {
+    // Each K split adds its partial product into C, so terms added once per
+    // output (bias, residual) rule splitting out.
+    const bool additive = d->bias != nullptr || d->residual != nullptr;
+    // waves are counted in CTA pairs for pair tiles
+    p.splits = split > 1 ? std::min(split, p.kblocks)
+                         : (additive ? 1 : choose_splits(tiles, p.kblocks, pair ? sms / 2 : sms));
+  } else if (autosplit) {
+    p.splits = choose_splits(tiles, p.kblocks, pair ? sms / 2 : sms);
+    p.zero_c = p.splits > 1;  // the splits add into C, which starts at zero
+  } else {
+    p.splits = 1;
+  }
+  p.units = tiles * p.splits;
+  p.units = tiles * p.splits;
+  p.bn = BN;
+  p.pair = pair;
+  // Ring depth and epilogue staging of the kernel the launch picks. A wide
+  // tile's epilogue is exposed (one accumulator), so its warps stage through
+  // two tiles each, with a ring stage fewer, when the epilogue reads an
+  // input tile, writes a pre-activation, adds into C, or has little K to
+  // hide behind: a chunk's TMA loads and stores then overlap the previous
+  // chunk's. Plain long-K products keep the fourth ring stage (measured 2-4%
+  // faster there). On 256-wide tiles the epilogue hides behind the next
+  // tile's MMAs, and a second staging tile measured no gain.
+  if (fused_transform) {
+    p.stages = 6;
+    p.staging = 2;
+  } else if (split3) {
+    p.stages = 3;
+  } else if (pair && BN == 512) {
+    const bool two_staging = p.kblocks < kWideMinKBlocks || d->accumulate || p.zero_c ||
+                             d->residual || d->pre_out || d->aux || d->beta != 0.0f;
+    p.stages = two_staging ? 3 : 4;
+    p.staging = two_staging ? 2 : 1;
+  } else if (pair) {
+    p.stages = 6;
+  } else {
+    p.stages = BN == 256 ? 4 : BN == 128 ? 6 : 8;
+  }
+  return p;
+}
+
 }  // namespace
 
 // Softmax fused into an attention product (the GemmArgs fields of the same
@@ -2023,154 +2213,27 @@ oxf_status gemm_run_fused(const oxf_gemm_desc* d, const GemmFuse* fuse, cudaStre
     sb = d->stride_b ? b_inner * b_outer : 0;
   }
 
-  // Tile width along N.
   const int sms = sm_count(dev);
-  // The one-CTA 3xTF32 kernel is instantiated for BN = 128 only.
-  int BN = 256;
-  if (split3 || d->N <= 128) BN = 128;
-  if (!split3 && d->N <= 64) BN = 64;
-  if (!split3 && BN == 256) {
-    const long long t256 = static_cast<long long>((d->M + BM - 1) / BM) * ((d->N + 255) / 256) *
-                           d->batch;
-    if (t256 < sms && !d->accumulate) BN = 128;  // more, smaller tiles when the grid is thin
+  const GemmPlan plan =
+      plan_gemm(d, fuse != nullptr, fuse != nullptr && fuse->stats_in != nullptr, sms);
+  const int BN = plan.bn;
+  const bool pair = plan.pair;
+  a.bm = plan.bm;
+  a.tiles_m = plan.tiles_m;
+  a.tiles_n = plan.tiles_n;
+  a.group_m = plan.group_m;
+  a.kblocks_item = plan.kblocks_item;
+  a.kblocks = plan.kblocks;
+  a.splits = plan.splits;
+  a.units = plan.units;
+  if (plan.zero_c) {
+    oxf_status zs = check_cuda(cudaMemset2DAsync(d->C, static_cast<size_t>(d->ldc) * 4, 0,
+                                                 static_cast<size_t>(d->N) * 4,
+                                                 static_cast<size_t>(d->M), stream),
+                               "oxf_gemm: zeroing C for split K");
+    if (zs != OXF_OK) return zs;
+    a.accumulate = 1;
   }
-  // A plain product: nothing in the epilogue but alpha, so K may be split.
-  const bool plain = !fuse && d->variant == 0 && !split3 && !d->accumulate && split <= 1 &&
-                     d->beta == 0.0f && !d->bias && !d->residual && !d->pre_out && !d->aux &&
-                     d->act == OXF_ACT_IDENTITY && !a.reduce_batch && d->batch == 1;
-  // A small plain product (at most half a wave of 128 x 64 tiles, K <= 1024;
-  // 512^3 has 32) runs on one-CTA 128 x 64 tiles, K split as below: a pair
-  // tile's longer set-up and per-tile drain outweigh its operand savings
-  // there (512^3: 9 against 13 us per call).
-  const bool small_tiles =
-      plain && (d->K + BK - 1) / BK <= 32 &&
-      static_cast<long long>((d->M + BM - 1) / BM) * ((d->N + 63) / 64) * 2 <= sms;
-  if (small_tiles) BN = 64;
-  // CTA pairs (256 x 256 tiles, half the L2->SM bytes per flop of a one-CTA
-  // tile) whenever there are enough of them to occupy every SM pair;
-  // variant 1 forces one CTA, 2 forces pairs.
-  bool pair = false, autosplit = false;
-  {
-    const long long tiles2 = static_cast<long long>((d->M + 2 * BM - 1) / (2 * BM)) *
-                             ((d->N + 255) / 256) * (d->reduce_batch ? 1 : d->batch);
-    // An accumulating product with long K reaches every pair through K
-    // splits even when it has fewer tiles than pairs (weight gradients).
-    const bool splittable = d->accumulate && split <= 1 && !d->bias && !d->residual &&
-                            static_cast<long long>((d->K + BK - 1) / BK) *
-                                    (d->reduce_batch ? d->batch : 1) >= 2 * kWideMinKBlocks;
-    // A plain product (nothing in the epilogue but alpha) with too few tiles
-    // to fill the GPU splits K: C is zeroed and the splits add into it.
-    autosplit = plain && d->M >= 2 * BM && tiles2 < (3 * sms / 2) / 4 &&
-                (d->K + BK - 1) / BK >= 16;
-    // One partly filled wave of pairs (at least 3/4 of them busy) beats
-    // 1.5-2 waves of one-CTA tiles with twice the operand bytes per flop.
-    const long long pair_min = (3 * (sms / 2)) / 4;
-    pair = fuse != nullptr || d->variant == 2 || d->variant == 3 ||
-           (d->variant == 0 && !small_tiles && d->M >= 2 * BM &&
-            (tiles2 >= pair_min || splittable || autosplit));
-    if (pair) BN = 256;
-  }
-  // Wide pair tiles (256 x 512): a quarter fewer operand bytes per flop
-  // through L2, but a tile fills TMEM, so its epilogue no longer overlaps the
-  // next tile's MMAs. Taken whenever the fewer, larger tiles fill the last
-  // wave of CTA pairs about as well and keep at least 3/4 of the pairs busy
-  // (config 3's 8192-row products: 64 wide units, against 64 or 128 on the
-  // 256 tile, run 3-18% faster wide), except for short-K products whose
-  // epilogue reads an input tile, writes a second output or applies an
-  // activation: there the exposed epilogue outweighs the saved bytes, and
-  // the 256-wide tile's two accumulators hide it. OXF_GEMM_TILE=256 / 512
-  // overrides the choice.
-  if (pair && !split3) {
-    const long long kbl = static_cast<long long>((d->K + BK - 1) / BK) *
-                          (d->reduce_batch ? d->batch : 1);
-    const long long mt = (d->M + 2 * BM - 1) / (2 * BM), nb = d->reduce_batch ? 1 : d->batch;
-    long long units_w = mt * ((d->N + 511) / 512) * nb;
-    long long units_n = mt * ((d->N + 255) / 256) * nb;
-    const long long pairs = sms / 2;
-    auto waves = [pairs](long long u) { return (u + pairs - 1) / pairs; };
-    auto fill = [pairs, waves](long long t) {
-      return static_cast<double>(t) / static_cast<double>(waves(t) * pairs);
-    };
-    const bool auto_split = d->accumulate && split <= 1 && !d->bias && !d->residual;
-    // For a K-split product: the estimated time of each tile in 256-tile K
-    // blocks. A wave of units costs its K blocks (a wide one 1.77: twice the
-    // flops at the wide tile's 13% higher rate) plus about 8 for the unit's
-    // pipeline start and drain.
-    double est_w = 0.0, est_n = 0.0;
-    if (auto_split) {
-      // split K as the launch below will, so that the fill compares units
-      const int sw = choose_splits(units_w, static_cast<int>(kbl), static_cast<int>(pairs));
-      const int sn = choose_splits(units_n, static_cast<int>(kbl), static_cast<int>(pairs));
-      units_w *= sw;
-      units_n *= sn;
-      est_w = static_cast<double>(waves(units_w)) * (1.77 * ((kbl + sw - 1) / sw) + 8.0);
-      est_n = static_cast<double>(waves(units_n)) * (static_cast<double>((kbl + sn - 1) / sn) + 8.0);
-    }
-    // an activation makes a drain of the same bytes about half as long again
-    const bool heavy_epilogue = d->pre_out || d->aux || d->residual || d->beta != 0.0f ||
-                                d->act != OXF_ACT_IDENTITY;
-    // A K-split product also takes wide tiles where the 256 tile fills the
-    // last wave better but only through several times more K splits, each a
-    // unit with its own pipeline start and drain, so that its estimated time
-    // is longer: config 3's weight gradients ran 18-21% faster on 64 wide
-    // units of 2 splits than on 512 narrow units of 8, and the Q/K/V weight
-    // gradients of a 16-sequence training step 16% faster on 288 wide units
-    // of 3 splits than on 960 narrow units of 5.
-    const bool split_prefers_wide = auto_split && est_w <= est_n;
-    bool wide = d->variant == 3 ||
-                (d->variant == 0 && d->N >= 512 && units_w >= (3 * pairs) / 4 &&
-                 (kbl >= kWideMinKBlocks || !heavy_epilogue) &&
-                 (fill(units_w) >= fill(units_n) - 0.02 || split_prefers_wide));
-    const char* env = std::getenv("OXF_GEMM_TILE");
-    if (env && d->variant == 0) {
-      if (std::strcmp(env, "256") == 0) wide = false;
-      if (std::strcmp(env, "512") == 0) wide = d->N >= 512;
-    }
-    // fused attention products: 256-wide tiles, whose two accumulators let the
-    // heavier epilogue (scores) or the 4-warp epilogue (P·V) overlap the MMAs;
-    // the transform kernel is instantiated at 256 only
-    if (fuse) wide = false;
-    if (wide) BN = 512;
-  }
-  a.bm = pair ? 2 * BM : BM;
-  a.tiles_m = (d->M + a.bm - 1) / a.bm;
-  a.tiles_n = (d->N + BN - 1) / BN;
-  // Raster order for L2 reuse. Concurrent tiles share A panels along a
-  // tile row and B panels along a tile column. With few column tiles (N up
-  // to 16 tiles) walk N fastest, so a handful of row panels and every
-  // column panel stay hot; with many, walk M fastest inside groups of 16
-  // tile rows. Both measured the lowest DRAM traffic on the transformer's
-  // GEMMs (e.g. 2.0 GB vs 3.5 GB for a 32768 x 8192 x 2048 product).
-  a.group_m = a.tiles_n <= 16 ? 1 : 16;
-  if (const char* g = std::getenv("OXF_GEMM_GROUP_M")) {  // measurement override
-    const int v = std::atoi(g);
-    if (v >= 1) a.group_m = std::min(v, a.tiles_m);
-  }
-  a.kblocks_item = (d->K + BK - 1) / BK;
-  a.kblocks = a.kblocks_item * (a.reduce_batch ? d->batch : 1);
-  const long long tiles =
-      static_cast<long long>(a.tiles_m) * a.tiles_n * (a.reduce_batch ? 1 : d->batch);
-  if (d->accumulate) {
-    // Each K split adds its partial product into C, so terms added once per
-    // output (bias, residual) rule splitting out.
-    const bool additive = d->bias != nullptr || d->residual != nullptr;
-    // waves are counted in CTA pairs for pair tiles
-    a.splits = split > 1 ? std::min(split, a.kblocks)
-                         : (additive ? 1 : choose_splits(tiles, a.kblocks, pair ? sms / 2 : sms));
-  } else if (autosplit) {
-    a.splits = choose_splits(tiles, a.kblocks, pair ? sms / 2 : sms);
-    if (a.splits > 1) {
-      oxf_status zs = check_cuda(cudaMemset2DAsync(d->C, static_cast<size_t>(d->ldc) * 4, 0,
-                                                   static_cast<size_t>(d->N) * 4,
-                                                   static_cast<size_t>(d->M), stream),
-                                 "oxf_gemm: zeroing C for split K");
-      if (zs != OXF_OK) return zs;
-      a.accumulate = 1;
-    }
-  } else {
-    a.splits = 1;
-  }
-  a.units = tiles * a.splits;
 
   CUtensorMap ta, tb, ta_lo, tb_lo;
   std::memset(&ta_lo, 0, sizeof(ta_lo));
@@ -2232,17 +2295,9 @@ oxf_status gemm_run_fused(const oxf_gemm_desc* d, const GemmFuse* fuse, cudaStre
   if (split3 && pair)
     return launch_pair<256, 3, true, 1>(ta, tb, ta_lo, tb_lo, em, a, stream, dev);
   if (split3) return launch_tcgen05<128, 3, true>(ta, tb, ta_lo, tb_lo, em, a, stream, dev);
-  // A wide tile's epilogue is exposed (one accumulator), so its warps stage
-  // through two tiles each, with a ring stage fewer, when the epilogue reads
-  // an input tile, writes a pre-activation, adds into C, or has little K to
-  // hide behind: a chunk's TMA loads and stores then overlap the previous
-  // chunk's. Plain long-K products keep the fourth ring stage (measured 2-4%
-  // faster there). On 256-wide tiles the epilogue hides behind the next
-  // tile's MMAs, and a second staging tile measured no gain.
+  // wide tiles: ring depth and staging as the plan gives them
   if (pair && BN == 512) {
-    const bool two_staging = a.kblocks < kWideMinKBlocks || a.accumulate || a.R || a.P || a.X ||
-                             a.beta != 0.0f;
-    if (two_staging) return launch_pair<512, 3, false, 2>(ta, tb, ta, tb, em, a, stream, dev);
+    if (plan.staging == 2) return launch_pair<512, 3, false, 2>(ta, tb, ta, tb, em, a, stream, dev);
     return launch_pair<512, 4, false, 1>(ta, tb, ta, tb, em, a, stream, dev);
   }
   if (pair) return launch_pair<256, 6, false, 1>(ta, tb, ta, tb, em, a, stream, dev);
@@ -2372,6 +2427,57 @@ oxf_status attention_forward(const float* q, const float* k, const float* v, con
                     stream);
   if (st != OXF_OK) return st;
   return gemm_run(&pv, stream);
+}
+
+// The path and kernel oxf_gemm takes for a descriptor, as gemm_run_fused
+// decides it (without fusion); sms <= 0 asks the current device.
+oxf_status gemm_plan_report(const oxf_gemm_desc* d, int sms, oxf_gemm_plan_info* out) {
+  if (!out) return set_error(OXF_ERR_INVALID_ARG, "oxf_gemm_plan: null output");
+  std::memset(out, 0, sizeof(*out));
+  const oxf_status valid = gemm_validate(d);
+  if (valid != OXF_OK) return valid;
+  if (d->M == 0 || d->N == 0) return OXF_OK;  // OXF_GEMM_PATH_NONE
+  const bool reduce = d->reduce_batch && d->batch > 1;
+  if (reduce && (d->stride_c || d->stride_r || d->stride_p || d->stride_x))
+    return set_error(OXF_ERR_INVALID_ARG,
+                     "oxf_gemm: reduce_batch writes one output (output strides must be 0)");
+  if (!gemm_tensor_core_path(d)) {
+    if (reduce)
+      return set_error(OXF_ERR_UNSUPPORTED_SHAPE,
+                       "oxf_gemm: reduce_batch runs on the tensor cores only (16-byte aligned "
+                       "operands, TF32 or TF32X3 precision)");
+    out->path = OXF_GEMM_PATH_SIMT;
+    out->tile_m = out->tile_n = 32;
+    out->splits = 1;
+    out->units = static_cast<long long>((d->M + 31) / 32) * ((d->N + 31) / 32) * d->batch;
+    return OXF_OK;
+  }
+  if (d->variant == 0 && d->precision == OXF_PREC_TF32 && !reduce && d->K <= SMALL_KMAX &&
+      static_cast<double>(d->M) * d->N * d->K * d->batch <= SMALL_MAX_MACS) {
+    out->path = OXF_GEMM_PATH_TINY;
+    out->tile_m = out->tile_n = SMALL_TILE;
+    out->splits = 1;
+    out->units = static_cast<long long>((d->M + SMALL_TILE - 1) / SMALL_TILE) *
+                 ((d->N + SMALL_TILE - 1) / SMALL_TILE) * d->batch;
+    return OXF_OK;
+  }
+  if (sms <= 0) {
+    int dev = 0;
+    const oxf_status st = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+    if (st != OXF_OK) return st;
+    sms = sm_count(dev);
+  }
+  const GemmPlan p = plan_gemm(d, false, false, sms);
+  out->path = p.pair ? OXF_GEMM_PATH_CTA_PAIR : OXF_GEMM_PATH_ONE_CTA;
+  out->tile_m = p.bm;
+  out->tile_n = p.bn;
+  out->stages = p.stages;
+  out->staging = p.staging;
+  out->splits = p.splits;
+  out->group_m = p.group_m;
+  out->zero_c = p.zero_c ? 1 : 0;
+  out->units = p.units;
+  return OXF_OK;
 }
 
 // ---------------------------------------------------------------- no-allocation variant

@@ -58,6 +58,18 @@ class GemmDesc(C.Structure):
     ]
 
 
+# oxf_gemm_plan (oxf.h): the path oxf_gemm takes and its tile, splits, raster.
+GEMM_PATH_NONE, GEMM_PATH_SIMT, GEMM_PATH_TINY, GEMM_PATH_ONE_CTA, GEMM_PATH_CTA_PAIR = range(5)
+
+
+class GemmPlanInfo(C.Structure):
+    _fields_ = [
+        ("path", C.c_int), ("tile_m", C.c_int), ("tile_n", C.c_int), ("stages", C.c_int),
+        ("staging", C.c_int), ("splits", C.c_int), ("group_m", C.c_int), ("zero_c", C.c_int),
+        ("units", C.c_longlong),
+    ]
+
+
 # Peer exchange (oxf.h): limits, device error codes, descriptor and handle.
 EXCHANGE_MAX_RANKS = 8
 EXCHANGE_MAX_BLOCKS = 1024
@@ -132,6 +144,7 @@ _SIGS = {
     "oxf_gemm_workspace_size": (C.c_size_t, [C.POINTER(GemmDesc)]),
     "oxf_gemm": (C.c_int, [C.POINTER(GemmDesc), C.c_void_p]),
     "oxf_gemm_tf32x3_noalloc": (C.c_int, [C.POINTER(GemmDesc), C.c_void_p]),
+    "oxf_gemm_plan": (C.c_int, [C.POINTER(GemmDesc), C.c_int, C.POINTER(GemmPlanInfo)]),
     "oxf_attention_stats_floats": (C.c_size_t, [C.c_int, C.c_int]),
     "oxf_attention_forward": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                         C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,

@@ -73,6 +73,7 @@ def _layouts():
         L.CSlice: ("oxf_cslice", same(L.CSlice)),
         L.Slice: ("oxf_slice", same(L.Slice)),
         L.GemmDesc: ("oxf_gemm_desc", same(L.GemmDesc)),
+        L.GemmPlanInfo: ("oxf_gemm_plan_info", same(L.GemmPlanInfo)),
         L.IpcHandle: ("oxf_ipc_handle", same(L.IpcHandle)),
         L.ExchangeDesc: ("oxf_exchange_desc", same(L.ExchangeDesc)),
         H.LayerSpec: ("oxf_layer_spec", same(H.LayerSpec, in_="in")),
@@ -94,6 +95,9 @@ _CONSTANTS = {
     "UNARY_ACT_FORWARD": "OXF_UNARY_ACT_FORWARD", "UNARY_ACT_DERIV": "OXF_UNARY_ACT_DERIV",
     "UNARY_HALF_SQUARE": "OXF_UNARY_HALF_SQUARE",
     "PREC_TF32": "OXF_PREC_TF32", "PREC_TF32X3": "OXF_PREC_TF32X3", "PREC_F32": "OXF_PREC_F32",
+    "GEMM_PATH_NONE": "OXF_GEMM_PATH_NONE", "GEMM_PATH_SIMT": "OXF_GEMM_PATH_SIMT",
+    "GEMM_PATH_TINY": "OXF_GEMM_PATH_TINY", "GEMM_PATH_ONE_CTA": "OXF_GEMM_PATH_ONE_CTA",
+    "GEMM_PATH_CTA_PAIR": "OXF_GEMM_PATH_CTA_PAIR",
     "NORM_RMS": "OXF_NORM_RMS", "NORM_LAYER": "OXF_NORM_LAYER",
     "EXCHANGE_MAX_RANKS": "OXF_EXCHANGE_MAX_RANKS",
     "EXCHANGE_MAX_BLOCKS": "OXF_EXCHANGE_MAX_BLOCKS",
