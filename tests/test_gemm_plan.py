@@ -81,6 +81,29 @@ def test_config5_training_products(L):
     assert kernel(dw1) == (PAIR, 256, 512, 3, 2) and dw1.splits == 15 and dw1.units == 1920
 
 
+def test_config4_inference_products(L):
+    """64 sequences x 2048 tokens, hidden 1024, FFN 4096: as in the config-4
+    launch list, P.V + residual and FFN1 (GELU, K = 1024) stay on the 256-wide
+    tile, everything else takes the 256 x 512 tile with two staging tiles."""
+    T, S, H, F = 131072, 2048, 1024, 4096
+    wide2 = (PAIR, 256, 512, 3, 2)
+    assert kernel(plan(L, T, H, H)) == wide2                                   # Q|K|V, y
+    assert kernel(plan(L, S, S, H, b_trans=True, batch=64)) == wide2           # scores
+    assert kernel(plan(L, S, H, S, batch=64, residual=True)) == (PAIR, 256, 256, 6, 1)
+    assert kernel(plan(L, T, F, H, act=L.ACT_GELU)) == (PAIR, 256, 256, 6, 1)  # FFN1
+    assert kernel(plan(L, T, H, F, residual=True)) == wide2                    # FFN2
+
+
+def test_one_rank_share_at_eight_gpus(L):
+    """16 sequences of config 5 (one rank's share at N = 8)."""
+    t = 16384
+    dwo = plan(L, 2048, 2048, t, a_trans=True, accumulate=True)
+    assert (dwo.tile_n, dwo.splits, dwo.units) == (512, 9, 288)
+    dw2 = plan(L, 8192, 2048, t, a_trans=True, accumulate=True)
+    assert (dw2.tile_n, dw2.splits, dw2.units) == (512, 4, 512)
+    assert kernel(plan(L, t, 8192, 2048, pre_out=True, act=L.ACT_GELU)) == (PAIR, 256, 256, 6, 1)
+
+
 def test_k_split_products_compare_estimated_times(L):
     """Weight gradients take wide tiles with few splits where the 256 tile
     would need several times more (config 3; one rank's share at N = 8)."""
