@@ -168,3 +168,23 @@ def test_plan_rejects_what_oxf_gemm_rejects(L):
     assert L.lib().oxf_gemm_plan(None, SMS, C.byref(out)) == L.INVALID_ARG
     L.lib().oxf_gemm_desc_init(C.byref(d), 4, 4, 4, 0, 0, ALIGNED, ALIGNED, ALIGNED)
     assert L.lib().oxf_gemm_plan(C.byref(d), SMS, None) == L.INVALID_ARG
+
+
+@pytest.mark.gpu
+def test_plan_for_the_current_device(L):
+    """sm_count 0 plans for the current GPU: on a B200 (148 SMs) it is the
+    148-SM plan the tests above pin."""
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    torch.cuda.set_device(0)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    shapes = [dict(M=131072, N=2048, K=8192, residual=True),
+              dict(M=4096, N=1024, K=8192, a_trans=True, accumulate=True),
+              dict(M=1024, N=1024, K=1024)]
+    for kw in shapes:
+        here = plan(L, sms=0, **kw)
+        want = plan(L, sms=sms, **kw)
+        assert (here.path, here.tile_m, here.tile_n, here.stages, here.staging, here.splits,
+                here.units) == (want.path, want.tile_m, want.tile_n, want.stages,
+                                want.staging, want.splits, want.units), kw
