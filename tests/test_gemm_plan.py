@@ -2,7 +2,7 @@
 
 The plan is a pure function of the descriptor and the SM count (148 on
 B200), so these tests pin, on CPU, the tile and K-split rule that the GPU
-parity tests and the measurements in profiles/ were taken with: each
+parity tests and the ncu measurements were taken with: each
 configuration's products, the small-product paths, and the fallbacks. The
 operand pointers only need the alignment TMA asks for; nothing is read.
 """
