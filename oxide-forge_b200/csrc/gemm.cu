@@ -1965,8 +1965,8 @@ GemmPlan plan_gemm(const oxf_gemm_desc* d, bool fused, bool fused_transform, int
   // through L2, but a tile fills TMEM, so its epilogue no longer overlaps the
   // next tile's MMAs. Taken whenever the fewer, larger tiles fill the last
   // wave of CTA pairs about as well and keep at least 3/4 of the pairs busy
-  // (config 3's 8192-row products: 64 wide units, against 64 or 128 on the
-  // 256 tile, run 3-18% faster wide), except for short-K products whose
+  // (config 3's residual products: 64 wide units in one partial wave ran 3%
+  // faster than 128 narrow ones in 1.73 waves), except for short-K products whose
   // epilogue reads an input tile, writes a second output or applies an
   // activation: there the exposed epilogue outweighs the saved bytes, and
   // the 256-wide tile's two accumulators hide it. OXF_GEMM_TILE=256 / 512
