@@ -877,6 +877,36 @@ __global__ void sum_cols_kernel(const float* __restrict__ m, float* __restrict__
   }
 }
 
+// Column sums of a wide, short matrix (the position gradient: a few
+// sequences' rows, S*H columns), where one strip of rows already covers the
+// matrix: each thread owns four columns and sums all rows in order with
+// 16-byte loads, four rows in flight at a time, and writes (or adds into)
+// its outputs without atomics.
+__global__ void sum_cols_vec_kernel(const float4* __restrict__ m, float4* __restrict__ out,
+                                    long long rows, long long cols4, int accumulate) {
+  pdl_enter();
+  const long long c = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (c >= cols4) return;
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  auto add = [&s](const float4 v) {
+    s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+  };
+  long long r = 0;
+  for (; r + 4 <= rows; r += 4) {
+    const float4 a = __ldcs(m + r * cols4 + c);
+    const float4 b = __ldcs(m + (r + 1) * cols4 + c);
+    const float4 e = __ldcs(m + (r + 2) * cols4 + c);
+    const float4 f = __ldcs(m + (r + 3) * cols4 + c);
+    add(a); add(b); add(e); add(f);
+  }
+  for (; r < rows; ++r) add(__ldcs(m + r * cols4 + c));
+  if (accumulate) {
+    const float4 o = out[c];
+    s = make_float4(o.x + s.x, o.y + s.y, o.z + s.z, o.w + s.w);
+  }
+  out[c] = s;
+}
+
 // layout.rs:9-55: 32x32 tiles through padded shared memory.
 __global__ void transpose_kernel(const float* __restrict__ in, float* __restrict__ out,
                                  long long rows, long long cols) {
@@ -1252,6 +1282,18 @@ oxf_status causal_mask(float* m, long long rows, long long cols, cudaStream_t s)
 oxf_status cols_sum(const float* m, float* out, long long rows, long long cols, int accumulate,
                     cudaStream_t s) {
   if (cols == 0) return OXF_OK;
+  // Wide and short (fewer rows than one strip of the strip kernel takes):
+  // one thread per four columns, no atomics.
+  if (rows > 0 && rows <= 128 && cols % 4 == 0 && aligned16(m) && aligned16(out) &&
+      (cols + 31) / 32 >= 2ll * sm_count_rows() * 4) {
+    const long long cols4 = cols / 4;
+    if ((cols4 + 255) / 256 > 0x7fffffffll)
+      return set_error(OXF_ERR_UNSUPPORTED_SHAPE, "too many columns");
+    return launch_pdl("sum_cols_vec_kernel", sum_cols_vec_kernel,
+                      dim3(static_cast<unsigned>((cols4 + 255) / 256)), dim3(256), s,
+                      reinterpret_cast<const float4*>(m), reinterpret_cast<float4*>(out), rows,
+                      cols4, accumulate);
+  }
   if (!accumulate) {
     oxf_status st = check_cuda(cudaMemsetAsync(out, 0, cols * 4, s), "memset");
     if (st != OXF_OK) return st;

@@ -162,6 +162,21 @@ def test_row_and_column_sums(K, rng):
         assert rel_err(host(outc), 2 * O.sum_cols(x)) < 1e-5
 
 
+@pytest.mark.parametrize("rows", [1, 6, 16, 128])
+def test_column_sums_of_wide_short_matrices(K, rng, rows):
+    """The position gradient's shape: a few sequences' rows of S*H = 2^21
+    columns (config 5), summed and accumulated into an existing gradient."""
+    cols = 1 << 21 if rows <= 16 else 1 << 18
+    x = rng.standard_normal((rows, cols)).astype(np.float32)
+    want = x.astype(np.float64).sum(axis=0)
+    outc = torch.empty(cols, device="cuda")
+    got = host(K.sum_cols(dev(x), outc))
+    assert np.abs(got - want).max() <= 1e-5 * max(1.0, np.abs(x).sum(axis=0).max())
+    assert rel_err(got, O.sum_cols(x)) < 1e-5
+    K.sum_cols(dev(x), outc, accumulate=True)
+    assert np.abs(host(outc) - 2 * want).max() <= 2e-5 * max(1.0, np.abs(x).sum(axis=0).max())
+
+
 def test_loss_rows_and_mse_grad(K, rng):
     for r, c in cases(rng, widths=[1, 36, 1024, 2048, 20000]):
         y = rng.standard_normal((r, c)).astype(np.float32)
