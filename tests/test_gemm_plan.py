@@ -151,6 +151,19 @@ def test_small_and_fallback_paths(L):
     assert kernel(plan(L, 8192, 8192, 8192, variant=2))[:3] == (PAIR, 256, 256)
 
 
+def test_measurement_overrides(L, monkeypatch):
+    """OXF_GEMM_TILE and OXF_GEMM_GROUP_M, read at every call, change the
+    plan as they change the launch (tile width, raster group)."""
+    monkeypatch.setenv("OXF_GEMM_TILE", "256")
+    assert plan(L, 8192, 8192, 8192).tile_n == 256
+    monkeypatch.setenv("OXF_GEMM_TILE", "512")
+    assert plan(L, 131072, 8192, 2048, pre_out=True, act=L.ACT_GELU).tile_n == 512
+    monkeypatch.delenv("OXF_GEMM_TILE")
+    assert plan(L, 131072, 8192, 2048, pre_out=True, act=L.ACT_GELU).group_m == 16
+    monkeypatch.setenv("OXF_GEMM_GROUP_M", "4")
+    assert plan(L, 131072, 8192, 2048, pre_out=True, act=L.ACT_GELU).group_m == 4
+
+
 def test_plan_scales_with_sm_count(L):
     """The wave arithmetic follows the SM count it is given: config 3's dW2
     takes 2 K splits on 74 CTA pairs, and 8 on 37 (four waves of 64)."""
